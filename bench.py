@@ -1,0 +1,323 @@
+"""Benchmark of the B200 MXFP4 MoE layer (the reference's headline metric:
+MoE layer tokens/s, decode HBM GB/s, prefill tensor throughput vs peak).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload at N = 1: BASELINE configs[3], the GPT-OSS-20B-shaped MoE layer
+prefill (hidden 2880, intermediate 2880, 32 experts, top-4, 8192 tokens, bf16
+activations, MXFP4 weights), seeded synthetic inputs (no dataset or
+checkpoint exists here).  A step is one full layer forward (router, permute,
+W1 + SwiGLU, W2, combine).  At N > 1 each rank runs its own 8192-token batch
+with the experts sharded expert-parallel (E / N per GPU) and the routed pairs
+exchanged by NCCL all-to-all (weak scaling).
+
+--impl reference times the CPU restatement of the reference's path (the
+reference's own Rust/wgpu code cannot be built or run on this box) on a
+bounded token sample per step, on all host cores; rank 0 only.
+"""
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path[:0] = [os.path.join(ROOT, "burn-extended_b200"), os.path.join(ROOT, "oracle")]
+
+import numpy as np  # noqa: E402
+
+METRIC = "MoE layer tokens/s (GPT-OSS-20B-shaped MXFP4 layer, prefill 8192 tokens/GPU)"
+UNIT = "tokens/s"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return j["hbm_gbs"], j["bf16_tflops"], j["bf16_tflops_sustained"], "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.tmp.flush()
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    return world, rank, local
+
+
+def cpu_reference(inp, sample_tokens, nthreads=0):
+    import oracle
+    c = oracle.cfg(inp.d, inp.f, inp.E, inp.k)
+    xs = inp.x[:sample_tokens]
+    t0 = time.perf_counter()
+    oracle.moe_forward(c, xs, inp.gamma, inp.gate_w, inp.gate_b, inp.host.w1_blocks, inp.host.w1_scales, inp.b1,
+                       inp.host.w2_blocks, inp.host.w2_scales, inp.b2, nthreads)
+    return time.perf_counter() - t0
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    import oracle
+    from mxmoe import synth
+    inp = synth.make_config("prefill", seed=args.seed)
+    sample = args.ref_sample
+    for _ in range(args.warmup if args.warmup < 1 else 1):
+        cpu_reference(inp, sample)
+    times = [cpu_reference(inp, sample) for _ in range(args.steps)]
+    total = sum(times)
+    value = sample * args.steps / total
+    cores = oracle.num_threads()
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE configs[3] shapes)",
+        "config": {"workload": "gptoss20b_moe_prefill", "tokens_per_step": sample, "d_model": inp.d,
+                   "ffn_hidden": inp.f, "experts": inp.E, "top_k": inp.k},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{sample} tokens of the 8192-token prefill batch per step (C oracle, OpenMP)"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "burn-extended's MoE path is Rust + wgpu (Metal); no Rust toolchain or graphics stack exists on "
+                "this box, so the timed reference is the C restatement of its CPU semantics",
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, world, rank, local):
+    import torch
+    import mxmoe
+    from mxmoe import synth
+
+    torch.cuda.set_device(local)
+    dev = torch.device(f"cuda:{local}")
+    if world > 1:
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev)
+    hbm_peak, tc_burst, tc_sust, peak_src = load_peaks()
+
+    inp = synth.make_config("prefill", seed=args.seed + rank)
+    n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
+    if world > 1:
+        from mxmoe import ep
+        runner = ep.ExpertParallelMoe(inp, world, rank, dev)
+        step = lambda x: runner.forward(x)  # noqa: E731
+        x = torch.from_numpy(inp.x).to(torch.bfloat16).to(dev)
+    else:
+        layer = mxmoe.MoeConfig(d, f, E, k).init(local)
+        layer.set_router(inp.gamma, inp.gate_w, inp.gate_b)
+        layer.set_resident(inp.host, inp.b1, inp.b2)
+        layer.reserve(n)
+        x = torch.from_numpy(inp.x).to(torch.bfloat16).to(dev)
+        y = torch.empty_like(x)
+        stream = torch.cuda.current_stream()
+
+        def step(xx):
+            mxmoe.lib()
+            mxmoe.check(mxmoe.lib().mxmoe_forward(layer._h, xx.data_ptr(), mxmoe.BF16, y.data_ptr(), mxmoe.BF16, n,
+                                                   stream.cuda_stream))
+            return y
+
+    for _ in range(args.warmup):
+        step(x)
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            torch.distributed.barrier()
+        start.record()
+        for _ in range(args.steps):
+            step(x)
+        stop.record()
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    ms_per_step = ms / args.steps
+    value = n * world * args.steps / (ms / 1e3)
+    clocks = clk.summary()
+
+    if world > 1:
+        stages, e2e = runner.profile(x, args.steps), None
+        if rank == 0:
+            line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+                    "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+                    "vs_baseline": None, "dtype": "e2m1 x e4m3(2 terms), f32 accum",
+                    "data": "synthetic (seeded, BASELINE configs[3] shapes)",
+                    "config": {"workload": "gptoss20b_moe_prefill", "tokens_per_gpu": n, "experts": E,
+                               "experts_per_gpu": E // world, "top_k": k, "parallelism": f"ep{world}",
+                               "l2": "working set > 126 MB L2 (expert weights alone 423 MB)"},
+                    "clocks": clocks, "stages_ms": stages, "gpu_launches": runner.launches_per_step * args.steps}
+            print(json.dumps(line), flush=True)
+        torch.distributed.destroy_process_group()
+        return
+
+    # per-stage device times (CUDA events on the forward's stream), separate pass
+    layer.set_profiling(True)
+    prof = []
+    for _ in range(args.steps):
+        step(x)
+        prof.append(layer.last_profile())
+    layer.set_profiling(False)
+    stages = {s: statistics.mean(p[s] for p in prof) for s in prof[0]}
+    P = n * k
+    w1_flops = 2.0 * P * (2 * f) * d
+    w2_flops = 2.0 * P * d * f
+    t_w1 = stages["w1_gemm"] / 1e3
+    achieved = w1_flops / t_w1 / 1e12
+    roofline = {"bound": "tensor", "kernel": "tc_moe_gemm_kernel (W1 + SwiGLU)", "achieved": achieved,
+                "peak": tc_sust, "unit": "TFLOP/s", "frac": achieved / tc_sust,
+                "peak_source": f"{peak_src} bf16 sustained (the 2-term E4M3 x E2M1 MMA pair issues at the bf16-equivalent rate)",
+                "traffic": None,
+                "flops_per_launch": w1_flops}
+    layer_flops = w1_flops + w2_flops
+    extra = {"layer_tflops": layer_flops / (ms_per_step / 1e3) / 1e12,
+             "w2_tflops": w2_flops / (stages["w2_gemm"] / 1e3) / 1e12}
+
+    # end to end through the public host-buffer entry point (pinned memory)
+    xh = x.cpu().pin_memory()
+    yh = torch.empty_like(xh).pin_memory()
+    layer.forward_host(xh, yh)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        layer.forward_host(xh, yh)
+    e2e_s = (time.perf_counter() - t0) / args.steps
+    e2e = {"value": n / e2e_s, "unit": UNIT, "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+           "d2h_bytes_per_step": yh.numel() * yh.element_size()}
+
+    # decode-shaped layer: HBM-bound, GB/s vs peak
+    dec = synth.make_config("decode", seed=args.seed)
+    dl = mxmoe.MoeConfig(dec.d, dec.f, dec.E, dec.k).init(local)
+    dl.set_router(dec.gamma, dec.gate_w, dec.gate_b)
+    dl.set_resident(dec.host, dec.b1, dec.b2)
+    xd = torch.from_numpy(dec.x).to(torch.bfloat16).to(dev)
+    for _ in range(3):
+        dl.forward(xd)
+    torch.cuda.synchronize()
+    s2, e2_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        dl.forward(xd)
+    e2_.record()
+    torch.cuda.synchronize()
+    dec_ms = s2.elapsed_time(e2_) / args.steps
+    rr = dl.routing_results(dec.n)
+    used = int((np.diff(rr["offsets"].cpu().numpy()) > 0).sum())
+    per_expert = 2 * f * d // 2 + 2 * f * d // 32 + d * f // 2 + d * f // 32 + 2 * (2 * f + d)
+    dec_bytes = used * per_expert + 2 * E * d + E * 2 + 2 * dec.n * d * 2
+    dl.set_profiling(True)
+    dp = []
+    for _ in range(args.steps):
+        dl.forward(xd)
+        dp.append(dl.last_profile())
+    dstages = {s: statistics.mean(p[s] for p in dp) for s in dp[0]}
+    dl.close()
+    extra["decode"] = {"config": "gptoss20b_moe_decode (64 tokens, 32 experts, top-4)",
+                       "tokens_per_s": dec.n / (dec_ms / 1e3), "ms_per_step": dec_ms,
+                       "algorithmic_bytes": dec_bytes, "hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
+                       "hbm_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak, "stages_ms": dstages}
+
+    cpu = None
+    if not args.no_cpu_baseline:
+        import oracle
+        sample = args.cpu_sample
+        cpu_reference(inp, 2)
+        dt = cpu_reference(inp, sample)
+        cpu = {"value": sample / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
+               "sample": f"{sample} tokens of the 8192-token prefill batch (C oracle, OpenMP, all host threads)"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e2m1 x e4m3(2 terms), f32 accum",
+        "data": "synthetic (seeded, BASELINE configs[3] shapes)",
+        "config": {"workload": "gptoss20b_moe_prefill", "tokens": n, "d_model": d, "ffn_hidden": f, "experts": E,
+                   "top_k": k, "parallelism": "ep1",
+                   "l2": "inputs+weights > 126 MB L2 (expert weights alone 423 MB); no flush"},
+        "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks, "stages_ms": stages,
+        "gpu_launches": 6 * args.steps, "extra": extra,
+    }
+    print(json.dumps(line), flush=True)
+    layer.close()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--cpu-sample", type=int, default=24)
+    ap.add_argument("--ref-sample", type=int, default=8)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_setup(args.gpus)
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+    else:
+        run_ours(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,801 @@
+// api.cu -- host runtime behind include/mxmoe.h: layer state, one-time weight
+// repack into the tensor-core operand layout, workspace management, TMA
+// descriptor creation and the forward orchestration
+//   router -> permute -> quantize -> W1 GEMM -> W2 GEMM -> combine.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+#include <vector>
+
+#include "../../include/mxmoe.h"
+#include "kernels.h"
+#include "layout.cuh"
+#include "tc_gemm.h"
+
+using namespace mxmoe;
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define CUDA_TRY(expr)                                                                        \
+  do {                                                                                        \
+    cudaError_t _e = (expr);                                                                  \
+    if (_e != cudaSuccess)                                                                    \
+      return fail(_e == cudaErrorMemoryAllocation ? MXMOE_ERR_OOM : MXMOE_ERR_CUDA, "%s: %s (%s:%d)", #expr, \
+                  cudaGetErrorString(_e), __FILE__, __LINE__);                                \
+  } while (0)
+
+#define TRY(expr)                  \
+  do {                             \
+    int _r = (expr);               \
+    if (_r != MXMOE_OK) return _r; \
+  } while (0)
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn get_encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 3-D tiled map: dims {inner, rows, outer}, byte strides {row, outer}, box {128, box_rows, 1}, 128-byte swizzle.
+int make_tmap(CUtensorMap* m, CUtensorMapDataType dt, void* base, uint64_t inner, uint64_t rows, uint64_t outer,
+              uint64_t row_stride, uint64_t outer_stride, uint32_t box_rows) {
+  EncodeTiledFn enc = get_encode_fn();
+  if (!enc) return fail(MXMOE_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  const cuuint64_t gdim[3] = {inner, rows, outer};
+  const cuuint64_t gstr[2] = {row_stride, outer_stride};
+  const cuuint32_t box[3] = {static_cast<cuuint32_t>(kTileK), box_rows, 1};
+  const cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = enc(m, dt, 3, base, gdim, gstr, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(MXMOE_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d): inner=%llu rows=%llu outer=%llu box_rows=%u",
+                static_cast<int>(r), (unsigned long long)inner, (unsigned long long)rows,
+                (unsigned long long)outer, box_rows);
+  return MXMOE_OK;
+}
+
+template <typename T>
+int dalloc(T** p, size_t count) {
+  *p = nullptr;
+  if (count == 0) return MXMOE_OK;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void**>(p), count * sizeof(T));
+  if (e != cudaSuccess) {
+    *p = nullptr;
+    return fail(MXMOE_ERR_OOM, "cudaMalloc(%zu bytes): %s", count * sizeof(T), cudaGetErrorString(e));
+  }
+  return MXMOE_OK;
+}
+template <typename T>
+void dfree(T*& p) {
+  if (p) cudaFree(p);
+  p = nullptr;
+}
+
+float bf16_to_f32(uint16_t h) {
+  uint32_t u = static_cast<uint32_t>(h) << 16;
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+void to_f32(const void* src, mxmoe_dtype dt, size_t n, float* dst) {
+  if (dt == MXMOE_F32) {
+    std::memcpy(dst, src, n * sizeof(float));
+  } else {
+    const uint16_t* s = static_cast<const uint16_t*>(src);
+    for (size_t i = 0; i < n; ++i) dst[i] = bf16_to_f32(s[i]);
+  }
+}
+
+cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
+
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int dev) {
+    cudaGetDevice(&prev);
+    if (prev != dev) cudaSetDevice(dev);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    cudaGetDevice(&cur);
+    if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+  }
+};
+
+constexpr int kNumTileWidths = 4;
+constexpr int kTileWidths[kNumTileWidths] = {32, 64, 128, 256};
+
+}  // namespace
+
+// Per-forward scratch sized for `cap_tokens` tokens x k pairs.
+struct Workspace {
+  uint32_t cap_tokens = 0;  // tokens
+  uint32_t cap_pairs = 0;   // n * k
+  uint32_t rows = 0;        // padded activation rows
+  uint32_t row_blocks = 0;  // scale-atom row blocks (rows / 128 + slack)
+  float* logits = nullptr;
+  int32_t* topk_idx = nullptr;
+  float* topk_w = nullptr;
+  float* rscale = nullptr;
+  int32_t* offsets = nullptr;
+  int32_t* perm_c = nullptr;
+  int32_t* inv_c = nullptr;
+  int32_t* poff = nullptr;
+  int32_t* counts = nullptr;
+  int32_t* ntile_prefix = nullptr;
+  int32_t* perm_p = nullptr;
+  int32_t* inv_p = nullptr;
+  uint8_t* xq = nullptr;   // [3][rows][kp1]
+  uint8_t* xsf = nullptr;  // [3][row_blocks][kp1/128][512]
+  uint8_t* aq = nullptr;   // [2][rows][kp2]
+  uint8_t* asf = nullptr;  // [2][row_blocks][kp2/128][512]
+  float* y_pair = nullptr; // [rows][d]
+  float* act_f32 = nullptr;// [rows][fp] (SIMT path only)
+  int32_t* local_idx = nullptr; // [cap_pairs] local expert ids (expert-parallel receive side)
+  CUtensorMap tmap_x[kNumTileWidths];
+  CUtensorMap tmap_act[kNumTileWidths];
+};
+
+struct mxmoe_layer {
+  mxmoe_config cfg{};
+  uint32_t d = 0, f = 0, fp = 0, E_total = 0, k = 0;
+  uint32_t e_begin = 0, e_count = 0;  // local expert shard
+  uint32_t kp1 = 0, kp2 = 0, m_tiles1 = 0, m_tiles2 = 0;
+  int num_sms = 148;
+  size_t smem_limit = 227 * 1024;
+  bool router_ready = false, experts_ready = false;
+  bool gamma_is_one = true;
+  float* gamma = nullptr;
+  float* gate_w = nullptr;
+  float* gate_b = nullptr;
+  uint8_t* w1q = nullptr;
+  uint8_t* w1sf = nullptr;
+  float* b1 = nullptr;
+  uint8_t* w2q = nullptr;
+  uint8_t* w2sf = nullptr;
+  float* b2 = nullptr;
+  int* err = nullptr;
+  CUtensorMap tmap_w1{}, tmap_w2{};
+  Workspace ws;
+  uint32_t last_n = 0;
+  bool profiling = false;
+  bool profile_valid = false;
+  cudaEvent_t ev[8] = {};
+};
+
+namespace {
+
+void free_workspace(Workspace& w) {
+  dfree(w.logits); dfree(w.topk_idx); dfree(w.topk_w); dfree(w.rscale);
+  dfree(w.offsets); dfree(w.perm_c); dfree(w.inv_c); dfree(w.poff); dfree(w.counts);
+  dfree(w.ntile_prefix); dfree(w.perm_p); dfree(w.inv_p);
+  dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
+  dfree(w.local_idx);
+  w.cap_tokens = w.cap_pairs = w.rows = w.row_blocks = 0;
+}
+
+// Sizes the workspace for n tokens with k pairs each (k = 1 for the
+// expert-parallel receive side).
+int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
+  Workspace& w = L->ws;
+  const uint64_t pairs = static_cast<uint64_t>(n_tokens) * k;
+  if (n_tokens <= w.cap_tokens && pairs <= w.cap_pairs && w.cap_tokens > 0) return MXMOE_OK;
+  if (pairs > (1u << 28)) return fail(MXMOE_ERR_TOO_LARGE, "too many pairs: %llu", (unsigned long long)pairs);
+  CUDA_TRY(cudaDeviceSynchronize());
+  free_workspace(w);
+  const uint32_t E = L->e_count, Et = L->E_total;
+  const uint32_t cap_t = std::max<uint32_t>(n_tokens, 1);
+  const uint32_t cap_p = std::max<uint32_t>(static_cast<uint32_t>(pairs), 1);
+  w.rows = round_up(cap_p, kRowBlock) + E * kRowBlock + 256;
+  w.row_blocks = w.rows / kRowBlock + 2;
+  const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
+  TRY(dalloc(&w.logits, static_cast<size_t>(cap_t) * Et));
+  TRY(dalloc(&w.topk_idx, cap_p));
+  TRY(dalloc(&w.topk_w, cap_p));
+  TRY(dalloc(&w.rscale, std::max(cap_t, cap_p)));
+  TRY(dalloc(&w.offsets, Et + 1));
+  TRY(dalloc(&w.perm_c, cap_p));
+  TRY(dalloc(&w.inv_c, cap_p));
+  TRY(dalloc(&w.poff, Et + 1));
+  TRY(dalloc(&w.counts, Et + 1));
+  TRY(dalloc(&w.ntile_prefix, Et + 1));
+  TRY(dalloc(&w.perm_p, w.rows));
+  TRY(dalloc(&w.inv_p, cap_p));
+  TRY(dalloc(&w.local_idx, cap_p));
+  TRY(dalloc(&w.xq, 3ull * w.rows * L->kp1));
+  TRY(dalloc(&w.xsf, 3ull * w.row_blocks * kc1 * kSfAtomBytes));
+  TRY(dalloc(&w.aq, 2ull * w.rows * L->kp2));
+  TRY(dalloc(&w.asf, 2ull * w.row_blocks * kc2 * kSfAtomBytes));
+  TRY(dalloc(&w.y_pair, static_cast<size_t>(w.rows) * L->d));
+  // Padding columns (K beyond d or f) and never-written scale bytes must read
+  // as zero codes / finite scales for every later forward.
+  CUDA_TRY(cudaMemset(w.xq, 0, 3ull * w.rows * L->kp1));
+  CUDA_TRY(cudaMemset(w.xsf, 0, 3ull * w.row_blocks * kc1 * kSfAtomBytes));
+  CUDA_TRY(cudaMemset(w.aq, 0, 2ull * w.rows * L->kp2));
+  CUDA_TRY(cudaMemset(w.asf, 0, 2ull * w.row_blocks * kc2 * kSfAtomBytes));
+  CUDA_TRY(cudaMemset(w.perm_p, 0, sizeof(int32_t) * w.rows));
+  for (int i = 0; i < kNumTileWidths; ++i) {
+    TRY(make_tmap(&w.tmap_x[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.xq, L->kp1, w.rows, 3, L->kp1,
+                  static_cast<uint64_t>(w.rows) * L->kp1, kTileWidths[i]));
+    TRY(make_tmap(&w.tmap_act[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.aq, L->kp2, w.rows, 2, L->kp2,
+                  static_cast<uint64_t>(w.rows) * L->kp2, kTileWidths[i]));
+  }
+  w.cap_tokens = cap_t;
+  w.cap_pairs = cap_p;
+  return MXMOE_OK;
+}
+
+// Tile width over routed pairs from the average pairs per expert; three-term
+// activations cap it at 128 so that the pipeline keeps >= 3 stages.
+int pick_tile_width_index(uint64_t pairs, uint32_t experts, int x_terms) {
+  const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
+  int i = 3;
+  if (avg <= 24) i = 0;
+  else if (avg <= 48) i = 1;
+  else if (avg <= 96) i = 2;
+  if (x_terms > 2 && i > 2) i = 2;
+  return i;
+}
+
+// Two E4M3 terms represent bf16 activations exactly when the RmsNorm gain is
+// one (the gain is then applied nowhere and 1/rms goes to the epilogue);
+// otherwise three terms keep the operand error near 2^-13.
+int x_terms_for(const mxmoe_layer* L, int x_dtype) {
+  return (x_dtype == MXMOE_BF16 && L->gamma_is_one) ? 2 : 3;
+}
+
+// Expert FFN over already-routed pairs: quantize -> W1 -> W2 (or the SIMT
+// pair) -> y_pair.  Uses ws.poff / counts / ntile_prefix / perm_p / inv_p.
+int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
+                const float* route_w, int tw_idx, int x_terms, cudaStream_t st) {
+  Workspace& w = L->ws;
+  const uint64_t P = static_cast<uint64_t>(n_tok) * k;
+  const int N = kTileWidths[tw_idx];
+  const float bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
+  if (L->cfg.flags & MXMOE_FLAG_SIMT) {
+    if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
+    CUDA_TRY(launch_simt_w1(x, x_dtype, L->d, k, L->gamma, rscale, L->w1q, L->w1sf, L->b1, L->fp, L->kp1, L->e_count,
+                            w.poff, w.counts, w.perm_p, L->cfg.swiglu_alpha, L->cfg.swiglu_limit, w.act_f32, st));
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
+    CUDA_TRY(launch_simt_w2(w.act_f32, L->fp, L->d, k, L->w2q, L->w2sf, L->b2, bias_mult, L->kp2, L->e_count, w.poff,
+                            w.counts, w.perm_p, route_w, w.y_pair, st));
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
+    return MXMOE_OK;
+  }
+  const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
+  CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
+                                 w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
+                                 static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
+  const uint64_t max_tiles_per_m = (P + N - 1) / N + L->e_count;
+  TcParams p{};
+  p.N = N;
+  p.E = L->e_count;
+  p.poff = w.poff;
+  p.counts = w.counts;
+  p.ntile_prefix = w.ntile_prefix;
+  p.alpha = L->cfg.swiglu_alpha;
+  p.limit = L->cfg.swiglu_limit;
+  p.rscale = rscale;
+  p.perm = w.perm_p;
+  p.k = static_cast<int>(k);
+  p.topk_w = route_w;
+  p.err = L->err;
+  p.d = L->d;
+  // W1 + SwiGLU: A = W1 codes, B = x terms, writes act terms.
+  p.mode = 1;
+  p.b_terms = x_terms;
+  p.stages = tc_gemm_max_stages(N, x_terms, L->smem_limit);
+  p.m_tiles = L->m_tiles1;
+  p.k_tiles = static_cast<int>(kc1);
+  p.a_sf = L->w1sf;
+  p.b_sf = w.xsf;
+  p.b_sf_term_stride = static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes;
+  p.bias = L->b1;
+  p.bias_stride = static_cast<int>(2 * L->fp);
+  p.rows_valid = static_cast<int>(2 * L->fp);
+  p.bias_mult = 1.0f;
+  p.act_codes = w.aq;
+  p.act_term_stride = static_cast<uint64_t>(w.rows) * L->kp2;
+  p.act_kp = static_cast<int>(L->kp2);
+  p.act_sf = w.asf;
+  p.act_sf_term_stride = static_cast<uint64_t>(w.row_blocks) * kc2 * kSfAtomBytes;
+  p.act_kchunks = static_cast<int>(kc2);
+  int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, L->m_tiles1 * max_tiles_per_m));
+  CUDA_TRY(tc_gemm_launch(L->tmap_w1, w.tmap_x[tw_idx], p, grid, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
+  // W2 + bias + route weight: A = W2 codes, B = act terms, writes y_pair.
+  p.mode = 2;
+  p.b_terms = 2;
+  p.stages = tc_gemm_max_stages(N, 2, L->smem_limit);
+  p.m_tiles = L->m_tiles2;
+  p.k_tiles = static_cast<int>(kc2);
+  p.a_sf = L->w2sf;
+  p.b_sf = w.asf;
+  p.b_sf_term_stride = static_cast<uint64_t>(w.row_blocks) * kc2 * kSfAtomBytes;
+  p.bias = L->b2;
+  p.bias_stride = static_cast<int>(L->d);
+  p.rows_valid = static_cast<int>(L->d);
+  p.bias_mult = bias_mult;
+  p.y_pair = w.y_pair;
+  grid = static_cast<int>(std::min<uint64_t>(L->num_sms, L->m_tiles2 * max_tiles_per_m));
+  CUDA_TRY(tc_gemm_launch(L->tmap_w2, w.tmap_act[tw_idx], p, grid, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
+  return MXMOE_OK;
+}
+
+int check_layer(const mxmoe_layer* L) {
+  if (!L) return fail(MXMOE_ERR_INVALID_ARG, "null layer");
+  return MXMOE_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mxmoe_abi_version(void) { return MXMOE_ABI_VERSION; }
+
+const char* mxmoe_build_info(void) {
+  return "mxmoe sm_100a: tcgen05 kind::mxf8f6f4.block_scale grouped GEMM (E2M1 weights x E4M3 hi/lo activations), "
+         "CUDA-core router/permute/combine";
+}
+
+int mxmoe_last_error(char* buf, size_t cap) {
+  if (!buf || cap == 0) return MXMOE_ERR_INVALID_ARG;
+  std::snprintf(buf, cap, "%s", g_last_error.c_str());
+  return MXMOE_OK;
+}
+
+int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out) {
+  if (!cfg || !out) return fail(MXMOE_ERR_INVALID_ARG, "null argument");
+  *out = nullptr;
+  if (cfg->d_model == 0 || cfg->ffn_hidden == 0 || cfg->num_experts == 0 || cfg->experts_per_token == 0)
+    return fail(MXMOE_ERR_INVALID_ARG, "zero dimension in config");
+  if (cfg->d_model % 32 != 0 || cfg->ffn_hidden % 32 != 0)
+    return fail(MXMOE_ERR_UNSUPPORTED, "d_model (%u) and ffn_hidden (%u) must be multiples of 32", cfg->d_model,
+                cfg->ffn_hidden);
+  if (cfg->experts_per_token > static_cast<uint32_t>(kMaxTopK) || cfg->experts_per_token > cfg->num_experts)
+    return fail(MXMOE_ERR_UNSUPPORTED, "experts_per_token %u unsupported (max %d, <= num_experts)",
+                cfg->experts_per_token, kMaxTopK);
+  if (cfg->num_experts > 1024) return fail(MXMOE_ERR_UNSUPPORTED, "num_experts %u > 1024", cfg->num_experts);
+  int ndev = 0;
+  CUDA_TRY(cudaGetDeviceCount(&ndev));
+  if (cfg->device < 0 || cfg->device >= ndev) return fail(MXMOE_ERR_INVALID_ARG, "bad device %d", cfg->device);
+  DeviceGuard g(cfg->device);
+  mxmoe_layer* L = new (std::nothrow) mxmoe_layer();
+  if (!L) return fail(MXMOE_ERR_OOM, "host allocation failed");
+  L->cfg = *cfg;
+  L->d = cfg->d_model;
+  L->f = cfg->ffn_hidden;
+  L->fp = round_up(L->f, kGluBlock);
+  L->E_total = cfg->num_experts;
+  L->k = cfg->experts_per_token;
+  L->e_begin = 0;
+  L->e_count = cfg->num_experts;
+  L->kp1 = round_up(L->d, kTileK);
+  L->kp2 = round_up(L->fp, kTileK);
+  L->m_tiles1 = 2 * L->fp / 128;
+  L->m_tiles2 = (L->d + 127) / 128;
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, cfg->device) == cudaSuccess) {
+    L->num_sms = prop.multiProcessorCount;
+    L->smem_limit = prop.sharedMemPerBlockOptin;
+  }
+  int rc = dalloc(&L->err, 1);
+  if (rc == MXMOE_OK && cudaMemset(L->err, 0, sizeof(int)) != cudaSuccess) rc = MXMOE_ERR_CUDA;
+  if (rc != MXMOE_OK) {
+    delete L;
+    return rc;
+  }
+  *out = L;
+  return MXMOE_OK;
+}
+
+int mxmoe_destroy(mxmoe_layer* L) {
+  if (!L) return MXMOE_OK;
+  DeviceGuard g(L->cfg.device);
+  cudaDeviceSynchronize();
+  free_workspace(L->ws);
+  dfree(L->gamma); dfree(L->gate_w); dfree(L->gate_b);
+  dfree(L->w1q); dfree(L->w1sf); dfree(L->b1); dfree(L->w2q); dfree(L->w2sf); dfree(L->b2);
+  dfree(L->err);
+  for (auto& e : L->ev)
+    if (e) cudaEventDestroy(e);
+  delete L;
+  return MXMOE_OK;
+}
+
+int mxmoe_set_router(mxmoe_layer* L, const void* norm_gamma, const void* gate_w, const void* gate_b,
+                     mxmoe_dtype dtype, void* stream) {
+  TRY(check_layer(L));
+  if (!norm_gamma || !gate_w || !gate_b) return fail(MXMOE_ERR_INVALID_ARG, "null router parameter");
+  if (dtype != MXMOE_F32 && dtype != MXMOE_BF16) return fail(MXMOE_ERR_INVALID_ARG, "bad dtype");
+  DeviceGuard g(L->cfg.device);
+  const size_t d = L->d, E = L->E_total;
+  std::vector<float> gm(d), w(E * d), b(E);
+  to_f32(norm_gamma, dtype, d, gm.data());
+  to_f32(gate_w, dtype, E * d, w.data());
+  to_f32(gate_b, dtype, E, b.data());
+  L->gamma_is_one = std::all_of(gm.begin(), gm.end(), [](float v) { return v == 1.0f; });
+  if (!L->gamma) TRY(dalloc(&L->gamma, d));
+  if (!L->gate_w) TRY(dalloc(&L->gate_w, E * d));
+  if (!L->gate_b) TRY(dalloc(&L->gate_b, E));
+  cudaStream_t st = as_stream(stream);
+  CUDA_TRY(cudaMemcpyAsync(L->gamma, gm.data(), d * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->gate_w, w.data(), E * d * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->gate_b, b.data(), E * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  L->router_ready = true;
+  return MXMOE_OK;
+}
+
+int mxmoe_set_expert_shard(mxmoe_layer* L, uint32_t expert_begin, uint32_t expert_count) {
+  TRY(check_layer(L));
+  if (expert_count == 0 || expert_begin + expert_count > L->E_total)
+    return fail(MXMOE_ERR_INVALID_ARG, "bad shard [%u, %u) of %u experts", expert_begin, expert_begin + expert_count,
+                L->E_total);
+  if (L->experts_ready) return fail(MXMOE_ERR_INVALID_ARG, "shard must be set before uploading experts");
+  DeviceGuard g(L->cfg.device);
+  free_workspace(L->ws);
+  L->e_begin = expert_begin;
+  L->e_count = expert_count;
+  return MXMOE_OK;
+}
+
+int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint8_t* w1_blocks,
+                         const uint8_t* w1_scales, const mxmoe_quant_desc* w2d, const uint8_t* w2_blocks,
+                         const uint8_t* w2_scales, const void* b1, const void* b2, mxmoe_dtype bias_dtype,
+                         void* stream) {
+  TRY(check_layer(L));
+  if (!w1d || !w2d || !w1_blocks || !w1_scales || !w2_blocks || !w2_scales || !b1 || !b2)
+    return fail(MXMOE_ERR_INVALID_ARG, "null expert parameter");
+  const uint64_t E = L->e_count, d = L->d, f = L->f, fp = L->fp;
+  if (w1d->experts != E || w1d->rows != 2 * f || w1d->cols != d || w1d->bpr != (d + 1) / 2 ||
+      w1d->gpr != (d + 31) / 32)
+    return fail(MXMOE_ERR_INVALID_ARG,
+                "W1 desc mismatch: got experts=%llu rows=%llu cols=%llu bpr=%llu gpr=%llu, want %llu/%llu/%llu/%llu/%llu",
+                (unsigned long long)w1d->experts, (unsigned long long)w1d->rows, (unsigned long long)w1d->cols,
+                (unsigned long long)w1d->bpr, (unsigned long long)w1d->gpr, (unsigned long long)E,
+                (unsigned long long)(2 * f), (unsigned long long)d, (unsigned long long)((d + 1) / 2),
+                (unsigned long long)((d + 31) / 32));
+  if (w2d->experts != E || w2d->rows != d || w2d->cols != f || w2d->bpr != (f + 1) / 2 || w2d->gpr != (f + 31) / 32)
+    return fail(MXMOE_ERR_INVALID_ARG, "W2 desc mismatch");
+  DeviceGuard g(L->cfg.device);
+  const bool inter = (L->cfg.flags & MXMOE_FLAG_INTERLEAVED_GLU) != 0;
+  const uint64_t kp1 = L->kp1, kp2 = L->kp2, kc1 = kp1 / kTileK, kc2 = kp2 / kTileK;
+  const uint64_t rows1 = 2 * fp, rb1 = rows1 / kRowBlock, rb2 = (d + kRowBlock - 1) / kRowBlock;
+  const uint64_t bpr1 = w1d->bpr, gpr1 = w1d->gpr, bpr2 = w2d->bpr, gpr2 = w2d->gpr;
+
+  auto sf_byte = [](uint8_t s, int ue8) -> uint8_t {
+    const int v = static_cast<int>(s) - ue8;
+    return static_cast<uint8_t>(v < 0 ? 0 : (v > 255 ? 255 : v));
+  };
+
+  std::vector<uint8_t> q1(E * rows1 * (kp1 / 2), 0), s1(E * rb1 * kc1 * kSfAtomBytes, 0);
+  std::vector<float> bb1(E * rows1, 0.0f), src_b1(E * 2 * f);
+  to_f32(b1, bias_dtype, E * 2 * f, src_b1.data());
+  for (uint64_t e = 0; e < E; ++e)
+    for (uint64_t j = 0; j < f; ++j)
+      for (uint32_t half = 0; half < 2; ++half) {
+        const uint64_t src = inter ? 2 * j + half : half * f + j;
+        const uint64_t dst = w1_packed_row(static_cast<uint32_t>(j), half);
+        std::memcpy(&q1[(e * rows1 + dst) * (kp1 / 2)], &w1_blocks[(e * 2 * f + src) * bpr1], bpr1);
+        uint8_t* atoms = &s1[e * rb1 * kc1 * kSfAtomBytes];
+        for (uint64_t gi = 0; gi < gpr1; ++gi)
+          atoms[sf_offset(static_cast<uint32_t>(dst), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc1))] =
+              sf_byte(w1_scales[(e * 2 * f + src) * gpr1 + gi], w1d->ue8_offset);
+        bb1[e * rows1 + dst] = src_b1[e * 2 * f + src];
+      }
+  std::vector<uint8_t> q2(E * d * (kp2 / 2), 0), s2(E * rb2 * kc2 * kSfAtomBytes, 0);
+  std::vector<float> bb2(E * d);
+  to_f32(b2, bias_dtype, E * d, bb2.data());
+  for (uint64_t e = 0; e < E; ++e)
+    for (uint64_t c = 0; c < d; ++c) {
+      std::memcpy(&q2[(e * d + c) * (kp2 / 2)], &w2_blocks[(e * d + c) * bpr2], bpr2);
+      uint8_t* atoms = &s2[e * rb2 * kc2 * kSfAtomBytes];
+      for (uint64_t gi = 0; gi < gpr2; ++gi)
+        atoms[sf_offset(static_cast<uint32_t>(c), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc2))] =
+            sf_byte(w2_scales[(e * d + c) * gpr2 + gi], w2d->ue8_offset);
+    }
+
+  dfree(L->w1q); dfree(L->w1sf); dfree(L->b1); dfree(L->w2q); dfree(L->w2sf); dfree(L->b2);
+  TRY(dalloc(&L->w1q, q1.size()));
+  TRY(dalloc(&L->w1sf, s1.size()));
+  TRY(dalloc(&L->b1, bb1.size()));
+  TRY(dalloc(&L->w2q, q2.size()));
+  TRY(dalloc(&L->w2sf, s2.size()));
+  TRY(dalloc(&L->b2, bb2.size()));
+  cudaStream_t st = as_stream(stream);
+  CUDA_TRY(cudaMemcpyAsync(L->w1q, q1.data(), q1.size(), cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->w1sf, s1.data(), s1.size(), cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->b1, bb1.data(), bb1.size() * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->w2q, q2.data(), q2.size(), cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->w2sf, s2.data(), s2.size(), cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->b2, bb2.data(), bb2.size() * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  TRY(make_tmap(&L->tmap_w1, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w1q, kp1, rows1, E, kp1 / 2,
+                rows1 * (kp1 / 2), 128));
+  TRY(make_tmap(&L->tmap_w2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w2q, kp2, d, E, kp2 / 2, d * (kp2 / 2), 128));
+  L->experts_ready = true;
+  return MXMOE_OK;
+}
+
+int mxmoe_reserve(mxmoe_layer* L, uint32_t max_tokens) {
+  TRY(check_layer(L));
+  DeviceGuard g(L->cfg.device);
+  return ensure_workspace(L, max_tokens, L->k);
+}
+
+int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, mxmoe_dtype y_dtype,
+                  uint32_t n_tokens, void* stream) {
+  TRY(check_layer(L));
+  if ((!x || !y) && n_tokens > 0) return fail(MXMOE_ERR_INVALID_ARG, "null x or y");
+  if ((x_dtype != MXMOE_F32 && x_dtype != MXMOE_BF16) || (y_dtype != MXMOE_F32 && y_dtype != MXMOE_BF16))
+    return fail(MXMOE_ERR_INVALID_ARG, "bad dtype");
+  DeviceGuard g(L->cfg.device);
+  cudaStream_t st = as_stream(stream);
+  L->last_n = n_tokens;
+  if (n_tokens == 0) return MXMOE_OK;
+  const size_t xbytes = static_cast<size_t>(n_tokens) * L->d * (x_dtype == MXMOE_F32 ? 4 : 2);
+  if (L->cfg.flags & MXMOE_FLAG_DISABLED) {
+    // MoeConfig.disabled (src/moe/mod.rs:106-108): y = x.
+    if (x_dtype == y_dtype) {
+      CUDA_TRY(cudaMemcpyAsync(y, x, xbytes, cudaMemcpyDeviceToDevice, st));
+    } else {
+      CUDA_TRY(launch_combine(x, x_dtype, nullptr, nullptr, nullptr, n_tokens, L->d, 0, 1, y, y_dtype, st));
+    }
+    return MXMOE_OK;
+  }
+  if (!L->router_ready || !L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "router or experts not uploaded");
+  if (L->e_count != L->E_total)
+    return fail(MXMOE_ERR_INVALID_ARG, "layer holds an expert shard; use the expert-parallel entry points");
+  TRY(ensure_workspace(L, n_tokens, L->k));
+  Workspace& w = L->ws;
+  const uint32_t k = L->k, E = L->e_count;
+  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
+  const int xt = x_terms_for(L, x_dtype);
+  const int tw = pick_tile_width_index(P, E, xt);
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  L->profile_valid = false;
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
+  CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
+                         w.logits, w.topk_idx, w.topk_w, w.rscale, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
+  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, kTileWidths[tw], w.offsets, w.perm_c,
+                          w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
+  TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tw, xt, st));
+  const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
+  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
+  if (L->profiling) {
+    CUDA_TRY(cudaEventRecord(L->ev[6], st));
+    L->profile_valid = true;
+  }
+  return MXMOE_OK;
+}
+
+int mxmoe_forward_host(mxmoe_layer* L, const void* x_host, mxmoe_dtype x_dtype, void* y_host, mxmoe_dtype y_dtype,
+                       uint32_t n_tokens, void* stream) {
+  TRY(check_layer(L));
+  if (n_tokens == 0) return MXMOE_OK;
+  if (!x_host || !y_host) return fail(MXMOE_ERR_INVALID_ARG, "null host buffer");
+  DeviceGuard g(L->cfg.device);
+  cudaStream_t st = as_stream(stream);
+  const size_t xb = static_cast<size_t>(n_tokens) * L->d * (x_dtype == MXMOE_F32 ? 4 : 2);
+  const size_t yb = static_cast<size_t>(n_tokens) * L->d * (y_dtype == MXMOE_F32 ? 4 : 2);
+  TRY(ensure_workspace(L, n_tokens, L->k));
+  // Staging buffers for the host call live in the workspace's activation-code
+  // area only if it is large enough; otherwise dedicated buffers are kept.
+  static thread_local void* dx = nullptr;
+  static thread_local void* dy = nullptr;
+  static thread_local size_t cx = 0, cy = 0;
+  if (cx < xb) {
+    if (dx) cudaFree(dx);
+    dx = nullptr;
+    CUDA_TRY(cudaMalloc(&dx, xb));
+    cx = xb;
+  }
+  if (cy < yb) {
+    if (dy) cudaFree(dy);
+    dy = nullptr;
+    CUDA_TRY(cudaMalloc(&dy, yb));
+    cy = yb;
+  }
+  CUDA_TRY(cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
+  TRY(mxmoe_forward(L, dx, x_dtype, dy, y_dtype, n_tokens, stream));
+  CUDA_TRY(cudaMemcpyAsync(y_host, dy, yb, cudaMemcpyDeviceToHost, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  int herr = 0;
+  CUDA_TRY(cudaMemcpy(&herr, L->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr != 0) return fail(MXMOE_ERR_TIMEOUT, "device-side wait gave up (code %d)", herr);
+  return MXMOE_OK;
+}
+
+int mxmoe_sync_status(mxmoe_layer* L, void* stream) {
+  TRY(check_layer(L));
+  DeviceGuard g(L->cfg.device);
+  CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
+  CUDA_TRY(cudaGetLastError());
+  int herr = 0;
+  CUDA_TRY(cudaMemcpy(&herr, L->err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (herr != 0) return fail(MXMOE_ERR_TIMEOUT, "device-side wait gave up (code %d)", herr);
+  return MXMOE_OK;
+}
+
+int mxmoe_routing_results(mxmoe_layer* L, const int32_t** topk_idx, const float** topk_w, const int32_t** offsets,
+                          const int32_t** perm, const int32_t** inv, const float** logits) {
+  TRY(check_layer(L));
+  if (!L->ws.cap_tokens) return fail(MXMOE_ERR_NOT_READY, "no forward has run");
+  if (topk_idx) *topk_idx = L->ws.topk_idx;
+  if (topk_w) *topk_w = L->ws.topk_w;
+  if (offsets) *offsets = L->ws.offsets;
+  if (perm) *perm = L->ws.perm_c;
+  if (inv) *inv = L->ws.inv_c;
+  if (logits) *logits = L->ws.logits;
+  return MXMOE_OK;
+}
+
+int mxmoe_dequant_mxfp4_bytes(const uint8_t* blocks, uint64_t rows_total, uint64_t b, const uint8_t* scales,
+                              float* out, void* stream) {
+  if (rows_total * b > 0 && (!blocks || !scales || !out)) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  CUDA_TRY(launch_dequant_bytes(blocks, rows_total, b, scales, out, as_stream(stream)));
+  return MXMOE_OK;
+}
+
+int mxmoe_dequant_rows(const mxmoe_quant_desc* desc, const uint8_t* blocks, const uint8_t* scales, float* out,
+                       void* stream) {
+  if (!desc) return fail(MXMOE_ERR_INVALID_ARG, "null desc");
+  const uint64_t rows = desc->experts * desc->rows;
+  if (rows * desc->cols > 0 && (!blocks || !scales || !out)) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (desc->bpr < (desc->cols + 1) / 2 || desc->gpr < (desc->cols + 31) / 32)
+    return fail(MXMOE_ERR_INVALID_ARG, "bpr/gpr too small for cols");
+  CUDA_TRY(launch_dequant_rows(blocks, scales, rows, desc->cols, desc->bpr, desc->gpr, desc->ue8_offset, out,
+                               as_stream(stream)));
+  return MXMOE_OK;
+}
+
+int mxmoe_topk_softmax(const float* logits, uint32_t n_tokens, uint32_t num_experts, uint32_t k, int32_t* topk_idx,
+                       float* topk_w, void* stream) {
+  if (k == 0 || k > static_cast<uint32_t>(kMaxTopK) || k > num_experts)
+    return fail(MXMOE_ERR_UNSUPPORTED, "k=%u unsupported", k);
+  if (n_tokens > 0 && (!logits || !topk_idx || !topk_w)) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  CUDA_TRY(launch_topk_softmax(logits, n_tokens, num_experts, k, topk_idx, topk_w, as_stream(stream)));
+  return MXMOE_OK;
+}
+
+int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k, uint32_t num_experts, int32_t* offsets,
+                  int32_t* perm, int32_t* inv, void* stream) {
+  if (num_experts == 0 || num_experts > 1024) return fail(MXMOE_ERR_UNSUPPORTED, "num_experts %u", num_experts);
+  if (!offsets || (n_tokens * k > 0 && (!topk_idx || !perm || !inv)))
+    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  // pad = 1 makes the padded maps equal to the canonical ones; the scratch
+  // outputs (poff, counts) are written to the tail of `offsets`' companion
+  // buffers allocated here.
+  int32_t* tmp = nullptr;
+  TRY(dalloc(&tmp, 2 * (num_experts + 1)));
+  cudaStream_t st = as_stream(stream);
+  CUDA_TRY(launch_permute(topk_idx, static_cast<int>(n_tokens * k), num_experts, 1, 1, offsets, nullptr, nullptr, tmp,
+                          tmp + num_experts + 1, nullptr, perm, inv, st));
+  CUDA_TRY(cudaStreamSynchronize(st));
+  dfree(tmp);
+  return MXMOE_OK;
+}
+
+int mxmoe_set_profiling(mxmoe_layer* L, int enable) {
+  TRY(check_layer(L));
+  DeviceGuard g(L->cfg.device);
+  if (enable && !L->ev[0])
+    for (auto& e : L->ev) CUDA_TRY(cudaEventCreate(&e));
+  L->profiling = enable != 0;
+  L->profile_valid = false;
+  return MXMOE_OK;
+}
+
+int mxmoe_last_profile(mxmoe_layer* L, float* ms, int cap, int* count) {
+  TRY(check_layer(L));
+  if (!L->profiling || !L->profile_valid) return fail(MXMOE_ERR_NOT_READY, "no profiled forward");
+  DeviceGuard g(L->cfg.device);
+  CUDA_TRY(cudaEventSynchronize(L->ev[6]));
+  const int n = 6;
+  for (int i = 0; i < n && i < cap; ++i) CUDA_TRY(cudaEventElapsedTime(&ms[i], L->ev[i], L->ev[i + 1]));
+  if (count) *count = n;
+  return MXMOE_OK;
+}
+
+int mxmoe_route(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, float* rscale,
+                int32_t* topk_idx, float* topk_w, int32_t* offsets, int32_t* perm, int32_t* inv, void* stream) {
+  TRY(check_layer(L));
+  if (!L->router_ready) return fail(MXMOE_ERR_NOT_READY, "router not uploaded");
+  if (n_tokens == 0) return MXMOE_OK;
+  if (!x || !rscale || !topk_idx || !topk_w) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  DeviceGuard g(L->cfg.device);
+  TRY(ensure_workspace(L, n_tokens, L->k));
+  Workspace& w = L->ws;
+  cudaStream_t st = as_stream(stream);
+  const uint32_t k = L->k;
+  CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
+                         w.logits, topk_idx, topk_w, rscale, st));
+  if (offsets || perm || inv) {
+    if (!offsets || !perm || !inv) return fail(MXMOE_ERR_INVALID_ARG, "offsets, perm and inv go together");
+    CUDA_TRY(launch_permute(topk_idx, static_cast<int>(n_tokens * k), L->E_total, 1, 1, offsets, nullptr, nullptr,
+                            w.poff, w.counts, nullptr, perm, inv, st));
+  }
+  return MXMOE_OK;
+}
+
+int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_t d_model, uint32_t k,
+                       const int32_t* perm, const float* rscale, const int32_t* topk_idx, const float* topk_w,
+                       void* out_x, float* out_rscale, int32_t* out_expert, float* out_w, void* stream) {
+  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
+  if (P == 0) return MXMOE_OK;
+  if (!x || !perm || !rscale || !topk_idx || !topk_w || !out_x) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  CUDA_TRY(launch_gather_pairs(x, x_dtype, d_model, k, static_cast<int>(P), perm, rscale, topk_idx, topk_w, out_x,
+                               out_rscale, out_expert, out_w, as_stream(stream)));
+  return MXMOE_OK;
+}
+
+int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, const float* rscale,
+                        const int32_t* expert, const float* weight, uint32_t n_pairs, float* out, void* stream) {
+  TRY(check_layer(L));
+  if (!L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "experts not uploaded");
+  if (n_pairs == 0) return MXMOE_OK;
+  if (!xr || !rscale || !expert || !weight || !out) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  DeviceGuard g(L->cfg.device);
+  TRY(ensure_workspace(L, n_pairs, 1));
+  Workspace& w = L->ws;
+  cudaStream_t st = as_stream(stream);
+  const int xt = x_terms_for(L, xr_dtype);
+  const int tw = pick_tile_width_index(n_pairs, L->e_count, xt);
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  CUDA_TRY(launch_localize(expert, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
+                           static_cast<int>(L->e_count), w.local_idx, L->err, st));
+  CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, kTileWidths[tw], nullptr,
+                          nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
+  TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, rscale, weight, tw, xt, st));
+  CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, 0, st));
+  return MXMOE_OK;
+}
+
+int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_t d_model, uint32_t k,
+                  const int32_t* topk_idx, const int32_t* inv, const float* pair_out, int residual, void* y,
+                  mxmoe_dtype y_dtype, void* stream) {
+  if (n_tokens == 0) return MXMOE_OK;
+  if (!y || (residual && !x) || (k > 0 && (!topk_idx || !inv || !pair_out)))
+    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (k > static_cast<uint32_t>(kMaxTopK)) return fail(MXMOE_ERR_UNSUPPORTED, "k=%u", k);
+  CUDA_TRY(launch_combine(x, x_dtype, pair_out, topk_idx, inv, n_tokens, d_model, k, residual, y, y_dtype,
+                          as_stream(stream)));
+  return MXMOE_OK;
+}
+
+}  // extern "C"

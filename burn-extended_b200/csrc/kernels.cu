@@ -1,0 +1,546 @@
+// kernels.cu -- the CUDA-core kernels of the MoE hot path: MXFP4 dequant,
+// router (RmsNorm + gate + top-k + softmax), canonical permutation, activation
+// quantization into block-scaled E4M3 terms, combine, and the SIMT expert FFN
+// (an independent GPU implementation used to cross-check the tensor-core one).
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+
+#include "kernels.h"
+#include "layout.cuh"
+#include "quant.cuh"
+
+namespace mxmoe {
+
+namespace {
+
+// E2M1 code -> value (src/loader/mxfp4.rs:11-13); codes 8..15 are negatives
+// of 0..7, with -0.0 for code 8.
+__constant__ float kFp4Lut[16] = {0.0f,  0.5f,  1.0f,  1.5f,  2.0f,  3.0f,  4.0f,  6.0f,
+                                  -0.0f, -0.5f, -1.0f, -1.5f, -2.0f, -3.0f, -4.0f, -6.0f};
+
+template <typename T>
+__device__ __forceinline__ float load_f32(const T* p, uint64_t i);
+template <>
+__device__ __forceinline__ float load_f32<float>(const float* p, uint64_t i) { return p[i]; }
+template <>
+__device__ __forceinline__ float load_f32<__nv_bfloat16>(const __nv_bfloat16* p, uint64_t i) {
+  return __bfloat162float(p[i]);
+}
+
+__device__ __forceinline__ float load_any(const void* p, int dtype, uint64_t i) {
+  return dtype == 0 ? static_cast<const float*>(p)[i]
+                    : __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
+}
+__device__ __forceinline__ void store_any(void* p, int dtype, uint64_t i, float v) {
+  if (dtype == 0) static_cast<float*>(p)[i] = v;
+  else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
+}
+
+// Butterfly sum over the warp: offsets 16, 8, 4, 2, 1.  Every lane ends with
+// the same value (IEEE addition is commutative).
+__device__ __forceinline__ float warp_sum_butterfly(float v) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// ------------------------------------------------------------------ dequant
+// src/loader/mxfp4.rs:57-79: out[r, 2i + {0,1}] = LUT[lo/hi] * 2^(s_r - 127).
+__global__ void dequant_bytes_kernel(const uint8_t* __restrict__ blocks, uint64_t rows, uint64_t b,
+                                     const uint8_t* __restrict__ scales, float* __restrict__ out) {
+  const uint64_t total = rows * b;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = i / b;
+    const float scale = ldexpf(1.0f, static_cast<int>(scales[r]) - 127);
+    const uint8_t byte = blocks[i];
+    out[2 * i] = kFp4Lut[byte & 0x0F] * scale;
+    out[2 * i + 1] = kFp4Lut[byte >> 4] * scale;
+  }
+}
+
+// MoE layout (src/quant/gpu.rs:124-134): blocks [rows][bpr], scales [rows][gpr].
+__global__ void dequant_rows_kernel(const uint8_t* __restrict__ blocks, const uint8_t* __restrict__ scales,
+                                    uint64_t rows, uint64_t cols, uint64_t bpr, uint64_t gpr, int ue8,
+                                    float* __restrict__ out) {
+  const uint64_t total = rows * cols;
+  for (uint64_t i = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const uint64_t r = i / cols, c = i % cols;
+    const uint8_t byte = blocks[r * bpr + (c >> 1)];
+    const uint8_t nib = (c & 1) ? (byte >> 4) : (byte & 0x0F);
+    const int e = static_cast<int>(scales[r * gpr + (c >> 5)]) - 127 - ue8;
+    out[i] = kFp4Lut[nib] * ldexpf(1.0f, e);
+  }
+}
+
+// ------------------------------------------------------------------ router
+// Top-k (ties to the lower index) + softmax over the k selected values
+// (src/moe/mod.rs:272-276).  One thread per token.
+__device__ void topk_softmax_row(const float* lg, int E, int k, int32_t* idx_out, float* w_out) {
+  int32_t idx[kMaxTopK];
+  float val[kMaxTopK];
+  for (int s = 0; s < k; ++s) {
+    int best = -1;
+    for (int e = 0; e < E; ++e) {
+      bool taken = false;
+      for (int q = 0; q < s; ++q) taken |= (idx[q] == e);
+      if (taken) continue;
+      if (best < 0 || lg[e] > lg[best]) best = e;
+    }
+    idx[s] = best;
+    val[s] = lg[best];
+  }
+  float ex[kMaxTopK];
+  float sum = 0.0f;
+  for (int s = 0; s < k; ++s) {
+    ex[s] = expf(__fsub_rn(val[s], val[0]));
+    sum = __fadd_rn(sum, ex[s]);
+  }
+  for (int s = 0; s < k; ++s) {
+    idx_out[s] = idx[s];
+    w_out[s] = __fdiv_rn(ex[s], sum);
+  }
+}
+
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int E, int k, int32_t* topk_idx,
+                                    float* topk_w) {
+  const int t = blockIdx.x * blockDim.x + threadIdx.x;
+  if (t >= n) return;
+  topk_softmax_row(logits + static_cast<uint64_t>(t) * E, E, k, topk_idx + static_cast<uint64_t>(t) * k,
+                   topk_w + static_cast<uint64_t>(t) * k);
+}
+
+// RmsNorm (src/moe/mod.rs:109) + gate Linear (:110) + top-k/softmax (:272-276).
+// kRouterTok tokens per block; the block's normalized rows sit in smem so
+// every gate weight read from L2 serves kRouterTok tokens.  Summation order
+// is fixed (32 lane chains of fused multiply-adds, then a butterfly) so that
+// the logits are reproducible bit for bit by the CPU restatement.
+constexpr int kRouterTok = 4;
+constexpr int kRouterThreads = 256;
+
+template <typename XT>
+__global__ void __launch_bounds__(kRouterThreads)
+    router_kernel(const XT* __restrict__ x, int n, int d, int E, int k, const float* __restrict__ gamma,
+                  const float* __restrict__ gate_w, const float* __restrict__ gate_b, float eps,
+                  float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                  float* __restrict__ rscale) {
+  extern __shared__ float sm[];
+  float* nrm = sm;                        // [kRouterTok][d]
+  float* lg = sm + kRouterTok * d;        // [kRouterTok][E]
+  float* rs = lg + kRouterTok * E;        // [kRouterTok]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t0 = blockIdx.x * kRouterTok;
+  const int nt = min(kRouterTok, n - t0);
+
+  if (warp < nt) {
+    const XT* xr = x + static_cast<uint64_t>(t0 + warp) * d;
+    float acc = 0.0f;
+    for (int c = lane; c < d; c += 32) {
+      const float v = load_f32(xr, c);
+      acc = __fmaf_rn(v, v, acc);
+    }
+    const float ss = warp_sum_butterfly(acc);
+    if (lane == 0) rs[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nt * d; i += blockDim.x) {
+    const int t = i / d, c = i - t * d;
+    const float v = load_f32(x, static_cast<uint64_t>(t0 + t) * d + c);
+    nrm[i] = __fmul_rn(__fmul_rn(v, rs[t]), gamma[c]);
+  }
+  __syncthreads();
+  for (int e = warp; e < E; e += kRouterThreads / 32) {
+    const float* w = gate_w + static_cast<uint64_t>(e) * d;
+    float acc[kRouterTok];
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0f;
+    for (int c = lane; c < d; c += 32) {
+      const float wv = __ldg(w + c);
+#pragma unroll
+      for (int t = 0; t < kRouterTok; ++t) acc[t] = __fmaf_rn(nrm[t * d + c], wv, acc[t]);
+    }
+#pragma unroll
+    for (int t = 0; t < kRouterTok; ++t) {
+      const float s = warp_sum_butterfly(acc[t]);
+      if (lane == 0) lg[t * E + e] = __fadd_rn(s, gate_b[e]);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < nt) {
+    const int t = t0 + threadIdx.x;
+    const float* l = lg + threadIdx.x * E;
+    if (logits_out)
+      for (int e = 0; e < E; ++e) logits_out[static_cast<uint64_t>(t) * E + e] = l[e];
+    topk_softmax_row(l, E, k, topk_idx + static_cast<uint64_t>(t) * k, topk_w + static_cast<uint64_t>(t) * k);
+    rscale[t] = rs[threadIdx.x];
+  }
+}
+
+// ------------------------------------------------------------------ permute
+// Canonical permutation (replaces src/moe/mod.rs:279-288): pairs p = t*k+s are
+// stably sorted by expert id.  One block of 1024 threads; warp w owns a
+// contiguous segment of pairs, so the order within an expert is (t, s).
+// Writes the unpadded canonical maps (offsets / perm_c / inv_c, optional)
+// and the padded maps used by the GEMMs, where every expert segment starts
+// at a multiple of `pad` rows.
+constexpr int kPermThreads = 1024;
+
+__global__ void __launch_bounds__(kPermThreads)
+    permute_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
+                   int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
+                   int32_t* perm_p, int32_t* inv_p) {
+  extern __shared__ int32_t cnt[];  // [32 warps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int seg = (P + 31) / 32;
+  const int p_begin = warp * seg, p_end = min(P, p_begin + seg);
+  for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) cnt[i] = 0;
+  __syncthreads();
+  for (int base = p_begin; base < p_end; base += 32) {
+    const int p = base + lane;
+    const int ex = p < p_end ? topk_idx[p] : -1;
+    const unsigned grp = __match_any_sync(0xFFFFFFFFu, ex);
+    if (ex >= 0 && lane == __ffs(grp) - 1) cnt[warp * E + ex] += __popc(grp);
+    __syncwarp();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0, prun = 0, trun = 0;
+    for (int e = 0; e < E; ++e) {
+      int tot = 0;
+      for (int w = 0; w < 32; ++w) tot += cnt[w * E + e];
+      if (offsets) offsets[e] = run;
+      poff[e] = prun;
+      counts[e] = tot;
+      if (ntile_prefix) ntile_prefix[e] = trun;
+      run += tot;
+      prun += (tot + pad - 1) / pad * pad;
+      trun += (tot + N - 1) / N;
+    }
+    if (offsets) offsets[E] = run;
+    poff[E] = prun;
+    if (ntile_prefix) ntile_prefix[E] = trun;
+  }
+  __syncthreads();
+  // per-warp running bases: [0] canonical, stored in place; padded = canonical - offsets + poff
+  if (threadIdx.x < E) {
+    const int e = threadIdx.x;
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+  }
+  __syncthreads();
+  for (int base = p_begin; base < p_end; base += 32) {
+    const int p = base + lane;
+    const int ex = p < p_end ? topk_idx[p] : -1;
+    const unsigned grp = __match_any_sync(0xFFFFFFFFu, ex);
+    if (ex >= 0) {
+      const int rank = cnt[warp * E + ex] + __popc(grp & ((1u << lane) - 1u));
+      const int pos_p = poff[ex] + rank;
+      perm_p[pos_p] = p;
+      inv_p[p] = pos_p;
+      if (perm_c) {
+        int o = 0;
+        for (int e = 0; e < ex; ++e) o += counts[e];
+        perm_c[o + rank] = p;
+        inv_c[p] = o + rank;
+      }
+    }
+    __syncwarp();
+    if (ex >= 0 && lane == __ffs(grp) - 1) cnt[warp * E + ex] += __popc(grp);
+    __syncwarp();
+  }
+}
+
+// ------------------------------------------------------------------ quantize
+// Gathers each routed pair's token row into its padded expert-sorted position
+// and writes it as `terms` block-scaled E4M3 terms (two reproduce bf16 input
+// with unit gain exactly; three are used for f32 input or a non-unit gain).
+// One warp per pair, sweeping 32-column blocks.
+__global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
+                                      const float* __restrict__ gamma, int gamma_is_one,
+                                      const int32_t* __restrict__ inv_p, int terms, uint8_t* codes,
+                                      uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride,
+                                      int kchunks) {
+  const int warps_total = gridDim.x * (blockDim.x >> 5);
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  const int P = n * k;
+  for (int p = gw; p < P; p += warps_total) {
+    const int t = p / k;
+    const int pos = inv_p[p];
+    for (int c0 = 0; c0 < d; c0 += 32) {
+      const int c = c0 + lane;
+      float u = c < d ? load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c) : 0.0f;
+      if (!gamma_is_one && c < d) u = __fmul_rn(u, gamma[c]);
+      uint8_t code[kMaxTerms], sbyte[kMaxTerms];
+      split_e4m3_terms(u, terms, code, sbyte);
+      const uint64_t off = static_cast<uint64_t>(pos) * kp + c;
+      const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(c0 / 32),
+                                    static_cast<uint32_t>(kchunks));
+      for (int q = 0; q < terms; ++q) {
+        if (c < d) codes[q * term_stride + off] = code[q];
+        if (lane == 0) sf[q * sf_term_stride + so] = sbyte[q];
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ combine
+// y[t] = x[t] + sum over the token's experts in increasing expert index of
+// y_pair (src/moe/mod.rs:279, :405, :411).
+__global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const float* __restrict__ y_pair,
+                               const int32_t* __restrict__ topk_idx, const int32_t* __restrict__ inv_p, int n, int d,
+                               int k, int residual, void* y, int y_dtype) {
+  const int t = blockIdx.x;
+  if (t >= n) return;
+  int ord[kMaxTopK];
+  int ex[kMaxTopK];
+  for (int s = 0; s < k; ++s) {
+    ord[s] = inv_p[t * k + s];
+    ex[s] = topk_idx[t * k + s];
+  }
+  for (int a = 1; a < k; ++a)
+    for (int b = a; b > 0 && ex[b - 1] > ex[b]; --b) {
+      int tmp = ex[b]; ex[b] = ex[b - 1]; ex[b - 1] = tmp;
+      tmp = ord[b]; ord[b] = ord[b - 1]; ord[b - 1] = tmp;
+    }
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float acc = 0.0f;
+    for (int s = 0; s < k; ++s) acc = __fadd_rn(acc, y_pair[static_cast<uint64_t>(ord[s]) * d + c]);
+    const float v = k == 0 ? load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c)
+                    : residual ? __fadd_rn(load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c), acc) : acc;
+    store_any(y, y_dtype, static_cast<uint64_t>(t) * d + c, v);
+  }
+}
+
+// ------------------------------------------------------------------ expert-parallel helpers
+// Global -> local expert ids for the receive side; ids outside the shard are
+// reported through *err (code 7) and mapped to expert 0 so indexing stays safe.
+__global__ void localize_kernel(const int32_t* __restrict__ expert, int P, int begin, int count, int32_t* local,
+                                int* err) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P) return;
+  int v = expert[i] - begin;
+  if (v < 0 || v >= count) {
+    atomicCAS(err, 0, 7);
+    v = 0;
+  }
+  local[i] = v;
+}
+
+// Dispatch packing: one block per permuted position q.
+__global__ void gather_pairs_kernel(const void* __restrict__ x, int x_dtype, int d, int k,
+                                    const int32_t* __restrict__ perm, const float* __restrict__ rscale,
+                                    const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
+                                    void* out_x, float* out_rscale, int32_t* out_expert, float* out_w) {
+  const int q = blockIdx.x;
+  const int p = perm[q];
+  const int t = p / k;
+  if (threadIdx.x == 0) {
+    if (out_rscale) out_rscale[q] = rscale[t];
+    if (out_expert) out_expert[q] = topk_idx[p];
+    if (out_w) out_w[q] = topk_w[p];
+  }
+  const uint64_t src = static_cast<uint64_t>(t) * d, dst = static_cast<uint64_t>(q) * d;
+  if (x_dtype == 0) {
+    const float* xs = static_cast<const float*>(x);
+    float* xd = static_cast<float*>(out_x);
+    for (int c = threadIdx.x; c < d; c += blockDim.x) xd[dst + c] = xs[src + c];
+  } else {
+    const uint16_t* xs = static_cast<const uint16_t*>(x);
+    uint16_t* xd = static_cast<uint16_t*>(out_x);
+    for (int c = threadIdx.x; c < d; c += blockDim.x) xd[dst + c] = xs[src + c];
+  }
+}
+
+// ------------------------------------------------------------------ SIMT FFN
+__device__ __forceinline__ float w_value(const uint8_t* codes, const uint8_t* sfa, uint64_t row_bytes, int kchunks,
+                                         uint32_t row, uint32_t col) {
+  const uint8_t byte = codes[row * row_bytes + (col >> 1)];
+  const uint8_t nib = (col & 1) ? (byte >> 4) : (byte & 0x0F);
+  const int s = static_cast<int>(sfa[sf_offset(row, col / 32, kchunks)]) - 127;
+  return kFp4Lut[nib] * ldexpf(1.0f, s);
+}
+
+// W1 + SwiGLU on CUDA cores: one warp per (expert, GLU unit j), looping over
+// the expert's pairs.  act [rows][fp] f32.
+__global__ void simt_w1_kernel(const void* __restrict__ x, int x_dtype, int d, int k, const float* __restrict__ gamma,
+                               const float* __restrict__ rscale, const uint8_t* __restrict__ w1q,
+                               const uint8_t* __restrict__ w1sf, const float* __restrict__ b1, int fp, int kp1,
+                               const int32_t* __restrict__ poff, const int32_t* __restrict__ counts,
+                               const int32_t* __restrict__ perm_p, float alpha, float limit, float* act) {
+  const int e = blockIdx.y;
+  const int j = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (j >= fp) return;
+  const uint64_t rows = 2ull * fp;
+  const uint8_t* codes = w1q + static_cast<uint64_t>(e) * rows * (kp1 / 2);
+  const uint8_t* sfa = w1sf + static_cast<uint64_t>(e) * (rows / kRowBlock) * (kp1 / kTileK) * kSfAtomBytes;
+  const uint32_t rg = w1_packed_row(j, 0), rl = w1_packed_row(j, 1);
+  const float bg = b1[static_cast<uint64_t>(e) * rows + rg];
+  const float bl = b1[static_cast<uint64_t>(e) * rows + rl];
+  const int p0 = poff[e], cnt = counts[e];
+  for (int i = 0; i < cnt; ++i) {
+    const int pos = p0 + i;
+    const int t = perm_p[pos] / k;
+    const float r = rscale[t];
+    float sg = 0.f, sl = 0.f;
+    for (int c = lane; c < d; c += 32) {
+      const float u = __fmul_rn(__fmul_rn(load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c), r), gamma[c]);
+      sg = fmaf(u, w_value(codes, sfa, kp1 / 2, kp1 / kTileK, rg, c), sg);
+      sl = fmaf(u, w_value(codes, sfa, kp1 / 2, kp1 / kTileK, rl, c), sl);
+    }
+    sg = warp_sum_butterfly(sg);
+    sl = warp_sum_butterfly(sl);
+    if (lane == 0) {
+      const float xg = fminf(sg + bg, limit);
+      const float xl = fmaxf(-limit, fminf(sl + bl, limit));
+      act[static_cast<uint64_t>(pos) * fp + j] = (xg / (1.0f + expf(-alpha * xg))) * (xl + 1.0f);
+    }
+  }
+}
+
+// W2 + bias + routing weight on CUDA cores: one warp per (expert, output c).
+__global__ void simt_w2_kernel(const float* __restrict__ act, int fp, int d, int k, const uint8_t* __restrict__ w2q,
+                               const uint8_t* __restrict__ w2sf, const float* __restrict__ b2, float bias_mult,
+                               int kp2, const int32_t* __restrict__ poff, const int32_t* __restrict__ counts,
+                               const int32_t* __restrict__ perm_p, const float* __restrict__ topk_w,
+                               float* y_pair) {
+  const int e = blockIdx.y;
+  const int c = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (c >= d) return;
+  const uint64_t row_blocks = (d + kRowBlock - 1) / kRowBlock;
+  const uint8_t* codes = w2q + static_cast<uint64_t>(e) * d * (kp2 / 2);
+  const uint8_t* sfa = w2sf + static_cast<uint64_t>(e) * row_blocks * (kp2 / kTileK) * kSfAtomBytes;
+  const float bb = b2[static_cast<uint64_t>(e) * d + c] * bias_mult;
+  const int p0 = poff[e], cnt = counts[e];
+  for (int i = 0; i < cnt; ++i) {
+    const int pos = p0 + i;
+    const float* a = act + static_cast<uint64_t>(pos) * fp;
+    float s = 0.f;
+    for (int j = lane; j < fp; j += 32) s = fmaf(a[j], w_value(codes, sfa, kp2 / 2, kp2 / kTileK, c, j), s);
+    s = warp_sum_butterfly(s);
+    if (lane == 0) y_pair[static_cast<uint64_t>(pos) * d + c] = (s + bb) * topk_w[perm_p[pos]];
+  }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ launchers
+cudaError_t launch_dequant_bytes(const uint8_t* blocks, uint64_t rows, uint64_t b, const uint8_t* scales, float* out,
+                                 cudaStream_t st) {
+  const uint64_t total = rows * b;
+  if (total == 0) return cudaSuccess;
+  const int grid = static_cast<int>(total / 256 + 1 < 148 * 16 ? total / 256 + 1 : 148 * 16);
+  dequant_bytes_kernel<<<grid, 256, 0, st>>>(blocks, rows, b, scales, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dequant_rows(const uint8_t* blocks, const uint8_t* scales, uint64_t rows, uint64_t cols,
+                                uint64_t bpr, uint64_t gpr, int ue8, float* out, cudaStream_t st) {
+  const uint64_t total = rows * cols;
+  if (total == 0) return cudaSuccess;
+  const int grid = static_cast<int>(total / 256 + 1 < 148 * 16 ? total / 256 + 1 : 148 * 16);
+  dequant_rows_kernel<<<grid, 256, 0, st>>>(blocks, scales, rows, cols, bpr, gpr, ue8, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_t* idx, float* w, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  topk_softmax_kernel<<<(n + 127) / 128, 128, 0, st>>>(logits, n, E, k, idx, w);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
+                          const float* gate_w, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
+                          float* topk_w, float* rscale, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  const size_t smem = (static_cast<size_t>(kRouterTok) * (d + E) + kRouterTok) * sizeof(float);
+  const int grid = (n + kRouterTok - 1) / kRouterTok;
+  if (x_dtype == 0) {
+    cudaFuncSetAttribute(router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    router_kernel<float><<<grid, kRouterThreads, smem, st>>>(static_cast<const float*>(x), n, d, E, k, gamma, gate_w,
+                                                             gate_b, eps, logits, topk_idx, topk_w, rscale);
+  } else {
+    cudaFuncSetAttribute(router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                         static_cast<int>(smem));
+    router_kernel<__nv_bfloat16><<<grid, kRouterThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), n, d, E,
+                                                                     k, gamma, gate_w, gate_b, eps, logits, topk_idx,
+                                                                     topk_w, rscale);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
+                           int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
+                           int32_t* inv_p, cudaStream_t st) {
+  const size_t smem = static_cast<size_t>(32) * E * sizeof(int32_t);
+  cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  permute_kernel<<<1, kPermThreads, smem, st>>>(topk_idx, P, E, pad, N, offsets, perm_c, inv_c, poff, counts,
+                                                ntile_prefix, perm_p, inv_p);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
+                                  int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
+                                  uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
+                                  cudaStream_t st) {
+  const int P = n * k;
+  if (P == 0) return cudaSuccess;
+  const int warps = P < 148 * 64 ? P : 148 * 64;
+  quantize_pairs_kernel<<<(warps + 7) / 8, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms,
+                                                         codes, term_stride, kp, sf, sf_term_stride, kchunks);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_combine(const void* x, int x_dtype, const float* y_pair, const int32_t* topk_idx,
+                           const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
+                           cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  combine_kernel<<<n, 256, 0, st>>>(x, x_dtype, y_pair, topk_idx, inv_p, n, d, k, residual, y, y_dtype);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, int32_t* local, int* err,
+                            cudaStream_t st) {
+  if (P == 0) return cudaSuccess;
+  localize_kernel<<<(P + 255) / 256, 256, 0, st>>>(expert, P, begin, count, local, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_gather_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
+                                const float* rscale, const int32_t* topk_idx, const float* topk_w, void* out_x,
+                                float* out_rscale, int32_t* out_expert, float* out_w, cudaStream_t st) {
+  if (P == 0) return cudaSuccess;
+  gather_pairs_kernel<<<P, 256, 0, st>>>(x, x_dtype, d, k, perm, rscale, topk_idx, topk_w, out_x, out_rscale,
+                                         out_expert, out_w);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
+                           const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
+                           const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
+                           float* act, cudaStream_t st) {
+  dim3 grid((fp + 7) / 8, E);
+  simt_w1_kernel<<<grid, 256, 0, st>>>(x, x_dtype, d, k, gamma, rscale, w1q, w1sf, b1, fp, kp1, poff, counts, perm_p,
+                                       alpha, limit, act);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_simt_w2(const float* act, int fp, int d, int k, const uint8_t* w2q, const uint8_t* w2sf,
+                           const float* b2, float bias_mult, int kp2, int E, const int32_t* poff,
+                           const int32_t* counts, const int32_t* perm_p, const float* topk_w, float* y_pair,
+                           cudaStream_t st) {
+  dim3 grid((d + 7) / 8, E);
+  simt_w2_kernel<<<grid, 256, 0, st>>>(act, fp, d, k, w2q, w2sf, b2, bias_mult, kp2, poff, counts, perm_p, topk_w,
+                                       y_pair);
+  return cudaGetLastError();
+}
+
+}  // namespace mxmoe

@@ -1,0 +1,42 @@
+// kernels.h -- launchers of the CUDA-core kernels (kernels.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <cstdint>
+
+namespace mxmoe {
+
+constexpr int kMaxTopK = 8;
+
+cudaError_t launch_dequant_bytes(const uint8_t* blocks, uint64_t rows, uint64_t b, const uint8_t* scales, float* out,
+                                 cudaStream_t st);
+cudaError_t launch_dequant_rows(const uint8_t* blocks, const uint8_t* scales, uint64_t rows, uint64_t cols,
+                                uint64_t bpr, uint64_t gpr, int ue8, float* out, cudaStream_t st);
+cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_t* idx, float* w, cudaStream_t st);
+cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
+                          const float* gate_w, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
+                          float* topk_w, float* rscale, cudaStream_t st);
+cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
+                           int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
+                           int32_t* inv_p, cudaStream_t st);
+cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
+                                  int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
+                                  uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
+                                  cudaStream_t st);
+cudaError_t launch_combine(const void* x, int x_dtype, const float* y_pair, const int32_t* topk_idx,
+                           const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
+                           cudaStream_t st);
+cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, int32_t* local, int* err,
+                            cudaStream_t st);
+cudaError_t launch_gather_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
+                                const float* rscale, const int32_t* topk_idx, const float* topk_w, void* out_x,
+                                float* out_rscale, int32_t* out_expert, float* out_w, cudaStream_t st);
+cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
+                           const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
+                           const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
+                           float* act, cudaStream_t st);
+cudaError_t launch_simt_w2(const float* act, int fp, int d, int k, const uint8_t* w2q, const uint8_t* w2sf,
+                           const float* b2, float bias_mult, int kp2, int E, const int32_t* poff,
+                           const int32_t* counts, const int32_t* perm_p, const float* topk_w, float* y_pair,
+                           cudaStream_t st);
+
+}  // namespace mxmoe

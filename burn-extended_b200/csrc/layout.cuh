@@ -1,0 +1,48 @@
+// layout.cuh -- device-resident data layouts shared by the host runtime and
+// the kernels.
+//
+// Weights (written once by mxmoe_upload_experts):
+//   W1 codes  [E][2*fp][Kp1/2]  E2M1 nibble pairs, rows regrouped into 64-row
+//             blocks that alternate GLU / linear (row of GLU unit j at
+//             w1_packed_row(j, 0), its linear partner at w1_packed_row(j, 1)),
+//             so one 128-row tensor-core tile holds 64 complete GLU pairs.
+//             fp = f rounded up to 64, Kp1 = d rounded up to 128 (zero codes).
+//   W2 codes  [E][d][Kp2/2], Kp2 = fp rounded up to 128.
+//   scales    E8M0 with the file offset removed, stored as 512-byte atoms that
+//             the MMA's scale-factor TMEM layout reads directly:
+//             atom (row block of 128, k chunk of 4 x 32 columns);
+//             byte (r % 32) * 16 + (r / 32 % 4) * 4 + (kb % 4).
+// Activations (per forward, rows = routed (token, expert) pairs sorted by
+// expert, every expert segment padded to a multiple of 128 rows):
+//   codes     [2 terms][rows][Kp] E4M3 (value = hi + lo, two block-scaled terms)
+//   scales    [2 terms][rows/128][Kp/128] atoms, same byte order as weights.
+#pragma once
+#include <cstdint>
+
+namespace mxmoe {
+
+constexpr int kTileK = 128;        // K elements per pipeline stage / TMA box
+constexpr int kRowBlock = 128;     // rows per scale-factor atom
+constexpr int kSfAtomBytes = 512;  // 128 rows x 4 scale bytes
+constexpr int kGluBlock = 64;      // GLU/linear interleave granularity (rows)
+constexpr int kTerms = 2;          // E4M3 terms per activation (hi, lo)
+
+__host__ __device__ inline uint32_t round_up(uint32_t v, uint32_t m) { return (v + m - 1) / m * m; }
+
+__host__ __device__ inline uint32_t sf_atom_byte(uint32_t row_in_block, uint32_t kb_in_chunk) {
+  return (row_in_block & 31u) * 16u + ((row_in_block >> 5) & 3u) * 4u + (kb_in_chunk & 3u);
+}
+
+// Packed W1 row of GLU unit j (half = 0) or its linear partner (half = 1).
+__host__ __device__ inline uint32_t w1_packed_row(uint32_t j, uint32_t half) {
+  return (j / kGluBlock) * (2 * kGluBlock) + half * kGluBlock + (j % kGluBlock);
+}
+
+// Byte offset of the scale of (row, k block) inside an atom array laid out
+// [row_blocks][k_chunks][512].
+__host__ __device__ inline uint64_t sf_offset(uint32_t row, uint32_t kb, uint32_t k_chunks) {
+  return (static_cast<uint64_t>(row / kRowBlock) * k_chunks + kb / 4) * kSfAtomBytes +
+         sf_atom_byte(row % kRowBlock, kb % 4);
+}
+
+}  // namespace mxmoe

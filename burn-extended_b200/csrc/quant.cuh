@@ -1,0 +1,52 @@
+// quant.cuh -- splitting an f32 activation into a sum of block-scaled E4M3
+// terms (the operand format of kind::mxf8f6f4 with E8M0 scales).
+//
+// A block is 32 consecutive K elements held by the 32 lanes of one warp.  Term
+// t is  code_t * 2^s_t  with s_t chosen so that the block's largest remaining
+// magnitude fits E4M3 (<= 448); the residual after each term is exact in f32,
+// so n terms carry about 4n significant bits: two terms reproduce a bf16 value
+// exactly, three cover f32 inputs to ~2^-13.
+#pragma once
+#include <cuda_fp8.h>
+#include <cstdint>
+
+namespace mxmoe {
+
+constexpr int kMaxTerms = 3;
+
+// E8M0 exponent s (value 2^s) such that amax * 2^-s <= 448 (E4M3 max).
+__device__ __forceinline__ int e4m3_block_exp(float amax) {
+  const uint32_t bits = __float_as_uint(amax);
+  const int ef = static_cast<int>((bits >> 23) & 0xFF);
+  if (ef == 0) return -127;  // zero or subnormal block
+  const uint32_t mant = bits & 0x7FFFFFu;
+  const int s = (ef - 127) - (mant <= 0x600000u ? 8 : 7);  // 1.75 * 2^8 == 448
+  return s < -127 ? -127 : (s > 127 ? 127 : s);
+}
+
+__device__ __forceinline__ float warp_max_abs(float v) {
+  v = fabsf(v);
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xFFFFFFFFu, v, o));
+  return v;
+}
+
+// Warp-collective: lane l holds element l of a 32-block.  Writes `terms`
+// codes and the per-term E8M0 bytes (same in every lane).
+__device__ __forceinline__ void split_e4m3_terms(float u, int terms, uint8_t (&code)[kMaxTerms],
+                                                 uint8_t (&sbyte)[kMaxTerms]) {
+  float r = u;
+#pragma unroll
+  for (int t = 0; t < kMaxTerms; ++t) {
+    if (t < terms) {
+      const int s = e4m3_block_exp(warp_max_abs(r));
+      const __nv_fp8_storage_t c = __nv_cvt_float_to_fp8(ldexpf(r, -s), __NV_SATFINITE, __NV_E4M3);
+      const float cv = __half2float(__half(__nv_cvt_fp8_to_halfraw(c, __NV_E4M3)));
+      r = r - ldexpf(cv, s);
+      code[t] = c;
+      sbyte[t] = static_cast<uint8_t>(s + 127);
+    }
+  }
+}
+
+}  // namespace mxmoe

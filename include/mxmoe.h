@@ -1,0 +1,257 @@
+/*
+ * mxmoe.h -- C ABI of the B200 (sm_100a) MXFP4 mixture-of-experts layer.
+ *
+ * This is the drop-in boundary for burn-extended's `moe` / `quant` modules:
+ * every entry point below replaces one reference item (cited file:line, paths
+ * relative to the burn-extended crate root).  All functions return an
+ * mxmoe_status; they never abort or throw across the boundary.  The message
+ * of the last failure on the calling thread is available from
+ * mxmoe_last_error().  `stream` arguments are cudaStream_t values passed as
+ * plain pointers (NULL = legacy default stream).
+ *
+ * Threading: a layer handle serves one stream at a time; distinct handles are
+ * independent.  Forward calls are stream-ordered and asynchronous.
+ */
+#ifndef MXMOE_H
+#define MXMOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MXMOE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define MXMOE_API __attribute__((visibility("default")))
+#else
+#define MXMOE_API
+#endif
+
+typedef enum mxmoe_status {
+  MXMOE_OK = 0,
+  MXMOE_ERR_INVALID_ARG = 1,   /* null pointer, bad shape, bad flag */
+  MXMOE_ERR_NOT_READY = 2,     /* forward before the weights were uploaded */
+  MXMOE_ERR_CUDA = 3,          /* a CUDA runtime/driver call failed */
+  MXMOE_ERR_OOM = 4,           /* device allocation failed */
+  MXMOE_ERR_UNSUPPORTED = 5,   /* shape outside what the kernels handle */
+  MXMOE_ERR_TIMEOUT = 6,       /* a bounded device-side wait gave up */
+  MXMOE_ERR_TOO_LARGE = 7      /* request exceeds a fixed-size buffer */
+} mxmoe_status;
+
+/* Element types of activation / bias buffers. */
+typedef enum mxmoe_dtype {
+  MXMOE_F32 = 0,
+  MXMOE_BF16 = 1
+} mxmoe_dtype;
+
+/* Behaviour flags (mxmoe_config.flags). */
+#define MXMOE_FLAG_INTERLEAVED_GLU 0x1u /* W1 rows interleaved [glu0, lin0, ...]
+                                           (src/activation/mod.rs:28-30);
+                                           default split-half rows [glu; lin]
+                                           as src/quant/gpu.rs:108-113 reads */
+#define MXMOE_FLAG_BIAS_PER_FTILE  0x2u /* reproduce src/quant/gpu.rs:191: b2 is
+                                           added once per 256-wide f tile */
+#define MXMOE_FLAG_NO_RESIDUAL     0x4u /* y = moe(x) (no x + ... at
+                                           src/moe/mod.rs:411) */
+#define MXMOE_FLAG_DISABLED        0x8u /* MoeConfig.disabled: y = x
+                                           (src/moe/mod.rs:106-108) */
+#define MXMOE_FLAG_SIMT            0x10u /* run the expert FFN on the CUDA-core
+                                            kernels instead of tcgen05 (a second,
+                                            independent GPU implementation used to
+                                            cross-check the tensor-core path) */
+
+/* Mirrors moe::MoeConfig (src/moe/mod.rs:22-33).  `initializer` and `verbose`
+ * have no device meaning; swiglu_alpha / swiglu_limit are honoured (the
+ * reference kernel hardcodes 1.702 / 7.0 at src/quant/gpu.rs:140-141). */
+typedef struct mxmoe_config {
+  uint32_t d_model;
+  uint32_t ffn_hidden;
+  uint32_t num_experts;
+  uint32_t experts_per_token;
+  float swiglu_alpha;
+  float swiglu_limit;
+  float rms_eps;          /* RmsNorm epsilon (model.bin header stores 1e-5) */
+  uint32_t flags;         /* MXMOE_FLAG_* */
+  int32_t device;         /* CUDA device ordinal the layer lives on */
+} mxmoe_config;
+
+/* Field-for-field quant::QuantLinearMxFp4Desc (src/quant/mod.rs:3-11).
+ * blocks: [experts][rows][bpr] bytes, two E2M1 codes per byte (low nibble =
+ * even column); scales: [experts][rows][gpr] E8M0 bytes, one per 32 columns;
+ * stored exponent = true exponent + 127 + ue8_offset (model.bin uses 14,
+ * src/loader/modelbin.rs:452-453). */
+typedef struct mxmoe_quant_desc {
+  uint64_t experts;
+  uint64_t rows;
+  uint64_t cols;
+  uint64_t bpr;
+  uint64_t gpr;
+  int32_t ue8_offset;
+} mxmoe_quant_desc;
+
+typedef struct mxmoe_layer mxmoe_layer;
+
+/* ABI version and a short build description. */
+MXMOE_API int mxmoe_abi_version(void);
+MXMOE_API const char* mxmoe_build_info(void);
+
+/* Thread-local message of the last failure (truncated to cap bytes). */
+MXMOE_API int mxmoe_last_error(char* buf, size_t cap);
+
+/* Replaces MoeConfig::init (src/moe/mod.rs:60-91): validates the config and
+ * creates an empty layer on cfg->device. */
+MXMOE_API int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out);
+
+/* Frees every device buffer the layer owns. */
+MXMOE_API int mxmoe_destroy(mxmoe_layer* layer);
+
+/* Router parameters: the MoE block's RmsNorm gain (`norm`, src/moe/mod.rs:37,
+ * [d]) and the gate Linear (`gate`, :38) as weight [E][d] (output-major; Burn's
+ * Linear keeps [d][E] -- the Rust shim transposes) and bias [E].  Host
+ * pointers; dtype applies to all three.  Copies are made; the caller keeps its
+ * buffers. */
+MXMOE_API int mxmoe_set_router(mxmoe_layer* layer, const void* norm_gamma,
+                     const void* gate_w, const void* gate_b, mxmoe_dtype dtype,
+                     void* stream);
+
+/* Replaces MoeQuantLayerResident::new (src/quant/gpu.rs:31-53) together with
+ * set_resident (src/moe/mod.rs:95-97) and the bias params (:42, :45).
+ * Host pointers; W1 is [E][2f][d] (split-half or interleaved rows per the
+ * config flag), W2 is [E][d][f].  The library repacks into its tensor-core
+ * operand layout (scale offset removed, rows/columns padded) and owns the
+ * device copies; the caller keeps its buffers.  b1 [E][2f], b2 [E][d] in
+ * bias_dtype. */
+MXMOE_API int mxmoe_upload_experts(mxmoe_layer* layer, const mxmoe_quant_desc* w1_desc,
+                         const uint8_t* w1_blocks, const uint8_t* w1_scales,
+                         const mxmoe_quant_desc* w2_desc,
+                         const uint8_t* w2_blocks, const uint8_t* w2_scales,
+                         const void* b1, const void* b2, mxmoe_dtype bias_dtype,
+                         void* stream);
+
+/* Pre-sizes the per-forward workspace for up to max_tokens tokens so that
+ * later forwards allocate nothing.  Optional. */
+MXMOE_API int mxmoe_reserve(mxmoe_layer* layer, uint32_t max_tokens);
+
+/* Replaces MoeGatedSwiGLU::forward (src/moe/mod.rs:99-115, forward_resident
+ * :122-412): y = x + sum_k w_k * FFN_{e_k}(RmsNorm(x)).  x and y are DEVICE
+ * pointers of n_tokens x d_model elements (row-major, batch and sequence
+ * flattened).  Stream-ordered; returns before the work finishes. */
+MXMOE_API int mxmoe_forward(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype,
+                  void* y, mxmoe_dtype y_dtype, uint32_t n_tokens, void* stream);
+
+/* Same computation on HOST buffers: copies x to the device, runs the forward
+ * and copies y back, then synchronizes `stream`.  Pinned host memory makes
+ * the copies asynchronous with respect to other streams. */
+MXMOE_API int mxmoe_forward_host(mxmoe_layer* layer, const void* x_host,
+                       mxmoe_dtype x_dtype, void* y_host, mxmoe_dtype y_dtype,
+                       uint32_t n_tokens, void* stream);
+
+/* Routing results of the most recent forward on this layer (device
+ * pointers owned by the layer, valid until the next forward):
+ *   topk_idx [n][k] int32, topk_w [n][k] f32, offsets [E+1] int32 (unpadded
+ *   prefix counts), perm [n*k] int32 (sorted position -> pair t*k+s),
+ *   inv [n*k] int32 (pair -> sorted position), logits [n][E] f32.
+ * Replaces the router tensors of src/moe/mod.rs:270-288 for parity checks. */
+MXMOE_API int mxmoe_routing_results(mxmoe_layer* layer, const int32_t** topk_idx,
+                          const float** topk_w, const int32_t** offsets,
+                          const int32_t** perm, const int32_t** inv,
+                          const float** logits);
+
+/* Replaces loader::mxfp4::dequant_mxfp4_bytes (src/loader/mxfp4.rs:57-79) on
+ * the device: blocks [rows_total][b] bytes, scales [rows_total] (one E8M0 per
+ * row of b bytes), out [rows_total][2b] f32, bit-exact.  Device pointers. */
+MXMOE_API int mxmoe_dequant_mxfp4_bytes(const uint8_t* blocks, uint64_t rows_total,
+                              uint64_t b, const uint8_t* scales, float* out,
+                              void* stream);
+
+/* Dequantizes expert weights in the MoE layout described by `desc` (the
+ * decode of src/quant/gpu.rs:124-134, with exact powers of two): out
+ * [experts][rows][cols] f32.  Device pointers. */
+MXMOE_API int mxmoe_dequant_rows(const mxmoe_quant_desc* desc, const uint8_t* blocks,
+                       const uint8_t* scales, float* out, void* stream);
+
+/* Top-k + softmax over given router logits [n][E] (the Burn ops of
+ * src/moe/mod.rs:272-276), for bit-exact index checks on identical logits.
+ * Device pointers. */
+MXMOE_API int mxmoe_topk_softmax(const float* logits, uint32_t n_tokens,
+                       uint32_t num_experts, uint32_t k, int32_t* topk_idx,
+                       float* topk_w, void* stream);
+
+/* Canonical permutation of given top-k indices (replaces the dense masks of
+ * src/moe/mod.rs:279-288): stable counting sort of pairs p = t*k+s by expert.
+ * offsets [E+1], perm [n*k], inv [n*k].  Device pointers. */
+MXMOE_API int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k,
+                  uint32_t num_experts, int32_t* offsets, int32_t* perm,
+                  int32_t* inv, void* stream);
+
+/* Synchronizes `stream` and reports a device-side failure of the layer's
+ * kernels since the last forward (MXMOE_ERR_TIMEOUT when a bounded wait gave
+ * up).  mxmoe_forward_host performs this check itself. */
+MXMOE_API int mxmoe_sync_status(mxmoe_layer* layer, void* stream);
+
+/* Per-stage timing of mxmoe_forward (no counterpart in the reference, whose
+ * timing is eprintln! of wall clock, src/models/gpt_oss.rs:223-281).  When
+ * enabled, every forward records CUDA events on its stream around the stages
+ * router, permute, quantize, W1 GEMM, W2 GEMM, combine; mxmoe_last_profile
+ * waits for the last forward and writes up to `cap` stage times in
+ * milliseconds (returns the stage count through *count). */
+MXMOE_API int mxmoe_set_profiling(mxmoe_layer* layer, int enable);
+MXMOE_API int mxmoe_last_profile(mxmoe_layer* layer, float* ms, int cap,
+                                 int* count);
+
+/* ---------------------------------------------------------------------------
+ * Expert parallelism (no counterpart in the single-rank reference, whose
+ * docs/gpt-oss-architecture.md:22 leaves sharding out): experts are split into
+ * contiguous shards, one per GPU; a host runtime moves routed pairs with an
+ * NCCL all-to-all and uses the entry points below on either side.
+ * ------------------------------------------------------------------------- */
+
+/* This layer holds experts [expert_begin, expert_begin + expert_count) of the
+ * global num_experts.  Must precede mxmoe_upload_experts, whose descriptors
+ * then cover only the local experts.  The router stays global. */
+MXMOE_API int mxmoe_set_expert_shard(mxmoe_layer* layer, uint32_t expert_begin,
+                           uint32_t expert_count);
+
+/* Router + canonical permutation on device x [n][d] (source side):
+ * rscale [n] (1 / rms), topk_idx [n][k], topk_w [n][k], offsets [E+1],
+ * perm [n*k], inv [n*k] (global expert ids; pairs sorted by expert are sorted
+ * by destination rank).  Device pointers owned by the caller. */
+MXMOE_API int mxmoe_route(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype,
+                uint32_t n_tokens, float* rscale, int32_t* topk_idx,
+                float* topk_w, int32_t* offsets, int32_t* perm, int32_t* inv,
+                void* stream);
+
+/* Packs routed pairs in permuted order for dispatch: for every position q,
+ * pair p = perm[q], token t = p / k: out_x[q] = x[t] (x's dtype),
+ * out_rscale[q] = rscale[t], out_expert[q] = topk_idx[p],
+ * out_w[q] = topk_w[p].  Device pointers. */
+MXMOE_API int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
+                       uint32_t d_model, uint32_t k, const int32_t* perm,
+                       const float* rscale, const int32_t* topk_idx,
+                       const float* topk_w, void* out_x, float* out_rscale,
+                       int32_t* out_expert, float* out_w, void* stream);
+
+/* Receive side: expert FFN of this layer's shard for dispatched pairs.
+ * xr [n_pairs][d] raw token rows (x's dtype), rscale [n_pairs], expert
+ * [n_pairs] GLOBAL ids inside the shard, weight [n_pairs];
+ * out [n_pairs][d] f32 = weight * (W2 act + b2).  Device pointers. */
+MXMOE_API int mxmoe_forward_local(mxmoe_layer* layer, const void* xr, mxmoe_dtype xr_dtype,
+                        const float* rscale, const int32_t* expert,
+                        const float* weight, uint32_t n_pairs, float* out,
+                        void* stream);
+
+/* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
+ * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out f32 in
+ * permuted order).  residual = 0 omits x.  Device pointers. */
+MXMOE_API int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
+                  uint32_t d_model, uint32_t k, const int32_t* topk_idx,
+                  const int32_t* inv, const float* pair_out, int residual,
+                  void* y, mxmoe_dtype y_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MXMOE_H */
