@@ -141,7 +141,7 @@ struct Workspace {
   uint32_t cap_tokens = 0;  // tokens
   uint32_t cap_pairs = 0;   // n * k
   uint32_t rows = 0;        // padded activation rows
-  uint32_t row_blocks = 0;  // scale-atom row blocks (rows / 128 + slack)
+  uint32_t row_blocks = 0;  // scale-atom row blocks (rows / 32 + slack)
   float* logits = nullptr;
   int32_t* topk_idx = nullptr;
   float* topk_w = nullptr;
@@ -216,7 +216,7 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   const uint32_t cap_t = std::max<uint32_t>(n_tokens, 1);
   const uint32_t cap_p = std::max<uint32_t>(static_cast<uint32_t>(pairs), 1);
   w.rows = round_up(cap_p, kRowBlock) + E * kRowBlock + 256;
-  w.row_blocks = w.rows / kRowBlock + 2;
+  w.row_blocks = w.rows / kTileWidths[0] + 2;  // enough atoms for the smallest tile width
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   TRY(dalloc(&w.logits, static_cast<size_t>(cap_t) * Et));
   TRY(dalloc(&w.topk_idx, cap_p));
@@ -295,11 +295,13 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
                                  w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
-                                 static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), st));
+                                 static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1),
+                                 std::min(N, kRowBlock), st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
   const uint64_t max_tiles_per_m = (P + N - 1) / N + L->e_count;
   TcParams p{};
   p.N = N;
+  p.sf_rows = std::min(N, kRowBlock);
   p.E = L->e_count;
   p.poff = w.poff;
   p.counts = w.counts;

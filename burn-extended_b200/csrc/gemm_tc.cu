@@ -122,8 +122,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int e, mt, nt, nte;
       decode_tile(p, t, e, mt, nt, nte);
       const int row0 = __ldg(p.poff + e) + nt * N;  // first activation row of the tile
-      const int off_in_atom = (nt * N) % kRowBlock;
-      const int natoms = (off_in_atom + N + kRowBlock - 1) / kRowBlock;
+      const int natoms = (N + p.sf_rows - 1) / p.sf_rows;  // scale atoms per tile and term
       const uint32_t tx = plan.a_bytes / 2 + terms * plan.b_bytes + kSfAtomBytes * (1 + terms * natoms);
       for (int kt = 0; kt < p.k_tiles; ++kt) {
         if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kDevTimeoutEmpty)) { ok = false; break; }
@@ -135,7 +134,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint8_t* sf = sb + plan.a_bytes + terms * plan.b_bytes;
         bulk_load(sf, p.a_sf + ((static_cast<uint64_t>(e) * p.m_tiles + mt) * p.k_tiles + kt) * kSfAtomBytes,
                   kSfAtomBytes, &full_bar[stage]);
-        const uint64_t rb = static_cast<uint64_t>(row0 - off_in_atom) / kRowBlock;
+        const uint64_t rb = static_cast<uint64_t>(row0) / p.sf_rows;
         for (int term = 0; term < terms; ++term)
           for (int a = 0; a < natoms; ++a)
             bulk_load(sf + kSfAtomBytes * (1 + term * 2 + a),
@@ -159,8 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       int e, mt, nt, nte;
       decode_tile(p, t, e, mt, nt, nte);
-      const int off_in_atom = (nt * N) % kRowBlock;
-      const int natoms = (off_in_atom + N + kRowBlock - 1) / kRowBlock;
+      const int natoms = (N + p.sf_rows - 1) / p.sf_rows;
       if (!mbar_wait(tmem_empty, acc_phase ^ 1u, err, kDevTimeoutTmemEmpty)) break;
       acc_phase ^= 1u;
       tc_fence_after();
@@ -185,8 +183,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t b_desc = make_smem_desc(b_addr0 + term * plan.b_bytes + kk * 32, 16, 1024, 2);
             const uint32_t idesc = make_idesc_mxf8f6f4(5u, 0u, 128u, static_cast<uint32_t>(N), kk, kk);
             const uint32_t sfa = (tmem_base + sfa_col) | (static_cast<uint32_t>(kk) << 30);
-            const uint32_t sfb = (tmem_base + sfa_col + 4 + term * 8 + off_in_atom / 32) |
-                                 (static_cast<uint32_t>(kk) << 30);
+            const uint32_t sfb = (tmem_base + sfa_col + 4 + term * 8) | (static_cast<uint32_t>(kk) << 30);
             tc_mma_mxf8f6f4(tmem_base, a_desc, b_desc, idesc, sfa, sfb, (kt | kk | term) != 0 ? 1u : 0u);
           }
         }
@@ -269,7 +266,7 @@ __global__ void __launch_bounds__(kThreads, 1)
               p.act_codes[p.act_term_stride + off] = code[1];
               if (lane == 0) {
                 const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(j / 32),
-                                              static_cast<uint32_t>(p.act_kchunks));
+                                              static_cast<uint32_t>(p.act_kchunks), static_cast<uint32_t>(p.sf_rows));
                 p.act_sf[so] = sbyte[0];
                 p.act_sf[p.act_sf_term_stride + so] = sbyte[1];
               }

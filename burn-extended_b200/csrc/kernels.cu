@@ -265,7 +265,7 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
                                       const float* __restrict__ gamma, int gamma_is_one,
                                       const int32_t* __restrict__ inv_p, int terms, uint8_t* codes,
                                       uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride,
-                                      int kchunks) {
+                                      int kchunks, int sf_rows) {
   const int warps_total = gridDim.x * (blockDim.x >> 5);
   const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -281,7 +281,7 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
       split_e4m3_terms(u, terms, code, sbyte);
       const uint64_t off = static_cast<uint64_t>(pos) * kp + c;
       const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(c0 / 32),
-                                    static_cast<uint32_t>(kchunks));
+                                    static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
       for (int q = 0; q < terms; ++q) {
         if (c < d) codes[q * term_stride + off] = code[q];
         if (lane == 0) sf[q * sf_term_stride + so] = sbyte[q];
@@ -490,12 +490,13 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
 cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
-                                  cudaStream_t st) {
+                                  int sf_rows, cudaStream_t st) {
   const int P = n * k;
   if (P == 0) return cudaSuccess;
   const int warps = P < 148 * 64 ? P : 148 * 64;
   quantize_pairs_kernel<<<(warps + 7) / 8, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms,
-                                                         codes, term_stride, kp, sf, sf_term_stride, kchunks);
+                                                         codes, term_stride, kp, sf, sf_term_stride, kchunks,
+                                                         sf_rows);
   return cudaGetLastError();
 }
 

@@ -15,7 +15,8 @@
 // Activations (per forward, rows = routed (token, expert) pairs sorted by
 // expert, every expert segment padded to a multiple of 128 rows):
 //   codes     [2 terms][rows][Kp] E4M3 (value = hi + lo, two block-scaled terms)
-//   scales    [2 terms][rows/128][Kp/128] atoms, same byte order as weights.
+//   scales    [terms][rows/R][Kp/128] atoms, same byte order as weights, with
+//             R = min(N, 128) rows per atom for tile width N.
 #pragma once
 #include <cstdint>
 
@@ -39,10 +40,13 @@ __host__ __device__ inline uint32_t w1_packed_row(uint32_t j, uint32_t half) {
 }
 
 // Byte offset of the scale of (row, k block) inside an atom array laid out
-// [row_blocks][k_chunks][512].
-__host__ __device__ inline uint64_t sf_offset(uint32_t row, uint32_t kb, uint32_t k_chunks) {
-  return (static_cast<uint64_t>(row / kRowBlock) * k_chunks + kb / 4) * kSfAtomBytes +
-         sf_atom_byte(row % kRowBlock, kb % 4);
+// [row_blocks][k_chunks][512], one atom per `block_rows` rows (128 for
+// weights; min(N, 128) for activations so that every N-row tile starts on an
+// atom and its scale factors land in TMEM lanes 0..N-1).
+__host__ __device__ inline uint64_t sf_offset(uint32_t row, uint32_t kb, uint32_t k_chunks,
+                                              uint32_t block_rows = kRowBlock) {
+  return (static_cast<uint64_t>(row / block_rows) * k_chunks + kb / 4) * kSfAtomBytes +
+         sf_atom_byte(row % block_rows, kb % 4);
 }
 
 }  // namespace mxmoe

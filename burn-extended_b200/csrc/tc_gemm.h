@@ -15,6 +15,7 @@ struct TcParams {
   int E;         // experts held by this layer
   int stages;    // smem pipeline depth
   int b_terms;   // E4M3 terms of the activation operand (2 or 3)
+  int sf_rows;   // rows per activation scale atom: min(N, 128)
   const int* poff;          // [E+1] padded segment starts (multiples of 128)
   const int* counts;        // [E] pairs per expert
   const int* ntile_prefix;  // [E+1] prefix sums of ceil(count / N)

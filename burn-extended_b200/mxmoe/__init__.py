@@ -240,12 +240,19 @@ class MoeGatedSwiGLU:
             pass
 
 
+_cudart = None
+
+
 def _copy_device(dst, src_ptr: int, nbytes: int):
-    torch = _torch()
-    cudart = torch.cuda.cudart()
-    # cudaMemcpyDeviceToDevice == 3
-    res = cudart.cudaMemcpy(dst.data_ptr(), src_ptr, nbytes, 3)
-    if int(res) != 0:
+    """Device-to-device copy from a library-owned buffer into a torch tensor."""
+    global _cudart
+    if _cudart is None:
+        lib()  # loads libcudart.so.12 as a dependency
+        _cudart = ctypes.CDLL("libcudart.so.12")
+        _cudart.cudaMemcpy.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_int]
+        _cudart.cudaMemcpy.restype = ctypes.c_int
+    res = _cudart.cudaMemcpy(dst.data_ptr(), src_ptr, nbytes, 3)  # cudaMemcpyDeviceToDevice
+    if res != 0:
         raise MxMoeError(3, f"cudaMemcpy failed ({res})")
 
 
