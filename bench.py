@@ -234,6 +234,11 @@ def run_ours(args, world, rank, local):
     extra = {"layer_tflops": layer_flops / (ms_per_step / 1e3) / 1e12,
              "w2_tflops": w2_flops / (stages["w2_gemm"] / 1e3) / 1e12}
 
+    if args.only == "prefill":
+        print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "ms_per_step": ms_per_step,
+                          "stages_ms": stages, "roofline": roofline, "clocks": clocks}), flush=True)
+        layer.close()
+        return
     # end to end through the public host-buffer entry point (pinned memory)
     xh = x.cpu().pin_memory()
     yh = torch.empty_like(xh).pin_memory()
@@ -311,6 +316,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=24)
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
+                    help="prefill: skip the decode / e2e / CPU legs (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":

@@ -184,7 +184,7 @@ struct mxmoe_layer {
   uint8_t* w2sf = nullptr;
   float* b2 = nullptr;
   int* err = nullptr;
-  CUtensorMap tmap_w1{}, tmap_w2{};
+  CUtensorMap tmap_w1[2] = {}, tmap_w2[2] = {};  // box rows 128 (weights-as-A) / 256 (tokens-as-A)
   Workspace ws;
   uint32_t last_n = 0;
   bool profiling = false;
@@ -254,16 +254,22 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   return MXMOE_OK;
 }
 
-// Tile width over routed pairs from the average pairs per expert; three-term
-// activations cap it at 128 so that the pipeline keeps >= 3 stages.
-int pick_tile_width_index(uint64_t pairs, uint32_t experts, int x_terms) {
+// Tile plan from the average routed pairs per expert:
+//   few pairs  -> weights-as-A, pair tiles of 32 / 64 / 128 (HBM-bound decode);
+//   many pairs -> tokens-as-A, pair tiles of 128 x weight tiles of 256 rows.
+// tw indexes the activation tensor maps (box rows 32, 64, 128, 256).
+struct TilePlan {
+  bool tok;
+  int pair_tile;
+  int tw;
+};
+
+TilePlan pick_tiles(uint64_t pairs, uint32_t experts) {
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
-  int i = 3;
-  if (avg <= 24) i = 0;
-  else if (avg <= 48) i = 1;
-  else if (avg <= 96) i = 2;
-  if (x_terms > 2 && i > 2) i = 2;
-  return i;
+  if (avg <= 24) return {false, 32, 0};
+  if (avg <= 48) return {false, 64, 1};
+  if (avg <= 96) return {false, 128, 2};
+  return {true, 128, 2};
 }
 
 // Two E4M3 terms represent bf16 activations exactly when the RmsNorm gain is
@@ -276,10 +282,10 @@ int x_terms_for(const mxmoe_layer* L, int x_dtype) {
 // Expert FFN over already-routed pairs: quantize -> W1 -> W2 (or the SIMT
 // pair) -> y_pair.  Uses ws.poff / counts / ntile_prefix / perm_p / inv_p.
 int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
-                const float* route_w, int tw_idx, int x_terms, cudaStream_t st) {
+                const float* route_w, const TilePlan& tp, int x_terms, cudaStream_t st) {
   Workspace& w = L->ws;
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
-  const int N = kTileWidths[tw_idx];
+  const int N = tp.pair_tile;
   const float bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
   if (L->cfg.flags & MXMOE_FLAG_SIMT) {
     if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
@@ -295,13 +301,15 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
                                  w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
-                                 static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1),
-                                 std::min(N, kRowBlock), st));
+                                 static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), N,
+                                 st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
-  const uint64_t max_tiles_per_m = (P + N - 1) / N + L->e_count;
+  const uint64_t max_pair_tiles = (P + N - 1) / N + L->e_count;
+  const bool tok = tp.tok;
+  const int wrows = tok ? 256 : 128;  // weight rows per tile
   TcParams p{};
-  p.N = N;
-  p.sf_rows = std::min(N, kRowBlock);
+  p.N = tok ? 256 : N;
+  p.sf_rows = N;
   p.E = L->e_count;
   p.poff = w.poff;
   p.counts = w.counts;
@@ -314,11 +322,13 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.topk_w = route_w;
   p.err = L->err;
   p.d = L->d;
-  // W1 + SwiGLU: A = W1 codes, B = x terms, writes act terms.
+  p.units = static_cast<int>(L->fp);
+  // W1 + SwiGLU: weights W1, activations x terms; writes act terms.
   p.mode = 1;
   p.b_terms = x_terms;
-  p.stages = tc_gemm_max_stages(N, x_terms, L->smem_limit);
-  p.m_tiles = L->m_tiles1;
+  p.stages = tc_gemm_max_stages(tok, p.N, x_terms, L->smem_limit);
+  p.m_tiles = static_cast<int>((2 * L->fp + wrows - 1) / wrows);
+  p.w_row_blocks = static_cast<int>(2 * L->fp / 128);
   p.k_tiles = static_cast<int>(kc1);
   p.a_sf = L->w1sf;
   p.b_sf = w.xsf;
@@ -333,14 +343,15 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.act_sf = w.asf;
   p.act_sf_term_stride = static_cast<uint64_t>(w.row_blocks) * kc2 * kSfAtomBytes;
   p.act_kchunks = static_cast<int>(kc2);
-  int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, L->m_tiles1 * max_tiles_per_m));
-  CUDA_TRY(tc_gemm_launch(L->tmap_w1, w.tmap_x[tw_idx], p, grid, st));
+  int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
+  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w1[tok ? 1 : 0], w.tmap_x[tp.tw], p, grid, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
-  // W2 + bias + route weight: A = W2 codes, B = act terms, writes y_pair.
+  // W2 + bias + route weight: weights W2, activations act terms; writes y_pair.
   p.mode = 2;
   p.b_terms = 2;
-  p.stages = tc_gemm_max_stages(N, 2, L->smem_limit);
-  p.m_tiles = L->m_tiles2;
+  p.stages = tc_gemm_max_stages(tok, p.N, 2, L->smem_limit);
+  p.m_tiles = static_cast<int>((L->d + wrows - 1) / wrows);
+  p.w_row_blocks = static_cast<int>((L->d + 127) / 128);
   p.k_tiles = static_cast<int>(kc2);
   p.a_sf = L->w2sf;
   p.b_sf = w.asf;
@@ -350,8 +361,8 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.rows_valid = static_cast<int>(L->d);
   p.bias_mult = bias_mult;
   p.y_pair = w.y_pair;
-  grid = static_cast<int>(std::min<uint64_t>(L->num_sms, L->m_tiles2 * max_tiles_per_m));
-  CUDA_TRY(tc_gemm_launch(L->tmap_w2, w.tmap_act[tw_idx], p, grid, st));
+  grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
+  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], w.tmap_act[tp.tw], p, grid, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
   return MXMOE_OK;
 }
@@ -545,9 +556,13 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
   CUDA_TRY(cudaMemcpyAsync(L->w2sf, s2.data(), s2.size(), cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(L->b2, bb2.data(), bb2.size() * 4, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaStreamSynchronize(st));
-  TRY(make_tmap(&L->tmap_w1, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w1q, kp1, rows1, E, kp1 / 2,
-                rows1 * (kp1 / 2), 128));
-  TRY(make_tmap(&L->tmap_w2, CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w2q, kp2, d, E, kp2 / 2, d * (kp2 / 2), 128));
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t box = i == 0 ? 128 : 256;
+    TRY(make_tmap(&L->tmap_w1[i], CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w1q, kp1, rows1, E, kp1 / 2,
+                  rows1 * (kp1 / 2), box));
+    TRY(make_tmap(&L->tmap_w2[i], CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w2q, kp2, d, E, kp2 / 2, d * (kp2 / 2),
+                  box));
+  }
   L->experts_ready = true;
   return MXMOE_OK;
 }
@@ -586,17 +601,17 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   const uint32_t k = L->k, E = L->e_count;
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
   const int xt = x_terms_for(L, x_dtype);
-  const int tw = pick_tile_width_index(P, E, xt);
+  const TilePlan tp = pick_tiles(P, E);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   L->profile_valid = false;
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
   CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
                          w.logits, w.topk_idx, w.topk_w, w.rscale, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
-  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, kTileWidths[tw], w.offsets, w.perm_c,
+  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, tp.pair_tile, w.offsets, w.perm_c,
                           w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
-  TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tw, xt, st));
+  TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
   const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
   CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
   if (L->profiling) {
@@ -777,13 +792,13 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   Workspace& w = L->ws;
   cudaStream_t st = as_stream(stream);
   const int xt = x_terms_for(L, xr_dtype);
-  const int tw = pick_tile_width_index(n_pairs, L->e_count, xt);
+  const TilePlan tp = pick_tiles(n_pairs, L->e_count);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   CUDA_TRY(launch_localize(expert, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
                            static_cast<int>(L->e_count), w.local_idx, L->err, st));
-  CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, kTileWidths[tw], nullptr,
+  CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, tp.pair_tile, nullptr,
                           nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
-  TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, rscale, weight, tw, xt, st));
+  TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, rscale, weight, tp, xt, st));
   CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, 0, st));
   return MXMOE_OK;
 }

@@ -1,18 +1,22 @@
 // gemm_tc.cu -- grouped expert GEMM on the 5th-generation tensor cores.
 //
-// One persistent kernel serves both expert projections of the MoE block
+// Persistent kernels serving both expert projections of the MoE block
 // (reference: w1_swiglu_dense_kernel / w2_scatter_dense_kernel,
 // src/quant/gpu.rs:89-146 and :148-192, launched per expert and f-tile at
 // src/moe/mod.rs:316-404):
 //   mode 1 (W1):  act = SwiGLUclamp(r_t * (W1_glu x_t) + b_glu, r_t * (W1_lin x_t) + b_lin)
 //                 written back as two block-scaled E4M3 terms for mode 2;
 //   mode 2 (W2):  y_pair = (W2 act + b2) * w_route.
-// Each tile is 128 weight rows (M) x N routed pairs (N = 32..256) of one
-// expert.  Operand A = MXFP4 weights exactly as stored (E2M1 codes + E8M0
-// scales, loaded by TMA with the 4-bit -> byte-container expansion); operand B
-// = activations as hi + lo E4M3 terms, so one k-step issues two
-// kind::mxf8f6f4.block_scale MMAs into the same fp32 TMEM accumulator.
+// Weights are the MXFP4 codes and E8M0 scales exactly as stored (TMA expands
+// the 4-bit codes into byte containers in shared memory); activations are a
+// sum of block-scaled E4M3 terms, so one k-step issues one
+// kind::mxf8f6f4.block_scale MMA per term into the same fp32 TMEM accumulator.
 //
+// Two tile shapes:
+//   weights-as-A (decode, few pairs per expert): 128 weight rows x N pairs,
+//     N = 32..128, double-buffered accumulator;
+//   tokens-as-A (prefill): 128 pairs x 256 weight rows, so that each epilogue
+//     thread owns one pair's row and quantizes 32-wide blocks on its own.
 // Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
 // issuer, warps 2..5 = epilogue (TMEM -> registers -> global).
 #include <cuda.h>
@@ -33,25 +37,45 @@ constexpr int kEpiThreads = 128;
 constexpr int kMaxStages = 8;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfTmemBase = 256;  // scale factors live in columns 256.. (32 per stage)
-constexpr int kXchgPitch = 17;         // floats per row of the GLU/linear exchange buffer
+constexpr int kChunk = 32;             // weights-as-A epilogue column chunk
+constexpr int kXPitch = kChunk + 1;    // linear-half exchange [64][33]
+constexpr int kAPitch = 64 + 1;        // activation staging [32][65]
 
 struct SmemPlan {
-  uint32_t a_bytes, b_bytes, stage_bytes;
+  uint32_t a_bytes, b_bytes, stage_bytes, a_terms, b_terms;
 };
 
-__host__ __device__ inline SmemPlan smem_plan(int N, int terms) {
+// Weights-as-A: A = 128 weight rows (FP4 in byte containers), B = N rows per term.
+// Tokens-as-A:  A = 128 token rows per term (E4M3), B = 256 weight rows.
+__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms) {
   SmemPlan s;
-  s.a_bytes = 128 * kTileK;                     // E2M1 codes expanded to byte containers
-  s.b_bytes = static_cast<uint32_t>(N) * kTileK;  // E4M3, one term
-  uint32_t raw = s.a_bytes + terms * s.b_bytes + kSfAtomBytes + terms * 2 * kSfAtomBytes;
+  if (!tok) {
+    s.a_terms = 1;
+    s.b_terms = terms;
+    s.a_bytes = 128 * kTileK;
+    s.b_bytes = static_cast<uint32_t>(N) * kTileK;
+  } else {
+    s.a_terms = terms;
+    s.b_terms = 1;
+    s.a_bytes = 128 * kTileK;
+    s.b_bytes = 256 * kTileK;
+  }
+  const uint32_t raw = s.a_terms * s.a_bytes + s.b_terms * s.b_bytes + 6 * kSfAtomBytes;
   s.stage_bytes = round_up(raw, 1024);
   return s;
 }
 
+__host__ __device__ inline uint32_t epi_smem_bytes(bool tok) {
+  return tok ? 0u : static_cast<uint32_t>((64 * kXPitch + kChunk * kAPitch + 2 * kChunk) * sizeof(float));
+}
+
 __device__ __forceinline__ void named_bar_epi() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Largest expert e in [0, E) whose first tile index is <= t.
-__device__ __forceinline__ void decode_tile(const TcParams& p, int t, int& e, int& mt, int& nt, int& nte) {
+// Tile t -> (expert e, weight tile wt, pair tile pt).  Tiles of expert e are
+// [m_tiles * prefix[e], m_tiles * prefix[e+1]), ordered weight tile major so
+// that the pair tiles sharing one weight tile run on neighbouring CTAs and
+// meet it in L2.
+__device__ __forceinline__ void decode_tile(const TcParams& p, int t, int& e, int& wt, int& pt) {
   int lo = 0, hi = p.E;
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
@@ -59,44 +83,71 @@ __device__ __forceinline__ void decode_tile(const TcParams& p, int t, int& e, in
   }
   e = lo;
   const int base = p.m_tiles * __ldg(p.ntile_prefix + e);
-  nte = __ldg(p.ntile_prefix + e + 1) - __ldg(p.ntile_prefix + e);
+  const int nte = __ldg(p.ntile_prefix + e + 1) - __ldg(p.ntile_prefix + e);
   const int local = t - base;
-  mt = nte > 0 ? local / nte : 0;
-  nt = nte > 0 ? local % nte : 0;
+  wt = nte > 0 ? local / nte : 0;
+  pt = nte > 0 ? local % nte : 0;
 }
 
+__device__ __forceinline__ float swiglu_clamp(float g, float l, float alpha, float limit) {
+  const float xg = fminf(g, limit);
+  const float xl = fmaxf(-limit, fminf(l, limit));
+  return (xg / (1.0f + expf(-alpha * xg))) * (xl + 1.0f);
+}
+
+__device__ __forceinline__ void store_block_terms(const TcParams& p, int pos, int j0,
+                                                  const uint32_t (&words)[kMaxTerms][8],
+                                                  const uint8_t (&sbyte)[kMaxTerms]) {
+  const uint64_t off = static_cast<uint64_t>(pos) * p.act_kp + j0;
+  const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(j0 / 32),
+                                static_cast<uint32_t>(p.act_kchunks), static_cast<uint32_t>(p.sf_rows));
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    uint4* dst = reinterpret_cast<uint4*>(p.act_codes + t * p.act_term_stride + off);
+    dst[0] = make_uint4(words[t][0], words[t][1], words[t][2], words[t][3]);
+    dst[1] = make_uint4(words[t][4], words[t][5], words[t][6], words[t][7]);
+    p.act_sf[t * p.act_sf_term_stride + so] = sbyte[t];
+  }
+}
+
+template <bool kTok>
 __global__ void __launch_bounds__(kThreads, 1)
-    tc_moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+    tc_moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                        const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemPlan plan = smem_plan(p.N, p.b_terms);
-  const int terms = p.b_terms;
+  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms);
   const int S = p.stages;
-  float* xchg = reinterpret_cast<float*>(smem + S * plan.stage_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(xchg + 64 * kXchgPitch);
+  float* epi = reinterpret_cast<float*>(smem + S * plan.stage_bytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi) + epi_smem_bytes(kTok));
   uint64_t* full_bar = bars;
   uint64_t* empty_bar = bars + kMaxStages;
-  uint64_t* tmem_full = bars + 2 * kMaxStages;
-  uint64_t* tmem_empty = tmem_full + 1;
-  uint64_t* drain_bar = tmem_full + 2;
+  uint64_t* tmem_full = bars + 2 * kMaxStages;  // [2]
+  uint64_t* tmem_empty = tmem_full + 2;         // [2]
+  uint64_t* drain_bar = tmem_full + 4;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = p.err;
+  const int N = p.N;                             // weights-as-A: pairs per tile; tokens-as-A: 256
+  const int PT = kTok ? 128 : N;                 // pairs per tile
+  const int nacc = (!kTok && N <= 128) ? 2 : 1;  // accumulator buffers
+  const int terms = p.b_terms;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(tmem_full, 1);
-    mbar_init(tmem_empty, kEpiThreads);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tmem_full[b], 1);
+      mbar_init(&tmem_empty[b], kEpiThreads);
+    }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
-    prefetch_tmap(&tmap_a);
-    prefetch_tmap(&tmap_b);
+    prefetch_tmap(&tmap_w);
+    prefetch_tmap(&tmap_x);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, kTmemCols);
@@ -106,9 +157,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-
   const int total_tiles = p.m_tiles * __ldg(p.ntile_prefix + p.E);
-  const int N = p.N;
+  const int natoms_x = kTok ? 1 : (N + p.sf_rows - 1) / p.sf_rows;  // activation atoms per term
+  const int natoms_w = kTok ? 2 : 1;                                 // weight atoms
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -116,167 +167,264 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t phase = 0;
     uint32_t issued_parity[kMaxStages];
     bool issued[kMaxStages];
-    for (int s = 0; s < kMaxStages; ++s) { issued[s] = false; issued_parity[s] = 0; }
+    for (int s = 0; s < kMaxStages; ++s) {
+      issued[s] = false;
+      issued_parity[s] = 0;
+    }
+    const uint32_t w_tx = (kTok ? 256 : 128) * kTileK / 2;  // packed FP4 bytes
+    const uint32_t x_tx = PT * kTileK;                      // E4M3 bytes per term
+    const uint32_t tx = w_tx + terms * x_tx + kSfAtomBytes * (natoms_w + terms * natoms_x);
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      int e, mt, nt, nte;
-      decode_tile(p, t, e, mt, nt, nte);
-      const int row0 = __ldg(p.poff + e) + nt * N;  // first activation row of the tile
-      const int natoms = (N + p.sf_rows - 1) / p.sf_rows;  // scale atoms per tile and term
-      const uint32_t tx = plan.a_bytes / 2 + terms * plan.b_bytes + kSfAtomBytes * (1 + terms * natoms);
+      int e, wt, pt;
+      decode_tile(p, t, e, wt, pt);
+      const int row0 = __ldg(p.poff + e) + pt * PT;  // first activation row of the tile
+      const uint64_t rbx = static_cast<uint64_t>(row0) / p.sf_rows;
       for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kDevTimeoutEmpty)) { ok = false; break; }
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
+          ok = false;
+          break;
+        }
         uint8_t* sb = smem + stage * plan.stage_bytes;
+        uint8_t* w_s = kTok ? sb + terms * plan.a_bytes : sb;
+        uint8_t* x_s = kTok ? sb : sb + plan.a_bytes;
+        const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
+        uint8_t* sf = sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes;
         mbar_arrive_expect_tx(&full_bar[stage], tx);
-        tma_load_3d(sb, &tmap_a, &full_bar[stage], kt * kTileK, mt * 128, e);
+        tma_load_3d(w_s, &tmap_w, &full_bar[stage], kt * kTileK, wt * (kTok ? 256 : 128), e);
         for (int term = 0; term < terms; ++term)
-          tma_load_3d(sb + plan.a_bytes + term * plan.b_bytes, &tmap_b, &full_bar[stage], kt * kTileK, row0, term);
-        uint8_t* sf = sb + plan.a_bytes + terms * plan.b_bytes;
-        bulk_load(sf, p.a_sf + ((static_cast<uint64_t>(e) * p.m_tiles + mt) * p.k_tiles + kt) * kSfAtomBytes,
-                  kSfAtomBytes, &full_bar[stage]);
-        const uint64_t rb = static_cast<uint64_t>(row0) / p.sf_rows;
+          tma_load_3d(x_s + term * x_stride, &tmap_x, &full_bar[stage], kt * kTileK, row0, term);
+        // scale atoms in smem: [weights x natoms_w][term 0 x natoms_x][term 1 ...]
+        for (int a = 0; a < natoms_w; ++a) {
+          int wa = wt * natoms_w + a;
+          if (wa >= p.w_row_blocks) wa = p.w_row_blocks - 1;  // rows past the end carry zero codes
+          bulk_load(sf + kSfAtomBytes * a,
+                    p.a_sf + ((static_cast<uint64_t>(e) * p.w_row_blocks + wa) * p.k_tiles + kt) * kSfAtomBytes,
+                    kSfAtomBytes, &full_bar[stage]);
+        }
         for (int term = 0; term < terms; ++term)
-          for (int a = 0; a < natoms; ++a)
-            bulk_load(sf + kSfAtomBytes * (1 + term * 2 + a),
-                      p.b_sf + term * p.b_sf_term_stride + ((rb + a) * p.k_tiles + kt) * kSfAtomBytes,
+          for (int a = 0; a < natoms_x; ++a)
+            bulk_load(sf + kSfAtomBytes * (natoms_w + term * natoms_x + a),
+                      p.b_sf + term * p.b_sf_term_stride + ((rbx + a) * p.k_tiles + kt) * kSfAtomBytes,
                       kSfAtomBytes, &full_bar[stage]);
         issued[stage] = true;
         issued_parity[stage] = phase;
-        if (++stage == S) { stage = 0; phase ^= 1u; }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
     }
-    // Drain: make sure no TMA write into this CTA's smem is still in flight.
+    // Drain: no TMA write into this CTA's shared memory may still be in flight.
     for (int s = 0; s < S; ++s)
-      if (issued[s]) {
-        mbar_wait(&full_bar[s], issued_parity[s], nullptr, kDevTimeoutDrain);
-      }
+      if (issued[s]) mbar_wait(&full_bar[s], issued_parity[s], nullptr, kDevTimeoutDrain);
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
     int stage = 0;
-    uint32_t phase = 0, acc_phase = 0;
+    uint32_t phase = 0;
+    uint32_t acc_phase[2] = {0, 0};
+    int acc = 0;
+    // tokens-as-A: A = x (E4M3, fmt 0), B = w (E2M1, fmt 5), M = 128 pairs, N = 256 rows
+    // weights-as-A: A = w (E2M1),       B = x (E4M3),        M = 128 rows,  N = pairs
+    const uint32_t a_fmt = kTok ? 0u : 5u, b_fmt = kTok ? 5u : 0u;
+    const uint32_t mma_n = kTok ? 256u : static_cast<uint32_t>(N);
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      int e, mt, nt, nte;
-      decode_tile(p, t, e, mt, nt, nte);
-      const int natoms = (N + p.sf_rows - 1) / p.sf_rows;
-      if (!mbar_wait(tmem_empty, acc_phase ^ 1u, err, kDevTimeoutTmemEmpty)) break;
-      acc_phase ^= 1u;
+      if (!mbar_wait(&tmem_empty[acc], acc_phase[acc] ^ 1u, err, kDevTimeoutTmemEmpty)) break;
+      acc_phase[acc] ^= 1u;
       tc_fence_after();
+      const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 128);
       for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull)) { ok = false; break; }
+        if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
         tc_fence_after();
         uint8_t* sb = smem + stage * plan.stage_bytes;
-        const uint32_t a_addr = smem_u32(sb);
-        const uint32_t b_addr0 = smem_u32(sb + plan.a_bytes);
-        const uint32_t sf_addr = smem_u32(sb + plan.a_bytes + terms * plan.b_bytes);
-        const uint32_t sfa_col = kSfTmemBase + stage * 32;
-        // scale factors: smem atoms -> TMEM (32 lanes x 16 B, replicated to 4 sub-partitions)
-        tc_cp_32x128b_warpx4(tmem_base + sfa_col, make_smem_desc(sf_addr, 0, 128, 0));
+        const uint32_t w_addr = smem_u32(kTok ? sb + terms * plan.a_bytes : sb);
+        const uint32_t x_addr = smem_u32(kTok ? sb : sb + plan.a_bytes);
+        const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
+        const uint32_t sf_addr = smem_u32(sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes);
+        const uint32_t col0 = kSfTmemBase + stage * 32;
+        // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
+        // activation term q at col0 + 8 + 8q (4 per 128 rows).
+        for (int a = 0; a < natoms_w; ++a)
+          tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
         for (int term = 0; term < terms; ++term)
-          for (int a = 0; a < natoms; ++a)
-            tc_cp_32x128b_warpx4(tmem_base + sfa_col + 4 + term * 8 + a * 4,
-                                 make_smem_desc(sf_addr + kSfAtomBytes * (1 + term * 2 + a), 0, 128, 0));
+          for (int a = 0; a < natoms_x; ++a)
+            tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
+                                 make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t a_desc = make_smem_desc(a_addr + kk * 32, 16, 1024, 2);
+          const uint64_t w_desc = make_smem_desc(w_addr + kk * 32, 16, 1024, 2);
           for (int term = 0; term < terms; ++term) {
-            const uint64_t b_desc = make_smem_desc(b_addr0 + term * plan.b_bytes + kk * 32, 16, 1024, 2);
-            const uint32_t idesc = make_idesc_mxf8f6f4(5u, 0u, 128u, static_cast<uint32_t>(N), kk, kk);
-            const uint32_t sfa = (tmem_base + sfa_col) | (static_cast<uint32_t>(kk) << 30);
-            const uint32_t sfb = (tmem_base + sfa_col + 4 + term * 8) | (static_cast<uint32_t>(kk) << 30);
-            tc_mma_mxf8f6f4(tmem_base, a_desc, b_desc, idesc, sfa, sfb, (kt | kk | term) != 0 ? 1u : 0u);
+            const uint64_t x_desc = make_smem_desc(x_addr + term * x_stride + kk * 32, 16, 1024, 2);
+            const uint32_t idesc = make_idesc_mxf8f6f4(a_fmt, b_fmt, 128u, mma_n, kk, kk);
+            const uint32_t sf_w = (tmem_base + col0) | (static_cast<uint32_t>(kk) << 30);
+            const uint32_t sf_x = (tmem_base + col0 + 8 + term * 8) | (static_cast<uint32_t>(kk) << 30);
+            const uint32_t accum = (kt | kk | term) != 0 ? 1u : 0u;
+            if (kTok)
+              tc_mma_mxf8f6f4(d_tmem, x_desc, w_desc, idesc, sf_x, sf_w, accum);
+            else
+              tc_mma_mxf8f6f4(d_tmem, w_desc, x_desc, idesc, sf_w, sf_x, accum);
           }
         }
         tc_commit(&empty_bar[stage]);
-        if (++stage == S) { stage = 0; phase ^= 1u; }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
       }
       if (!ok) break;
-      tc_commit(tmem_full);
+      tc_commit(&tmem_full[acc]);
+      if (++acc == nacc) acc = 0;
     }
     // Drain: every MMA issued by this thread has finished before TMEM is freed.
     tc_commit(drain_bar);
     mbar_wait(drain_bar, 0, nullptr, kDevTimeoutDrain);
   } else if (warp >= 2) {
     // ------------------------------------------------------------ epilogue
-    const int sp = warp & 3;              // TMEM sub-partition this warp may access
-    const int m = sp * 32 + lane;         // accumulator row (weight row within the tile)
-    const uint32_t trow = tmem_base + (static_cast<uint32_t>(sp * 32) << 16);
-    uint32_t acc_phase = 0;
+    const int sp = warp & 3;          // TMEM sub-partition this warp may access
+    const int m = sp * 32 + lane;     // accumulator row
+    const int et = threadIdx.x - 64;  // 0..127 epilogue thread id
+    uint32_t acc_phase[2] = {0, 0};
+    int acc = 0;
+    float* xl = epi;                   // [64][kXPitch] linear half (weights-as-A)
+    float* as = epi + 64 * kXPitch;    // [kChunk][kAPitch] activations (weights-as-A)
+    float* rs = as + kChunk * kAPitch; // [kChunk] 1/rms per column
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      int e, mt, nt, nte;
-      decode_tile(p, t, e, mt, nt, nte);
-      if (!mbar_wait(tmem_full, acc_phase, err, kDevTimeoutTmemFull)) break;
-      acc_phase ^= 1u;
+      int e, wt, pt;
+      decode_tile(p, t, e, wt, pt);
+      if (!mbar_wait(&tmem_full[acc], acc_phase[acc], err, kDevTimeoutTmemFull)) break;
+      acc_phase[acc] ^= 1u;
       tc_fence_after();
+      const uint32_t trow = tmem_base + static_cast<uint32_t>(acc * 128) + (static_cast<uint32_t>(sp * 32) << 16);
       const int cnt = __ldg(p.counts + e);
-      const int n_valid = min(N, cnt - nt * N);
-      const int pos0 = __ldg(p.poff + e) + nt * N;
-      if (p.mode == 2) {
-        const int c = mt * 128 + m;
-        const bool row_ok = c < p.rows_valid;
-        const float bias = row_ok ? __ldg(p.bias + static_cast<uint64_t>(e) * p.bias_stride + c) * p.bias_mult : 0.f;
-        for (int c0 = 0; c0 < n_valid; c0 += 16) {
-          float v[16];
-          tmem_ld_32x32b_x16(trow + c0, v);
-          if (row_ok) {
+      const int n_valid = min(PT, cnt - pt * PT);
+      const int pos0 = __ldg(p.poff + e) + pt * PT;
+      const uint64_t bias_e = static_cast<uint64_t>(e) * p.bias_stride;
+      if (kTok) {
+        // thread = pair row m; columns = the 256 weight rows of tile wt
+        const bool valid = m < n_valid;
+        const int pos = pos0 + m;
+        const int pair = valid ? __ldg(p.perm + pos) : 0;
+        if (p.mode == 2) {
+          const float w = valid ? __ldg(p.topk_w + pair) : 0.f;
+          for (int c0 = 0; c0 < 256; c0 += 16) {
+            const int cf = wt * 256 + c0;  // output feature of column c0
+            if (cf >= p.rows_valid) break; // uniform across the CTA
+            float v[16];
+            tmem_ld_32x32b_x16(trow + c0, v);
+            if (valid) {
+              float4* dst = reinterpret_cast<float4*>(p.y_pair + static_cast<uint64_t>(pos) * p.d + cf);
+              const float* bb = p.bias + bias_e + cf;
 #pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int n = c0 + i;
-              if (n < n_valid) {
-                const int pos = pos0 + n;
-                const float w = __ldg(p.topk_w + __ldg(p.perm + pos));
-                p.y_pair[static_cast<uint64_t>(pos) * p.d + c] = (v[i] + bias) * w;
+              for (int q = 0; q < 4; ++q) {
+                float4 o;
+                o.x = (v[4 * q + 0] + __ldg(bb + 4 * q + 0) * p.bias_mult) * w;
+                o.y = (v[4 * q + 1] + __ldg(bb + 4 * q + 1) * p.bias_mult) * w;
+                o.z = (v[4 * q + 2] + __ldg(bb + 4 * q + 2) * p.bias_mult) * w;
+                o.w = (v[4 * q + 3] + __ldg(bb + 4 * q + 3) * p.bias_mult) * w;
+                dst[q] = o;
+              }
+            }
+          }
+        } else {
+          const float r = valid ? __ldg(p.rscale + pair / p.k) : 0.f;
+          for (int h = 0; h < 2; ++h) {
+            const int unit0 = wt * 128 + h * 64;  // GLU unit of column h*128
+            if (unit0 >= p.units) break;          // uniform
+            for (int sb = 0; sb < 2; ++sb) {
+              float g[32], l[32];
+              tmem_ld_32x32b_x16(trow + h * 128 + sb * 32, *reinterpret_cast<float(*)[16]>(&g[0]));
+              tmem_ld_32x32b_x16(trow + h * 128 + sb * 32 + 16, *reinterpret_cast<float(*)[16]>(&g[16]));
+              tmem_ld_32x32b_x16(trow + h * 128 + 64 + sb * 32, *reinterpret_cast<float(*)[16]>(&l[0]));
+              tmem_ld_32x32b_x16(trow + h * 128 + 64 + sb * 32 + 16, *reinterpret_cast<float(*)[16]>(&l[16]));
+              if (valid) {
+                const float* bg = p.bias + bias_e + wt * 256 + h * 128 + sb * 32;  // packed W1 row of g[0]
+#pragma unroll
+                for (int i = 0; i < 32; ++i)
+                  g[i] = swiglu_clamp(fmaf(g[i], r, __ldg(bg + i)), fmaf(l[i], r, __ldg(bg + 64 + i)), p.alpha,
+                                      p.limit);
+                uint32_t words[kMaxTerms][8];
+                uint8_t sbyte[kMaxTerms];
+                quantize_block32(g, 2, words, sbyte);
+                store_block_terms(p, pos, unit0 + sb * 32, words, sbyte);
               }
             }
           }
         }
       } else {
-        // W1: lanes 0..63 hold GLU rows, 64..127 the matching linear rows.
-        const bool glu = m < 64;
-        const int jl = glu ? m : m - 64;
-        const int j = mt * 64 + jl;  // GLU unit index
-        const uint64_t brow = static_cast<uint64_t>(e) * p.bias_stride;
-        const float b_g = __ldg(p.bias + brow + mt * 128 + jl);
-        const float b_l = __ldg(p.bias + brow + mt * 128 + 64 + jl);
-        for (int c0 = 0; c0 < n_valid; c0 += 16) {
-          float v[16];
-          tmem_ld_32x32b_x16(trow + c0, v);
-          if (!glu) {
+        // weights-as-A: thread = weight row m of tile wt; columns = pairs
+        if (p.mode == 2) {
+          const int c = wt * 128 + m;
+          const bool row_ok = c < p.rows_valid;
+          const float bias = row_ok ? __ldg(p.bias + bias_e + c) * p.bias_mult : 0.f;
+          for (int c0 = 0; c0 < n_valid; c0 += 16) {
+            float v[16];
+            tmem_ld_32x32b_x16(trow + c0, v);
+            if (row_ok) {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) xchg[jl * kXchgPitch + i] = v[i];
-          }
-          named_bar_epi();
-          if (glu) {
-#pragma unroll 1
-            for (int i = 0; i < 16; ++i) {
-              const int n = c0 + i;
-              if (n >= n_valid) break;  // uniform across the warp
-              const int pos = pos0 + n;
-              const int tok = __ldg(p.perm + pos) / p.k;
-              const float r = __ldg(p.rscale + tok);
-              const float g = fmaf(v[i], r, b_g);
-              const float l = fmaf(xchg[jl * kXchgPitch + i], r, b_l);
-              const float xg = fminf(g, p.limit);
-              const float xl = fmaxf(-p.limit, fminf(l, p.limit));
-              const float a = (xg / (1.0f + expf(-p.alpha * xg))) * (xl + 1.0f);
-              uint8_t code[kMaxTerms], sbyte[kMaxTerms];
-              split_e4m3_terms(a, 2, code, sbyte);
-              const uint64_t off = static_cast<uint64_t>(pos) * p.act_kp + j;
-              p.act_codes[off] = code[0];
-              p.act_codes[p.act_term_stride + off] = code[1];
-              if (lane == 0) {
-                const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(j / 32),
-                                              static_cast<uint32_t>(p.act_kchunks), static_cast<uint32_t>(p.sf_rows));
-                p.act_sf[so] = sbyte[0];
-                p.act_sf[p.act_sf_term_stride + so] = sbyte[1];
+              for (int i = 0; i < 16; ++i) {
+                const int n = c0 + i;
+                if (n < n_valid) {
+                  const int pos = pos0 + n;
+                  const float w = __ldg(p.topk_w + __ldg(p.perm + pos));
+                  p.y_pair[static_cast<uint64_t>(pos) * p.d + c] = (v[i] + bias) * w;
+                }
               }
             }
           }
-          named_bar_epi();
+        } else {
+          // lanes 0..63: GLU rows, 64..127: linear rows of units j0..j0+63
+          const bool glu = m < 64;
+          const int jl = glu ? m : m - 64;
+          const int j0 = wt * 64;
+          const float b_g = __ldg(p.bias + bias_e + wt * 128 + jl);
+          const float b_l = __ldg(p.bias + bias_e + wt * 128 + 64 + jl);
+          for (int c0 = 0; c0 < n_valid; c0 += kChunk) {
+            float v[kChunk];
+            tmem_ld_32x32b_x16(trow + c0, *reinterpret_cast<float(*)[16]>(&v[0]));
+            tmem_ld_32x32b_x16(trow + c0 + 16, *reinterpret_cast<float(*)[16]>(&v[16]));
+            if (!glu) {
+#pragma unroll
+              for (int i = 0; i < kChunk; ++i) xl[jl * kXPitch + i] = v[i];
+            }
+            if (et < kChunk) {
+              const int n = c0 + et;
+              rs[et] = n < n_valid ? __ldg(p.rscale + __ldg(p.perm + pos0 + n) / p.k) : 0.f;
+            }
+            named_bar_epi();
+            if (glu) {
+#pragma unroll 4
+              for (int i = 0; i < kChunk; ++i) {
+                const float r = rs[i];
+                as[i * kAPitch + jl] =
+                    swiglu_clamp(fmaf(v[i], r, b_g), fmaf(xl[jl * kXPitch + i], r, b_l), p.alpha, p.limit);
+              }
+            }
+            named_bar_epi();
+            // two 32-unit blocks per column: thread et -> (column et / 2, block et % 2)
+            if (et < 2 * kChunk) {
+              const int col = et >> 1, blk = et & 1;
+              const int n = c0 + col;
+              if (n < n_valid && j0 + blk * 32 < p.units) {
+                float a[32];
+#pragma unroll
+                for (int i = 0; i < 32; ++i) a[i] = as[col * kAPitch + blk * 32 + i];
+                uint32_t words[kMaxTerms][8];
+                uint8_t sbyte[kMaxTerms];
+                quantize_block32(a, 2, words, sbyte);
+                store_block_terms(p, pos0 + n, j0 + blk * 32, words, sbyte);
+              }
+            }
+            named_bar_epi();
+          }
         }
       }
       tc_fence_before();
-      mbar_arrive(tmem_empty);
+      mbar_arrive(&tmem_empty[acc]);
+      if (++acc == nacc) acc = 0;
     }
   }
 
@@ -289,25 +437,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(int N, int terms, int stages) {
-  const SmemPlan plan = smem_plan(N, terms);
-  return 1024 + static_cast<size_t>(stages) * plan.stage_bytes + 64 * kXchgPitch * sizeof(float) +
-         (2 * kMaxStages + 4) * sizeof(uint64_t);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages) {
+  const SmemPlan plan = smem_plan(tokens_as_a, N, terms);
+  return 1024 + static_cast<size_t>(stages) * plan.stage_bytes + epi_smem_bytes(tokens_as_a) +
+         (2 * kMaxStages + 8) * sizeof(uint64_t);
 }
 
-int tc_gemm_max_stages(int N, int terms, size_t smem_limit) {
-  int s = kMaxStages;
-  while (s > 1 && tc_gemm_smem_bytes(N, terms, s) > smem_limit) --s;
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit) {
+  int s = kMaxStages - 1;  // 7 stages x 32 scale columns fit above column 256
+  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s) > smem_limit) --s;
   return s;
 }
 
-cudaError_t tc_gemm_launch(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const TcParams& p, int grid,
-                           cudaStream_t stream) {
-  const size_t smem = tc_gemm_smem_bytes(p.N, p.b_terms, p.stages);
-  cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        static_cast<int>(smem));
-  if (st != cudaSuccess) return st;
-  tc_moe_gemm_kernel<<<grid, kThreads, smem, stream>>>(tmap_a, tmap_b, p);
+cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                           const TcParams& p, int grid, cudaStream_t stream) {
+  const size_t smem = tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages);
+  if (tokens_as_a) {
+    cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+    if (st != cudaSuccess) return st;
+    tc_moe_gemm_kernel<true><<<grid, kThreads, smem, stream>>>(tmap_w, tmap_x, p);
+  } else {
+    cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          static_cast<int>(smem));
+    if (st != cudaSuccess) return st;
+    tc_moe_gemm_kernel<false><<<grid, kThreads, smem, stream>>>(tmap_w, tmap_x, p);
+  }
   return cudaGetLastError();
 }
 

@@ -260,32 +260,58 @@ __global__ void __launch_bounds__(kPermThreads)
 // Gathers each routed pair's token row into its padded expert-sorted position
 // and writes it as `terms` block-scaled E4M3 terms (two reproduce bf16 input
 // with unit gain exactly; three are used for f32 input or a non-unit gain).
-// One warp per pair, sweeping 32-column blocks.
+// One thread per (pair, 32-column block): reads 32 inputs, quantizes them on
+// its own and writes 32 code bytes per term with 16-byte stores.
 __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                                       const float* __restrict__ gamma, int gamma_is_one,
                                       const int32_t* __restrict__ inv_p, int terms, uint8_t* codes,
                                       uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride,
                                       int kchunks, int sf_rows) {
-  const int warps_total = gridDim.x * (blockDim.x >> 5);
-  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int P = n * k;
-  for (int p = gw; p < P; p += warps_total) {
+  const int nb = d / 32;
+  const uint64_t items = static_cast<uint64_t>(n) * k * nb;
+  for (uint64_t it = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; it < items;
+       it += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
+    const int p = static_cast<int>(it / nb);
+    const int b = static_cast<int>(it - static_cast<uint64_t>(p) * nb);
     const int t = p / k;
-    const int pos = inv_p[p];
-    for (int c0 = 0; c0 < d; c0 += 32) {
-      const int c = c0 + lane;
-      float u = c < d ? load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c) : 0.0f;
-      if (!gamma_is_one && c < d) u = __fmul_rn(u, gamma[c]);
-      uint8_t code[kMaxTerms], sbyte[kMaxTerms];
-      split_e4m3_terms(u, terms, code, sbyte);
-      const uint64_t off = static_cast<uint64_t>(pos) * kp + c;
-      const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(c0 / 32),
-                                    static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
-      for (int q = 0; q < terms; ++q) {
-        if (c < d) codes[q * term_stride + off] = code[q];
-        if (lane == 0) sf[q * sf_term_stride + so] = sbyte[q];
+    const int pos = __ldg(inv_p + p);
+    float v[32];
+    const uint64_t src = static_cast<uint64_t>(t) * d + b * 32;
+    if (x_dtype == 1) {
+      const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + src);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const uint4 u = __ldg(xs + q);
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          v[q * 8 + 2 * h] = __uint_as_float(w4[h] << 16);
+          v[q * 8 + 2 * h + 1] = __uint_as_float(w4[h] & 0xFFFF0000u);
+        }
       }
+    } else {
+      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + src);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 u = __ldg(xs + q);
+        v[4 * q] = u.x; v[4 * q + 1] = u.y; v[4 * q + 2] = u.z; v[4 * q + 3] = u.w;
+      }
+    }
+    if (!gamma_is_one) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + b * 32 + i));
+    }
+    uint32_t words[kMaxTerms][8];
+    uint8_t sbyte[kMaxTerms];
+    quantize_block32(v, terms, words, sbyte);
+    const uint64_t off = static_cast<uint64_t>(pos) * kp + b * 32;
+    const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(b),
+                                  static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
+    for (int q = 0; q < terms; ++q) {
+      uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
+      dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
+      dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
+      sf[q * sf_term_stride + so] = sbyte[q];
     }
   }
 }
@@ -491,12 +517,12 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
                                   int sf_rows, cudaStream_t st) {
-  const int P = n * k;
-  if (P == 0) return cudaSuccess;
-  const int warps = P < 148 * 64 ? P : 148 * 64;
-  quantize_pairs_kernel<<<(warps + 7) / 8, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms,
-                                                         codes, term_stride, kp, sf, sf_term_stride, kchunks,
-                                                         sf_rows);
+  const uint64_t items = static_cast<uint64_t>(n) * k * (d / 32);
+  if (items == 0) return cudaSuccess;
+  const uint64_t blocks = (items + 255) / 256;
+  const int grid = static_cast<int>(blocks < 148 * 32 ? blocks : 148 * 32);
+  quantize_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
+                                              term_stride, kp, sf, sf_term_stride, kchunks, sf_rows);
   return cudaGetLastError();
 }
 

@@ -50,3 +50,40 @@ __device__ __forceinline__ void split_e4m3_terms(float u, int terms, uint8_t (&c
 }
 
 }  // namespace mxmoe
+
+namespace mxmoe {
+
+// Thread-local variant: one thread owns a whole 32-element block `v` and
+// writes `terms` x 32 codes (as 8 packed 32-bit words per term) plus the
+// per-term E8M0 bytes.  Same arithmetic as split_e4m3_terms.
+__device__ __forceinline__ void quantize_block32(float (&v)[32], int terms, uint32_t (&words)[kMaxTerms][8],
+                                                 uint8_t (&sbyte)[kMaxTerms]) {
+#pragma unroll
+  for (int t = 0; t < kMaxTerms; ++t) {
+    if (t < terms) {
+      float amax = 0.0f;
+#pragma unroll
+      for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+      const int s = e4m3_block_exp(amax);
+      const float inv = ldexpf(1.0f, -s), back = ldexpf(1.0f, s);
+      const bool inv_ok = (s > -127) && (s < 127);  // both powers of two are normal
+#pragma unroll
+      for (int w = 0; w < 8; ++w) {
+        uint32_t word = 0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int i = w * 4 + b;
+          const float sv = inv_ok ? v[i] * inv : ldexpf(v[i], -s);
+          const __nv_fp8_storage_t c = __nv_cvt_float_to_fp8(sv, __NV_SATFINITE, __NV_E4M3);
+          const float cv = __half2float(__half(__nv_cvt_fp8_to_halfraw(c, __NV_E4M3)));
+          v[i] = v[i] - (inv_ok ? cv * back : ldexpf(cv, s));
+          word |= static_cast<uint32_t>(c) << (8 * b);
+        }
+        words[t][w] = word;
+      }
+      sbyte[t] = static_cast<uint8_t>(s + 127);
+    }
+  }
+}
+
+}  // namespace mxmoe

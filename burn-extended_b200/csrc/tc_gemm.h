@@ -9,13 +9,15 @@ namespace mxmoe {
 
 struct TcParams {
   int mode;      // 1 = W1 + SwiGLU (writes act codes), 2 = W2 + bias + route weight (writes y_pair)
-  int N;         // routed pairs per tile: 32, 64, 128 or 256
-  int m_tiles;   // 128-row weight tiles per expert
+  int N;         // weights-as-A: routed pairs per tile (32, 64, 128); tokens-as-A: 256 weight rows
+  int m_tiles;   // weight tiles per expert (128 rows weights-as-A, 256 rows tokens-as-A)
+  int w_row_blocks;  // 128-row scale atoms per expert of the weight operand
+  int units;     // W1: GLU units written to the activation operand (f padded to 64)
   int k_tiles;   // K / 128
   int E;         // experts held by this layer
   int stages;    // smem pipeline depth
   int b_terms;   // E4M3 terms of the activation operand (2 or 3)
-  int sf_rows;   // rows per activation scale atom: min(N, 128)
+  int sf_rows;   // rows per activation scale atom (= pairs per tile, <= 128)
   const int* poff;          // [E+1] padded segment starts (multiples of 128)
   const int* counts;        // [E] pairs per expert
   const int* ntile_prefix;  // [E+1] prefix sums of ceil(count / N)
@@ -41,9 +43,11 @@ struct TcParams {
   int* err;                 // device status word (0 = ok)
 };
 
-size_t tc_gemm_smem_bytes(int N, int terms, int stages);
-int tc_gemm_max_stages(int N, int terms, size_t smem_limit);
-cudaError_t tc_gemm_launch(const CUtensorMap& tmap_a, const CUtensorMap& tmap_b, const TcParams& p, int grid,
-                           cudaStream_t stream);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages);
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit);
+// tmap_w: weight codes (box 128 rows weights-as-A, 256 rows tokens-as-A);
+// tmap_x: activation terms (box = pairs per tile rows).
+cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
+                           const TcParams& p, int grid, cudaStream_t stream);
 
 }  // namespace mxmoe
