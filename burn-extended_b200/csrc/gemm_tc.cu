@@ -17,8 +17,9 @@
 //     N = 32..128, double-buffered accumulator;
 //   tokens-as-A (prefill): 128 pairs x 256 weight rows, so that each epilogue
 //     thread owns one pair's row and quantizes 32-wide blocks on its own.
-// Warp roles (192 threads): warp 0 = TMA producer, warp 1 = TMEM owner + MMA
-// issuer, warps 2..5 = epilogue (TMEM -> registers -> global).
+// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, the
+// rest = epilogue (TMEM -> registers -> global): warps 2..5 for weights-as-A,
+// warps 2..9 for tokens-as-A.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -32,8 +33,10 @@ namespace mxmoe {
 
 namespace {
 
-constexpr int kThreads = 192;
-constexpr int kEpiThreads = 128;
+// weights-as-A: 6 warps (4 epilogue); tokens-as-A: 10 warps (8 epilogue, two
+// per TMEM sub-partition, one per 128-column half of the accumulator).
+__host__ __device__ constexpr int num_threads(bool tok) { return tok ? 320 : 192; }
+__host__ __device__ constexpr int num_epi_threads(bool tok) { return tok ? 256 : 128; }
 constexpr int kMaxStages = 8;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfTmemBase = 256;  // scale factors live in columns 256.. (32 per stage)
@@ -92,7 +95,9 @@ __device__ __forceinline__ void decode_tile(const TcParams& p, int t, int& e, in
 __device__ __forceinline__ float swiglu_clamp(float g, float l, float alpha, float limit) {
   const float xg = fminf(g, limit);
   const float xl = fmaxf(-limit, fminf(l, limit));
-  return (xg / (1.0f + expf(-alpha * xg))) * (xl + 1.0f);
+  // x * sigmoid(alpha x) with the fast exponential and divide (relative error
+  // ~1e-7, far inside the layer tolerance); a huge exponent gives 0.
+  return __fdividef(xg, 1.0f + __expf(-alpha * xg)) * (xl + 1.0f);
 }
 
 __device__ __forceinline__ void store_block_terms(const TcParams& p, int pos, int j0,
@@ -111,7 +116,7 @@ __device__ __forceinline__ void store_block_terms(const TcParams& p, int pos, in
 }
 
 template <bool kTok>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(num_threads(kTok), 1)
     tc_moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                        const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -142,7 +147,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tmem_full[b], 1);
-      mbar_init(&tmem_empty[b], kEpiThreads);
+      mbar_init(&tmem_empty[b], num_epi_threads(kTok));
     }
     mbar_init(drain_bar, 1);
     fence_barrier_init();
@@ -282,11 +287,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Drain: every MMA issued by this thread has finished before TMEM is freed.
     tc_commit(drain_bar);
     mbar_wait(drain_bar, 0, nullptr, kDevTimeoutDrain);
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && (kTok || warp < 6)) {
     // ------------------------------------------------------------ epilogue
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int m = sp * 32 + lane;     // accumulator row
-    const int et = threadIdx.x - 64;  // 0..127 epilogue thread id
+    const int et = threadIdx.x - 64;  // epilogue thread id
     uint32_t acc_phase[2] = {0, 0};
     int acc = 0;
     float* xl = epi;                   // [64][kXPitch] linear half (weights-as-A)
@@ -304,56 +309,65 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int pos0 = __ldg(p.poff + e) + pt * PT;
       const uint64_t bias_e = static_cast<uint64_t>(e) * p.bias_stride;
       if (kTok) {
-        // thread = pair row m; columns = the 256 weight rows of tile wt
+        // Thread = pair row m; this warp owns columns [half*128, half*128 + 128)
+        // of the 256 weight rows of tile wt.  The accumulator is copied to
+        // registers and released before any math, so the next tile's MMAs
+        // overlap this epilogue.
+        const int half = (warp - 2) >> 2;
+        float v[128];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(trow + half * 128 + q * 32, v + q * 32);
+        tmem_wait_ld();
+        tc_fence_before();
+        mbar_arrive(&tmem_empty[acc]);
+        if (++acc == nacc) acc = 0;
         const bool valid = m < n_valid;
         const int pos = pos0 + m;
-        const int pair = valid ? __ldg(p.perm + pos) : 0;
+        if (!valid) continue;
+        const int pair = __ldg(p.perm + pos);
         if (p.mode == 2) {
-          const float w = valid ? __ldg(p.topk_w + pair) : 0.f;
-          for (int c0 = 0; c0 < 256; c0 += 16) {
-            const int cf = wt * 256 + c0;  // output feature of column c0
-            if (cf >= p.rows_valid) break; // uniform across the CTA
-            float v[16];
-            tmem_ld_32x32b_x16(trow + c0, v);
-            if (valid) {
-              float4* dst = reinterpret_cast<float4*>(p.y_pair + static_cast<uint64_t>(pos) * p.d + cf);
-              const float* bb = p.bias + bias_e + cf;
+          const float w = __ldg(p.topk_w + pair);
+          const int cf0 = wt * 256 + half * 128;  // output feature of v[0]
+          float4* dst = reinterpret_cast<float4*>(p.y_pair + static_cast<uint64_t>(pos) * p.d + cf0);
+          const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + cf0);
 #pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                float4 o;
-                o.x = (v[4 * q + 0] + __ldg(bb + 4 * q + 0) * p.bias_mult) * w;
-                o.y = (v[4 * q + 1] + __ldg(bb + 4 * q + 1) * p.bias_mult) * w;
-                o.z = (v[4 * q + 2] + __ldg(bb + 4 * q + 2) * p.bias_mult) * w;
-                o.w = (v[4 * q + 3] + __ldg(bb + 4 * q + 3) * p.bias_mult) * w;
-                dst[q] = o;
-              }
+          for (int q = 0; q < 32; ++q) {
+            if (cf0 + 4 * q < p.rows_valid) {
+              const float4 b4 = __ldg(bb + q);
+              float4 o;
+              o.x = fmaf(b4.x, p.bias_mult, v[4 * q + 0]) * w;
+              o.y = fmaf(b4.y, p.bias_mult, v[4 * q + 1]) * w;
+              o.z = fmaf(b4.z, p.bias_mult, v[4 * q + 2]) * w;
+              o.w = fmaf(b4.w, p.bias_mult, v[4 * q + 3]) * w;
+              dst[q] = o;
             }
           }
         } else {
-          const float r = valid ? __ldg(p.rscale + pair / p.k) : 0.f;
-          for (int h = 0; h < 2; ++h) {
-            const int unit0 = wt * 128 + h * 64;  // GLU unit of column h*128
-            if (unit0 >= p.units) break;          // uniform
-            for (int sb = 0; sb < 2; ++sb) {
-              float g[32], l[32];
-              tmem_ld_32x32b_x16(trow + h * 128 + sb * 32, *reinterpret_cast<float(*)[16]>(&g[0]));
-              tmem_ld_32x32b_x16(trow + h * 128 + sb * 32 + 16, *reinterpret_cast<float(*)[16]>(&g[16]));
-              tmem_ld_32x32b_x16(trow + h * 128 + 64 + sb * 32, *reinterpret_cast<float(*)[16]>(&l[0]));
-              tmem_ld_32x32b_x16(trow + h * 128 + 64 + sb * 32 + 16, *reinterpret_cast<float(*)[16]>(&l[16]));
-              if (valid) {
-                const float* bg = p.bias + bias_e + wt * 256 + h * 128 + sb * 32;  // packed W1 row of g[0]
+          const int unit0 = wt * 128 + half * 64;  // GLU unit of v[0]
+          if (unit0 >= p.units) continue;
+          const float r = __ldg(p.rscale + pair / p.k);
+          const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + wt * 256 + half * 128);
 #pragma unroll
-                for (int i = 0; i < 32; ++i)
-                  g[i] = swiglu_clamp(fmaf(g[i], r, __ldg(bg + i)), fmaf(l[i], r, __ldg(bg + 64 + i)), p.alpha,
-                                      p.limit);
-                uint32_t words[kMaxTerms][8];
-                uint8_t sbyte[kMaxTerms];
-                quantize_block32(g, 2, words, sbyte);
-                store_block_terms(p, pos, unit0 + sb * 32, words, sbyte);
-              }
+          for (int sb = 0; sb < 2; ++sb) {
+            float a[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 bg = __ldg(bb + sb * 8 + q);       // GLU biases
+              const float4 bl = __ldg(bb + 16 + sb * 8 + q);  // linear biases (64 columns later)
+              const float* gv = v + sb * 32 + 4 * q;
+              const float* lv = v + 64 + sb * 32 + 4 * q;
+              a[4 * q + 0] = swiglu_clamp(fmaf(gv[0], r, bg.x), fmaf(lv[0], r, bl.x), p.alpha, p.limit);
+              a[4 * q + 1] = swiglu_clamp(fmaf(gv[1], r, bg.y), fmaf(lv[1], r, bl.y), p.alpha, p.limit);
+              a[4 * q + 2] = swiglu_clamp(fmaf(gv[2], r, bg.z), fmaf(lv[2], r, bl.z), p.alpha, p.limit);
+              a[4 * q + 3] = swiglu_clamp(fmaf(gv[3], r, bg.w), fmaf(lv[3], r, bl.w), p.alpha, p.limit);
             }
+            uint32_t words[kMaxTerms][8];
+            uint8_t sbyte[kMaxTerms];
+            quantize_block32(a, 2, words, sbyte);
+            store_block_terms(p, pos, unit0 + sb * 32, words, sbyte);
           }
         }
+        continue;
       } else {
         // weights-as-A: thread = weight row m of tile wt; columns = pairs
         if (p.mode == 2) {
@@ -456,12 +470,12 @@ cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CU
     cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(smem));
     if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<true><<<grid, kThreads, smem, stream>>>(tmap_w, tmap_x, p);
+    tc_moe_gemm_kernel<true><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
   } else {
     cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                           static_cast<int>(smem));
     if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<false><<<grid, kThreads, smem, stream>>>(tmap_w, tmap_x, p);
+    tc_moe_gemm_kernel<false><<<grid, num_threads(false), smem, stream>>>(tmap_w, tmap_x, p);
   }
   return cudaGetLastError();
 }

@@ -53,9 +53,25 @@ __device__ __forceinline__ void split_e4m3_terms(float u, int terms, uint8_t (&c
 
 namespace mxmoe {
 
+// Two f32 -> E4M3 codes in one instruction (lo lands in the low byte) and the
+// exact decode of a code pair back to f32.
+__device__ __forceinline__ uint32_t cvt_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+__device__ __forceinline__ void dec_e4m3x2(uint32_t codes16, float& lo, float& hi) {
+  uint32_t h2;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(h2) : "h"(static_cast<uint16_t>(codes16)));
+  lo = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xFFFFu)));
+  hi = __half2float(__ushort_as_half(static_cast<unsigned short>(h2 >> 16)));
+}
+
 // Thread-local variant: one thread owns a whole 32-element block `v` and
 // writes `terms` x 32 codes (as 8 packed 32-bit words per term) plus the
-// per-term E8M0 bytes.  Same arithmetic as split_e4m3_terms.
+// per-term E8M0 bytes.  Same arithmetic as split_e4m3_terms: the block
+// exponent of every term keeps the block's largest residual within E4M3
+// range, and each residual is exact in f32.
 __device__ __forceinline__ void quantize_block32(float (&v)[32], int terms, uint32_t (&words)[kMaxTerms][8],
                                                  uint8_t (&sbyte)[kMaxTerms]) {
 #pragma unroll
@@ -65,19 +81,36 @@ __device__ __forceinline__ void quantize_block32(float (&v)[32], int terms, uint
 #pragma unroll
       for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
       const int s = e4m3_block_exp(amax);
-      const float inv = ldexpf(1.0f, -s), back = ldexpf(1.0f, s);
-      const bool inv_ok = (s > -127) && (s < 127);  // both powers of two are normal
+      // 2^-s and 2^s as normal floats when both exist; the extreme exponents
+      // take the exact ldexpf path.
+      const bool fast = (s > -126) && (s < 127);
+      const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
+      const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
         uint32_t word = 0;
 #pragma unroll
-        for (int b = 0; b < 4; ++b) {
-          const int i = w * 4 + b;
-          const float sv = inv_ok ? v[i] * inv : ldexpf(v[i], -s);
-          const __nv_fp8_storage_t c = __nv_cvt_float_to_fp8(sv, __NV_SATFINITE, __NV_E4M3);
-          const float cv = __half2float(__half(__nv_cvt_fp8_to_halfraw(c, __NV_E4M3)));
-          v[i] = v[i] - (inv_ok ? cv * back : ldexpf(cv, s));
-          word |= static_cast<uint32_t>(c) << (8 * b);
+        for (int hp = 0; hp < 2; ++hp) {
+          const int i = w * 4 + hp * 2;
+          float a, b;
+          if (fast) {
+            a = v[i] * inv;
+            b = v[i + 1] * inv;
+          } else {
+            a = ldexpf(v[i], -s);
+            b = ldexpf(v[i + 1], -s);
+          }
+          const uint32_t c = cvt_e4m3x2(a, b);
+          float da, db;
+          dec_e4m3x2(c, da, db);
+          if (fast) {
+            v[i] = fmaf(-da, back, v[i]);
+            v[i + 1] = fmaf(-db, back, v[i + 1]);
+          } else {
+            v[i] = v[i] - ldexpf(da, s);
+            v[i + 1] = v[i + 1] - ldexpf(db, s);
+          }
+          word |= c << (16 * hp);
         }
         words[t][w] = word;
       }
