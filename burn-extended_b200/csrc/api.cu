@@ -372,6 +372,13 @@ int check_layer(const mxmoe_layer* L) {
   return MXMOE_OK;
 }
 
+// Device status word -> ABI status.
+int device_status(int code) {
+  if (code == 0) return MXMOE_OK;
+  if (code == 7) return fail(MXMOE_ERR_INVALID_ARG, "a dispatched pair names an expert outside this layer's shard");
+  return fail(MXMOE_ERR_TIMEOUT, "a bounded device-side wait gave up (code %d)", code);
+}
+
 }  // namespace
 
 extern "C" {
@@ -589,7 +596,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
     if (x_dtype == y_dtype) {
       CUDA_TRY(cudaMemcpyAsync(y, x, xbytes, cudaMemcpyDeviceToDevice, st));
     } else {
-      CUDA_TRY(launch_combine(x, x_dtype, nullptr, nullptr, nullptr, n_tokens, L->d, 0, 1, y, y_dtype, st));
+      CUDA_TRY(launch_combine(x, x_dtype, nullptr, 0, nullptr, nullptr, n_tokens, L->d, 0, 1, y, y_dtype, st));
     }
     return MXMOE_OK;
   }
@@ -613,7 +620,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
   TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
   const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
-  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
+  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, MXMOE_F32, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
   if (L->profiling) {
     CUDA_TRY(cudaEventRecord(L->ev[6], st));
     L->profile_valid = true;
@@ -654,8 +661,7 @@ int mxmoe_forward_host(mxmoe_layer* L, const void* x_host, mxmoe_dtype x_dtype, 
   CUDA_TRY(cudaStreamSynchronize(st));
   int herr = 0;
   CUDA_TRY(cudaMemcpy(&herr, L->err, sizeof(int), cudaMemcpyDeviceToHost));
-  if (herr != 0) return fail(MXMOE_ERR_TIMEOUT, "device-side wait gave up (code %d)", herr);
-  return MXMOE_OK;
+  return device_status(herr);
 }
 
 int mxmoe_sync_status(mxmoe_layer* L, void* stream) {
@@ -665,8 +671,7 @@ int mxmoe_sync_status(mxmoe_layer* L, void* stream) {
   CUDA_TRY(cudaGetLastError());
   int herr = 0;
   CUDA_TRY(cudaMemcpy(&herr, L->err, sizeof(int), cudaMemcpyDeviceToHost));
-  if (herr != 0) return fail(MXMOE_ERR_TIMEOUT, "device-side wait gave up (code %d)", herr);
-  return MXMOE_OK;
+  return device_status(herr);
 }
 
 int mxmoe_routing_results(mxmoe_layer* L, const int32_t** topk_idx, const float** topk_w, const int32_t** offsets,
@@ -782,7 +787,8 @@ int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, ui
 }
 
 int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, const float* rscale,
-                        const int32_t* expert, const float* weight, uint32_t n_pairs, float* out, void* stream) {
+                        const int32_t* expert, const float* weight, uint32_t n_pairs, void* out,
+                        mxmoe_dtype out_dtype, void* stream) {
   TRY(check_layer(L));
   if (!L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "experts not uploaded");
   if (n_pairs == 0) return MXMOE_OK;
@@ -799,18 +805,18 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, tp.pair_tile, nullptr,
                           nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
   TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, rscale, weight, tp, xt, st));
-  CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, 0, st));
+  CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, MXMOE_F32, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, out_dtype, st));
   return MXMOE_OK;
 }
 
 int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_t d_model, uint32_t k,
-                  const int32_t* topk_idx, const int32_t* inv, const float* pair_out, int residual, void* y,
-                  mxmoe_dtype y_dtype, void* stream) {
+                  const int32_t* topk_idx, const int32_t* inv, const void* pair_out, mxmoe_dtype pair_dtype,
+                  int residual, void* y, mxmoe_dtype y_dtype, void* stream) {
   if (n_tokens == 0) return MXMOE_OK;
   if (!y || (residual && !x) || (k > 0 && (!topk_idx || !inv || !pair_out)))
     return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   if (k > static_cast<uint32_t>(kMaxTopK)) return fail(MXMOE_ERR_UNSUPPORTED, "k=%u", k);
-  CUDA_TRY(launch_combine(x, x_dtype, pair_out, topk_idx, inv, n_tokens, d_model, k, residual, y, y_dtype,
+  CUDA_TRY(launch_combine(x, x_dtype, pair_out, pair_dtype, topk_idx, inv, n_tokens, d_model, k, residual, y, y_dtype,
                           as_stream(stream)));
   return MXMOE_OK;
 }

@@ -319,9 +319,10 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
 // ------------------------------------------------------------------ combine
 // y[t] = x[t] + sum over the token's experts in increasing expert index of
 // y_pair (src/moe/mod.rs:279, :405, :411).
-__global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const float* __restrict__ y_pair,
-                               const int32_t* __restrict__ topk_idx, const int32_t* __restrict__ inv_p, int n, int d,
-                               int k, int residual, void* y, int y_dtype) {
+__global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const void* __restrict__ y_pair,
+                               int pair_dtype, const int32_t* __restrict__ topk_idx,
+                               const int32_t* __restrict__ inv_p, int n, int d, int k, int residual, void* y,
+                               int y_dtype) {
   const int t = blockIdx.x;
   if (t >= n) return;
   int ord[kMaxTopK];
@@ -337,7 +338,8 @@ __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const fl
     }
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float acc = 0.0f;
-    for (int s = 0; s < k; ++s) acc = __fadd_rn(acc, y_pair[static_cast<uint64_t>(ord[s]) * d + c]);
+    for (int s = 0; s < k; ++s)
+      acc = __fadd_rn(acc, load_any(y_pair, pair_dtype, static_cast<uint64_t>(ord[s]) * d + c));
     const float v = k == 0 ? load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c)
                     : residual ? __fadd_rn(load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c), acc) : acc;
     store_any(y, y_dtype, static_cast<uint64_t>(t) * d + c, v);
@@ -526,11 +528,11 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
   return cudaGetLastError();
 }
 
-cudaError_t launch_combine(const void* x, int x_dtype, const float* y_pair, const int32_t* topk_idx,
+cudaError_t launch_combine(const void* x, int x_dtype, const void* y_pair, int pair_dtype, const int32_t* topk_idx,
                            const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
                            cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  combine_kernel<<<n, 256, 0, st>>>(x, x_dtype, y_pair, topk_idx, inv_p, n, d, k, residual, y, y_dtype);
+  combine_kernel<<<n, 256, 0, st>>>(x, x_dtype, y_pair, pair_dtype, topk_idx, inv_p, n, d, k, residual, y, y_dtype);
   return cudaGetLastError();
 }
 

@@ -22,7 +22,7 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
                                   int sf_rows, cudaStream_t st);
-cudaError_t launch_combine(const void* x, int x_dtype, const float* y_pair, const int32_t* topk_idx,
+cudaError_t launch_combine(const void* x, int x_dtype, const void* y_pair, int pair_dtype, const int32_t* topk_idx,
                            const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
                            cudaStream_t st);
 cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, int32_t* local, int* err,

@@ -1,5 +1,5 @@
 // ptx.cuh -- thin inline-PTX wrappers for the sm_100a features the MoE kernels
-// use: mbarriers, TMA tensor / bulk copies (no multicast anywhere), tcgen05
+// use: mbarriers, TMA tensor / bulk copies (plain loads only, no cluster-wide copies), tcgen05
 // (TMEM alloc, block-scaled MMA, smem->TMEM copy, TMEM loads, commits).
 #pragma once
 #include <cstdint>

@@ -223,9 +223,12 @@ class MoeGatedSwiGLU:
                                 topk_w.data_ptr(), ptr(offsets), ptr(perm), ptr(inv), _stream_ptr(stream)))
 
     def forward_local(self, xr, rscale, expert, weight, out, stream=None):
+        """Expert FFN of this layer's shard for dispatched pairs (out: f32 or bf16)."""
         n = expert.numel()
+        if n == 0:
+            return
         check(lib().mxmoe_forward_local(self._h, xr.data_ptr(), _dtype_code(xr), rscale.data_ptr(),
-                                        expert.data_ptr(), weight.data_ptr(), n, out.data_ptr(),
+                                        expert.data_ptr(), weight.data_ptr(), n, out.data_ptr(), _dtype_code(out),
                                         _stream_ptr(stream)))
 
     def close(self):
@@ -266,8 +269,11 @@ def gather_pairs(x, k: int, perm, rscale, topk_idx, topk_w, out_x, out_rscale, o
 
 def combine(x, k: int, topk_idx, inv, pair_out, y, residual: bool = True, stream=None):
     n = y.numel() // y.shape[-1]
+    if n == 0:
+        return
     check(lib().mxmoe_combine(x.data_ptr() if x is not None else None, _dtype_code(x) if x is not None else 0, n,
-                              y.shape[-1], k, topk_idx.data_ptr(), inv.data_ptr(), pair_out.data_ptr(),
+                              y.shape[-1], k, topk_idx.data_ptr(), inv.data_ptr(),
+                              pair_out.data_ptr() if pair_out.numel() else None, _dtype_code(pair_out),
                               1 if residual else 0, y.data_ptr(), _dtype_code(y), _stream_ptr(stream)))
 
 

@@ -1,0 +1,202 @@
+"""Expert-parallel MoE layer: one process per GPU, experts split into
+contiguous shards, routed pairs moved by all-to-all (NCCL over NVLink on the
+GPU path, gloo in the CPU tests).
+
+The reference is single-rank (docs/gpt-oss-architecture.md:22 leaves
+world_size sharding out); this module adds the expert-parallel form of
+MoeGatedSwiGLU::forward (src/moe/mod.rs:99-115):
+
+  1. every rank routes its own tokens with the full router (RmsNorm, gate,
+     top-k, softmax) and sorts its (token, slot) pairs by expert -- pairs of
+     one destination rank are then contiguous;
+  2. the per-destination pair counts are exchanged, then the pairs' raw token
+     rows and their (1/rms, expert, weight) metadata are dispatched;
+  3. each rank runs its expert shard over the pairs it received;
+  4. the per-pair outputs travel back on the reverse all-to-all and every rank
+     combines its tokens' k contributions in increasing expert index and adds
+     the residual.
+
+The rank-local compute sits behind a backend object (route / gather / local /
+combine): CudaExpertBackend runs libmxmoe's kernels; the CPU tests plug in
+the oracle so that the dispatch logic is checked with gloo ranks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional
+
+from . import MoeConfig, MoeQuantLayerHost, QuantLinearMxFp4Desc, combine, gather_pairs
+
+
+def shard_bounds(num_experts: int, world: int, rank: int):
+    """Contiguous expert shard of `rank` (experts must divide evenly)."""
+    if num_experts % world != 0:
+        raise ValueError(f"{num_experts} experts do not split over {world} ranks")
+    per = num_experts // world
+    return rank * per, per
+
+
+def slice_host(host: MoeQuantLayerHost, begin: int, count: int) -> MoeQuantLayerHost:
+    """The expert shard [begin, begin + count) of a host weight payload."""
+    d1, d2 = host.w1_desc, host.w2_desc
+    return MoeQuantLayerHost(
+        QuantLinearMxFp4Desc(count, d1.rows, d1.cols, d1.bpr, d1.gpr, d1.ue8_offset),
+        QuantLinearMxFp4Desc(count, d2.rows, d2.cols, d2.bpr, d2.gpr, d2.ue8_offset),
+        host.w1_blocks[begin:begin + count], host.w1_scales[begin:begin + count],
+        host.w2_blocks[begin:begin + count], host.w2_scales[begin:begin + count])
+
+
+@dataclass
+class Routed:
+    rscale: object    # [n] 1 / rms per token
+    topk_idx: object  # [n, k] global expert ids
+    topk_w: object    # [n, k]
+    offsets: object   # [E + 1] prefix sums of pairs per expert (canonical order)
+    perm: object      # [n * k] sorted position -> pair
+    inv: object       # [n * k] pair -> sorted position
+
+
+class CudaExpertBackend:
+    """Rank-local compute on libmxmoe: the full router plus this rank's
+    expert shard."""
+
+    def __init__(self, cfg: MoeConfig, device, begin: int, count: int, gamma, gate_w, gate_b,
+                 host: MoeQuantLayerHost, b1, b2, pair_dtype=None):
+        import torch
+        self.torch = torch
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.layer = cfg.init(self.device.index or 0)
+        self.layer.set_router(gamma, gate_w, gate_b)
+        self.layer.set_expert_shard(begin, count)
+        self.layer.set_resident(slice_host(host, begin, count), b1[begin:begin + count], b2[begin:begin + count])
+        # per-pair outputs travel back in bf16: half the combine traffic, and
+        # the rounding (2^-9 relative per contribution) is far inside tolerance
+        self.pair_dtype = pair_dtype or torch.bfloat16
+
+    def route(self, x) -> Routed:
+        t = self.torch
+        n, k, E = x.shape[0], self.cfg.experts_per_token, self.cfg.num_experts
+        dev = x.device
+        r = Routed(t.empty(n, dtype=t.float32, device=dev), t.empty(n, k, dtype=t.int32, device=dev),
+                   t.empty(n, k, dtype=t.float32, device=dev), t.empty(E + 1, dtype=t.int32, device=dev),
+                   t.empty(n * k, dtype=t.int32, device=dev), t.empty(n * k, dtype=t.int32, device=dev))
+        if n:
+            self.layer.route(x, r.rscale, r.topk_idx, r.topk_w, r.offsets, r.perm, r.inv)
+        else:
+            r.offsets.zero_()
+        return r
+
+    def gather(self, x, r: Routed):
+        t = self.torch
+        P = r.perm.numel()
+        out_x = t.empty(P, x.shape[1], dtype=x.dtype, device=x.device)
+        rs = t.empty(P, dtype=t.float32, device=x.device)
+        ex = t.empty(P, dtype=t.int32, device=x.device)
+        w = t.empty(P, dtype=t.float32, device=x.device)
+        if P:
+            gather_pairs(x, self.cfg.experts_per_token, r.perm, r.rscale, r.topk_idx, r.topk_w, out_x, rs, ex, w)
+        meta = t.stack([rs.view(t.int32), ex, w.view(t.int32)], dim=1)  # [P, 3] 32-bit words
+        return out_x, meta
+
+    def local(self, xr, meta):
+        t = self.torch
+        out = t.empty(xr.shape[0], xr.shape[1], dtype=self.pair_dtype, device=xr.device)
+        if xr.shape[0]:
+            rs = meta[:, 0].contiguous().view(t.float32)
+            ex = meta[:, 1].contiguous()
+            w = meta[:, 2].contiguous().view(t.float32)
+            self.layer.forward_local(xr, rs, ex, w, out)
+        return out
+
+    def combine(self, x, r: Routed, pair_out, out_dtype=None):
+        t = self.torch
+        y = t.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+        combine(x, self.cfg.experts_per_token, r.topk_idx, r.inv, pair_out, y, residual=self.cfg.residual)
+        return y
+
+    def empty(self, shape, dtype):
+        return self.torch.empty(shape, dtype=dtype, device=self.device)
+
+    def to_host_list(self, t) -> List[int]:
+        return [int(v) for v in t.cpu().tolist()]
+
+
+class ExpertParallelMoe:
+    """One rank of the expert-parallel layer (see the module docstring)."""
+
+    # router, permute, gather, localize, permute, quantize, W1, W2, un-permute, combine
+    launches_per_step = 10
+
+    def __init__(self, backend, num_experts: int, world: int, rank: int, group=None):
+        import torch.distributed as dist
+        self.dist = dist
+        self.backend = backend
+        self.E = num_experts
+        self.world = world
+        self.rank = rank
+        self.group = group
+        self.Eg = num_experts // world
+
+    def _a2a(self, out, inp, out_splits, in_splits):
+        self.dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def _dispatch(self, x, r):
+        import torch
+        b = self.backend
+        offs = b.to_host_list(r.offsets[:: self.Eg])  # world + 1 boundaries
+        send = [offs[g + 1] - offs[g] for g in range(self.world)]
+        send_t = b.empty((self.world,), torch.int64)
+        send_t.copy_(torch.tensor(send, dtype=torch.int64))
+        recv_t = b.empty((self.world,), torch.int64)
+        self._a2a(recv_t, send_t, None, None)
+        recv = b.to_host_list(recv_t)
+        xs, meta = b.gather(x, r)
+        R = sum(recv)
+        xr = b.empty((R, x.shape[1]), x.dtype)
+        mr = b.empty((R, 3), torch.int32)
+        self._a2a(xr, xs, recv, send)
+        self._a2a(mr, meta, recv, send)
+        return send, recv, xr, mr
+
+    def forward(self, x, out_dtype=None):
+        b = self.backend
+        r = b.route(x)
+        send, recv, xr, mr = self._dispatch(x, r)
+        out = b.local(xr, mr)
+        back = b.empty((sum(send), x.shape[1]), out.dtype)
+        self._a2a(back, out, send, recv)
+        return b.combine(x, r, back, out_dtype)
+
+    def profile(self, x, steps: int = 3):
+        """Per-phase device times in ms (CUDA events on the current stream)."""
+        import torch
+        b = self.backend
+        names = ["route", "dispatch", "experts", "combine_a2a", "combine"]
+        acc = {n: 0.0 for n in names}
+        for _ in range(steps):
+            ev = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
+            ev[0].record()
+            r = b.route(x)
+            ev[1].record()
+            send, recv, xr, mr = self._dispatch(x, r)
+            ev[2].record()
+            out = b.local(xr, mr)
+            ev[3].record()
+            back = b.empty((sum(send), x.shape[1]), out.dtype)
+            self._a2a(back, out, send, recv)
+            ev[4].record()
+            b.combine(x, r, back)
+            ev[5].record()
+            torch.cuda.synchronize()
+            for i, n in enumerate(names):
+                acc[n] += ev[i].elapsed_time(ev[i + 1]) / steps
+        return acc
+
+
+def build_cuda_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig] = None, group=None):
+    """ExpertParallelMoe over libmxmoe for synthetic inputs `inp` (mxmoe.synth)."""
+    cfg = cfg or MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    begin, count = shard_bounds(inp.E, world, rank)
+    be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    return ExpertParallelMoe(be, inp.E, world, rank, group)

@@ -237,19 +237,20 @@ MXMOE_API int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_
 /* Receive side: expert FFN of this layer's shard for dispatched pairs.
  * xr [n_pairs][d] raw token rows (x's dtype), rscale [n_pairs], expert
  * [n_pairs] GLOBAL ids inside the shard, weight [n_pairs];
- * out [n_pairs][d] f32 = weight * (W2 act + b2).  Device pointers. */
+ * out [n_pairs][d] (out_dtype) = weight * (W2 act + b2).  Device pointers. */
 MXMOE_API int mxmoe_forward_local(mxmoe_layer* layer, const void* xr, mxmoe_dtype xr_dtype,
                         const float* rscale, const int32_t* expert,
-                        const float* weight, uint32_t n_pairs, float* out,
-                        void* stream);
+                        const float* weight, uint32_t n_pairs, void* out,
+                        mxmoe_dtype out_dtype, void* stream);
 
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
- * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out f32 in
- * permuted order).  residual = 0 omits x.  Device pointers. */
+ * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
+ * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers. */
 MXMOE_API int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
                   uint32_t d_model, uint32_t k, const int32_t* topk_idx,
-                  const int32_t* inv, const float* pair_out, int residual,
-                  void* y, mxmoe_dtype y_dtype, void* stream);
+                  const int32_t* inv, const void* pair_out,
+                  mxmoe_dtype pair_dtype, int residual, void* y,
+                  mxmoe_dtype y_dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,0 +1,54 @@
+"""Expert-parallel entry points on one GPU: the layer's experts split over
+several shard layers on the same device, the dispatch emulated by slicing
+(no collective), against the single-layer forward and the oracle."""
+import pytest
+
+import mxmoe
+from moe_testutil import assert_close, make_layer, oracle_forward, to_device_x
+from mxmoe import synth
+from mxmoe.ep import CudaExpertBackend, shard_bounds
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_sharded_layers_match_full_layer(world):
+    import torch
+    inp = synth.make_inputs(1024, 512, 8, 4, 200, True, seed=21)
+    full = make_layer(inp)
+    x = to_device_x(inp)
+    y_full = full.forward(x, out_dtype=torch.float32)
+    cfg = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    shards = []
+    for r in range(world):
+        b, c = shard_bounds(inp.E, world, r)
+        shards.append(CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, inp.gate_w, inp.gate_b, inp.host,
+                                        inp.b1, inp.b2, pair_dtype=torch.float32))
+    src = shards[0]
+    routed = src.route(x)
+    xs, meta = src.gather(x, routed)
+    offs = routed.offsets.cpu().numpy()
+    Eg = inp.E // world
+    outs = [shards[r].local(xs[offs[r * Eg]:offs[(r + 1) * Eg]].contiguous(),
+                            meta[offs[r * Eg]:offs[(r + 1) * Eg]].contiguous()) for r in range(world)]
+    y = src.combine(x, routed, torch.cat(outs, 0), out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert_close(y.cpu().numpy(), y_full.cpu().numpy(), "sharded vs full")
+    want, _, _ = oracle_forward(inp)
+    assert_close(y.cpu().numpy(), want, "sharded vs oracle")
+    rr = full.routing_results(inp.n)
+    assert torch.equal(rr["perm"], routed.perm)
+    assert torch.equal(rr["inv"], routed.inv)
+    full.close()
+
+
+def test_forward_local_rejects_foreign_expert():
+    import torch
+    inp = synth.make_inputs(256, 256, 4, 2, 8, True, seed=2)
+    cfg = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    be = CudaExpertBackend(cfg, "cuda:0", 2, 2, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    meta = torch.zeros(inp.n, 3, dtype=torch.int32, device="cuda:0")
+    meta[:, 1] = 0  # expert 0 lives on another shard
+    be.local(to_device_x(inp), meta)
+    with pytest.raises(mxmoe.MxMoeError):
+        be.layer.sync_status()
