@@ -10,6 +10,7 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 #include <string>
 #include <vector>
@@ -730,6 +731,56 @@ int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k, uint32
                           tmp + num_experts + 1, nullptr, perm, inv, st));
   CUDA_TRY(cudaStreamSynchronize(st));
   dfree(tmp);
+  return MXMOE_OK;
+}
+
+}  // extern "C"
+
+// Scratch of mxmoe_permute_noalloc: per-expert padded offsets and counts
+// (2 x (kNoAllocMaxExperts + 1) int32 = 8 KB).  It lives in the library's own
+// device memory on every GPU that loads it, for the life of the process.
+namespace {
+constexpr uint32_t kNoAllocMaxExperts = 1024;
+static __device__ __align__(256) int32_t g_permute_scratch[2 * (kNoAllocMaxExperts + 1)];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+int32_t* g_scratch_ptr[kMaxDevices] = {};
+
+// Device address of the scratch array for the current device, looked up once
+// per device.  Host code cannot pass g_permute_scratch itself: on the host
+// that name is only a stand-in, not a device address.
+int scratch_for_current_device(int32_t** out) {
+  int dev = -1;
+  CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(MXMOE_ERR_UNSUPPORTED, "device ordinal %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    CUDA_TRY(cudaGetSymbolAddress(&p, g_permute_scratch));
+    g_scratch_ptr[dev] = static_cast<int32_t*>(p);
+  }
+  *out = g_scratch_ptr[dev];
+  return MXMOE_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int mxmoe_permute_noalloc(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k, uint32_t num_experts,
+                          int32_t* offsets, int32_t* perm, int32_t* inv, void* stream) {
+  if (num_experts == 0)
+    return fail(MXMOE_ERR_UNSUPPORTED, "num_experts must be at least 1");
+  if (num_experts > kNoAllocMaxExperts)
+    return fail(MXMOE_ERR_TOO_LARGE, "mxmoe_permute_noalloc handles at most %u experts (got %u)",
+                kNoAllocMaxExperts, num_experts);
+  if (!offsets || (n_tokens * k > 0 && (!topk_idx || !perm || !inv)))
+    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  int32_t* scratch = nullptr;
+  TRY(scratch_for_current_device(&scratch));
+  // The kernel writes every scratch entry it reads, so nothing needs clearing.
+  CUDA_TRY(launch_permute(topk_idx, static_cast<int>(n_tokens * k), num_experts, 1, 1, offsets, nullptr, nullptr,
+                          scratch, scratch + num_experts + 1, nullptr, perm, inv, as_stream(stream)));
   return MXMOE_OK;
 }
 

@@ -65,6 +65,7 @@ _SIGS = {
     "mxmoe_dequant_rows": ([ctypes.POINTER(QuantDesc), _vp, _vp, _vp, _vp], _i32),
     "mxmoe_topk_softmax": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp], _i32),
     "mxmoe_permute": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp], _i32),
+    "mxmoe_permute_noalloc": ([_vp, _u32, _u32, _u32, _vp, _vp, _vp, _vp], _i32),
     "mxmoe_sync_status": ([_vp, _vp], _i32),
     "mxmoe_set_expert_shard": ([_vp, _u32, _u32], _i32),
     "mxmoe_set_profiling": ([_vp, _i32], _i32),

@@ -187,6 +187,23 @@ MXMOE_API int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t
                   uint32_t num_experts, int32_t* offsets, int32_t* perm,
                   int32_t* inv, void* stream);
 
+/* mxmoe_permute without any device allocation.  No counterpart in the
+ * reference: it is for callers that cannot call cudaMalloc, for instance code
+ * running under a caching or arena allocator that owns all device memory, or
+ * an embedding runtime that forbids allocation after start-up.  Its scratch
+ * (per-expert offsets and counts) is a fixed 8 KB array inside the library,
+ * held on every GPU that loads it until the process exits; num_experts above
+ * 1024 is rejected with MXMOE_ERR_TOO_LARGE.  The first call on a device
+ * looks the array's device address up (cudaGetSymbolAddress) -- make that
+ * first call before any stream capture.  All calls share the one array, so
+ * calls that overlap on the GPU (different streams, different threads) race;
+ * serialize them.  Unlike mxmoe_permute it does not synchronize `stream`.
+ * Device pointers, same meaning as mxmoe_permute. */
+MXMOE_API int mxmoe_permute_noalloc(const int32_t* topk_idx, uint32_t n_tokens,
+                                    uint32_t k, uint32_t num_experts,
+                                    int32_t* offsets, int32_t* perm,
+                                    int32_t* inv, void* stream);
+
 /* Synchronizes `stream` and reports a device-side failure of the layer's
  * kernels since the last forward (MXMOE_ERR_TIMEOUT when a bounded wait gave
  * up).  mxmoe_forward_host performs this check itself. */
