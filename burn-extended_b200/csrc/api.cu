@@ -211,11 +211,19 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   const uint64_t pairs = static_cast<uint64_t>(n_tokens) * k;
   if (n_tokens <= w.cap_tokens && pairs <= w.cap_pairs && w.cap_tokens > 0) return MXMOE_OK;
   if (pairs > (1u << 28)) return fail(MXMOE_ERR_TOO_LARGE, "too many pairs: %llu", (unsigned long long)pairs);
+  // Capacities only grow (the expert-parallel receive side alternates sizes
+  // from step to step), with an eighth of headroom on the requested growth.
+  const uint32_t old_t = w.cap_tokens, old_p = w.cap_pairs;
   CUDA_TRY(cudaDeviceSynchronize());
   free_workspace(w);
   const uint32_t E = L->e_count, Et = L->E_total;
-  const uint32_t cap_t = std::max<uint32_t>(n_tokens, 1);
-  const uint32_t cap_p = std::max<uint32_t>(static_cast<uint32_t>(pairs), 1);
+  auto grow = [](uint32_t old, uint64_t want) -> uint32_t {
+    if (want <= old) return old;
+    const uint64_t g = old ? want + want / 8 : want;
+    return static_cast<uint32_t>(std::max<uint64_t>(std::min<uint64_t>(g, 1u << 28), 1));
+  };
+  const uint32_t cap_t = grow(old_t, n_tokens);
+  const uint32_t cap_p = grow(old_p, pairs);
   w.rows = round_up(cap_p, kRowBlock) + E * kRowBlock + 256;
   w.row_blocks = w.rows / kTileWidths[0] + 2;  // enough atoms for the smallest tile width
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
@@ -828,12 +836,14 @@ int mxmoe_route(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32_t n_t
 
 int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_t d_model, uint32_t k,
                        const int32_t* perm, const float* rscale, const int32_t* topk_idx, const float* topk_w,
-                       void* out_x, float* out_rscale, int32_t* out_expert, float* out_w, void* stream) {
+                       void* out_x, uint32_t* out_meta, void* stream) {
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
   if (P == 0) return MXMOE_OK;
-  if (!x || !perm || !rscale || !topk_idx || !topk_w || !out_x) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (!x || !perm || !rscale || !topk_idx || !topk_w || !out_x || !out_meta)
+    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (d_model % 32 != 0) return fail(MXMOE_ERR_UNSUPPORTED, "d_model must be a multiple of 32");
   CUDA_TRY(launch_gather_pairs(x, x_dtype, d_model, k, static_cast<int>(P), perm, rscale, topk_idx, topk_w, out_x,
-                               out_rscale, out_expert, out_w, as_stream(stream)));
+                               out_meta, as_stream(stream)));
   return MXMOE_OK;
 }
 

@@ -361,29 +361,26 @@ __global__ void localize_kernel(const int32_t* __restrict__ expert, int P, int b
   local[i] = v;
 }
 
-// Dispatch packing: one block per permuted position q.
-__global__ void gather_pairs_kernel(const void* __restrict__ x, int x_dtype, int d, int k,
+// Dispatch packing: one warp per permuted position q copies the token row
+// with 16-byte moves (rows are multiples of 64 bytes) and writes the pair's
+// metadata as three 32-bit words (1/rms bits, expert id, route weight bits).
+__global__ void gather_pairs_kernel(const void* __restrict__ x, uint32_t row_bytes, int k, int P,
                                     const int32_t* __restrict__ perm, const float* __restrict__ rscale,
                                     const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
-                                    void* out_x, float* out_rscale, int32_t* out_expert, float* out_w) {
-  const int q = blockIdx.x;
-  const int p = perm[q];
+                                    void* out_x, uint32_t* out_meta) {
+  const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= P) return;
+  const int p = __ldg(perm + q);
   const int t = p / k;
-  if (threadIdx.x == 0) {
-    if (out_rscale) out_rscale[q] = rscale[t];
-    if (out_expert) out_expert[q] = topk_idx[p];
-    if (out_w) out_w[q] = topk_w[p];
+  if (lane == 0) {
+    out_meta[3 * static_cast<uint64_t>(q) + 0] = __float_as_uint(__ldg(rscale + t));
+    out_meta[3 * static_cast<uint64_t>(q) + 1] = static_cast<uint32_t>(__ldg(topk_idx + p));
+    out_meta[3 * static_cast<uint64_t>(q) + 2] = __float_as_uint(__ldg(topk_w + p));
   }
-  const uint64_t src = static_cast<uint64_t>(t) * d, dst = static_cast<uint64_t>(q) * d;
-  if (x_dtype == 0) {
-    const float* xs = static_cast<const float*>(x);
-    float* xd = static_cast<float*>(out_x);
-    for (int c = threadIdx.x; c < d; c += blockDim.x) xd[dst + c] = xs[src + c];
-  } else {
-    const uint16_t* xs = static_cast<const uint16_t*>(x);
-    uint16_t* xd = static_cast<uint16_t*>(out_x);
-    for (int c = threadIdx.x; c < d; c += blockDim.x) xd[dst + c] = xs[src + c];
-  }
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + static_cast<uint64_t>(t) * row_bytes);
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out_x) + static_cast<uint64_t>(q) * row_bytes);
+  for (uint32_t i = lane; i < row_bytes / 16; i += 32) dst[i] = __ldg(src + i);
 }
 
 // ------------------------------------------------------------------ SIMT FFN
@@ -545,10 +542,11 @@ cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, 
 
 cudaError_t launch_gather_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
                                 const float* rscale, const int32_t* topk_idx, const float* topk_w, void* out_x,
-                                float* out_rscale, int32_t* out_expert, float* out_w, cudaStream_t st) {
+                                uint32_t* out_meta, cudaStream_t st) {
   if (P == 0) return cudaSuccess;
-  gather_pairs_kernel<<<P, 256, 0, st>>>(x, x_dtype, d, k, perm, rscale, topk_idx, topk_w, out_x, out_rscale,
-                                         out_expert, out_w);
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * (x_dtype == 0 ? 4u : 2u);
+  gather_pairs_kernel<<<(P + 7) / 8, 256, 0, st>>>(x, row_bytes, k, P, perm, rscale, topk_idx, topk_w, out_x,
+                                                   out_meta);
   return cudaGetLastError();
 }
 

@@ -29,7 +29,7 @@ cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, 
                             cudaStream_t st);
 cudaError_t launch_gather_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
                                 const float* rscale, const int32_t* topk_idx, const float* topk_w, void* out_x,
-                                float* out_rscale, int32_t* out_expert, float* out_w, cudaStream_t st);
+                                uint32_t* out_meta, cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
                            const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
                            const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,

@@ -259,12 +259,12 @@ def _copy_device(dst, src_ptr: int, nbytes: int):
         raise MxMoeError(3, f"cudaMemcpy failed ({res})")
 
 
-def gather_pairs(x, k: int, perm, rscale, topk_idx, topk_w, out_x, out_rscale, out_expert, out_w, stream=None):
+def gather_pairs(x, k: int, perm, rscale, topk_idx, topk_w, out_x, out_meta, stream=None):
+    """Dispatch packing: out_x[q] = x[perm[q] // k], out_meta[q] = (rscale, expert, weight) as int32 words."""
     n = rscale.numel()
     check(lib().mxmoe_gather_pairs(x.data_ptr(), _dtype_code(x), n, x.shape[-1], k, perm.data_ptr(),
                                    rscale.data_ptr(), topk_idx.data_ptr(), topk_w.data_ptr(), out_x.data_ptr(),
-                                   out_rscale.data_ptr(), out_expert.data_ptr(), out_w.data_ptr(),
-                                   _stream_ptr(stream)))
+                                   out_meta.data_ptr(), _stream_ptr(stream)))
 
 
 def combine(x, k: int, topk_idx, inv, pair_out, y, residual: bool = True, stream=None):

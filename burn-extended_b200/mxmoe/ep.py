@@ -91,12 +91,9 @@ class CudaExpertBackend:
         t = self.torch
         P = r.perm.numel()
         out_x = t.empty(P, x.shape[1], dtype=x.dtype, device=x.device)
-        rs = t.empty(P, dtype=t.float32, device=x.device)
-        ex = t.empty(P, dtype=t.int32, device=x.device)
-        w = t.empty(P, dtype=t.float32, device=x.device)
+        meta = t.empty(P, 3, dtype=t.int32, device=x.device)  # (1/rms bits, expert, weight bits)
         if P:
-            gather_pairs(x, self.cfg.experts_per_token, r.perm, r.rscale, r.topk_idx, r.topk_w, out_x, rs, ex, w)
-        meta = t.stack([rs.view(t.int32), ex, w.view(t.int32)], dim=1)  # [P, 3] 32-bit words
+            gather_pairs(x, self.cfg.experts_per_token, r.perm, r.rscale, r.topk_idx, r.topk_w, out_x, meta)
         return out_x, meta
 
     def local(self, xr, meta):
@@ -144,6 +141,7 @@ class ExpertParallelMoe:
     def _dispatch(self, x, r):
         import torch
         b = self.backend
+        xs, meta = b.gather(x, r)  # enqueued before the host waits on the counts
         offs = b.to_host_list(r.offsets[:: self.Eg])  # world + 1 boundaries
         send = [offs[g + 1] - offs[g] for g in range(self.world)]
         send_t = b.empty((self.world,), torch.int64)
@@ -151,7 +149,6 @@ class ExpertParallelMoe:
         recv_t = b.empty((self.world,), torch.int64)
         self._a2a(recv_t, send_t, None, None)
         recv = b.to_host_list(recv_t)
-        xs, meta = b.gather(x, r)
         R = sum(recv)
         xr = b.empty((R, x.shape[1]), x.dtype)
         mr = b.empty((R, 3), torch.int32)

@@ -242,14 +242,14 @@ MXMOE_API int mxmoe_route(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype
                 void* stream);
 
 /* Packs routed pairs in permuted order for dispatch: for every position q,
- * pair p = perm[q], token t = p / k: out_x[q] = x[t] (x's dtype),
- * out_rscale[q] = rscale[t], out_expert[q] = topk_idx[p],
- * out_w[q] = topk_w[p].  Device pointers. */
+ * pair p = perm[q], token t = p / k: out_x[q] = x[t] (x's dtype, rows must
+ * start on 16-byte boundaries), and out_meta[q] = three 32-bit words
+ * {bits of rscale[t], topk_idx[p], bits of topk_w[p]}.  Device pointers. */
 MXMOE_API int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
                        uint32_t d_model, uint32_t k, const int32_t* perm,
                        const float* rscale, const int32_t* topk_idx,
-                       const float* topk_w, void* out_x, float* out_rscale,
-                       int32_t* out_expert, float* out_w, void* stream);
+                       const float* topk_w, void* out_x, uint32_t* out_meta,
+                       void* stream);
 
 /* Receive side: expert FFN of this layer's shard for dispatched pairs.
  * xr [n_pairs][d] raw token rows (x's dtype), rscale [n_pairs], expert
