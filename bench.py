@@ -139,6 +139,47 @@ def run_reference(args, world, rank):
     print(json.dumps(line), flush=True)
 
 
+def measure_decode(args, local, dev, hbm_peak):
+    """Decode-shaped layer (64 tokens, 32 experts, top-4):
+    HBM-bound; GB/s = algorithmic bytes (weights of the experts touched, router,
+    x and y) per forward time."""
+    import torch
+    import mxmoe
+    from mxmoe import synth
+    dec = synth.make_config("decode", seed=args.seed)
+    d, f, E = dec.d, dec.f, dec.E
+    dl = mxmoe.MoeConfig(dec.d, dec.f, dec.E, dec.k).init(local)
+    dl.set_router(dec.gamma, dec.gate_w, dec.gate_b)
+    dl.set_resident(dec.host, dec.b1, dec.b2)
+    xd = torch.from_numpy(dec.x).to(torch.bfloat16).to(dev)
+    for _ in range(3):
+        dl.forward(xd)
+    torch.cuda.synchronize()
+    s2, e2_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s2.record()
+    for _ in range(args.steps):
+        dl.forward(xd)
+    e2_.record()
+    torch.cuda.synchronize()
+    dec_ms = s2.elapsed_time(e2_) / args.steps
+    rr = dl.routing_results(dec.n)
+    used = int((np.diff(rr["offsets"].cpu().numpy()) > 0).sum())
+    per_expert = 2 * f * d // 2 + 2 * f * d // 32 + d * f // 2 + d * f // 32 + 2 * (2 * f + d)
+    dec_bytes = used * per_expert + 2 * E * d + E * 2 + 2 * dec.n * d * 2
+    dl.set_profiling(True)
+    dp = []
+    for _ in range(args.steps):
+        dl.forward(xd)
+        dp.append(dl.last_profile())
+    dstages = {s: statistics.mean(p[s] for p in dp) for s in dp[0]}
+    dl.close()
+    return {"config": "gptoss20b_moe_decode (64 tokens, 32 experts, top-4)",
+            "tokens_per_s": dec.n / (dec_ms / 1e3), "ms_per_step": dec_ms,
+            "algorithmic_bytes": dec_bytes, "hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
+            "hbm_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak, "stages_ms": dstages,
+            "l2": "weights of the 32 experts (423 MB) exceed the 126 MB L2; no flush"}
+
+
 def run_ours(args, world, rank, local):
     import torch
     import mxmoe
@@ -150,6 +191,9 @@ def run_ours(args, world, rank, local):
         import torch.distributed as dist
         dist.init_process_group("nccl", device_id=dev)
     hbm_peak, tc_burst, tc_sust, peak_src = load_peaks()
+    if args.only == "decode":
+        print(json.dumps({"decode": measure_decode(args, local, dev, hbm_peak)}), flush=True)
+        return
 
     inp = synth.make_config("prefill", seed=args.seed + rank)
     n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
@@ -250,37 +294,7 @@ def run_ours(args, world, rank, local):
     e2e = {"value": n / e2e_s, "unit": UNIT, "h2d_bytes_per_step": xh.numel() * xh.element_size(),
            "d2h_bytes_per_step": yh.numel() * yh.element_size()}
 
-    # decode-shaped layer: HBM-bound, GB/s vs peak
-    dec = synth.make_config("decode", seed=args.seed)
-    dl = mxmoe.MoeConfig(dec.d, dec.f, dec.E, dec.k).init(local)
-    dl.set_router(dec.gamma, dec.gate_w, dec.gate_b)
-    dl.set_resident(dec.host, dec.b1, dec.b2)
-    xd = torch.from_numpy(dec.x).to(torch.bfloat16).to(dev)
-    for _ in range(3):
-        dl.forward(xd)
-    torch.cuda.synchronize()
-    s2, e2_ = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s2.record()
-    for _ in range(args.steps):
-        dl.forward(xd)
-    e2_.record()
-    torch.cuda.synchronize()
-    dec_ms = s2.elapsed_time(e2_) / args.steps
-    rr = dl.routing_results(dec.n)
-    used = int((np.diff(rr["offsets"].cpu().numpy()) > 0).sum())
-    per_expert = 2 * f * d // 2 + 2 * f * d // 32 + d * f // 2 + d * f // 32 + 2 * (2 * f + d)
-    dec_bytes = used * per_expert + 2 * E * d + E * 2 + 2 * dec.n * d * 2
-    dl.set_profiling(True)
-    dp = []
-    for _ in range(args.steps):
-        dl.forward(xd)
-        dp.append(dl.last_profile())
-    dstages = {s: statistics.mean(p[s] for p in dp) for s in dp[0]}
-    dl.close()
-    extra["decode"] = {"config": "gptoss20b_moe_decode (64 tokens, 32 experts, top-4)",
-                       "tokens_per_s": dec.n / (dec_ms / 1e3), "ms_per_step": dec_ms,
-                       "algorithmic_bytes": dec_bytes, "hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
-                       "hbm_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak, "stages_ms": dstages}
+    extra["decode"] = measure_decode(args, local, dev, hbm_peak)
 
     cpu = None
     if not args.no_cpu_baseline:
@@ -317,7 +331,7 @@ def main():
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
-                    help="prefill: skip the decode / e2e / CPU legs (profiling runs)")
+                    help="prefill / decode: run only that leg (profiling runs)")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":

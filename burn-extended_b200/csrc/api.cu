@@ -132,8 +132,9 @@ struct DeviceGuard {
   }
 };
 
-constexpr int kNumTileWidths = 4;
-constexpr int kTileWidths[kNumTileWidths] = {32, 64, 128, 256};
+// Box rows of the activation tensor maps; 16-row boxes feed the stacked tiles.
+constexpr int kNumTileWidths = 5;
+constexpr int kTileWidths[kNumTileWidths] = {32, 64, 128, 256, 16};
 
 }  // namespace
 
@@ -267,18 +268,22 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
 //   few pairs  -> weights-as-A, pair tiles of 32 / 64 / 128 (HBM-bound decode);
 //   many pairs -> tokens-as-A, pair tiles of 128 x weight tiles of 256 rows.
 // tw indexes the activation tensor maps (box rows 32, 64, 128, 256).
+// Few pairs per expert (decode) with two-term activations: stacked 64-pair
+// tiles, both terms in one MMA operand, so the tensor work per weight byte is
+// halved.
 struct TilePlan {
   bool tok;
   int pair_tile;
   int tw;
+  bool stacked;
 };
 
-TilePlan pick_tiles(uint64_t pairs, uint32_t experts) {
+TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms) {
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
-  if (avg <= 24) return {false, 32, 0};
-  if (avg <= 48) return {false, 64, 1};
-  if (avg <= 96) return {false, 128, 2};
-  return {true, 128, 2};
+  if (avg <= 48 && x_terms == 2) return {true, 64, 4, true};
+  if (avg <= 24) return {true, 32, 0, false};
+  if (avg <= 48) return {true, 64, 1, false};
+  return {true, 128, 2, false};
 }
 
 // Two E4M3 terms represent bf16 activations exactly when the RmsNorm gain is
@@ -311,7 +316,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
                                  w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
                                  static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), N,
-                                 st));
+                                 tp.stacked ? 1 : 0, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
   const uint64_t max_pair_tiles = (P + N - 1) / N + L->e_count;
   const bool tok = tp.tok;
@@ -319,6 +324,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   TcParams p{};
   p.N = tok ? 256 : N;
   p.sf_rows = N;
+  p.stacked = tp.stacked ? 1 : 0;
   p.E = L->e_count;
   p.poff = w.poff;
   p.counts = w.counts;
@@ -335,7 +341,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   // W1 + SwiGLU: weights W1, activations x terms; writes act terms.
   p.mode = 1;
   p.b_terms = x_terms;
-  p.stages = tc_gemm_max_stages(tok, p.N, x_terms, L->smem_limit);
+  p.stages = tc_gemm_max_stages(tok, p.N, x_terms, L->smem_limit, N);
   p.m_tiles = static_cast<int>((2 * L->fp + wrows - 1) / wrows);
   p.w_row_blocks = static_cast<int>(2 * L->fp / 128);
   p.k_tiles = static_cast<int>(kc1);
@@ -358,7 +364,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   // W2 + bias + route weight: weights W2, activations act terms; writes y_pair.
   p.mode = 2;
   p.b_terms = 2;
-  p.stages = tc_gemm_max_stages(tok, p.N, 2, L->smem_limit);
+  p.stages = tc_gemm_max_stages(tok, p.N, 2, L->smem_limit, N);
   p.m_tiles = static_cast<int>((L->d + wrows - 1) / wrows);
   p.w_row_blocks = static_cast<int>((L->d + 127) / 128);
   p.k_tiles = static_cast<int>(kc2);
@@ -617,7 +623,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   const uint32_t k = L->k, E = L->e_count;
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
   const int xt = x_terms_for(L, x_dtype);
-  const TilePlan tp = pick_tiles(P, E);
+  const TilePlan tp = pick_tiles(P, E, xt);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   L->profile_valid = false;
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
@@ -859,7 +865,7 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   Workspace& w = L->ws;
   cudaStream_t st = as_stream(stream);
   const int xt = x_terms_for(L, xr_dtype);
-  const TilePlan tp = pick_tiles(n_pairs, L->e_count);
+  const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   CUDA_TRY(launch_localize(expert, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
                            static_cast<int>(L->e_count), w.local_idx, L->err, st));

@@ -17,9 +17,10 @@
 //     N = 32..128, double-buffered accumulator;
 //   tokens-as-A (prefill): 128 pairs x 256 weight rows, so that each epilogue
 //     thread owns one pair's row and quantizes 32-wide blocks on its own.
-// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, the
-// rest = epilogue (TMEM -> registers -> global): warps 2..5 for weights-as-A,
-// warps 2..9 for tokens-as-A.
+// Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, then the
+// epilogue warps (TMEM -> registers -> global: 2..5 for weights-as-A, 2..9 for
+// tokens-as-A) and one warp that moves each stage's scale factors from shared
+// memory into TMEM so that the MMA thread only issues MMAs.
 #include <cuda.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
@@ -28,15 +29,18 @@
 #include "ptx.cuh"
 #include "quant.cuh"
 #include "tc_gemm.h"
+#include "launch_util.h"
 
 namespace mxmoe {
 
 namespace {
 
-// weights-as-A: 6 warps (4 epilogue); tokens-as-A: 10 warps (8 epilogue, two
-// per TMEM sub-partition, one per 128-column half of the accumulator).
-__host__ __device__ constexpr int num_threads(bool tok) { return tok ? 320 : 192; }
+// weights-as-A: 7 warps (4 epilogue); tokens-as-A: 11 warps (8 epilogue, two
+// per TMEM sub-partition, one per 128-column half of the accumulator).  The
+// last warp copies each stage's scale factors into TMEM, off the MMA thread.
+__host__ __device__ constexpr int num_threads(bool tok) { return tok ? 352 : 224; }
 __host__ __device__ constexpr int num_epi_threads(bool tok) { return tok ? 256 : 128; }
+__host__ __device__ constexpr int sf_warp(bool tok) { return tok ? 10 : 6; }
 constexpr int kMaxStages = 8;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfTmemBase = 256;  // scale factors live in columns 256.. (32 per stage)
@@ -50,7 +54,10 @@ struct SmemPlan {
 
 // Weights-as-A: A = 128 weight rows (FP4 in byte containers), B = N rows per term.
 // Tokens-as-A:  A = 128 token rows per term (E4M3), B = 256 weight rows.
-__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms) {
+// Tokens-as-A loads only the PT (= pair tile) rows of each activation term;
+// the MMA still reads 128 rows, the rows past PT falling into the next buffer
+// of the same stage and only feeding accumulator rows that are discarded.
+__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms, int PT) {
   SmemPlan s;
   if (!tok) {
     s.a_terms = 1;
@@ -60,7 +67,7 @@ __host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms) {
   } else {
     s.a_terms = terms;
     s.b_terms = 1;
-    s.a_bytes = 128 * kTileK;
+    s.a_bytes = static_cast<uint32_t>(PT) * kTileK;
     s.b_bytes = 256 * kTileK;
   }
   const uint32_t raw = s.a_terms * s.a_bytes + s.b_terms * s.b_bytes + 6 * kSfAtomBytes;
@@ -100,18 +107,28 @@ __device__ __forceinline__ float swiglu_clamp(float g, float l, float alpha, flo
   return __fdividef(xg, 1.0f + __expf(-alpha * xg)) * (xl + 1.0f);
 }
 
+// Scale byte of (row pos, term t, k block kb) in the activation atom arrays:
+// plain (one atom per sf_rows rows and term, term arrays act_sf_term_stride
+// apart) or stacked (layout.cuh, stacked_sf_offset).
+__device__ __forceinline__ uint64_t act_sf_offset(const TcParams& p, int pos, int t, int kb) {
+  if (p.stacked)
+    return stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(t), static_cast<uint32_t>(kb),
+                             static_cast<uint32_t>(p.act_kchunks));
+  return t * p.act_sf_term_stride + sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(kb),
+                                              static_cast<uint32_t>(p.act_kchunks),
+                                              static_cast<uint32_t>(p.sf_rows));
+}
+
 __device__ __forceinline__ void store_block_terms(const TcParams& p, int pos, int j0,
                                                   const uint32_t (&words)[kMaxTerms][8],
                                                   const uint8_t (&sbyte)[kMaxTerms]) {
   const uint64_t off = static_cast<uint64_t>(pos) * p.act_kp + j0;
-  const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(j0 / 32),
-                                static_cast<uint32_t>(p.act_kchunks), static_cast<uint32_t>(p.sf_rows));
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
     uint4* dst = reinterpret_cast<uint4*>(p.act_codes + t * p.act_term_stride + off);
     dst[0] = make_uint4(words[t][0], words[t][1], words[t][2], words[t][3]);
     dst[1] = make_uint4(words[t][4], words[t][5], words[t][6], words[t][7]);
-    p.act_sf[t * p.act_sf_term_stride + so] = sbyte[t];
+    p.act_sf[act_sf_offset(p, pos, t, j0 / 32)] = sbyte[t];
   }
 }
 
@@ -121,7 +138,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
                        const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms);
+  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms, p.sf_rows);
   const int S = p.stages;
   float* epi = reinterpret_cast<float*>(smem + S * plan.stage_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi) + epi_smem_bytes(kTok));
@@ -130,13 +147,15 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
   uint64_t* tmem_full = bars + 2 * kMaxStages;  // [2]
   uint64_t* tmem_empty = tmem_full + 2;         // [2]
   uint64_t* drain_bar = tmem_full + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  uint64_t* sf_drain = tmem_full + 5;
+  uint64_t* sf_full = tmem_full + 6;  // [kMaxStages] scale factors of the stage are in TMEM
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sf_full + kMaxStages);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = p.err;
   const int N = p.N;                             // weights-as-A: pairs per tile; tokens-as-A: 256
-  const int PT = kTok ? 128 : N;                 // pairs per tile
+  const int PT = kTok ? p.sf_rows : N;           // pairs per tile
   const int nacc = (!kTok && N <= 128) ? 2 : 1;  // accumulator buffers
   const int terms = p.b_terms;
 
@@ -150,6 +169,8 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
       mbar_init(&tmem_empty[b], num_epi_threads(kTok));
     }
     mbar_init(drain_bar, 1);
+    mbar_init(sf_drain, 1);
+    for (int s = 0; s < S; ++s) mbar_init(&sf_full[s], 1);
     fence_barrier_init();
     prefetch_tmap(&tmap_w);
     prefetch_tmap(&tmap_x);
@@ -178,7 +199,8 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
     }
     const uint32_t w_tx = (kTok ? 256 : 128) * kTileK / 2;  // packed FP4 bytes
     const uint32_t x_tx = PT * kTileK;                      // E4M3 bytes per term
-    const uint32_t tx = w_tx + terms * x_tx + kSfAtomBytes * (natoms_w + terms * natoms_x);
+    const int nsf_x = (kTok && p.stacked) ? 1 : terms * natoms_x;  // activation scale atoms per stage
+    const uint32_t tx = w_tx + terms * x_tx + kSfAtomBytes * (natoms_w + nsf_x);
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       int e, wt, pt;
@@ -197,8 +219,16 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         uint8_t* sf = sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes;
         mbar_arrive_expect_tx(&full_bar[stage], tx);
         tma_load_3d(w_s, &tmap_w, &full_bar[stage], kt * kTileK, wt * (kTok ? 256 : 128), e);
-        for (int term = 0; term < terms; ++term)
-          tma_load_3d(x_s + term * x_stride, &tmap_x, &full_bar[stage], kt * kTileK, row0, term);
+        if (kTok && p.stacked) {
+          // 16-row boxes: pairs 16g..16g+15 of term q go to smem rows 32g + 16q
+          for (int term = 0; term < 2; ++term)
+            for (int gq = 0; gq < 4; ++gq)
+              tma_load_3d(x_s + (gq * 32 + 16 * term) * kTileK, &tmap_x, &full_bar[stage], kt * kTileK,
+                          row0 + gq * 16, term);
+        } else {
+          for (int term = 0; term < terms; ++term)
+            tma_load_3d(x_s + term * x_stride, &tmap_x, &full_bar[stage], kt * kTileK, row0, term);
+        }
         // scale atoms in smem: [weights x natoms_w][term 0 x natoms_x][term 1 ...]
         for (int a = 0; a < natoms_w; ++a) {
           int wa = wt * natoms_w + a;
@@ -207,11 +237,16 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
                     p.a_sf + ((static_cast<uint64_t>(e) * p.w_row_blocks + wa) * p.k_tiles + kt) * kSfAtomBytes,
                     kSfAtomBytes, &full_bar[stage]);
         }
-        for (int term = 0; term < terms; ++term)
-          for (int a = 0; a < natoms_x; ++a)
-            bulk_load(sf + kSfAtomBytes * (natoms_w + term * natoms_x + a),
-                      p.b_sf + term * p.b_sf_term_stride + ((rbx + a) * p.k_tiles + kt) * kSfAtomBytes,
-                      kSfAtomBytes, &full_bar[stage]);
+        if (kTok && p.stacked) {
+          bulk_load(sf + kSfAtomBytes * natoms_w, p.b_sf + (rbx * p.k_tiles + kt) * kSfAtomBytes, kSfAtomBytes,
+                    &full_bar[stage]);
+        } else {
+          for (int term = 0; term < terms; ++term)
+            for (int a = 0; a < natoms_x; ++a)
+              bulk_load(sf + kSfAtomBytes * (natoms_w + term * natoms_x + a),
+                        p.b_sf + term * p.b_sf_term_stride + ((rbx + a) * p.k_tiles + kt) * kSfAtomBytes,
+                        kSfAtomBytes, &full_bar[stage]);
+        }
         issued[stage] = true;
         issued_parity[stage] = phase;
         if (++stage == S) {
@@ -240,7 +275,9 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 128);
       for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull)) {
+        // the scale-factor warp waits for the stage's TMA data, copies the
+        // scales into TMEM and commits sf_full: data and scales are then ready
+        if (!mbar_wait(&sf_full[stage], phase, err, kDevTimeoutFull)) {
           ok = false;
           break;
         }
@@ -249,20 +286,12 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         const uint32_t w_addr = smem_u32(kTok ? sb + terms * plan.a_bytes : sb);
         const uint32_t x_addr = smem_u32(kTok ? sb : sb + plan.a_bytes);
         const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
-        const uint32_t sf_addr = smem_u32(sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes);
         const uint32_t col0 = kSfTmemBase + stage * 32;
-        // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
-        // activation term q at col0 + 8 + 8q (4 per 128 rows).
-        for (int a = 0; a < natoms_w; ++a)
-          tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
-        for (int term = 0; term < terms; ++term)
-          for (int a = 0; a < natoms_x; ++a)
-            tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
-                                 make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
+        const int mma_terms = (kTok && p.stacked) ? 1 : terms;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const uint64_t w_desc = make_smem_desc(w_addr + kk * 32, 16, 1024, 2);
-          for (int term = 0; term < terms; ++term) {
+          for (int term = 0; term < mma_terms; ++term) {
             const uint64_t x_desc = make_smem_desc(x_addr + term * x_stride + kk * 32, 16, 1024, 2);
             const uint32_t idesc = make_idesc_mxf8f6f4(a_fmt, b_fmt, 128u, mma_n, kk, kk);
             const uint32_t sf_w = (tmem_base + col0) | (static_cast<uint32_t>(kk) << 30);
@@ -287,7 +316,40 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
     // Drain: every MMA issued by this thread has finished before TMEM is freed.
     tc_commit(drain_bar);
     mbar_wait(drain_bar, 0, nullptr, kDevTimeoutDrain);
-  } else if (warp >= 2 && (kTok || warp < 6)) {
+  } else if (warp == sf_warp(kTok) && lane == 0) {
+    // ------------------------------------------------------------ scale factors -> TMEM
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    const int mma_terms = (kTok && p.stacked) ? 1 : terms;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      for (int kt = 0; kt < p.k_tiles; ++kt) {
+        if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        uint8_t* sb = smem + stage * plan.stage_bytes;
+        const uint32_t sf_addr = smem_u32(sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes);
+        const uint32_t col0 = kSfTmemBase + stage * 32;
+        // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
+        // activation term q at col0 + 8 + 8q (4 per 128 rows).
+        for (int a = 0; a < natoms_w; ++a)
+          tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
+        for (int term = 0; term < mma_terms; ++term)
+          for (int a = 0; a < natoms_x; ++a)
+            tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
+                                 make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
+        tc_commit(&sf_full[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    tc_commit(sf_drain);
+    mbar_wait(sf_drain, 0, nullptr, kDevTimeoutDrain);
+  } else if (warp >= 2 && warp < 2 + num_epi_threads(kTok) / 32) {
     // ------------------------------------------------------------ epilogue
     const int sp = warp & 3;          // TMEM sub-partition this warp may access
     const int m = sp * 32 + lane;     // accumulator row
@@ -321,8 +383,15 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         tc_fence_before();
         mbar_arrive(&tmem_empty[acc]);
         if (++acc == nacc) acc = 0;
-        const bool valid = m < n_valid;
-        const int pos = pos0 + m;
+        int jrow = m;  // pair index within the tile
+        if (p.stacked) {
+          // lanes 16..31 hold the lo-term rows of the pairs in lanes 0..15
+#pragma unroll
+          for (int i = 0; i < 128; ++i) v[i] += __shfl_down_sync(0xFFFFFFFFu, v[i], 16);
+          jrow = lane < 16 ? sp * 16 + lane : PT;
+        }
+        const bool valid = jrow < n_valid;
+        const int pos = pos0 + jrow;
         if (!valid) continue;
         const int pair = __ldg(p.perm + pos);
         if (p.mode == 2) {
@@ -451,29 +520,27 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages) {
-  const SmemPlan plan = smem_plan(tokens_as_a, N, terms);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile) {
+  const SmemPlan plan = smem_plan(tokens_as_a, N, terms, pair_tile);
   return 1024 + static_cast<size_t>(stages) * plan.stage_bytes + epi_smem_bytes(tokens_as_a) +
-         (2 * kMaxStages + 8) * sizeof(uint64_t);
+         (3 * kMaxStages + 10) * sizeof(uint64_t);
 }
 
-int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit) {
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile) {
   int s = kMaxStages - 1;  // 7 stages x 32 scale columns fit above column 256
-  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s) > smem_limit) --s;
+  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s, pair_tile) > smem_limit) --s;
   return s;
 }
 
 cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
                            const TcParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages);
+  const size_t smem = tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages, p.sf_rows);
   if (tokens_as_a) {
-    cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(smem));
+    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<true>), smem);
     if (st != cudaSuccess) return st;
     tc_moe_gemm_kernel<true><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
   } else {
-    cudaError_t st = cudaFuncSetAttribute(tc_moe_gemm_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          static_cast<int>(smem));
+    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<false>), smem);
     if (st != cudaSuccess) return st;
     tc_moe_gemm_kernel<false><<<grid, num_threads(false), smem, stream>>>(tmap_w, tmap_x, p);
   }

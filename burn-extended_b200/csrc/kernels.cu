@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include "kernels.h"
+#include "launch_util.h"
 #include "layout.cuh"
 #include "quant.cuh"
 
@@ -112,69 +113,59 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int
                    topk_w + static_cast<uint64_t>(t) * k);
 }
 
-// RmsNorm (src/moe/mod.rs:109) + gate Linear (:110) + top-k/softmax (:272-276).
-// kRouterTok tokens per block; the block's normalized rows sit in smem so
-// every gate weight read from L2 serves kRouterTok tokens.  Summation order
-// is fixed (32 lane chains of fused multiply-adds, then a butterfly) so that
-// the logits are reproducible bit for bit by the CPU restatement.
-constexpr int kRouterTok = 4;
+// RmsNorm (src/moe/mod.rs:109) + gate Linear (:110): router logits.
+// Block (bx, by) handles tokens [TOK*bx, TOK*bx + TOK) and experts
+// [8*by, 8*by + 8), one expert per warp; its tokens' normalized rows sit in
+// smem so every gate weight read serves TOK tokens.  Summation order is fixed
+// (32 lane chains of fused multiply-adds, then a butterfly), so the logits are
+// reproducible bit for bit by the CPU restatement whatever the grid shape.
 constexpr int kRouterThreads = 256;
+constexpr int kRouterExperts = kRouterThreads / 32;
 
-template <typename XT>
+template <typename XT, int TOK>
 __global__ void __launch_bounds__(kRouterThreads)
-    router_kernel(const XT* __restrict__ x, int n, int d, int E, int k, const float* __restrict__ gamma,
-                  const float* __restrict__ gate_w, const float* __restrict__ gate_b, float eps,
-                  float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
-                  float* __restrict__ rscale) {
+    router_logits_kernel(const XT* __restrict__ x, int n, int d, int E, const float* __restrict__ gamma,
+                         const float* __restrict__ gate_w, const float* __restrict__ gate_b, float eps,
+                         float* __restrict__ logits_out, float* __restrict__ rscale) {
   extern __shared__ float sm[];
-  float* nrm = sm;                        // [kRouterTok][d]
-  float* lg = sm + kRouterTok * d;        // [kRouterTok][E]
-  float* rs = lg + kRouterTok * E;        // [kRouterTok]
+  float* nrm = sm;             // [TOK][d]
+  float* rs = sm + TOK * d;    // [TOK]
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * kRouterTok;
-  const int nt = min(kRouterTok, n - t0);
-
-  if (warp < nt) {
-    const XT* xr = x + static_cast<uint64_t>(t0 + warp) * d;
+  const int t0 = blockIdx.x * TOK;
+  const int nt = min(TOK, n - t0);
+  for (int t = warp; t < nt; t += kRouterExperts) {
+    const XT* xr = x + static_cast<uint64_t>(t0 + t) * d;
     float acc = 0.0f;
     for (int c = lane; c < d; c += 32) {
       const float v = load_f32(xr, c);
       acc = __fmaf_rn(v, v, acc);
     }
     const float ss = warp_sum_butterfly(acc);
-    if (lane == 0) rs[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
+    if (lane == 0) rs[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
   }
   __syncthreads();
   for (int i = threadIdx.x; i < nt * d; i += blockDim.x) {
     const int t = i / d, c = i - t * d;
-    const float v = load_f32(x, static_cast<uint64_t>(t0 + t) * d + c);
-    nrm[i] = __fmul_rn(__fmul_rn(v, rs[t]), gamma[c]);
+    nrm[i] = __fmul_rn(__fmul_rn(load_f32(x, static_cast<uint64_t>(t0 + t) * d + c), rs[t]), gamma[c]);
   }
+  if (blockIdx.y == 0 && threadIdx.x < nt) rscale[t0 + threadIdx.x] = rs[threadIdx.x];
   __syncthreads();
-  for (int e = warp; e < E; e += kRouterThreads / 32) {
+  for (int e = blockIdx.y * kRouterExperts + warp; e < E; e += gridDim.y * kRouterExperts) {
     const float* w = gate_w + static_cast<uint64_t>(e) * d;
-    float acc[kRouterTok];
+    float acc[TOK];
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) acc[t] = 0.0f;
+    for (int t = 0; t < TOK; ++t) acc[t] = 0.0f;
     for (int c = lane; c < d; c += 32) {
       const float wv = __ldg(w + c);
 #pragma unroll
-      for (int t = 0; t < kRouterTok; ++t) acc[t] = __fmaf_rn(nrm[t * d + c], wv, acc[t]);
+      for (int t = 0; t < TOK; ++t)
+        if (t < nt) acc[t] = __fmaf_rn(nrm[t * d + c], wv, acc[t]);
     }
 #pragma unroll
-    for (int t = 0; t < kRouterTok; ++t) {
+    for (int t = 0; t < TOK; ++t) {
       const float s = warp_sum_butterfly(acc[t]);
-      if (lane == 0) lg[t * E + e] = __fadd_rn(s, gate_b[e]);
+      if (lane == 0 && t < nt) logits_out[static_cast<uint64_t>(t0 + t) * E + e] = __fadd_rn(s, gate_b[e]);
     }
-  }
-  __syncthreads();
-  if (threadIdx.x < nt) {
-    const int t = t0 + threadIdx.x;
-    const float* l = lg + threadIdx.x * E;
-    if (logits_out)
-      for (int e = 0; e < E; ++e) logits_out[static_cast<uint64_t>(t) * E + e] = l[e];
-    topk_softmax_row(l, E, k, topk_idx + static_cast<uint64_t>(t) * k, topk_w + static_cast<uint64_t>(t) * k);
-    rscale[t] = rs[threadIdx.x];
   }
 }
 
@@ -266,7 +257,7 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
                                       const float* __restrict__ gamma, int gamma_is_one,
                                       const int32_t* __restrict__ inv_p, int terms, uint8_t* codes,
                                       uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride,
-                                      int kchunks, int sf_rows) {
+                                      int kchunks, int sf_rows, int stacked) {
   const int nb = d / 32;
   const uint64_t items = static_cast<uint64_t>(n) * k * nb;
   for (uint64_t it = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; it < items;
@@ -311,7 +302,11 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
       uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
       dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
       dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
-      sf[q * sf_term_stride + so] = sbyte[q];
+      if (stacked)
+        sf[stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q), static_cast<uint32_t>(b),
+                             static_cast<uint32_t>(kchunks))] = sbyte[q];
+      else
+        sf[q * sf_term_stride + so] = sbyte[q];
     }
   }
 }
@@ -482,31 +477,44 @@ cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_
   return cudaGetLastError();
 }
 
+template <int TOK>
+static cudaError_t launch_router_tok(const void* x, int x_dtype, int n, int d, int E, const float* gamma,
+                                     const float* gate_w, const float* gate_b, float eps, float* logits,
+                                     float* rscale, cudaStream_t st) {
+  const size_t smem = (static_cast<size_t>(TOK) * d + TOK) * sizeof(float);
+  // few tokens: experts spread over grid.y for parallelism; many tokens: one
+  // block row covers all experts so the normalization is done once
+  const int gy = n >= 2048 ? 1 : (E + kRouterExperts - 1) / kRouterExperts;
+  const dim3 grid((n + TOK - 1) / TOK, gy);
+  if (x_dtype == 0) {
+    ensure_dynamic_smem(reinterpret_cast<const void*>(router_logits_kernel<float, TOK>), smem);
+    router_logits_kernel<float, TOK><<<grid, kRouterThreads, smem, st>>>(static_cast<const float*>(x), n, d, E, gamma,
+                                                                         gate_w, gate_b, eps, logits, rscale);
+  } else {
+    ensure_dynamic_smem(reinterpret_cast<const void*>(router_logits_kernel<__nv_bfloat16, TOK>), smem);
+    router_logits_kernel<__nv_bfloat16, TOK><<<grid, kRouterThreads, smem, st>>>(
+        static_cast<const __nv_bfloat16*>(x), n, d, E, gamma, gate_w, gate_b, eps, logits, rscale);
+  }
+  return cudaGetLastError();
+}
+
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_w, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  const size_t smem = (static_cast<size_t>(kRouterTok) * (d + E) + kRouterTok) * sizeof(float);
-  const int grid = (n + kRouterTok - 1) / kRouterTok;
-  if (x_dtype == 0) {
-    cudaFuncSetAttribute(router_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
-    router_kernel<float><<<grid, kRouterThreads, smem, st>>>(static_cast<const float*>(x), n, d, E, k, gamma, gate_w,
-                                                             gate_b, eps, logits, topk_idx, topk_w, rscale);
-  } else {
-    cudaFuncSetAttribute(router_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                         static_cast<int>(smem));
-    router_kernel<__nv_bfloat16><<<grid, kRouterThreads, smem, st>>>(static_cast<const __nv_bfloat16*>(x), n, d, E,
-                                                                     k, gamma, gate_w, gate_b, eps, logits, topk_idx,
-                                                                     topk_w, rscale);
-  }
-  return cudaGetLastError();
+  const cudaError_t e = n >= 2048 ? launch_router_tok<8>(x, x_dtype, n, d, E, gamma, gate_w, gate_b, eps, logits,
+                                                         rscale, st)
+                                  : launch_router_tok<2>(x, x_dtype, n, d, E, gamma, gate_w, gate_b, eps, logits,
+                                                         rscale, st);
+  if (e != cudaSuccess) return e;
+  return launch_topk_softmax(logits, n, E, k, topk_idx, topk_w, st);
 }
 
 cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
                            int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
                            int32_t* inv_p, cudaStream_t st) {
   const size_t smem = static_cast<size_t>(32) * E * sizeof(int32_t);
-  cudaFuncSetAttribute(permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
   permute_kernel<<<1, kPermThreads, smem, st>>>(topk_idx, P, E, pad, N, offsets, perm_c, inv_c, poff, counts,
                                                 ntile_prefix, perm_p, inv_p);
   return cudaGetLastError();
@@ -515,13 +523,13 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
 cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
-                                  int sf_rows, cudaStream_t st) {
+                                  int sf_rows, int stacked, cudaStream_t st) {
   const uint64_t items = static_cast<uint64_t>(n) * k * (d / 32);
   if (items == 0) return cudaSuccess;
   const uint64_t blocks = (items + 255) / 256;
   const int grid = static_cast<int>(blocks < 148 * 32 ? blocks : 148 * 32);
   quantize_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
-                                              term_stride, kp, sf, sf_term_stride, kchunks, sf_rows);
+                                              term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked);
   return cudaGetLastError();
 }
 

@@ -21,7 +21,7 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
 cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
-                                  int sf_rows, cudaStream_t st);
+                                  int sf_rows, int stacked, cudaStream_t st);
 cudaError_t launch_combine(const void* x, int x_dtype, const void* y_pair, int pair_dtype, const int32_t* topk_idx,
                            const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
                            cudaStream_t st);

@@ -49,4 +49,14 @@ __host__ __device__ inline uint64_t sf_offset(uint32_t row, uint32_t kb, uint32_
          sf_atom_byte(row % block_rows, kb % 4);
 }
 
+// Stacked activation scales (tiles of 64 pairs, two terms in one 128-row MMA
+// operand): one atom per 64 rows and k chunk holding both terms; pair j of
+// the tile at atom row (j / 16) * 32 + j % 16 + 16 * term, so every 32-lane
+// TMEM sub-partition carries 16 pairs' hi rows followed by their lo rows.
+__host__ __device__ inline uint64_t stacked_sf_offset(uint32_t row, uint32_t term, uint32_t kb, uint32_t k_chunks) {
+  const uint32_t j = row % 64u;
+  const uint32_t r = (j / 16u) * 32u + j % 16u + 16u * term;
+  return (static_cast<uint64_t>(row / 64u) * k_chunks + kb / 4) * kSfAtomBytes + sf_atom_byte(r, kb % 4);
+}
+
 }  // namespace mxmoe

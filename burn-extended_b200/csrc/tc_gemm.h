@@ -18,6 +18,7 @@ struct TcParams {
   int stages;    // smem pipeline depth
   int b_terms;   // E4M3 terms of the activation operand (2 or 3)
   int sf_rows;   // rows per activation scale atom (= pairs per tile, <= 128)
+  int stacked;   // tokens-as-A tiles of 64 pairs with both activation terms in one 128-row operand
   const int* poff;          // [E+1] padded segment starts (multiples of 128)
   const int* counts;        // [E] pairs per expert
   const int* ntile_prefix;  // [E+1] prefix sums of ceil(count / N)
@@ -43,8 +44,8 @@ struct TcParams {
   int* err;                 // device status word (0 = ok)
 };
 
-size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages);
-int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile);
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile);
 // tmap_w: weight codes (box 128 rows weights-as-A, 256 rows tokens-as-A);
 // tmap_x: activation terms (box = pairs per tile rows).
 cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
