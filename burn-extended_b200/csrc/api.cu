@@ -163,6 +163,7 @@ struct Workspace {
   float* y_pair = nullptr; // [rows][d]
   float* act_f32 = nullptr;// [rows][fp] (SIMT path only)
   int32_t* local_idx = nullptr; // [cap_pairs] local expert ids (expert-parallel receive side)
+  int pair_dtype = MXMOE_F32;   // element type the last run_experts wrote y_pair in
   CUtensorMap tmap_x[kNumTileWidths];
   CUtensorMap tmap_act[kNumTileWidths];
 };
@@ -303,6 +304,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   const float bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
   if (L->cfg.flags & MXMOE_FLAG_SIMT) {
     if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
+    w.pair_dtype = MXMOE_F32;
     if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
     CUDA_TRY(launch_simt_w1(x, x_dtype, L->d, k, L->gamma, rscale, L->w1q, L->w1sf, L->b1, L->fp, L->kp1, L->e_count,
                             w.poff, w.counts, w.perm_p, L->cfg.swiglu_alpha, L->cfg.swiglu_limit, w.act_f32, st));
@@ -376,6 +378,8 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.rows_valid = static_cast<int>(L->d);
   p.bias_mult = bias_mult;
   p.y_pair = w.y_pair;
+  p.y_pair_bf16 = reinterpret_cast<__nv_bfloat16*>(w.y_pair);
+  w.pair_dtype = MXMOE_BF16;
   grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
   CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], w.tmap_act[tp.tw], p, grid, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
@@ -635,7 +639,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
   TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
   const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
-  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, MXMOE_F32, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
+  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, w.pair_dtype, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
   if (L->profiling) {
     CUDA_TRY(cudaEventRecord(L->ev[6], st));
     L->profile_valid = true;
@@ -872,7 +876,7 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, tp.pair_tile, nullptr,
                           nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
   TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, rscale, weight, tp, xt, st));
-  CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, MXMOE_F32, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, out_dtype, st));
+  CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, w.pair_dtype, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, out_dtype, st));
   return MXMOE_OK;
 }
 

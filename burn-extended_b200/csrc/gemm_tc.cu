@@ -22,6 +22,7 @@
 // tokens-as-A) and one warp that moves each stage's scale factors from shared
 // memory into TMEM so that the MMA thread only issues MMAs.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
@@ -397,18 +398,17 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         if (p.mode == 2) {
           const float w = __ldg(p.topk_w + pair);
           const int cf0 = wt * 256 + half * 128;  // output feature of v[0]
-          float4* dst = reinterpret_cast<float4*>(p.y_pair + static_cast<uint64_t>(pos) * p.d + cf0);
           const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + cf0);
+          uint2* dst = reinterpret_cast<uint2*>(p.y_pair_bf16 + static_cast<uint64_t>(pos) * p.d + cf0);
 #pragma unroll
           for (int q = 0; q < 32; ++q) {
             if (cf0 + 4 * q < p.rows_valid) {
               const float4 b4 = __ldg(bb + q);
-              float4 o;
-              o.x = fmaf(b4.x, p.bias_mult, v[4 * q + 0]) * w;
-              o.y = fmaf(b4.y, p.bias_mult, v[4 * q + 1]) * w;
-              o.z = fmaf(b4.z, p.bias_mult, v[4 * q + 2]) * w;
-              o.w = fmaf(b4.w, p.bias_mult, v[4 * q + 3]) * w;
-              dst[q] = o;
+              const __nv_bfloat162 lo = __floats2bfloat162_rn(fmaf(b4.x, p.bias_mult, v[4 * q + 0]) * w,
+                                                               fmaf(b4.y, p.bias_mult, v[4 * q + 1]) * w);
+              const __nv_bfloat162 hi = __floats2bfloat162_rn(fmaf(b4.z, p.bias_mult, v[4 * q + 2]) * w,
+                                                               fmaf(b4.w, p.bias_mult, v[4 * q + 3]) * w);
+              dst[q] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
             }
           }
         } else {

@@ -105,11 +105,19 @@ __device__ void topk_softmax_row(const float* lg, int E, int k, int32_t* idx_out
   }
 }
 
+// One thread per token; the block's logit rows are staged in shared memory
+// with coalesced loads first (tpb tokens per block).
 __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int E, int k, int32_t* topk_idx,
                                     float* topk_w) {
-  const int t = blockIdx.x * blockDim.x + threadIdx.x;
-  if (t >= n) return;
-  topk_softmax_row(logits + static_cast<uint64_t>(t) * E, E, k, topk_idx + static_cast<uint64_t>(t) * k,
+  extern __shared__ float lg_s[];  // [tpb][E + 1] (odd pitch: no bank conflicts)
+  const int tpb = blockDim.x;
+  const int t0 = blockIdx.x * tpb;
+  const int nt = min(tpb, n - t0);
+  for (int i = threadIdx.x; i < nt * E; i += tpb) lg_s[(i / E) * (E + 1) + i % E] = logits[static_cast<uint64_t>(t0) * E + i];
+  __syncthreads();
+  if (static_cast<int>(threadIdx.x) >= nt) return;
+  const int t = t0 + threadIdx.x;
+  topk_softmax_row(lg_s + threadIdx.x * (E + 1), E, k, topk_idx + static_cast<uint64_t>(t) * k,
                    topk_w + static_cast<uint64_t>(t) * k);
 }
 
@@ -119,7 +127,7 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int
 // smem so every gate weight read serves TOK tokens.  Summation order is fixed
 // (32 lane chains of fused multiply-adds, then a butterfly), so the logits are
 // reproducible bit for bit by the CPU restatement whatever the grid shape.
-constexpr int kRouterThreads = 256;
+constexpr int kRouterThreads = 512;
 constexpr int kRouterExperts = kRouterThreads / 32;
 
 template <typename XT, int TOK>
@@ -155,11 +163,32 @@ __global__ void __launch_bounds__(kRouterThreads)
     float acc[TOK];
 #pragma unroll
     for (int t = 0; t < TOK; ++t) acc[t] = 0.0f;
-    for (int c = lane; c < d; c += 32) {
+    // four gate loads in flight per lane, the next four issued before the
+    // current multiply-adds; each lane's chain still runs over c = lane,
+    // lane + 32, ... in increasing order (rows t >= nt are unused)
+    int c = lane;
+    float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
+    if (c + 96 < d) {
+      w0 = __ldg(w + c); w1 = __ldg(w + c + 32); w2 = __ldg(w + c + 64); w3 = __ldg(w + c + 96);
+    }
+    for (; c + 96 < d; c += 128) {
+      const float a0 = w0, a1 = w1, a2 = w2, a3 = w3;
+      if (c + 128 + 96 < d) {
+        w0 = __ldg(w + c + 128); w1 = __ldg(w + c + 160); w2 = __ldg(w + c + 192); w3 = __ldg(w + c + 224);
+      }
+#pragma unroll
+      for (int t = 0; t < TOK; ++t) {
+        const float* nr = nrm + t * d + c;
+        acc[t] = __fmaf_rn(nr[0], a0, acc[t]);
+        acc[t] = __fmaf_rn(nr[32], a1, acc[t]);
+        acc[t] = __fmaf_rn(nr[64], a2, acc[t]);
+        acc[t] = __fmaf_rn(nr[96], a3, acc[t]);
+      }
+    }
+    for (; c < d; c += 32) {
       const float wv = __ldg(w + c);
 #pragma unroll
-      for (int t = 0; t < TOK; ++t)
-        if (t < nt) acc[t] = __fmaf_rn(nrm[t * d + c], wv, acc[t]);
+      for (int t = 0; t < TOK; ++t) acc[t] = __fmaf_rn(nrm[t * d + c], wv, acc[t]);
     }
 #pragma unroll
     for (int t = 0; t < TOK; ++t) {
@@ -182,12 +211,15 @@ __global__ void __launch_bounds__(kPermThreads)
     permute_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
                    int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
                    int32_t* perm_p, int32_t* inv_p) {
-  extern __shared__ int32_t cnt[];  // [32 warps][E]
+  extern __shared__ int32_t cnt[];     // [32 warps][E], then canonical and padded starts [E] each
+  int32_t* cstart = cnt + 32 * E;
+  int32_t* pstart = cstart + E;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int seg = (P + 31) / 32;
   const int p_begin = warp * seg, p_end = min(P, p_begin + seg);
   for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
+  // pass 1: per-warp expert histogram of the warp's contiguous segment
   for (int base = p_begin; base < p_end; base += 32) {
     const int p = base + lane;
     const int ex = p < p_end ? topk_idx[p] : -1;
@@ -196,11 +228,23 @@ __global__ void __launch_bounds__(kPermThreads)
     __syncwarp();
   }
   __syncthreads();
+  // per expert: totals, and each warp's base within the expert
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int run = 0;
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt[w * E + e];
+      cnt[w * E + e] = run;
+      run += c;
+    }
+    cstart[e] = run;  // total, turned into the start below
+  }
+  __syncthreads();
   if (threadIdx.x == 0) {
     int run = 0, prun = 0, trun = 0;
     for (int e = 0; e < E; ++e) {
-      int tot = 0;
-      for (int w = 0; w < 32; ++w) tot += cnt[w * E + e];
+      const int tot = cstart[e];
+      cstart[e] = run;
+      pstart[e] = prun;
       if (offsets) offsets[e] = run;
       poff[e] = prun;
       counts[e] = tot;
@@ -214,31 +258,19 @@ __global__ void __launch_bounds__(kPermThreads)
     if (ntile_prefix) ntile_prefix[E] = trun;
   }
   __syncthreads();
-  // per-warp running bases: [0] canonical, stored in place; padded = canonical - offsets + poff
-  if (threadIdx.x < E) {
-    const int e = threadIdx.x;
-    int run = 0;
-    for (int w = 0; w < 32; ++w) {
-      const int c = cnt[w * E + e];
-      cnt[w * E + e] = run;
-      run += c;
-    }
-  }
-  __syncthreads();
+  // pass 2: stable ranks within each expert, (token, slot) order
   for (int base = p_begin; base < p_end; base += 32) {
     const int p = base + lane;
     const int ex = p < p_end ? topk_idx[p] : -1;
     const unsigned grp = __match_any_sync(0xFFFFFFFFu, ex);
     if (ex >= 0) {
       const int rank = cnt[warp * E + ex] + __popc(grp & ((1u << lane) - 1u));
-      const int pos_p = poff[ex] + rank;
+      const int pos_p = pstart[ex] + rank;
       perm_p[pos_p] = p;
       inv_p[p] = pos_p;
       if (perm_c) {
-        int o = 0;
-        for (int e = 0; e < ex; ++e) o += counts[e];
-        perm_c[o + rank] = p;
-        inv_c[p] = o + rank;
+        perm_c[cstart[ex] + rank] = p;
+        inv_c[p] = cstart[ex] + rank;
       }
     }
     __syncwarp();
@@ -251,21 +283,20 @@ __global__ void __launch_bounds__(kPermThreads)
 // Gathers each routed pair's token row into its padded expert-sorted position
 // and writes it as `terms` block-scaled E4M3 terms (two reproduce bf16 input
 // with unit gain exactly; three are used for f32 input or a non-unit gain).
-// One thread per (pair, 32-column block): reads 32 inputs, quantizes them on
-// its own and writes 32 code bytes per term with 16-byte stores.
+// One thread per (token, 32-column block): reads 32 inputs, quantizes them on
+// its own once and writes the codes (16-byte stores) and scale bytes to the
+// positions of all k pairs of the token.
 __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                                       const float* __restrict__ gamma, int gamma_is_one,
                                       const int32_t* __restrict__ inv_p, int terms, uint8_t* codes,
                                       uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride,
                                       int kchunks, int sf_rows, int stacked) {
   const int nb = d / 32;
-  const uint64_t items = static_cast<uint64_t>(n) * k * nb;
+  const uint64_t items = static_cast<uint64_t>(n) * nb;
   for (uint64_t it = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; it < items;
        it += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const int p = static_cast<int>(it / nb);
-    const int b = static_cast<int>(it - static_cast<uint64_t>(p) * nb);
-    const int t = p / k;
-    const int pos = __ldg(inv_p + p);
+    const int t = static_cast<int>(it / nb);
+    const int b = static_cast<int>(it - static_cast<uint64_t>(t) * nb);
     float v[32];
     const uint64_t src = static_cast<uint64_t>(t) * d + b * 32;
     if (x_dtype == 1) {
@@ -295,25 +326,45 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
     uint32_t words[kMaxTerms][8];
     uint8_t sbyte[kMaxTerms];
     quantize_block32(v, terms, words, sbyte);
-    const uint64_t off = static_cast<uint64_t>(pos) * kp + b * 32;
-    const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(b),
-                                  static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
-    for (int q = 0; q < terms; ++q) {
-      uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
-      dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
-      dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
-      if (stacked)
-        sf[stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q), static_cast<uint32_t>(b),
-                             static_cast<uint32_t>(kchunks))] = sbyte[q];
-      else
-        sf[q * sf_term_stride + so] = sbyte[q];
+    for (int s = 0; s < k; ++s) {
+      const int pos = __ldg(inv_p + static_cast<uint64_t>(t) * k + s);
+      const uint64_t off = static_cast<uint64_t>(pos) * kp + b * 32;
+      const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(b),
+                                    static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
+      for (int q = 0; q < terms; ++q) {
+        uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
+        dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
+        dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
+        if (stacked)
+          sf[stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q), static_cast<uint32_t>(b),
+                               static_cast<uint32_t>(kchunks))] = sbyte[q];
+        else
+          sf[q * sf_term_stride + so] = sbyte[q];
+      }
     }
   }
 }
 
 // ------------------------------------------------------------------ combine
 // y[t] = x[t] + sum over the token's experts in increasing expert index of
-// y_pair (src/moe/mod.rs:279, :405, :411).
+// y_pair (src/moe/mod.rs:279, :405, :411).  One block per token, four
+// consecutive columns per thread (d is a multiple of 32).  k == 0 copies x.
+__device__ __forceinline__ float4 load4(const void* p, int dtype, uint64_t i) {
+  if (dtype == 0) return *reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+  const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(p) + i);
+  return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                     __uint_as_float(u.y & 0xFFFF0000u));
+}
+__device__ __forceinline__ void store4(void* p, int dtype, uint64_t i, float4 v) {
+  if (dtype == 0) {
+    *reinterpret_cast<float4*>(static_cast<float*>(p) + i) = v;
+  } else {
+    const __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+    *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p) + i) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b));
+  }
+}
+
 __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const void* __restrict__ y_pair,
                                int pair_dtype, const int32_t* __restrict__ topk_idx,
                                const int32_t* __restrict__ inv_p, int n, int d, int k, int residual, void* y,
@@ -331,13 +382,26 @@ __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const vo
       int tmp = ex[b]; ex[b] = ex[b - 1]; ex[b - 1] = tmp;
       tmp = ord[b]; ord[b] = ord[b - 1]; ord[b - 1] = tmp;
     }
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    float acc = 0.0f;
-    for (int s = 0; s < k; ++s)
-      acc = __fadd_rn(acc, load_any(y_pair, pair_dtype, static_cast<uint64_t>(ord[s]) * d + c));
-    const float v = k == 0 ? load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c)
-                    : residual ? __fadd_rn(load_any(x, x_dtype, static_cast<uint64_t>(t) * d + c), acc) : acc;
-    store_any(y, y_dtype, static_cast<uint64_t>(t) * d + c, v);
+  for (int c = 4 * threadIdx.x; c < d; c += 4 * blockDim.x) {
+    const uint64_t xi = static_cast<uint64_t>(t) * d + c;
+    float4 v;
+    if (k == 0) {
+      v = load4(x, x_dtype, xi);
+    } else {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int s = 0; s < k; ++s) {
+        const float4 q = load4(y_pair, pair_dtype, static_cast<uint64_t>(ord[s]) * d + c);
+        acc.x = __fadd_rn(acc.x, q.x); acc.y = __fadd_rn(acc.y, q.y);
+        acc.z = __fadd_rn(acc.z, q.z); acc.w = __fadd_rn(acc.w, q.w);
+      }
+      if (residual) {
+        const float4 xv = load4(x, x_dtype, xi);
+        acc.x = __fadd_rn(xv.x, acc.x); acc.y = __fadd_rn(xv.y, acc.y);
+        acc.z = __fadd_rn(xv.z, acc.z); acc.w = __fadd_rn(xv.w, acc.w);
+      }
+      v = acc;
+    }
+    store4(y, y_dtype, xi, v);
   }
 }
 
@@ -473,7 +537,11 @@ cudaError_t launch_dequant_rows(const uint8_t* blocks, const uint8_t* scales, ui
 
 cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_t* idx, float* w, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  topk_softmax_kernel<<<(n + 127) / 128, 128, 0, st>>>(logits, n, E, k, idx, w);
+  int tpb = 128;
+  while (tpb > 32 && static_cast<size_t>(tpb) * (E + 1) * sizeof(float) > 48 * 1024) tpb >>= 1;
+  const size_t smem = static_cast<size_t>(tpb) * (E + 1) * sizeof(float);
+  ensure_dynamic_smem(reinterpret_cast<const void*>(topk_softmax_kernel), smem);
+  topk_softmax_kernel<<<(n + tpb - 1) / tpb, tpb, smem, st>>>(logits, n, E, k, idx, w);
   return cudaGetLastError();
 }
 
@@ -513,7 +581,7 @@ cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k
 cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
                            int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
                            int32_t* inv_p, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(32) * E * sizeof(int32_t);
+  const size_t smem = static_cast<size_t>(34) * E * sizeof(int32_t);
   ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
   permute_kernel<<<1, kPermThreads, smem, st>>>(topk_idx, P, E, pad, N, offsets, perm_c, inv_c, poff, counts,
                                                 ntile_prefix, perm_p, inv_p);
@@ -524,8 +592,8 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
                                   int sf_rows, int stacked, cudaStream_t st) {
-  const uint64_t items = static_cast<uint64_t>(n) * k * (d / 32);
-  if (items == 0) return cudaSuccess;
+  const uint64_t items = static_cast<uint64_t>(n) * (d / 32);
+  if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 255) / 256;
   const int grid = static_cast<int>(blocks < 148 * 32 ? blocks : 148 * 32);
   quantize_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,

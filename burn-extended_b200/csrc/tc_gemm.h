@@ -1,6 +1,7 @@
 // tc_gemm.h -- host-side interface of the tcgen05 grouped expert GEMM.
 #pragma once
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <cstddef>
 #include <cstdint>
@@ -39,7 +40,8 @@ struct TcParams {
   uint8_t* act_sf;          // W1 output atoms [2][row_blocks][act_kchunks][512]
   uint64_t act_sf_term_stride;
   int act_kchunks;
-  float* y_pair;            // W2 output [rows][d]
+  float* y_pair;            // W2 output [rows][d] f32 (weights-as-A)
+  __nv_bfloat16* y_pair_bf16;  // W2 output [rows][d] bf16 (tokens-as-A)
   int d;
   int* err;                 // device status word (0 = ok)
 };
