@@ -29,6 +29,11 @@ sys.path[:0] = [os.path.join(ROOT, "burn-extended_b200"), os.path.join(ROOT, "or
 
 import numpy as np  # noqa: E402
 
+# DRAM bytes (read + write) of one launch, from the ncu captures summarised in
+# profiles/tc_moe_gemm_prefill_gptoss20b.txt and profiles/tc_moe_gemm_decode_gptoss20b.txt.
+W1_PREFILL_TRAFFIC = 500.8e6 + 174.2e6
+W1_DECODE_TRAFFIC = 302.0e6 + 5.6e6
+
 METRIC = "MoE layer tokens/s (GPT-OSS-20B-shaped MXFP4 layer, prefill 8192 tokens/GPU)"
 UNIT = "tokens/s"
 
@@ -177,6 +182,11 @@ def measure_decode(args, local, dev, hbm_peak):
             "tokens_per_s": dec.n / (dec_ms / 1e3), "ms_per_step": dec_ms,
             "algorithmic_bytes": dec_bytes, "hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
             "hbm_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak, "stages_ms": dstages,
+            "roofline_w1": {"bound": "hbm", "kernel": "tc_moe_gemm_kernel (W1 + SwiGLU, stacked tiles)",
+                            "achieved": 32 * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9,
+                            "peak": hbm_peak, "unit": "GB/s",
+                            "frac": 32 * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9 / hbm_peak,
+                            "traffic": W1_DECODE_TRAFFIC},
             "l2": "weights of the 32 experts (423 MB) exceed the 126 MB L2; no flush"}
 
 
@@ -272,7 +282,8 @@ def run_ours(args, world, rank, local):
     roofline = {"bound": "tensor", "kernel": "tc_moe_gemm_kernel (W1 + SwiGLU)", "achieved": achieved,
                 "peak": tc_sust, "unit": "TFLOP/s", "frac": achieved / tc_sust,
                 "peak_source": f"{peak_src} bf16 sustained (the 2-term E4M3 x E2M1 MMA pair issues at the bf16-equivalent rate)",
-                "traffic": None,
+                "traffic": W1_PREFILL_TRAFFIC, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                "of one W1 launch (profiles/tc_moe_gemm_prefill_gptoss20b.txt)",
                 "flops_per_launch": w1_flops}
     layer_flops = w1_flops + w2_flops
     extra = {"layer_tflops": layer_flops / (ms_per_step / 1e3) / 1e12,
