@@ -183,9 +183,9 @@ def measure_decode(args, local, dev, hbm_peak):
             "algorithmic_bytes": dec_bytes, "hbm_gbs": dec_bytes / (dec_ms / 1e3) / 1e9,
             "hbm_frac": dec_bytes / (dec_ms / 1e3) / 1e9 / hbm_peak, "stages_ms": dstages,
             "roofline_w1": {"bound": "hbm", "kernel": "tc_moe_gemm_kernel (W1 + SwiGLU, stacked tiles)",
-                            "achieved": 32 * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9,
+                            "achieved": used * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9,
                             "peak": hbm_peak, "unit": "GB/s",
-                            "frac": 32 * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9 / hbm_peak,
+                            "frac": used * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9 / hbm_peak,
                             "traffic": W1_DECODE_TRAFFIC},
             "l2": "weights of the 32 experts (423 MB) exceed the 126 MB L2; no flush"}
 
