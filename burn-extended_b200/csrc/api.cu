@@ -178,7 +178,7 @@ struct mxmoe_layer {
   bool router_ready = false, experts_ready = false;
   bool gamma_is_one = true;
   float* gamma = nullptr;
-  float* gate_w = nullptr;
+  float* gate_w = nullptr;  // packed for the router kernel (pack_router_gate)
   float* gate_b = nullptr;
   uint8_t* w1q = nullptr;
   uint8_t* w1sf = nullptr;
@@ -400,6 +400,10 @@ int device_status(int code) {
 
 }  // namespace
 
+// The vectorized token-row kernels (activation quantization, gather,
+// combine) move 16 bytes per access; the router takes any alignment.
+static bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
 extern "C" {
 
 int mxmoe_abi_version(void) { return MXMOE_ABI_VERSION; }
@@ -487,11 +491,13 @@ int mxmoe_set_router(mxmoe_layer* L, const void* norm_gamma, const void* gate_w,
   to_f32(gate_b, dtype, E, b.data());
   L->gamma_is_one = std::all_of(gm.begin(), gm.end(), [](float v) { return v == 1.0f; });
   if (!L->gamma) TRY(dalloc(&L->gamma, d));
-  if (!L->gate_w) TRY(dalloc(&L->gate_w, E * d));
+  std::vector<float> wp(router_gate_packed_floats(static_cast<int>(E), static_cast<int>(d)));
+  pack_router_gate(w.data(), static_cast<int>(E), static_cast<int>(d), wp.data());
+  if (!L->gate_w) TRY(dalloc(&L->gate_w, wp.size()));
   if (!L->gate_b) TRY(dalloc(&L->gate_b, E));
   cudaStream_t st = as_stream(stream);
   CUDA_TRY(cudaMemcpyAsync(L->gamma, gm.data(), d * 4, cudaMemcpyHostToDevice, st));
-  CUDA_TRY(cudaMemcpyAsync(L->gate_w, w.data(), E * d * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->gate_w, wp.data(), wp.size() * 4, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(L->gate_b, b.data(), E * 4, cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaStreamSynchronize(st));
   L->router_ready = true;
@@ -603,6 +609,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
                   uint32_t n_tokens, void* stream) {
   TRY(check_layer(L));
   if ((!x || !y) && n_tokens > 0) return fail(MXMOE_ERR_INVALID_ARG, "null x or y");
+  if (!aligned16(x) || !aligned16(y)) return fail(MXMOE_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
   if ((x_dtype != MXMOE_F32 && x_dtype != MXMOE_BF16) || (y_dtype != MXMOE_F32 && y_dtype != MXMOE_BF16))
     return fail(MXMOE_ERR_INVALID_ARG, "bad dtype");
   DeviceGuard g(L->cfg.device);
@@ -852,6 +859,7 @@ int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, ui
   if (!x || !perm || !rscale || !topk_idx || !topk_w || !out_x || !out_meta)
     return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   if (d_model % 32 != 0) return fail(MXMOE_ERR_UNSUPPORTED, "d_model must be a multiple of 32");
+  if (!aligned16(x) || !aligned16(out_x)) return fail(MXMOE_ERR_INVALID_ARG, "x and out_x must be 16-byte aligned");
   CUDA_TRY(launch_gather_pairs(x, x_dtype, d_model, k, static_cast<int>(P), perm, rscale, topk_idx, topk_w, out_x,
                                out_meta, as_stream(stream)));
   return MXMOE_OK;
@@ -864,6 +872,7 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   if (!L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "experts not uploaded");
   if (n_pairs == 0) return MXMOE_OK;
   if (!xr || !rscale || !expert || !weight || !out) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(xr) || !aligned16(out)) return fail(MXMOE_ERR_INVALID_ARG, "xr and out must be 16-byte aligned");
   DeviceGuard g(L->cfg.device);
   TRY(ensure_workspace(L, n_pairs, 1));
   Workspace& w = L->ws;
@@ -887,6 +896,8 @@ int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_
   if (!y || (residual && !x) || (k > 0 && (!topk_idx || !inv || !pair_out)))
     return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   if (k > static_cast<uint32_t>(kMaxTopK)) return fail(MXMOE_ERR_UNSUPPORTED, "k=%u", k);
+  if (!aligned16(x) || !aligned16(pair_out) || !aligned16(y))
+    return fail(MXMOE_ERR_INVALID_ARG, "x, pair_out and y must be 16-byte aligned");
   CUDA_TRY(launch_combine(x, x_dtype, pair_out, pair_dtype, topk_idx, inv, n_tokens, d_model, k, residual, y, y_dtype,
                           as_stream(stream)));
   return MXMOE_OK;

@@ -77,123 +77,204 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ blocks, const ui
 }
 
 // ------------------------------------------------------------------ router
-// Top-k (ties to the lower index) + softmax over the k selected values
-// (src/moe/mod.rs:272-276).  One thread per token.
-__device__ void topk_softmax_row(const float* lg, int E, int k, int32_t* idx_out, float* w_out) {
-  int32_t idx[kMaxTopK];
-  float val[kMaxTopK];
-  for (int s = 0; s < k; ++s) {
-    int best = -1;
-    for (int e = 0; e < E; ++e) {
-      bool taken = false;
-      for (int q = 0; q < s; ++q) taken |= (idx[q] == e);
-      if (taken) continue;
-      if (best < 0 || lg[e] > lg[best]) best = e;
-    }
-    idx[s] = best;
-    val[s] = lg[best];
-  }
-  float ex[kMaxTopK];
-  float sum = 0.0f;
-  for (int s = 0; s < k; ++s) {
-    ex[s] = expf(__fsub_rn(val[s], val[0]));
-    sum = __fadd_rn(sum, ex[s]);
-  }
-  for (int s = 0; s < k; ++s) {
-    idx_out[s] = idx[s];
-    w_out[s] = __fdiv_rn(ex[s], sum);
-  }
-}
-
-// One thread per token; the block's logit rows are staged in shared memory
-// with coalesced loads first (tpb tokens per block).
+// Top-k (ties to the lower expert index) + softmax over the k selected values
+// (src/moe/mod.rs:272-276).  One warp per token: lane l holds logits l,
+// l + 32, ...; each of the k rounds is a warp-wide argmax, then lane 0 forms
+// the softmax over the k values.
+constexpr int kTopkMaxPerLane = 32;  // E <= 1024
 __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int E, int k, int32_t* topk_idx,
                                     float* topk_w) {
-  extern __shared__ float lg_s[];  // [tpb][E + 1] (odd pitch: no bank conflicts)
-  const int tpb = blockDim.x;
-  const int t0 = blockIdx.x * tpb;
-  const int nt = min(tpb, n - t0);
-  for (int i = threadIdx.x; i < nt * E; i += tpb) lg_s[(i / E) * (E + 1) + i % E] = logits[static_cast<uint64_t>(t0) * E + i];
-  __syncthreads();
-  if (static_cast<int>(threadIdx.x) >= nt) return;
-  const int t = t0 + threadIdx.x;
-  topk_softmax_row(lg_s + threadIdx.x * (E + 1), E, k, topk_idx + static_cast<uint64_t>(t) * k,
-                   topk_w + static_cast<uint64_t>(t) * k);
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const float* lg = logits + static_cast<uint64_t>(t) * E;
+  float v[kTopkMaxPerLane];
+  uint32_t taken = 0;
+#pragma unroll
+  for (int i = 0; i < kTopkMaxPerLane; ++i) v[i] = lane + 32 * i < E ? lg[lane + 32 * i] : 0.0f;
+  const int per_lane = (E + 31) / 32;
+  float sel_v[kMaxTopK];
+  int sel_i[kMaxTopK];
+  for (int s = 0; s < k; ++s) {
+    float bv = 0.0f;
+    int bi = -1;
+#pragma unroll
+    for (int i = 0; i < kTopkMaxPerLane; ++i) {
+      const int e = lane + 32 * i;
+      if (i < per_lane && e < E && !((taken >> i) & 1u) && (bi < 0 || v[i] > bv)) {
+        bv = v[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xFFFFFFFFu, bv, o);
+      const int oi = __shfl_xor_sync(0xFFFFFFFFu, bi, o);
+      if (oi >= 0 && (bi < 0 || ov > bv || (ov == bv && oi < bi))) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+    sel_v[s] = bv;
+    sel_i[s] = bi;
+  }
+  if (lane == 0) {
+    float ex[kMaxTopK];
+    float sum = 0.0f;
+    for (int s = 0; s < k; ++s) {
+      ex[s] = expf(__fsub_rn(sel_v[s], sel_v[0]));
+      sum = __fadd_rn(sum, ex[s]);
+    }
+    for (int s = 0; s < k; ++s) {
+      topk_idx[static_cast<uint64_t>(t) * k + s] = sel_i[s];
+      topk_w[static_cast<uint64_t>(t) * k + s] = __fdiv_rn(ex[s], sum);
+    }
+  }
 }
 
 // RmsNorm (src/moe/mod.rs:109) + gate Linear (:110): router logits.
-// Block (bx, by) handles tokens [TOK*bx, TOK*bx + TOK) and experts
-// [8*by, 8*by + 8), one expert per warp; its tokens' normalized rows sit in
-// smem so every gate weight read serves TOK tokens.  Summation order is fixed
-// (32 lane chains of fused multiply-adds, then a butterfly), so the logits are
-// reproducible bit for bit by the CPU restatement whatever the grid shape.
-constexpr int kRouterThreads = 512;
-constexpr int kRouterExperts = kRouterThreads / 32;
+// Block (bx, by) handles BT = WT*TT tokens starting at BT*bx and the 32
+// experts of group by.  Column chunks of the raw token rows and of the packed
+// gate weights (pack_router_gate) stream through a kRouterStages-deep cp.async
+// pipeline in shared memory; each thread owns one lane chain (c = lane,
+// lane + 32, ...) of a TT x TE register tile of (token, expert) accumulators
+// and normalizes x on the fly, (x * 1/rms) * gamma, exactly as the CPU
+// restatement rounds it.  Summation order is fixed -- 32 lane chains of fused
+// multiply-adds over c in increasing order, then a butterfly -- so the logits
+// are reproducible bit for bit whatever the tiling.
+constexpr int kRouterThreads = 256;
+constexpr int kRouterWarps = kRouterThreads / 32;
+constexpr int kRouterStages = 4;
 
-template <typename XT, int TOK>
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+template <typename XT, int BT>
+__host__ __device__ constexpr int router_stage_bytes() {
+  return ((BT * kRouterChunk * static_cast<int>(sizeof(XT)) + 15) / 16) * 16 + kRouterGroup * kRouterChunk * 4;
+}
+
+template <typename XT, int TT, int TE>
 __global__ void __launch_bounds__(kRouterThreads)
     router_logits_kernel(const XT* __restrict__ x, int n, int d, int E, const float* __restrict__ gamma,
-                         const float* __restrict__ gate_w, const float* __restrict__ gate_b, float eps,
-                         float* __restrict__ logits_out, float* __restrict__ rscale) {
-  extern __shared__ float sm[];
-  float* nrm = sm;             // [TOK][d]
-  float* rs = sm + TOK * d;    // [TOK]
+                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
+                         float* __restrict__ logits_out, float* __restrict__ rscale, int x_aligned) {
+  constexpr int WE = kRouterGroup / TE;       // warps along experts
+  constexpr int WT = kRouterWarps / WE;       // warps along tokens
+  constexpr int BT = WT * TT;                 // tokens per block
+  constexpr int C = kRouterChunk;
+  constexpr int kXBytes = ((BT * C * static_cast<int>(sizeof(XT)) + 15) / 16) * 16;
+  constexpr int kStage = router_stage_bytes<XT, BT>();
+  constexpr int kXPieces = C * static_cast<int>(sizeof(XT)) / 16;  // 16-byte pieces per token row
+  static_assert(WE * TE == kRouterGroup && WT * WE == kRouterWarps, "router tile");
+  extern __shared__ __align__(16) uint8_t router_smem[];
+  __shared__ float rs[BT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t0 = blockIdx.x * TOK;
-  const int nt = min(TOK, n - t0);
-  for (int t = warp; t < nt; t += kRouterExperts) {
+  const int t0 = blockIdx.x * BT;
+  const int e_base = blockIdx.y * kRouterGroup;
+  const int nt = min(BT, n - t0);
+  const int nch = (d + C - 1) / C;
+  const float* gsrc = gate_packed + static_cast<uint64_t>(blockIdx.y) * nch * kRouterGroup * C;
+
+  auto issue = [&](int ch) {
+    if (ch < nch) {
+      uint8_t* st = router_smem + (ch % kRouterStages) * kStage;
+      const int cb = ch * C;
+      for (int pc = threadIdx.x; pc < BT * kXPieces; pc += kRouterThreads) {
+        const int row = pc / kXPieces, col = (pc % kXPieces) * (16 / static_cast<int>(sizeof(XT)));
+        XT* dst = reinterpret_cast<XT*>(st) + row * C + col;
+        const int valid = row < nt ? min(max(d - (cb + col), 0), 16 / static_cast<int>(sizeof(XT))) : 0;
+        const XT* src = x + static_cast<uint64_t>(t0 + (row < nt ? row : 0)) * d + (valid ? cb + col : 0);
+        if (x_aligned) {
+          cp_async16(dst, src, valid * static_cast<int>(sizeof(XT)));
+        } else {
+          for (int q = 0; q < 16 / static_cast<int>(sizeof(XT)); ++q) dst[q] = q < valid ? src[q] : XT(0.0f);
+        }
+      }
+      const float* wsrc = gsrc + static_cast<uint64_t>(ch) * kRouterGroup * C;
+      float* wdst = reinterpret_cast<float*>(st + kXBytes);
+      for (int pc = threadIdx.x; pc < kRouterGroup * C / 4; pc += kRouterThreads) cp_async16(wdst + pc * 4, wsrc + pc * 4, 16);
+    }
+    cp_async_commit();  // an empty group past the last chunk keeps the wait count uniform
+  };
+#pragma unroll
+  for (int s = 0; s < kRouterStages - 1; ++s) issue(s);
+
+  for (int t = warp; t < nt; t += kRouterWarps) {
     const XT* xr = x + static_cast<uint64_t>(t0 + t) * d;
     float acc = 0.0f;
-    for (int c = lane; c < d; c += 32) {
-      const float v = load_f32(xr, c);
-      acc = __fmaf_rn(v, v, acc);
+    // eight loads in flight per lane, then the chain in increasing c
+    for (int c0 = lane; c0 < d; c0 += 32 * 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = c0 + 32 * u < d ? load_f32(xr, c0 + 32 * u) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (c0 + 32 * u < d) acc = __fmaf_rn(v[u], v[u], acc);
     }
     const float ss = warp_sum_butterfly(acc);
     if (lane == 0) rs[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < nt * d; i += blockDim.x) {
-    const int t = i / d, c = i - t * d;
-    nrm[i] = __fmul_rn(__fmul_rn(load_f32(x, static_cast<uint64_t>(t0 + t) * d + c), rs[t]), gamma[c]);
-  }
   if (blockIdx.y == 0 && threadIdx.x < nt) rscale[t0 + threadIdx.x] = rs[threadIdx.x];
-  __syncthreads();
-  for (int e = blockIdx.y * kRouterExperts + warp; e < E; e += gridDim.y * kRouterExperts) {
-    const float* w = gate_w + static_cast<uint64_t>(e) * d;
-    float acc[TOK];
+
+  const int tw = warp / WE, ew = warp % WE;  // this warp's token group and expert group
+  float rsv[TT];
 #pragma unroll
-    for (int t = 0; t < TOK; ++t) acc[t] = 0.0f;
-    // four gate loads in flight per lane, the next four issued before the
-    // current multiply-adds; each lane's chain still runs over c = lane,
-    // lane + 32, ... in increasing order (rows t >= nt are unused)
-    int c = lane;
-    float w0 = 0.f, w1 = 0.f, w2 = 0.f, w3 = 0.f;
-    if (c + 96 < d) {
-      w0 = __ldg(w + c); w1 = __ldg(w + c + 32); w2 = __ldg(w + c + 64); w3 = __ldg(w + c + 96);
-    }
-    for (; c + 96 < d; c += 128) {
-      const float a0 = w0, a1 = w1, a2 = w2, a3 = w3;
-      if (c + 128 + 96 < d) {
-        w0 = __ldg(w + c + 128); w1 = __ldg(w + c + 160); w2 = __ldg(w + c + 192); w3 = __ldg(w + c + 224);
+  for (int t = 0; t < TT; ++t) rsv[t] = tw * TT + t < nt ? rs[tw * TT + t] : 0.0f;
+  float acc[TT][TE];
+#pragma unroll
+  for (int t = 0; t < TT; ++t)
+#pragma unroll
+    for (int e = 0; e < TE; ++e) acc[t][e] = 0.0f;
+
+  for (int ch = 0; ch < nch; ++ch) {
+    cp_async_wait<kRouterStages - 2>();
+    __syncthreads();  // chunk ch landed for every thread; stage (ch - 1) fully consumed
+    issue(ch + kRouterStages - 1);
+    const uint8_t* st = router_smem + (ch % kRouterStages) * kStage;
+    const XT* xs = reinterpret_cast<const XT*>(st);
+    const float* ws = reinterpret_cast<const float*>(st + kXBytes);
+    const int cb = ch * C;
+    const int jmax = min(C / 32, (d - cb - lane + 31) / 32);  // lane's chain values in this chunk
+#pragma unroll
+    for (int j4 = 0; j4 < C / 128; ++j4) {
+      if (4 * j4 >= jmax) break;
+      float4 wv[TE];
+#pragma unroll
+      for (int e = 0; e < TE; ++e) wv[e] = *reinterpret_cast<const float4*>(ws + (ew * TE + e) * C + j4 * 128 + lane * 4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int j = 4 * j4 + q;
+        if (j >= jmax) break;
+        const int c = lane + 32 * j;
+        const float g = __ldg(gamma + cb + c);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const float xv =
+              __fmul_rn(__fmul_rn(load_f32(xs, static_cast<uint64_t>((tw * TT + t) * C + c)), rsv[t]), g);
+#pragma unroll
+          for (int e = 0; e < TE; ++e) acc[t][e] = __fmaf_rn(xv, reinterpret_cast<const float*>(&wv[e])[q], acc[t][e]);
+        }
       }
-#pragma unroll
-      for (int t = 0; t < TOK; ++t) {
-        const float* nr = nrm + t * d + c;
-        acc[t] = __fmaf_rn(nr[0], a0, acc[t]);
-        acc[t] = __fmaf_rn(nr[32], a1, acc[t]);
-        acc[t] = __fmaf_rn(nr[64], a2, acc[t]);
-        acc[t] = __fmaf_rn(nr[96], a3, acc[t]);
-      }
     }
-    for (; c < d; c += 32) {
-      const float wv = __ldg(w + c);
+  }
+  cp_async_wait<0>();
 #pragma unroll
-      for (int t = 0; t < TOK; ++t) acc[t] = __fmaf_rn(nrm[t * d + c], wv, acc[t]);
-    }
+  for (int t = 0; t < TT; ++t) {
 #pragma unroll
-    for (int t = 0; t < TOK; ++t) {
-      const float s = warp_sum_butterfly(acc[t]);
-      if (lane == 0 && t < nt) logits_out[static_cast<uint64_t>(t0 + t) * E + e] = __fadd_rn(s, gate_b[e]);
+    for (int e = 0; e < TE; ++e) {
+      const float s = warp_sum_butterfly(acc[t][e]);
+      const int tok = tw * TT + t, ex = e_base + ew * TE + e;
+      if (lane == 0 && tok < nt && ex < E) logits_out[static_cast<uint64_t>(t0 + tok) * E + ex] = __fadd_rn(s, gate_b[ex]);
     }
   }
 }
@@ -537,43 +618,41 @@ cudaError_t launch_dequant_rows(const uint8_t* blocks, const uint8_t* scales, ui
 
 cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_t* idx, float* w, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  int tpb = 128;
-  while (tpb > 32 && static_cast<size_t>(tpb) * (E + 1) * sizeof(float) > 48 * 1024) tpb >>= 1;
-  const size_t smem = static_cast<size_t>(tpb) * (E + 1) * sizeof(float);
-  ensure_dynamic_smem(reinterpret_cast<const void*>(topk_softmax_kernel), smem);
-  topk_softmax_kernel<<<(n + tpb - 1) / tpb, tpb, smem, st>>>(logits, n, E, k, idx, w);
+  topk_softmax_kernel<<<(n + 7) / 8, 256, 0, st>>>(logits, n, E, k, idx, w);
   return cudaGetLastError();
 }
 
-template <int TOK>
-static cudaError_t launch_router_tok(const void* x, int x_dtype, int n, int d, int E, const float* gamma,
-                                     const float* gate_w, const float* gate_b, float eps, float* logits,
-                                     float* rscale, cudaStream_t st) {
-  const size_t smem = (static_cast<size_t>(TOK) * d + TOK) * sizeof(float);
-  // few tokens: experts spread over grid.y for parallelism; many tokens: one
-  // block row covers all experts so the normalization is done once
-  const int gy = n >= 2048 ? 1 : (E + kRouterExperts - 1) / kRouterExperts;
-  const dim3 grid((n + TOK - 1) / TOK, gy);
-  if (x_dtype == 0) {
-    ensure_dynamic_smem(reinterpret_cast<const void*>(router_logits_kernel<float, TOK>), smem);
-    router_logits_kernel<float, TOK><<<grid, kRouterThreads, smem, st>>>(static_cast<const float*>(x), n, d, E, gamma,
-                                                                         gate_w, gate_b, eps, logits, rscale);
-  } else {
-    ensure_dynamic_smem(reinterpret_cast<const void*>(router_logits_kernel<__nv_bfloat16, TOK>), smem);
-    router_logits_kernel<__nv_bfloat16, TOK><<<grid, kRouterThreads, smem, st>>>(
-        static_cast<const __nv_bfloat16*>(x), n, d, E, gamma, gate_w, gate_b, eps, logits, rscale);
-  }
+template <typename XT, int TT, int TE>
+static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, const float* gamma, const float* gate_packed,
+                                      const float* gate_b, float eps, float* logits, float* rscale, cudaStream_t st) {
+  constexpr int BT = (kRouterWarps / (kRouterGroup / TE)) * TT;
+  const dim3 grid((n + BT - 1) / BT, (E + kRouterGroup - 1) / kRouterGroup);
+  const size_t smem = static_cast<size_t>(kRouterStages) * router_stage_bytes<XT, BT>();
+  const auto fn = router_logits_kernel<XT, TT, TE>;
+  ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+  const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
+  fn<<<grid, kRouterThreads, smem, st>>>(x, n, d, E, gamma, gate_packed, gate_b, eps, logits, rscale, aligned);
   return cudaGetLastError();
+}
+
+template <typename XT>
+static cudaError_t launch_router_x(const XT* x, int n, int d, int E, const float* gamma, const float* gate_packed,
+                                   const float* gate_b, float eps, float* logits, float* rscale, cudaStream_t st) {
+  // large batches: 16 tokens x 32 experts per block (8x8 per thread);
+  // small ones: one token per block so that enough blocks run
+  return n >= 2048 ? launch_router_tile<XT, 8, 8>(x, n, d, E, gamma, gate_packed, gate_b, eps, logits, rscale, st)
+                   : launch_router_tile<XT, 1, 4>(x, n, d, E, gamma, gate_packed, gate_b, eps, logits, rscale, st);
 }
 
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
-                          const float* gate_w, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
+                          const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  const cudaError_t e = n >= 2048 ? launch_router_tok<8>(x, x_dtype, n, d, E, gamma, gate_w, gate_b, eps, logits,
-                                                         rscale, st)
-                                  : launch_router_tok<2>(x, x_dtype, n, d, E, gamma, gate_w, gate_b, eps, logits,
-                                                         rscale, st);
+  const cudaError_t e =
+      x_dtype == 0 ? launch_router_x(static_cast<const float*>(x), n, d, E, gamma, gate_packed, gate_b, eps, logits,
+                                     rscale, st)
+                   : launch_router_x(static_cast<const __nv_bfloat16*>(x), n, d, E, gamma, gate_packed, gate_b, eps,
+                                     logits, rscale, st);
   if (e != cudaSuccess) return e;
   return launch_topk_softmax(logits, n, E, k, topk_idx, topk_w, st);
 }

@@ -12,8 +12,31 @@ cudaError_t launch_dequant_bytes(const uint8_t* blocks, uint64_t rows, uint64_t 
 cudaError_t launch_dequant_rows(const uint8_t* blocks, const uint8_t* scales, uint64_t rows, uint64_t cols,
                                 uint64_t bpr, uint64_t gpr, int ue8, float* out, cudaStream_t st);
 cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_t* idx, float* w, cudaStream_t st);
+// Router gate weights in the router kernel's chunk order: expert groups of
+// kRouterGroup rows, column chunks of kRouterChunk; inside a chunk, row r's
+// column c = l + 32*j (l = c % 32) sits at r*kRouterChunk + (j/4)*128 + l*4 +
+// j%4, zero past d and past E.  One chunk of a group is one contiguous copy.
+constexpr int kRouterGroup = 32;
+constexpr int kRouterChunk = 128;
+inline size_t router_gate_packed_floats(int E, int d) {
+  const size_t groups = (E + kRouterGroup - 1) / kRouterGroup, chunks = (d + kRouterChunk - 1) / kRouterChunk;
+  return groups * chunks * kRouterGroup * kRouterChunk;
+}
+inline void pack_router_gate(const float* w, int E, int d, float* out) {
+  const int chunks = (d + kRouterChunk - 1) / kRouterChunk;
+  for (size_t i = 0; i < router_gate_packed_floats(E, d); ++i) out[i] = 0.0f;
+  for (int e = 0; e < E; ++e)
+    for (int c = 0; c < d; ++c) {
+      const int g = e / kRouterGroup, r = e % kRouterGroup, ch = c / kRouterChunk, cc = c % kRouterChunk;
+      const int l = cc % 32, j = cc / 32;
+      const size_t base = (static_cast<size_t>(g) * chunks + ch) * kRouterGroup * kRouterChunk;
+      out[base + r * kRouterChunk + (j / 4) * 128 + l * 4 + j % 4] = w[static_cast<size_t>(e) * d + c];
+    }
+}
+
+// gate_packed: pack_router_gate layout.
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
-                          const float* gate_w, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
+                          const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st);
 cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
                            int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,

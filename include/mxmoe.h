@@ -138,7 +138,8 @@ MXMOE_API int mxmoe_reserve(mxmoe_layer* layer, uint32_t max_tokens);
 /* Replaces MoeGatedSwiGLU::forward (src/moe/mod.rs:99-115, forward_resident
  * :122-412): y = x + sum_k w_k * FFN_{e_k}(RmsNorm(x)).  x and y are DEVICE
  * pointers of n_tokens x d_model elements (row-major, batch and sequence
- * flattened).  Stream-ordered; returns before the work finishes. */
+ * flattened), both starting on 16-byte boundaries (MXMOE_ERR_INVALID_ARG
+ * otherwise).  Stream-ordered; returns before the work finishes. */
 MXMOE_API int mxmoe_forward(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype,
                   void* y, mxmoe_dtype y_dtype, uint32_t n_tokens, void* stream);
 
@@ -235,7 +236,8 @@ MXMOE_API int mxmoe_set_expert_shard(mxmoe_layer* layer, uint32_t expert_begin,
 /* Router + canonical permutation on device x [n][d] (source side):
  * rscale [n] (1 / rms), topk_idx [n][k], topk_w [n][k], offsets [E+1],
  * perm [n*k], inv [n*k] (global expert ids; pairs sorted by expert are sorted
- * by destination rank).  Device pointers owned by the caller. */
+ * by destination rank).  Device pointers owned by the caller; x may start
+ * at any element boundary. */
 MXMOE_API int mxmoe_route(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype,
                 uint32_t n_tokens, float* rscale, int32_t* topk_idx,
                 float* topk_w, int32_t* offsets, int32_t* perm, int32_t* inv,
@@ -254,7 +256,8 @@ MXMOE_API int mxmoe_gather_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_
 /* Receive side: expert FFN of this layer's shard for dispatched pairs.
  * xr [n_pairs][d] raw token rows (x's dtype), rscale [n_pairs], expert
  * [n_pairs] GLOBAL ids inside the shard, weight [n_pairs];
- * out [n_pairs][d] (out_dtype) = weight * (W2 act + b2).  Device pointers. */
+ * out [n_pairs][d] (out_dtype) = weight * (W2 act + b2).  Device pointers;
+ * xr and out start on 16-byte boundaries. */
 MXMOE_API int mxmoe_forward_local(mxmoe_layer* layer, const void* xr, mxmoe_dtype xr_dtype,
                         const float* rscale, const int32_t* expert,
                         const float* weight, uint32_t n_pairs, void* out,
@@ -262,7 +265,8 @@ MXMOE_API int mxmoe_forward_local(mxmoe_layer* layer, const void* xr, mxmoe_dtyp
 
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
- * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers. */
+ * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers, each
+ * starting on a 16-byte boundary. */
 MXMOE_API int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
                   uint32_t d_model, uint32_t k, const int32_t* topk_idx,
                   const int32_t* inv, const void* pair_out,

@@ -99,6 +99,58 @@ def test_router_bit_exact(torch, name, n):
     layer.close()
 
 
+def _check_routing(layer, inp, x, n):
+    layer.forward(x)
+    rr = layer.routing_results(n)
+    r = oracle.route(oracle.cfg(inp.d, inp.f, inp.E, inp.k), inp.x, inp.gamma, inp.gate_w, inp.gate_b)
+    assert np.array_equal(rr["logits"].cpu().numpy().reshape(n, inp.E).view(np.uint32), r["logits"].view(np.uint32))
+    assert np.array_equal(rr["topk_idx"].cpu().numpy().reshape(n, inp.k), r["topk_idx"])
+    import torch as t
+    rs = t.empty(n, dtype=t.float32, device=x.device)
+    ti = t.empty(n, inp.k, dtype=t.int32, device=x.device)
+    tw = t.empty(n, inp.k, dtype=t.float32, device=x.device)
+    layer.route(x, rs, ti, tw)
+    assert np.array_equal(rs.cpu().numpy().view(np.uint32), r["rscale"].view(np.uint32))
+    assert np.array_equal(ti.cpu().numpy(), r["topk_idx"])
+
+
+# ragged column chunks (d % 128 != 0), token counts off the block tile, an
+# expert count off the 32-expert groups, E = 1, f32 and bf16 activations, and
+# both router tilings (n >= 2048 and below)
+@pytest.mark.parametrize("d,E,k,n,bf16", [(2880, 32, 4, 2500, True), (96, 40, 2, 2100, False),
+                                          (96, 1, 1, 37, True), (352, 72, 8, 300, False)])
+def test_router_bit_exact_shapes(torch, d, E, k, n, bf16):
+    inp = synth.make_inputs(d, 128, E, k, n, bf16, seed=d + E + n, zipf_router_bias=0.5)
+    layer = make_layer(inp)
+    _check_routing(layer, inp, to_device_x(inp), n)
+    layer.close()
+
+
+def test_router_bit_exact_misaligned_x(torch):
+    # x starting 2 bytes past a 16-byte boundary: mxmoe_route takes the
+    # router's plain-load path instead of cp.async; the full forward, whose
+    # row kernels move 16-byte vectors, refuses such x with INVALID_ARG
+    n = 70
+    inp = synth.make_inputs(256, 128, 8, 2, n, True, seed=5)
+    buf = torch.zeros(n * 256 + 8, dtype=torch.bfloat16, device="cuda")
+    x = buf[1:1 + n * 256].view(n, 256)
+    x.copy_(torch.from_numpy(inp.x).to(torch.bfloat16))
+    assert x.data_ptr() % 16 != 0
+    layer = make_layer(inp)
+    r = oracle.route(oracle.cfg(inp.d, inp.f, inp.E, inp.k), inp.x, inp.gamma, inp.gate_w, inp.gate_b)
+    rs = torch.empty(n, dtype=torch.float32, device="cuda")
+    ti = torch.empty(n, inp.k, dtype=torch.int32, device="cuda")
+    tw = torch.empty(n, inp.k, dtype=torch.float32, device="cuda")
+    layer.route(x, rs, ti, tw)
+    assert np.array_equal(rs.cpu().numpy().view(np.uint32), r["rscale"].view(np.uint32))
+    assert np.array_equal(ti.cpu().numpy(), r["topk_idx"])
+    with pytest.raises(mxmoe.MxMoeError) as ei:
+        layer.forward(x)
+    assert ei.value.code == 1  # MXMOE_ERR_INVALID_ARG
+    torch.cuda.synchronize()
+    layer.close()
+
+
 # ---------------------------------------------------------------- layer
 @pytest.mark.parametrize("simt", [False, True])
 def test_tiny_layer_against_golden(torch, simt):
