@@ -36,6 +36,9 @@ W1_DECODE_TRAFFIC = 302.0e6 + 5.6e6
 
 METRIC = "MoE layer tokens/s (GPT-OSS-20B-shaped MXFP4 layer, prefill 8192 tokens/GPU)"
 UNIT = "tokens/s"
+# kernels one mxmoe_forward launches: rms, router logits, top-k, permute,
+# activation quantization, W1, W2, combine
+LAUNCHES_PER_FORWARD = 8
 
 
 def load_peaks():
@@ -325,7 +328,7 @@ def run_ours(args, world, rank, local):
                    "top_k": k, "parallelism": "ep1",
                    "l2": "inputs+weights > 126 MB L2 (expert weights alone 423 MB); no flush"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks, "stages_ms": stages,
-        "gpu_launches": 6 * args.steps, "extra": extra,
+        "gpu_launches": LAUNCHES_PER_FORWARD * args.steps, "extra": extra,
     }
     print(json.dumps(line), flush=True)
     layer.close()

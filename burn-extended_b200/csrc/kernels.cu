@@ -133,19 +133,10 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int
   }
 }
 
-// RmsNorm (src/moe/mod.rs:109) + gate Linear (:110): router logits.
-// Block (bx, by) handles BT = WT*TT tokens starting at BT*bx and the 32
-// experts of group by.  Column chunks of the raw token rows and of the packed
-// gate weights (pack_router_gate) stream through a kRouterStages-deep cp.async
-// pipeline in shared memory; each thread owns one lane chain (c = lane,
-// lane + 32, ...) of a TT x TE register tile of (token, expert) accumulators
-// and normalizes x on the fly, (x * 1/rms) * gamma, exactly as the CPU
-// restatement rounds it.  Summation order is fixed -- 32 lane chains of fused
-// multiply-adds over c in increasing order, then a butterfly -- so the logits
-// are reproducible bit for bit whatever the tiling.
+// RmsNorm (src/moe/mod.rs:109) + gate Linear (:110): router logits, as two
+// kernels -- rms_kernel (1 / rms per token) and router_logits_kernel.
 constexpr int kRouterThreads = 256;
 constexpr int kRouterWarps = kRouterThreads / 32;
-constexpr int kRouterStages = 4;
 
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
   const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
@@ -157,26 +148,66 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-template <typename XT, int BT>
-__host__ __device__ constexpr int router_stage_bytes() {
-  return ((BT * kRouterChunk * static_cast<int>(sizeof(XT)) + 15) / 16) * 16 + kRouterGroup * kRouterChunk * 4;
+// 1 / rms per token (src/moe/mod.rs:109): one warp per token, 32 loads in
+// flight per lane, then the lane chain of fused multiply-adds over
+// c = lane, lane + 32, ... in increasing order and a butterfly.
+template <typename XT>
+__global__ void __launch_bounds__(256) rms_kernel(const XT* __restrict__ x, int n, int d, float eps,
+                                                  float* __restrict__ rscale) {
+  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const XT* xr = x + static_cast<uint64_t>(t) * d;
+  float acc = 0.0f;
+  for (int c0 = lane; c0 < d; c0 += 32 * 32) {
+    float v[32];
+#pragma unroll
+    for (int u = 0; u < 32; ++u) v[u] = c0 + 32 * u < d ? load_f32(xr, c0 + 32 * u) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < 32; ++u)
+      if (c0 + 32 * u < d) acc = __fmaf_rn(v[u], v[u], acc);
+  }
+  const float ss = warp_sum_butterfly(acc);
+  if (lane == 0) rscale[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
 }
 
+template <typename XT, int BT>
+__host__ __device__ constexpr int router_x_bytes() {
+  return ((BT * kRouterChunk * static_cast<int>(sizeof(XT)) + 15) / 16) * 16;
+}
+template <typename XT, int BT>
+__host__ __device__ constexpr int router_stage_bytes() {
+  return router_x_bytes<XT, BT>() + kRouterChunk * 4 + kRouterGroup * kRouterChunk * 4;
+}
+template <int BT>
+__host__ __device__ constexpr int router_stages() {
+  return BT <= 2 ? 8 : 4;  // small token tiles: deeper pipeline, one block per SM
+}
+
+// Gate logits for a block of BT = WT*TT tokens and the 32 experts of group
+// blockIdx.y.  Per column chunk of kRouterChunk, a stage holds the raw token
+// rows, the gamma slice and the packed gate weights (pack_router_gate); the
+// stages stream through a cp.async pipeline.  Each thread owns one lane chain
+// (c = lane, lane + 32, ...) of a TT x TE register tile of (token, expert)
+// accumulators and normalizes x on the fly, (x * 1/rms) * gamma, exactly as
+// the CPU restatement rounds it.  Summation order is fixed -- 32 lane chains
+// of fused multiply-adds over c in increasing order, then a butterfly -- so
+// the logits are reproducible bit for bit whatever the tiling.
 template <typename XT, int TT, int TE>
 __global__ void __launch_bounds__(kRouterThreads)
     router_logits_kernel(const XT* __restrict__ x, int n, int d, int E, const float* __restrict__ gamma,
-                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
-                         float* __restrict__ logits_out, float* __restrict__ rscale, int x_aligned) {
+                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b,
+                         const float* __restrict__ rscale, float* __restrict__ logits_out, int x_aligned) {
   constexpr int WE = kRouterGroup / TE;       // warps along experts
   constexpr int WT = kRouterWarps / WE;       // warps along tokens
   constexpr int BT = WT * TT;                 // tokens per block
   constexpr int C = kRouterChunk;
-  constexpr int kXBytes = ((BT * C * static_cast<int>(sizeof(XT)) + 15) / 16) * 16;
+  constexpr int kXBytes = router_x_bytes<XT, BT>();
   constexpr int kStage = router_stage_bytes<XT, BT>();
+  constexpr int kStages = router_stages<BT>();
   constexpr int kXPieces = C * static_cast<int>(sizeof(XT)) / 16;  // 16-byte pieces per token row
   static_assert(WE * TE == kRouterGroup && WT * WE == kRouterWarps, "router tile");
   extern __shared__ __align__(16) uint8_t router_smem[];
-  __shared__ float rs[BT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * BT;
   const int e_base = blockIdx.y * kRouterGroup;
@@ -186,7 +217,7 @@ __global__ void __launch_bounds__(kRouterThreads)
 
   auto issue = [&](int ch) {
     if (ch < nch) {
-      uint8_t* st = router_smem + (ch % kRouterStages) * kStage;
+      uint8_t* st = router_smem + (ch % kStages) * kStage;
       const int cb = ch * C;
       for (int pc = threadIdx.x; pc < BT * kXPieces; pc += kRouterThreads) {
         const int row = pc / kXPieces, col = (pc % kXPieces) * (16 / static_cast<int>(sizeof(XT)));
@@ -199,37 +230,24 @@ __global__ void __launch_bounds__(kRouterThreads)
           for (int q = 0; q < 16 / static_cast<int>(sizeof(XT)); ++q) dst[q] = q < valid ? src[q] : XT(0.0f);
         }
       }
+      float* gdst = reinterpret_cast<float*>(st + kXBytes);
+      for (int pc = threadIdx.x; pc < C / 4; pc += kRouterThreads) {
+        const int valid = min(max(d - (cb + 4 * pc), 0), 4);
+        cp_async16(gdst + 4 * pc, gamma + (valid ? cb + 4 * pc : 0), valid * 4);
+      }
       const float* wsrc = gsrc + static_cast<uint64_t>(ch) * kRouterGroup * C;
-      float* wdst = reinterpret_cast<float*>(st + kXBytes);
+      float* wdst = gdst + C;
       for (int pc = threadIdx.x; pc < kRouterGroup * C / 4; pc += kRouterThreads) cp_async16(wdst + pc * 4, wsrc + pc * 4, 16);
     }
     cp_async_commit();  // an empty group past the last chunk keeps the wait count uniform
   };
 #pragma unroll
-  for (int s = 0; s < kRouterStages - 1; ++s) issue(s);
-
-  for (int t = warp; t < nt; t += kRouterWarps) {
-    const XT* xr = x + static_cast<uint64_t>(t0 + t) * d;
-    float acc = 0.0f;
-    // eight loads in flight per lane, then the chain in increasing c
-    for (int c0 = lane; c0 < d; c0 += 32 * 8) {
-      float v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = c0 + 32 * u < d ? load_f32(xr, c0 + 32 * u) : 0.0f;
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (c0 + 32 * u < d) acc = __fmaf_rn(v[u], v[u], acc);
-    }
-    const float ss = warp_sum_butterfly(acc);
-    if (lane == 0) rs[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
-  }
-  __syncthreads();
-  if (blockIdx.y == 0 && threadIdx.x < nt) rscale[t0 + threadIdx.x] = rs[threadIdx.x];
+  for (int s = 0; s < kStages - 1; ++s) issue(s);
 
   const int tw = warp / WE, ew = warp % WE;  // this warp's token group and expert group
   float rsv[TT];
 #pragma unroll
-  for (int t = 0; t < TT; ++t) rsv[t] = tw * TT + t < nt ? rs[tw * TT + t] : 0.0f;
+  for (int t = 0; t < TT; ++t) rsv[t] = tw * TT + t < nt ? __ldg(rscale + t0 + tw * TT + t) : 0.0f;
   float acc[TT][TE];
 #pragma unroll
   for (int t = 0; t < TT; ++t)
@@ -237,12 +255,13 @@ __global__ void __launch_bounds__(kRouterThreads)
     for (int e = 0; e < TE; ++e) acc[t][e] = 0.0f;
 
   for (int ch = 0; ch < nch; ++ch) {
-    cp_async_wait<kRouterStages - 2>();
+    cp_async_wait<kStages - 2>();
     __syncthreads();  // chunk ch landed for every thread; stage (ch - 1) fully consumed
-    issue(ch + kRouterStages - 1);
-    const uint8_t* st = router_smem + (ch % kRouterStages) * kStage;
+    issue(ch + kStages - 1);
+    const uint8_t* st = router_smem + (ch % kStages) * kStage;
     const XT* xs = reinterpret_cast<const XT*>(st);
-    const float* ws = reinterpret_cast<const float*>(st + kXBytes);
+    const float* gs = reinterpret_cast<const float*>(st + kXBytes);
+    const float* ws = gs + C;
     const int cb = ch * C;
     const int jmax = min(C / 32, (d - cb - lane + 31) / 32);  // lane's chain values in this chunk
 #pragma unroll
@@ -256,7 +275,7 @@ __global__ void __launch_bounds__(kRouterThreads)
         const int j = 4 * j4 + q;
         if (j >= jmax) break;
         const int c = lane + 32 * j;
-        const float g = __ldg(gamma + cb + c);
+        const float g = gs[c];
 #pragma unroll
         for (int t = 0; t < TT; ++t) {
           const float xv =
@@ -624,24 +643,25 @@ cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_
 
 template <typename XT, int TT, int TE>
 static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, const float* gamma, const float* gate_packed,
-                                      const float* gate_b, float eps, float* logits, float* rscale, cudaStream_t st) {
+                                      const float* gate_b, const float* rscale, float* logits, cudaStream_t st) {
   constexpr int BT = (kRouterWarps / (kRouterGroup / TE)) * TT;
   const dim3 grid((n + BT - 1) / BT, (E + kRouterGroup - 1) / kRouterGroup);
-  const size_t smem = static_cast<size_t>(kRouterStages) * router_stage_bytes<XT, BT>();
+  const size_t smem = static_cast<size_t>(router_stages<BT>()) * router_stage_bytes<XT, BT>();
   const auto fn = router_logits_kernel<XT, TT, TE>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
   const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
-  fn<<<grid, kRouterThreads, smem, st>>>(x, n, d, E, gamma, gate_packed, gate_b, eps, logits, rscale, aligned);
+  fn<<<grid, kRouterThreads, smem, st>>>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, aligned);
   return cudaGetLastError();
 }
 
 template <typename XT>
 static cudaError_t launch_router_x(const XT* x, int n, int d, int E, const float* gamma, const float* gate_packed,
                                    const float* gate_b, float eps, float* logits, float* rscale, cudaStream_t st) {
+  rms_kernel<XT><<<(n + 7) / 8, 256, 0, st>>>(x, n, d, eps, rscale);
   // large batches: 16 tokens x 32 experts per block (8x8 per thread);
   // small ones: one token per block so that enough blocks run
-  return n >= 2048 ? launch_router_tile<XT, 8, 8>(x, n, d, E, gamma, gate_packed, gate_b, eps, logits, rscale, st)
-                   : launch_router_tile<XT, 1, 4>(x, n, d, E, gamma, gate_packed, gate_b, eps, logits, rscale, st);
+  return n >= 2048 ? launch_router_tile<XT, 8, 8>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, st)
+                   : launch_router_tile<XT, 1, 4>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, st);
 }
 
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,

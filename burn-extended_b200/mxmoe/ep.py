@@ -122,8 +122,9 @@ class CudaExpertBackend:
 class ExpertParallelMoe:
     """One rank of the expert-parallel layer (see the module docstring)."""
 
-    # router, permute, gather, localize, permute, quantize, W1, W2, un-permute, combine
-    launches_per_step = 10
+    # rms, router logits, top-k, permute, gather, localize, permute, quantize,
+    # W1, W2, un-permute, combine
+    launches_per_step = 12
 
     def __init__(self, backend, num_experts: int, world: int, rank: int, group=None):
         import torch.distributed as dist
