@@ -78,30 +78,22 @@ __global__ void dequant_rows_kernel(const uint8_t* __restrict__ blocks, const ui
 
 // ------------------------------------------------------------------ router
 // Top-k (ties to the lower expert index) + softmax over the k selected values
-// (src/moe/mod.rs:272-276).  One warp per token: lane l holds logits l,
-// l + 32, ...; each of the k rounds is a warp-wide argmax, then lane 0 forms
-// the softmax over the k values.
-constexpr int kTopkMaxPerLane = 32;  // E <= 1024
-__global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int E, int k, int32_t* topk_idx,
-                                    float* topk_w) {
-  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= n) return;
-  const float* lg = logits + static_cast<uint64_t>(t) * E;
-  float v[kTopkMaxPerLane];
+// (src/moe/mod.rs:272-276) for one token, by one warp: lane l holds logits
+// l, l + 32, ... (PL per lane, E <= 32*PL); each of the k rounds is a
+// warp-wide argmax, then lane 0 forms the softmax over the k values.
+template <int PL>
+__device__ __forceinline__ void warp_topk_softmax(const float (&v)[PL], int E, int k, int lane, int32_t* idx_out,
+                                                  float* w_out) {
   uint32_t taken = 0;
-#pragma unroll
-  for (int i = 0; i < kTopkMaxPerLane; ++i) v[i] = lane + 32 * i < E ? lg[lane + 32 * i] : 0.0f;
-  const int per_lane = (E + 31) / 32;
-  float sel_v[kMaxTopK];
-  int sel_i[kMaxTopK];
+  float my_v = 0.0f;  // lane s < k keeps the s-th selection
+  int my_i = 0;
   for (int s = 0; s < k; ++s) {
     float bv = 0.0f;
     int bi = -1;
 #pragma unroll
-    for (int i = 0; i < kTopkMaxPerLane; ++i) {
+    for (int i = 0; i < PL; ++i) {
       const int e = lane + 32 * i;
-      if (i < per_lane && e < E && !((taken >> i) & 1u) && (bi < 0 || v[i] > bv)) {
+      if (e < E && !((taken >> i) & 1u) && (bi < 0 || v[i] > bv)) {
         bv = v[i];
         bi = e;
       }
@@ -116,21 +108,34 @@ __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int
       }
     }
     if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
-    sel_v[s] = bv;
-    sel_i[s] = bi;
-  }
-  if (lane == 0) {
-    float ex[kMaxTopK];
-    float sum = 0.0f;
-    for (int s = 0; s < k; ++s) {
-      ex[s] = expf(__fsub_rn(sel_v[s], sel_v[0]));
-      sum = __fadd_rn(sum, ex[s]);
-    }
-    for (int s = 0; s < k; ++s) {
-      topk_idx[static_cast<uint64_t>(t) * k + s] = sel_i[s];
-      topk_w[static_cast<uint64_t>(t) * k + s] = __fdiv_rn(ex[s], sum);
+    if (lane == s) {
+      my_v = bv;
+      my_i = bi;
     }
   }
+  // softmax: exp(v_s - v_0), summed in increasing s
+  const float v0 = __shfl_sync(0xFFFFFFFFu, my_v, 0);
+  const float ex = lane < k ? expf(__fsub_rn(my_v, v0)) : 0.0f;
+  float sum = 0.0f;
+  for (int s = 0; s < k; ++s) sum = __fadd_rn(sum, __shfl_sync(0xFFFFFFFFu, ex, s));
+  if (lane < k) {
+    idx_out[lane] = my_i;
+    w_out[lane] = __fdiv_rn(ex, sum);
+  }
+}
+
+// One warp per token over a logits matrix [n][E].
+template <int PL>
+__global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int E, int k, int32_t* topk_idx,
+                                    float* topk_w) {
+  const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  const float* lg = logits + static_cast<uint64_t>(t) * E;
+  float v[PL];
+#pragma unroll
+  for (int i = 0; i < PL; ++i) v[i] = lane + 32 * i < E ? lg[lane + 32 * i] : 0.0f;
+  warp_topk_softmax<PL>(v, E, k, lane, topk_idx + static_cast<uint64_t>(t) * k, topk_w + static_cast<uint64_t>(t) * k);
 }
 
 // RmsNorm (src/moe/mod.rs:109) + gate Linear (:110): router logits, as two
@@ -148,24 +153,60 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
 
-// 1 / rms per token (src/moe/mod.rs:109): one warp per token, 32 loads in
-// flight per lane, then the lane chain of fused multiply-adds over
-// c = lane, lane + 32, ... in increasing order and a butterfly.
+// 1 / rms per token (src/moe/mod.rs:109), one warp per token: the lane chain
+// of fused multiply-adds over c = lane, lane + 32, ... in increasing order,
+// then a butterfly.  With 16-byte aligned rows the warp moves its row in
+// segments of 512 bytes per load round (four 16-byte vectors per lane, the
+// next segment's loads in flight while the current one is summed) through a
+// shared-memory buffer from which each lane reads its own chain values.
+constexpr int kRmsVec = 4;  // 16-byte vectors per lane per segment
 template <typename XT>
 __global__ void __launch_bounds__(256) rms_kernel(const XT* __restrict__ x, int n, int d, float eps,
-                                                  float* __restrict__ rscale) {
-  const int t = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+                                                  float* __restrict__ rscale, int aligned) {
+  constexpr int kEpv = 16 / static_cast<int>(sizeof(XT));  // elements per vector
+  constexpr int kSeg = 32 * kRmsVec * kEpv;                  // elements per segment
+  __shared__ __align__(16) XT buf[8][kSeg];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x * 8 + warp;
   if (t >= n) return;
   const XT* xr = x + static_cast<uint64_t>(t) * d;
   float acc = 0.0f;
-  for (int c0 = lane; c0 < d; c0 += 32 * 32) {
-    float v[32];
+  if (aligned) {
+    const uint4* xv = reinterpret_cast<const uint4*>(xr);
+    const int nvec = d / kEpv;
+    uint4 cur[kRmsVec];
 #pragma unroll
-    for (int u = 0; u < 32; ++u) v[u] = c0 + 32 * u < d ? load_f32(xr, c0 + 32 * u) : 0.0f;
+    for (int v = 0; v < kRmsVec; ++v) {
+      const int vi = lane + 32 * v;
+      cur[v] = vi < nvec ? __ldg(xv + vi) : make_uint4(0, 0, 0, 0);
+    }
+    for (int s0 = 0; s0 < d; s0 += kSeg) {
+      __syncwarp();
 #pragma unroll
-    for (int u = 0; u < 32; ++u)
-      if (c0 + 32 * u < d) acc = __fmaf_rn(v[u], v[u], acc);
+      for (int v = 0; v < kRmsVec; ++v) reinterpret_cast<uint4*>(buf[warp])[lane + 32 * v] = cur[v];
+      __syncwarp();
+      const int nv0 = (s0 + kSeg) / kEpv;
+#pragma unroll
+      for (int v = 0; v < kRmsVec; ++v) {
+        const int vi = nv0 + lane + 32 * v;
+        cur[v] = vi < nvec ? __ldg(xv + vi) : make_uint4(0, 0, 0, 0);
+      }
+      const int len = min(kSeg, d - s0);
+#pragma unroll 8
+      for (int c = lane; c < len; c += 32) {
+        const float f = load_f32(buf[warp], c);
+        acc = __fmaf_rn(f, f, acc);
+      }
+    }
+  } else {
+    for (int c0 = lane; c0 < d; c0 += 32 * 32) {
+      float v[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) v[u] = c0 + 32 * u < d ? load_f32(xr, c0 + 32 * u) : 0.0f;
+#pragma unroll
+      for (int u = 0; u < 32; ++u)
+        if (c0 + 32 * u < d) acc = __fmaf_rn(v[u], v[u], acc);
+    }
   }
   const float ss = warp_sum_butterfly(acc);
   if (lane == 0) rscale[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
@@ -187,17 +228,21 @@ __host__ __device__ constexpr int router_stages() {
 // Gate logits for a block of BT = WT*TT tokens and the 32 experts of group
 // blockIdx.y.  Per column chunk of kRouterChunk, a stage holds the raw token
 // rows, the gamma slice and the packed gate weights (pack_router_gate); the
-// stages stream through a cp.async pipeline.  Each thread owns one lane chain
-// (c = lane, lane + 32, ...) of a TT x TE register tile of (token, expert)
-// accumulators and normalizes x on the fly, (x * 1/rms) * gamma, exactly as
-// the CPU restatement rounds it.  Summation order is fixed -- 32 lane chains
-// of fused multiply-adds over c in increasing order, then a butterfly -- so
-// the logits are reproducible bit for bit whatever the tiling.
+// stages stream through a cp.async pipeline.  One chunk ahead of the FMAs,
+// the block normalizes the chunk's token values, (x * 1/rms) * gamma rounded
+// exactly as the CPU restatement rounds them, into a float buffer laid out
+// like the packed gate (column c = l + 32*j at (j/4)*128 + l*4 + j%4).  Each
+// thread owns one lane chain (c = lane, lane + 32, ...) of a TT x TE register
+// tile of (token, expert) accumulators and reads four chain values of a token
+// or an expert as one float4.  Summation order is fixed -- 32 lane chains of
+// fused multiply-adds over c in increasing order, then a butterfly -- so the
+// logits are reproducible bit for bit whatever the tiling.
 template <typename XT, int TT, int TE>
 __global__ void __launch_bounds__(kRouterThreads)
     router_logits_kernel(const XT* __restrict__ x, int n, int d, int E, const float* __restrict__ gamma,
                          const float* __restrict__ gate_packed, const float* __restrict__ gate_b,
-                         const float* __restrict__ rscale, float* __restrict__ logits_out, int x_aligned) {
+                         const float* __restrict__ rscale, float* __restrict__ logits_out, int x_aligned,
+                         int k, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w) {
   constexpr int WE = kRouterGroup / TE;       // warps along experts
   constexpr int WT = kRouterWarps / WE;       // warps along tokens
   constexpr int BT = WT * TT;                 // tokens per block
@@ -207,7 +252,10 @@ __global__ void __launch_bounds__(kRouterThreads)
   constexpr int kStages = router_stages<BT>();
   constexpr int kXPieces = C * static_cast<int>(sizeof(XT)) / 16;  // 16-byte pieces per token row
   static_assert(WE * TE == kRouterGroup && WT * WE == kRouterWarps, "router tile");
+  static_assert(kStages >= 3, "normalization runs one chunk ahead");
   extern __shared__ __align__(16) uint8_t router_smem[];
+  float* nbuf = reinterpret_cast<float*>(router_smem + kStages * kStage);  // [2][BT][C] normalized chunks
+  __shared__ float rs_s[BT];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t0 = blockIdx.x * BT;
   const int e_base = blockIdx.y * kRouterGroup;
@@ -241,13 +289,34 @@ __global__ void __launch_bounds__(kRouterThreads)
     }
     cp_async_commit();  // an empty group past the last chunk keeps the wait count uniform
   };
+  // chunk ch's raw rows and gamma (landed) -> nbuf[ch % 2]
+  auto normalize = [&](int ch) {
+    if (ch >= nch) return;
+    const uint8_t* st = router_smem + (ch % kStages) * kStage;
+    const XT* xs = reinterpret_cast<const XT*>(st);
+    const float* gs = reinterpret_cast<const float*>(st + kXBytes);
+    float* nb = nbuf + (ch & 1) * BT * C;
+    for (int pc = threadIdx.x; pc < BT * (C / 4); pc += kRouterThreads) {
+      const int row = pc / (C / 4), p = pc % (C / 4), j4 = p >> 5, l = p & 31;
+      const float r = rs_s[row];
+      float4 v;
+      float* vp = reinterpret_cast<float*>(&v);
 #pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int c = l + 32 * (4 * j4 + q);
+        vp[q] = __fmul_rn(__fmul_rn(load_f32(xs, row * C + c), r), gs[c]);
+      }
+      *reinterpret_cast<float4*>(nb + row * C + j4 * 128 + l * 4) = v;
+    }
+  };
+
   for (int s = 0; s < kStages - 1; ++s) issue(s);
+  if (threadIdx.x < BT) rs_s[threadIdx.x] = threadIdx.x < nt ? __ldg(rscale + t0 + threadIdx.x) : 0.0f;
+  cp_async_wait<kStages - 2>();  // chunk 0 landed
+  __syncthreads();
+  normalize(0);
 
   const int tw = warp / WE, ew = warp % WE;  // this warp's token group and expert group
-  float rsv[TT];
-#pragma unroll
-  for (int t = 0; t < TT; ++t) rsv[t] = tw * TT + t < nt ? __ldg(rscale + t0 + tw * TT + t) : 0.0f;
   float acc[TT][TE];
 #pragma unroll
   for (int t = 0; t < TT; ++t)
@@ -255,46 +324,70 @@ __global__ void __launch_bounds__(kRouterThreads)
     for (int e = 0; e < TE; ++e) acc[t][e] = 0.0f;
 
   for (int ch = 0; ch < nch; ++ch) {
-    cp_async_wait<kStages - 2>();
-    __syncthreads();  // chunk ch landed for every thread; stage (ch - 1) fully consumed
+    cp_async_wait<kStages - 3>();  // chunk ch + 1 landed
+    __syncthreads();  // nbuf[ch % 2] complete; stage (ch - 1) and nbuf[(ch + 1) % 2] fully consumed
     issue(ch + kStages - 1);
-    const uint8_t* st = router_smem + (ch % kStages) * kStage;
-    const XT* xs = reinterpret_cast<const XT*>(st);
-    const float* gs = reinterpret_cast<const float*>(st + kXBytes);
-    const float* ws = gs + C;
-    const int cb = ch * C;
-    const int jmax = min(C / 32, (d - cb - lane + 31) / 32);  // lane's chain values in this chunk
+    normalize(ch + 1);
+    const float* ws = reinterpret_cast<const float*>(router_smem + (ch % kStages) * kStage + kXBytes) + C;
+    const float* nb = nbuf + (ch & 1) * BT * C;
+    const int cw = min(C, d - ch * C);
+    if (cw == C) {
 #pragma unroll
-    for (int j4 = 0; j4 < C / 128; ++j4) {
-      if (4 * j4 >= jmax) break;
-      float4 wv[TE];
+      for (int j4 = 0; j4 < C / 128; ++j4) {
+        float4 wv[TE];
 #pragma unroll
-      for (int e = 0; e < TE; ++e) wv[e] = *reinterpret_cast<const float4*>(ws + (ew * TE + e) * C + j4 * 128 + lane * 4);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const int j = 4 * j4 + q;
-        if (j >= jmax) break;
-        const int c = lane + 32 * j;
-        const float g = gs[c];
+        for (int e = 0; e < TE; ++e)
+          wv[e] = *reinterpret_cast<const float4*>(ws + (ew * TE + e) * C + j4 * 128 + lane * 4);
 #pragma unroll
         for (int t = 0; t < TT; ++t) {
-          const float xv =
-              __fmul_rn(__fmul_rn(load_f32(xs, static_cast<uint64_t>((tw * TT + t) * C + c)), rsv[t]), g);
+          const float4 xv = *reinterpret_cast<const float4*>(nb + (tw * TT + t) * C + j4 * 128 + lane * 4);
 #pragma unroll
-          for (int e = 0; e < TE; ++e) acc[t][e] = __fmaf_rn(xv, reinterpret_cast<const float*>(&wv[e])[q], acc[t][e]);
+          for (int e = 0; e < TE; ++e) {
+            acc[t][e] = __fmaf_rn(xv.x, wv[e].x, acc[t][e]);
+            acc[t][e] = __fmaf_rn(xv.y, wv[e].y, acc[t][e]);
+            acc[t][e] = __fmaf_rn(xv.z, wv[e].z, acc[t][e]);
+            acc[t][e] = __fmaf_rn(xv.w, wv[e].w, acc[t][e]);
+          }
+        }
+      }
+    } else {
+      // ragged last chunk: only the lane's columns below d join its chain
+      const int jmax = (cw - lane + 31) / 32;
+      for (int j = 0; j < jmax; ++j) {
+        const int pos = (j >> 2) * 128 + lane * 4 + (j & 3);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          const float xv = nb[(tw * TT + t) * C + pos];
+#pragma unroll
+          for (int e = 0; e < TE; ++e) acc[t][e] = __fmaf_rn(xv, ws[(ew * TE + e) * C + pos], acc[t][e]);
         }
       }
     }
   }
   cp_async_wait<0>();
+  // all experts in this block (E <= 32): the block also does top-k + softmax
+  const bool fused = topk_idx != nullptr;
+  float* lg_s = nbuf;  // [BT][33]; nbuf is free once every warp passed the barrier below
+  if (fused) __syncthreads();
 #pragma unroll
   for (int t = 0; t < TT; ++t) {
 #pragma unroll
     for (int e = 0; e < TE; ++e) {
       const float s = warp_sum_butterfly(acc[t][e]);
       const int tok = tw * TT + t, ex = e_base + ew * TE + e;
-      if (lane == 0 && tok < nt && ex < E) logits_out[static_cast<uint64_t>(t0 + tok) * E + ex] = __fadd_rn(s, gate_b[ex]);
+      if (lane == 0 && tok < nt && ex < E) {
+        const float l = __fadd_rn(s, gate_b[ex]);
+        logits_out[static_cast<uint64_t>(t0 + tok) * E + ex] = l;
+        if (fused) lg_s[tok * 33 + ex] = l;
+      }
     }
+  }
+  if (!fused) return;
+  __syncthreads();
+  for (int tok = warp; tok < nt; tok += kRouterWarps) {
+    const float v[1] = {lane < E ? lg_s[tok * 33 + lane] : 0.0f};
+    warp_topk_softmax<1>(v, E, k, lane, topk_idx + static_cast<uint64_t>(t0 + tok) * k,
+                         topk_w + static_cast<uint64_t>(t0 + tok) * k);
   }
 }
 
@@ -637,44 +730,62 @@ cudaError_t launch_dequant_rows(const uint8_t* blocks, const uint8_t* scales, ui
 
 cudaError_t launch_topk_softmax(const float* logits, int n, int E, int k, int32_t* idx, float* w, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  topk_softmax_kernel<<<(n + 7) / 8, 256, 0, st>>>(logits, n, E, k, idx, w);
+  const dim3 grid((n + 7) / 8);
+  if (E <= 32) topk_softmax_kernel<1><<<grid, 256, 0, st>>>(logits, n, E, k, idx, w);
+  else if (E <= 64) topk_softmax_kernel<2><<<grid, 256, 0, st>>>(logits, n, E, k, idx, w);
+  else if (E <= 128) topk_softmax_kernel<4><<<grid, 256, 0, st>>>(logits, n, E, k, idx, w);
+  else if (E <= 256) topk_softmax_kernel<8><<<grid, 256, 0, st>>>(logits, n, E, k, idx, w);
+  else if (E <= 512) topk_softmax_kernel<16><<<grid, 256, 0, st>>>(logits, n, E, k, idx, w);
+  else topk_softmax_kernel<32><<<grid, 256, 0, st>>>(logits, n, E, k, idx, w);
   return cudaGetLastError();
 }
 
 template <typename XT, int TT, int TE>
-static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, const float* gamma, const float* gate_packed,
-                                      const float* gate_b, const float* rscale, float* logits, cudaStream_t st) {
+static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, int k, const float* gamma,
+                                      const float* gate_packed, const float* gate_b, const float* rscale,
+                                      float* logits, int aligned, int32_t* topk_idx, float* topk_w, cudaStream_t st) {
   constexpr int BT = (kRouterWarps / (kRouterGroup / TE)) * TT;
   const dim3 grid((n + BT - 1) / BT, (E + kRouterGroup - 1) / kRouterGroup);
-  const size_t smem = static_cast<size_t>(router_stages<BT>()) * router_stage_bytes<XT, BT>();
+  const size_t smem = static_cast<size_t>(router_stages<BT>()) * router_stage_bytes<XT, BT>() +
+                      2 * static_cast<size_t>(BT) * kRouterChunk * sizeof(float);
   const auto fn = router_logits_kernel<XT, TT, TE>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
-  const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
-  fn<<<grid, kRouterThreads, smem, st>>>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, aligned);
+  fn<<<grid, kRouterThreads, smem, st>>>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, aligned, k, topk_idx,
+                                         topk_w);
   return cudaGetLastError();
 }
 
+// rms_kernel, then the logits; with E <= 32 the logits blocks hold every
+// expert of their tokens and also write top-k + softmax, else a separate
+// top-k kernel follows.
 template <typename XT>
-static cudaError_t launch_router_x(const XT* x, int n, int d, int E, const float* gamma, const float* gate_packed,
-                                   const float* gate_b, float eps, float* logits, float* rscale, cudaStream_t st) {
-  rms_kernel<XT><<<(n + 7) / 8, 256, 0, st>>>(x, n, d, eps, rscale);
+static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, const float* gamma,
+                                   const float* gate_packed, const float* gate_b, float eps, float* logits,
+                                   int32_t* topk_idx, float* topk_w, float* rscale, cudaStream_t st) {
+  const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
+  rms_kernel<XT><<<(n + 7) / 8, 256, 0, st>>>(x, n, d, eps, rscale, aligned);
+  const bool fuse = E <= kRouterGroup;
+  int32_t* fi = fuse ? topk_idx : nullptr;
+  float* fw = fuse ? topk_w : nullptr;
   // large batches: 16 tokens x 32 experts per block (8x8 per thread);
   // small ones: one token per block so that enough blocks run
-  return n >= 2048 ? launch_router_tile<XT, 8, 8>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, st)
-                   : launch_router_tile<XT, 1, 4>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, st);
+  const cudaError_t e =
+      n >= 2048 ? launch_router_tile<XT, 8, 8>(x, n, d, E, k, gamma, gate_packed, gate_b, rscale, logits, aligned, fi,
+                                               fw, st)
+                : launch_router_tile<XT, 1, 4>(x, n, d, E, k, gamma, gate_packed, gate_b, rscale, logits, aligned, fi,
+                                               fw, st);
+  if (e != cudaSuccess || fuse) return e;
+  return launch_topk_softmax(logits, n, E, k, topk_idx, topk_w, st);
 }
 
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  const cudaError_t e =
-      x_dtype == 0 ? launch_router_x(static_cast<const float*>(x), n, d, E, gamma, gate_packed, gate_b, eps, logits,
-                                     rscale, st)
-                   : launch_router_x(static_cast<const __nv_bfloat16*>(x), n, d, E, gamma, gate_packed, gate_b, eps,
-                                     logits, rscale, st);
-  if (e != cudaSuccess) return e;
-  return launch_topk_softmax(logits, n, E, k, topk_idx, topk_w, st);
+  return x_dtype == 0 ? launch_router_x(static_cast<const float*>(x), n, d, E, k, gamma, gate_packed, gate_b, eps,
+                                        logits, topk_idx, topk_w, rscale, st)
+                      : launch_router_x(static_cast<const __nv_bfloat16*>(x), n, d, E, k, gamma, gate_packed, gate_b,
+                                        eps, logits, topk_idx, topk_w, rscale, st);
 }
 
 cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
