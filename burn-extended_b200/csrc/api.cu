@@ -163,6 +163,7 @@ struct Workspace {
   float* y_pair = nullptr; // [rows][d]
   float* act_f32 = nullptr;// [rows][fp] (SIMT path only)
   int32_t* local_idx = nullptr; // [cap_pairs] local expert ids (expert-parallel receive side)
+  int32_t* perm_scratch = nullptr; // multi-block permutation (permute_scratch_ints)
   int pair_dtype = MXMOE_F32;   // element type the last run_experts wrote y_pair in
   CUtensorMap tmap_x[kNumTileWidths];
   CUtensorMap tmap_act[kNumTileWidths];
@@ -203,6 +204,7 @@ void free_workspace(Workspace& w) {
   dfree(w.ntile_prefix); dfree(w.perm_p); dfree(w.inv_p);
   dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
   dfree(w.local_idx);
+  dfree(w.perm_scratch);
   w.cap_tokens = w.cap_pairs = w.rows = w.row_blocks = 0;
 }
 
@@ -242,6 +244,9 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   TRY(dalloc(&w.perm_p, w.rows));
   TRY(dalloc(&w.inv_p, cap_p));
   TRY(dalloc(&w.local_idx, cap_p));
+  const size_t pscr = permute_scratch_ints(static_cast<int>(cap_p), static_cast<int>(Et));
+  TRY(dalloc(&w.perm_scratch, pscr));
+  CUDA_TRY(cudaMemset(w.perm_scratch, 0, pscr * sizeof(int32_t)));
   TRY(dalloc(&w.xq, 3ull * w.rows * L->kp1));
   TRY(dalloc(&w.xsf, 3ull * w.row_blocks * kc1 * kSfAtomBytes));
   TRY(dalloc(&w.aq, 2ull * w.rows * L->kp2));
@@ -642,7 +647,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
                          w.logits, w.topk_idx, w.topk_w, w.rscale, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
   CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, tp.pair_tile, w.offsets, w.perm_c,
-                          w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
+                          w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
   TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
   const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
@@ -846,7 +851,7 @@ int mxmoe_route(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32_t n_t
   if (offsets || perm || inv) {
     if (!offsets || !perm || !inv) return fail(MXMOE_ERR_INVALID_ARG, "offsets, perm and inv go together");
     CUDA_TRY(launch_permute(topk_idx, static_cast<int>(n_tokens * k), L->E_total, 1, 1, offsets, nullptr, nullptr,
-                            w.poff, w.counts, nullptr, perm, inv, st));
+                            w.poff, w.counts, nullptr, perm, inv, st, w.perm_scratch));
   }
   return MXMOE_OK;
 }
@@ -883,7 +888,8 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   CUDA_TRY(launch_localize(expert, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
                            static_cast<int>(L->e_count), w.local_idx, L->err, st));
   CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, tp.pair_tile, nullptr,
-                          nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st));
+                          nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st,
+                          w.perm_scratch));
   TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, rscale, weight, tp, xt, st));
   CUDA_TRY(launch_combine(nullptr, 0, w.y_pair, w.pair_dtype, w.local_idx, w.inv_p, n_pairs, L->d, 1, 0, out, out_dtype, st));
   return MXMOE_OK;

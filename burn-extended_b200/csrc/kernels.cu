@@ -33,10 +33,6 @@ __device__ __forceinline__ float load_any(const void* p, int dtype, uint64_t i) 
   return dtype == 0 ? static_cast<const float*>(p)[i]
                     : __bfloat162float(static_cast<const __nv_bfloat16*>(p)[i]);
 }
-__device__ __forceinline__ void store_any(void* p, int dtype, uint64_t i, float v) {
-  if (dtype == 0) static_cast<float*>(p)[i] = v;
-  else static_cast<__nv_bfloat16*>(p)[i] = __float2bfloat16_rn(v);
-}
 
 // Butterfly sum over the warp: offsets 16, 8, 4, 2, 1.  Every lane ends with
 // the same value (IEEE addition is commutative).
@@ -399,26 +395,63 @@ __global__ void __launch_bounds__(kRouterThreads)
 // and the padded maps used by the GEMMs, where every expert segment starts
 // at a multiple of `pad` rows.
 constexpr int kPermThreads = 1024;
+constexpr int kPermBatch = 16;  // rows of 32 pairs whose expert ids are loaded together
+
+// Lanes of the warp holding the same expert id (ex = -1 for none), from one
+// ballot per bit of ex + 1 -- cheaper than a match instruction.
+__device__ __forceinline__ unsigned same_expert_lanes(int ex, int nbits) {
+  const unsigned v = static_cast<unsigned>(ex + 1);
+  unsigned m = 0xFFFFFFFFu;
+  for (int i = 0; i < nbits; ++i) {
+    const unsigned bit = (v >> i) & 1u;
+    const unsigned bal = __ballot_sync(0xFFFFFFFFu, bit);
+    m &= bit ? bal : ~bal;
+  }
+  return m;
+}
+
+// Expert ids of pairs [base0, base0 + 32*kPermBatch) (-1 past p_end) into a
+// warp's staging buffer; all loads in flight together.
+__device__ __forceinline__ void stage_expert_ids(const int32_t* __restrict__ topk_idx, int base0, int p_end, int lane,
+                                                 int32_t* stg) {
+  int v[kPermBatch];
+#pragma unroll
+  for (int b = 0; b < kPermBatch; ++b) {
+    const int p = base0 + 32 * b + lane;
+    v[b] = p < p_end ? __ldg(topk_idx + p) : -1;
+  }
+  __syncwarp();  // the previous batch is consumed
+#pragma unroll
+  for (int b = 0; b < kPermBatch; ++b) stg[32 * b + lane] = v[b];
+  __syncwarp();
+}
 
 __global__ void __launch_bounds__(kPermThreads)
     permute_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
                    int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
                    int32_t* perm_p, int32_t* inv_p) {
-  extern __shared__ int32_t cnt[];     // [32 warps][E], then canonical and padded starts [E] each
+  extern __shared__ int32_t cnt[];  // [32 warps][E], canonical and padded starts [E] each, staging
   int32_t* cstart = cnt + 32 * E;
   int32_t* pstart = cstart + E;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* stg = pstart + E + warp * 32 * kPermBatch;  // this warp's staged expert ids
   const int seg = (P + 31) / 32;
   const int p_begin = warp * seg, p_end = min(P, p_begin + seg);
+  const int nbits = 32 - __clz(E);  // bits of the largest ex + 1
   for (int i = threadIdx.x; i < 32 * E; i += blockDim.x) cnt[i] = 0;
   __syncthreads();
-  // pass 1: per-warp expert histogram of the warp's contiguous segment
-  for (int base = p_begin; base < p_end; base += 32) {
-    const int p = base + lane;
-    const int ex = p < p_end ? topk_idx[p] : -1;
-    const unsigned grp = __match_any_sync(0xFFFFFFFFu, ex);
-    if (ex >= 0 && lane == __ffs(grp) - 1) cnt[warp * E + ex] += __popc(grp);
-    __syncwarp();
+  // pass 1: per-warp expert histogram of the warp's contiguous segment.  The
+  // expert ids of kPermBatch rows of 32 pairs are loaded together into the
+  // warp's staging buffer, then consumed by a rolled loop (a one-block kernel
+  // runs each instruction once, so the loop body is kept small).
+  for (int base0 = p_begin; base0 < p_end; base0 += 32 * kPermBatch) {
+    stage_expert_ids(topk_idx, base0, p_end, lane, stg);
+    for (int b = 0; b < kPermBatch && base0 + 32 * b < p_end; ++b) {
+      const int ex = stg[32 * b + lane];
+      const unsigned grp = same_expert_lanes(ex, nbits);
+      if (ex >= 0 && lane == __ffs(grp) - 1) cnt[warp * E + ex] += __popc(grp);
+      __syncwarp();
+    }
   }
   __syncthreads();
   // per expert: totals, and each warp's base within the expert
@@ -452,12 +485,182 @@ __global__ void __launch_bounds__(kPermThreads)
   }
   __syncthreads();
   // pass 2: stable ranks within each expert, (token, slot) order
-  for (int base = p_begin; base < p_end; base += 32) {
-    const int p = base + lane;
-    const int ex = p < p_end ? topk_idx[p] : -1;
-    const unsigned grp = __match_any_sync(0xFFFFFFFFu, ex);
+  for (int base0 = p_begin; base0 < p_end; base0 += 32 * kPermBatch) {
+    stage_expert_ids(topk_idx, base0, p_end, lane, stg);
+    for (int b = 0; b < kPermBatch && base0 + 32 * b < p_end; ++b) {
+      const int p = base0 + 32 * b + lane;
+      const int ex = stg[32 * b + lane];
+      const unsigned grp = same_expert_lanes(ex, nbits);
+      if (ex >= 0) {
+        const int rank = cnt[warp * E + ex] + __popc(grp & ((1u << lane) - 1u));
+        const int pos_p = pstart[ex] + rank;
+        perm_p[pos_p] = p;
+        inv_p[p] = pos_p;
+        if (perm_c) {
+          perm_c[cstart[ex] + rank] = p;
+          inv_c[p] = cstart[ex] + rank;
+        }
+      }
+      __syncwarp();
+      if (ex >= 0 && lane == __ffs(grp) - 1) cnt[warp * E + ex] += __popc(grp);
+      __syncwarp();
+    }
+  }
+}
+
+// Multi-block form of the same permutation for large pair counts: chunks of
+// kPermChunk pairs, one block each.  perm_hist_kernel counts each chunk's
+// experts; the last block to finish (atomic ticket after a fence -- no block
+// waits on another) turns the chunk counts into per-expert exclusive bases
+// and scans the expert totals into the offsets.  perm_scatter_kernel then
+// ranks each chunk's pairs stably: chunk base + earlier warps of the chunk +
+// earlier lanes of the warp.  Scratch (int32): [0] ticket, [32, 32+E) canonical
+// starts, [32+E, 32+2E) padded starts, then counts [chunks][E].
+constexpr int kPermChunk = 512;
+constexpr int kPermChunkThreads = 256;  // 8 warps x 2 rows of 32 pairs
+
+// In-place exclusive scan of a[0, len) in shared memory by the whole block
+// (len <= 4 * blockDim.x); returns the total.  Every thread must call it.
+__device__ int block_exclusive_scan(int* a, int len, int* warp_tot) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const int i0 = 4 * threadIdx.x;
+  int v[4], s = 0;
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    v[j] = i0 + j < len ? a[i0 + j] : 0;
+    s += v[j];
+  }
+  int inc = s;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int u = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+    if (lane >= o) inc += u;
+  }
+  if (lane == 31) warp_tot[warp] = inc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int w = 0; w < nw; ++w) {
+      const int t = warp_tot[w];
+      warp_tot[w] = run;
+      run += t;
+    }
+    warp_tot[nw] = run;
+  }
+  __syncthreads();
+  int run = warp_tot[warp] + inc - s;
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+    if (i0 + j < len) {
+      a[i0 + j] = run;
+      run += v[j];
+    }
+  const int total = warp_tot[nw];
+  __syncthreads();
+  return total;
+}
+
+__global__ void __launch_bounds__(kPermChunkThreads)
+    perm_hist_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* scratch,
+                     int32_t* offsets, int32_t* poff, int32_t* counts, int32_t* ntile_prefix) {
+  extern __shared__ int32_t sh[];  // [E] counts, then 3 x [E] scan arrays
+  __shared__ int warp_tot[kPermChunkThreads / 32 + 1];
+  __shared__ bool last;
+  const int nch = (P + kPermChunk - 1) / kPermChunk;
+  int32_t* hist = scratch + 32 + 2 * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
+  __syncthreads();
+  const int p0 = blockIdx.x * kPermChunk;
+  for (int p = p0 + threadIdx.x; p < min(P, p0 + kPermChunk); p += blockDim.x) atomicAdd(&sh[__ldg(topk_idx + p)], 1);
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) hist[static_cast<uint64_t>(blockIdx.x) * E + e] = sh[e];
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(scratch, 1) == nch - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  // per expert: exclusive bases over chunks, and the totals
+  int* tot = sh;
+  int* pc = sh + E;   // padded sizes -> padded starts
+  int* tc = sh + 2 * E;  // tiles -> tile prefix
+  int* cs = sh + 3 * E;  // totals -> canonical starts
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int base = 0;
+    for (int c = 0; c < nch; ++c) {
+      int32_t* h = hist + static_cast<uint64_t>(c) * E + e;
+      const int v = __ldcg(h);
+      *h = base;
+      base += v;
+    }
+    tot[e] = base;
+    cs[e] = base;
+    pc[e] = (base + pad - 1) / pad * pad;
+    tc[e] = (base + N - 1) / N;
+  }
+  __syncthreads();
+  const int run = block_exclusive_scan(cs, E, warp_tot);
+  const int prun = block_exclusive_scan(pc, E, warp_tot);
+  const int trun = block_exclusive_scan(tc, E, warp_tot);
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    if (offsets) offsets[e] = cs[e];
+    poff[e] = pc[e];
+    counts[e] = tot[e];
+    if (ntile_prefix) ntile_prefix[e] = tc[e];
+    scratch[32 + e] = cs[e];
+    scratch[32 + E + e] = pc[e];
+  }
+  if (threadIdx.x == 0) {
+    if (offsets) offsets[E] = run;
+    poff[E] = prun;
+    if (ntile_prefix) ntile_prefix[E] = trun;
+    scratch[0] = 0;  // ticket for the next launch
+  }
+}
+
+__global__ void __launch_bounds__(kPermChunkThreads)
+    perm_scatter_kernel(const int32_t* __restrict__ topk_idx, int P, int E, const int32_t* __restrict__ scratch,
+                        int32_t* perm_c, int32_t* inv_c, int32_t* perm_p, int32_t* inv_p) {
+  constexpr int kWarps = kPermChunkThreads / 32;
+  constexpr int kRows = kPermChunk / kPermChunkThreads;
+  extern __shared__ int32_t wcnt[];  // [kWarps][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbits = 32 - __clz(E);
+  const int32_t* cstart = scratch + 32;
+  const int32_t* pstart = scratch + 32 + E;
+  const int32_t* hist = scratch + 32 + 2 * E + static_cast<uint64_t>(blockIdx.x) * E;
+  for (int i = threadIdx.x; i < kWarps * E; i += blockDim.x) wcnt[i] = 0;
+  const int pw = blockIdx.x * kPermChunk + warp * 32 * kRows;  // this warp's first pair
+  int exv[kRows];
+  unsigned grp[kRows];
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const int p = pw + 32 * r + lane;
+    exv[r] = p < P ? __ldg(topk_idx + p) : -1;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    grp[r] = same_expert_lanes(exv[r], nbits);
+    if (exv[r] >= 0 && lane == __ffs(grp[r]) - 1) wcnt[warp * E + exv[r]] += __popc(grp[r]);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int base = hist[e];
+    for (int w = 0; w < kWarps; ++w) {
+      const int c = wcnt[w * E + e];
+      wcnt[w * E + e] = base;
+      base += c;
+    }
+  }
+  __syncthreads();
+#pragma unroll
+  for (int r = 0; r < kRows; ++r) {
+    const int ex = exv[r];
     if (ex >= 0) {
-      const int rank = cnt[warp * E + ex] + __popc(grp & ((1u << lane) - 1u));
+      const int p = pw + 32 * r + lane;
+      const int rank = wcnt[warp * E + ex] + __popc(grp[r] & ((1u << lane) - 1u));
       const int pos_p = pstart[ex] + rank;
       perm_p[pos_p] = p;
       inv_p[p] = pos_p;
@@ -467,7 +670,7 @@ __global__ void __launch_bounds__(kPermThreads)
       }
     }
     __syncwarp();
-    if (ex >= 0 && lane == __ffs(grp) - 1) cnt[warp * E + ex] += __popc(grp);
+    if (ex >= 0 && lane == __ffs(grp[r]) - 1) wcnt[warp * E + ex] += __popc(grp[r]);
     __syncwarp();
   }
 }
@@ -479,21 +682,37 @@ __global__ void __launch_bounds__(kPermThreads)
 // One thread per (token, 32-column block): reads 32 inputs, quantizes them on
 // its own once and writes the codes (16-byte stores) and scale bytes to the
 // positions of all k pairs of the token.
-__global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
-                                      const float* __restrict__ gamma, int gamma_is_one,
-                                      const int32_t* __restrict__ inv_p, int terms, uint8_t* codes,
-                                      uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride,
-                                      int kchunks, int sf_rows, int stacked) {
+__global__ void __launch_bounds__(256, 3)
+    quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
+                          const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
+                          int terms, uint8_t* codes, uint64_t term_stride, int kp, uint8_t* sf,
+                          uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked) {
+  // items (t, b) with b padded to a multiple of 4, so the four lanes of one
+  // aligned lane quad hold the four 32-blocks of one scale word; lanes with
+  // b >= d / 32 only contribute zero scale bytes (the K padding)
   const int nb = d / 32;
-  const uint64_t items = static_cast<uint64_t>(n) * nb;
-  for (uint64_t it = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; it < items;
-       it += static_cast<uint64_t>(gridDim.x) * blockDim.x) {
-    const int t = static_cast<int>(it / nb);
-    const int b = static_cast<int>(it - static_cast<uint64_t>(t) * nb);
+  const int nbp = (nb + 3) & ~3;
+  const uint64_t items = static_cast<uint64_t>(n) * nbp;
+  const int lane = threadIdx.x & 31;
+  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
+  // every lane of a warp runs the same number of iterations (the shuffles
+  // below need the whole warp): the loop bound is rounded up to the stride
+  const uint64_t it_end = (items + stride - 1) / stride * stride;
+  for (uint64_t it = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; it < it_end; it += stride) {
+    const bool in = it < items;
+    const int t = in ? static_cast<int>(it / nbp) : 0;
+    const int b = in ? static_cast<int>(it - static_cast<uint64_t>(t) * nbp) : nb;
+    const bool active = b < nb;
+    int pos[kMaxTopK];
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s) pos[s] = in && s < k ? __ldg(inv_p + static_cast<uint64_t>(t) * k + s) : 0;
     float v[32];
-    const uint64_t src = static_cast<uint64_t>(t) * d + b * 32;
-    if (x_dtype == 1) {
-      const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + src);
+    if (!active) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+    } else if (x_dtype == 1) {
+      const uint4* xs =
+          reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + static_cast<uint64_t>(t) * d + b * 32);
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         const uint4 u = __ldg(xs + q);
@@ -505,34 +724,55 @@ __global__ void quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, i
         }
       }
     } else {
-      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + src);
+      const float4* xs =
+          reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<uint64_t>(t) * d + b * 32);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const float4 u = __ldg(xs + q);
         v[4 * q] = u.x; v[4 * q + 1] = u.y; v[4 * q + 2] = u.z; v[4 * q + 3] = u.w;
       }
     }
-    if (!gamma_is_one) {
+    if (!gamma_is_one && active) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + b * 32 + i));
     }
     uint32_t words[kMaxTerms][8];
     uint8_t sbyte[kMaxTerms];
     quantize_block32(v, terms, words, sbyte);
-    for (int s = 0; s < k; ++s) {
-      const int pos = __ldg(inv_p + static_cast<uint64_t>(t) * k + s);
-      const uint64_t off = static_cast<uint64_t>(pos) * kp + b * 32;
-      const uint64_t so = sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(b),
+    if (!active) {
+#pragma unroll
+      for (int q = 0; q < kMaxTerms; ++q) sbyte[q] = 0;
+    }
+    // the quad's four scale bytes as one word, stored by the quad's first lane
+    uint32_t sword[kMaxTerms];
+#pragma unroll
+    for (int q = 0; q < kMaxTerms; ++q) {
+      uint32_t w = static_cast<uint32_t>(sbyte[q]) << (8 * (lane & 3));
+      w |= __shfl_xor_sync(0xFFFFFFFFu, w, 1);
+      w |= __shfl_xor_sync(0xFFFFFFFFu, w, 2);
+      sword[q] = w;
+    }
+    if (!in) continue;
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s) {
+      if (s >= k) break;
+      const uint64_t off = static_cast<uint64_t>(pos[s]) * kp + b * 32;
+      const uint64_t so = sf_offset(static_cast<uint32_t>(pos[s]), static_cast<uint32_t>(b),
                                     static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
-      for (int q = 0; q < terms; ++q) {
-        uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
-        dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
-        dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
-        if (stacked)
-          sf[stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q), static_cast<uint32_t>(b),
-                               static_cast<uint32_t>(kchunks))] = sbyte[q];
-        else
-          sf[q * sf_term_stride + so] = sbyte[q];
+#pragma unroll
+      for (int q = 0; q < kMaxTerms; ++q) {
+        if (q >= terms) break;
+        if (active) {
+          uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
+          dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
+          dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
+        }
+        if ((lane & 3) == 0) {
+          const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos[s]), static_cast<uint32_t>(q),
+                                                         static_cast<uint32_t>(b), static_cast<uint32_t>(kchunks))
+                                     : q * sf_term_stride + so;
+          *reinterpret_cast<uint32_t*>(sf + o) = sword[q];
+        }
       }
     }
   }
@@ -788,10 +1028,26 @@ cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k
                                         eps, logits, topk_idx, topk_w, rscale, st);
 }
 
+size_t permute_scratch_ints(int P, int E) {
+  return 32 + 2 * static_cast<size_t>(E) + static_cast<size_t>((P + kPermChunk - 1) / kPermChunk) * E;
+}
+
 cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
                            int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
-                           int32_t* inv_p, cudaStream_t st) {
-  const size_t smem = static_cast<size_t>(34) * E * sizeof(int32_t);
+                           int32_t* inv_p, cudaStream_t st, int32_t* scratch) {
+  if (scratch && P >= kPermMultiBlockMin) {
+    const int nch = (P + kPermChunk - 1) / kPermChunk;
+    const size_t hsmem = 4 * static_cast<size_t>(E) * sizeof(int32_t);
+    ensure_dynamic_smem(reinterpret_cast<const void*>(perm_hist_kernel), hsmem);
+    perm_hist_kernel<<<nch, kPermChunkThreads, hsmem, st>>>(topk_idx, P, E, pad, N, scratch, offsets, poff, counts,
+                                                             ntile_prefix);
+    const size_t ssmem = (kPermChunkThreads / 32) * static_cast<size_t>(E) * sizeof(int32_t);
+    ensure_dynamic_smem(reinterpret_cast<const void*>(perm_scatter_kernel), ssmem);
+    perm_scatter_kernel<<<nch, kPermChunkThreads, ssmem, st>>>(topk_idx, P, E, scratch, perm_c, inv_c, perm_p,
+                                                                inv_p);
+    return cudaGetLastError();
+  }
+  const size_t smem = (static_cast<size_t>(34) * E + 32 * 32 * kPermBatch) * sizeof(int32_t);
   ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
   permute_kernel<<<1, kPermThreads, smem, st>>>(topk_idx, P, E, pad, N, offsets, perm_c, inv_c, poff, counts,
                                                 ntile_prefix, perm_p, inv_p);
@@ -802,7 +1058,7 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
                                   int sf_rows, int stacked, cudaStream_t st) {
-  const uint64_t items = static_cast<uint64_t>(n) * (d / 32);
+  const uint64_t items = static_cast<uint64_t>(n) * (((d / 32) + 3) & ~3);
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 255) / 256;
   const int grid = static_cast<int>(blocks < 148 * 32 ? blocks : 148 * 32);

@@ -38,9 +38,14 @@ inline void pack_router_gate(const float* w, int E, int d, float* out) {
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st);
+// Canonical permutation.  With scratch (permute_scratch_ints(P, E) int32,
+// zeroed once before first use) and P >= kPermMultiBlockMin it runs on many
+// blocks; otherwise on one block with no scratch.
+constexpr int kPermMultiBlockMin = 2048;
+size_t permute_scratch_ints(int P, int E);
 cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N, int32_t* offsets, int32_t* perm_c,
                            int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
-                           int32_t* inv_p, cudaStream_t st);
+                           int32_t* inv_p, cudaStream_t st, int32_t* scratch = nullptr);
 cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,

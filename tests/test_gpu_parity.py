@@ -105,6 +105,11 @@ def _check_routing(layer, inp, x, n):
     r = oracle.route(oracle.cfg(inp.d, inp.f, inp.E, inp.k), inp.x, inp.gamma, inp.gate_w, inp.gate_b)
     assert np.array_equal(rr["logits"].cpu().numpy().reshape(n, inp.E).view(np.uint32), r["logits"].view(np.uint32))
     assert np.array_equal(rr["topk_idx"].cpu().numpy().reshape(n, inp.k), r["topk_idx"])
+    # canonical maps (pair counts >= 2048 take the multi-block permutation)
+    offs, perm, inv = oracle.permute(r["topk_idx"], inp.E)
+    assert np.array_equal(rr["offsets"].cpu().numpy(), offs)
+    assert np.array_equal(rr["perm"].cpu().numpy(), perm)
+    assert np.array_equal(rr["inv"].cpu().numpy(), inv)
     import torch as t
     rs = t.empty(n, dtype=t.float32, device=x.device)
     ti = t.empty(n, inp.k, dtype=t.int32, device=x.device)
