@@ -133,8 +133,8 @@ struct DeviceGuard {
 };
 
 // Box rows of the activation tensor maps; 16-row boxes feed the stacked tiles.
-constexpr int kNumTileWidths = 5;
-constexpr int kTileWidths[kNumTileWidths] = {32, 64, 128, 256, 16};
+constexpr int kNumTileWidths = 4;
+constexpr int kTileWidths[kNumTileWidths] = {32, 64, 128, 256};
 
 }  // namespace
 
@@ -143,7 +143,7 @@ struct Workspace {
   uint32_t cap_tokens = 0;  // tokens
   uint32_t cap_pairs = 0;   // n * k
   uint32_t rows = 0;        // padded activation rows
-  uint32_t row_blocks = 0;  // scale-atom row blocks (rows / 32 + slack)
+  uint32_t row_blocks = 0;  // scale-atom row blocks (rows / 16 + slack)
   float* logits = nullptr;
   int32_t* topk_idx = nullptr;
   float* topk_w = nullptr;
@@ -167,6 +167,8 @@ struct Workspace {
   int pair_dtype = MXMOE_F32;   // element type the last run_experts wrote y_pair in
   CUtensorMap tmap_x[kNumTileWidths];
   CUtensorMap tmap_act[kNumTileWidths];
+  // stacked tiles of 16 / 32 / 64 pairs: boxes of 32 / 64 / 128 rows over 2 x rows code rows
+  CUtensorMap tmap_x_stk[3], tmap_act_stk[3];
 };
 
 struct mxmoe_layer {
@@ -229,7 +231,7 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   const uint32_t cap_t = grow(old_t, n_tokens);
   const uint32_t cap_p = grow(old_p, pairs);
   w.rows = round_up(cap_p, kRowBlock) + E * kRowBlock + 256;
-  w.row_blocks = w.rows / kTileWidths[0] + 2;  // enough atoms for the smallest tile width
+  w.row_blocks = w.rows / 16 + 2;  // enough atoms for the smallest (16-pair stacked) tile
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   TRY(dalloc(&w.logits, static_cast<size_t>(cap_t) * Et));
   TRY(dalloc(&w.topk_idx, cap_p));
@@ -259,6 +261,13 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   CUDA_TRY(cudaMemset(w.aq, 0, 2ull * w.rows * L->kp2));
   CUDA_TRY(cudaMemset(w.asf, 0, 2ull * w.row_blocks * kc2 * kSfAtomBytes));
   CUDA_TRY(cudaMemset(w.perm_p, 0, sizeof(int32_t) * w.rows));
+  for (int i = 0; i < 3; ++i) {
+    const uint32_t box = 32u << i;
+    TRY(make_tmap(&w.tmap_x_stk[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.xq, L->kp1, 2ull * w.rows, 1, L->kp1,
+                  2ull * w.rows * L->kp1, box));
+    TRY(make_tmap(&w.tmap_act_stk[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.aq, L->kp2, 2ull * w.rows, 1, L->kp2,
+                  2ull * w.rows * L->kp2, box));
+  }
   for (int i = 0; i < kNumTileWidths; ++i) {
     TRY(make_tmap(&w.tmap_x[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.xq, L->kp1, w.rows, 3, L->kp1,
                   static_cast<uint64_t>(w.rows) * L->kp1, kTileWidths[i]));
@@ -286,7 +295,10 @@ struct TilePlan {
 
 TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms) {
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
-  if (avg <= 48 && x_terms == 2) return {true, 64, 4, true};
+  // two-term activations: stacked tiles (tw indexes tmap_x_stk / tmap_act_stk)
+  if (x_terms == 2 && avg <= 12) return {true, 16, 0, true};
+  if (x_terms == 2 && avg <= 24) return {true, 32, 1, true};
+  if (x_terms == 2 && avg <= 48) return {true, 64, 2, true};
   if (avg <= 24) return {true, 32, 0, false};
   if (avg <= 48) return {true, 64, 1, false};
   return {true, 128, 2, false};
@@ -348,9 +360,9 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   // W1 + SwiGLU: weights W1, activations x terms; writes act terms.
   p.mode = 1;
   p.b_terms = x_terms;
-  p.stages = tc_gemm_max_stages(tok, p.N, x_terms, L->smem_limit, N);
+  p.stages = tc_gemm_max_stages(tok, p.N, x_terms, L->smem_limit, N, tp.stacked);
   p.m_tiles = static_cast<int>((2 * L->fp + wrows - 1) / wrows);
-  p.w_row_blocks = static_cast<int>(2 * L->fp / 128);
+  p.w_row_pairs = static_cast<int>(w_sf_row_pairs(2 * L->fp));
   p.k_tiles = static_cast<int>(kc1);
   p.a_sf = L->w1sf;
   p.b_sf = w.xsf;
@@ -366,14 +378,14 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.act_sf_term_stride = static_cast<uint64_t>(w.row_blocks) * kc2 * kSfAtomBytes;
   p.act_kchunks = static_cast<int>(kc2);
   int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
-  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w1[tok ? 1 : 0], w.tmap_x[tp.tw], p, grid, st));
+  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w1[tok ? 1 : 0], tp.stacked ? w.tmap_x_stk[tp.tw] : w.tmap_x[tp.tw], p, grid, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
   // W2 + bias + route weight: weights W2, activations act terms; writes y_pair.
   p.mode = 2;
   p.b_terms = 2;
-  p.stages = tc_gemm_max_stages(tok, p.N, 2, L->smem_limit, N);
+  p.stages = tc_gemm_max_stages(tok, p.N, 2, L->smem_limit, N, tp.stacked);
   p.m_tiles = static_cast<int>((L->d + wrows - 1) / wrows);
-  p.w_row_blocks = static_cast<int>((L->d + 127) / 128);
+  p.w_row_pairs = static_cast<int>(w_sf_row_pairs(L->d));
   p.k_tiles = static_cast<int>(kc2);
   p.a_sf = L->w2sf;
   p.b_sf = w.asf;
@@ -386,7 +398,8 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.y_pair_bf16 = reinterpret_cast<__nv_bfloat16*>(w.y_pair);
   w.pair_dtype = MXMOE_BF16;
   grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
-  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], w.tmap_act[tp.tw], p, grid, st));
+  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tp.stacked ? w.tmap_act_stk[tp.tw] : w.tmap_act[tp.tw], p, grid,
+                          st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
   return MXMOE_OK;
 }
@@ -543,7 +556,7 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
   DeviceGuard g(L->cfg.device);
   const bool inter = (L->cfg.flags & MXMOE_FLAG_INTERLEAVED_GLU) != 0;
   const uint64_t kp1 = L->kp1, kp2 = L->kp2, kc1 = kp1 / kTileK, kc2 = kp2 / kTileK;
-  const uint64_t rows1 = 2 * fp, rb1 = rows1 / kRowBlock, rb2 = (d + kRowBlock - 1) / kRowBlock;
+  const uint64_t rows1 = 2 * fp;
   const uint64_t bpr1 = w1d->bpr, gpr1 = w1d->gpr, bpr2 = w2d->bpr, gpr2 = w2d->gpr;
 
   auto sf_byte = [](uint8_t s, int ue8) -> uint8_t {
@@ -551,7 +564,8 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
     return static_cast<uint8_t>(v < 0 ? 0 : (v > 255 ? 255 : v));
   };
 
-  std::vector<uint8_t> q1(E * rows1 * (kp1 / 2), 0), s1(E * rb1 * kc1 * kSfAtomBytes, 0);
+  const uint64_t rp1 = w_sf_row_pairs(static_cast<uint32_t>(rows1)), rp2 = w_sf_row_pairs(static_cast<uint32_t>(d));
+  std::vector<uint8_t> q1(E * rows1 * (kp1 / 2), 0), s1(E * rp1 * kc1 * kWSfPairBytes, 0);
   std::vector<float> bb1(E * rows1, 0.0f), src_b1(E * 2 * f);
   to_f32(b1, bias_dtype, E * 2 * f, src_b1.data());
   for (uint64_t e = 0; e < E; ++e)
@@ -560,21 +574,21 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
         const uint64_t src = inter ? 2 * j + half : half * f + j;
         const uint64_t dst = w1_packed_row(static_cast<uint32_t>(j), half);
         std::memcpy(&q1[(e * rows1 + dst) * (kp1 / 2)], &w1_blocks[(e * 2 * f + src) * bpr1], bpr1);
-        uint8_t* atoms = &s1[e * rb1 * kc1 * kSfAtomBytes];
+        uint8_t* atoms = &s1[e * rp1 * kc1 * kWSfPairBytes];
         for (uint64_t gi = 0; gi < gpr1; ++gi)
-          atoms[sf_offset(static_cast<uint32_t>(dst), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc1))] =
+          atoms[w_sf_offset(static_cast<uint32_t>(dst), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc1))] =
               sf_byte(w1_scales[(e * 2 * f + src) * gpr1 + gi], w1d->ue8_offset);
         bb1[e * rows1 + dst] = src_b1[e * 2 * f + src];
       }
-  std::vector<uint8_t> q2(E * d * (kp2 / 2), 0), s2(E * rb2 * kc2 * kSfAtomBytes, 0);
+  std::vector<uint8_t> q2(E * d * (kp2 / 2), 0), s2(E * rp2 * kc2 * kWSfPairBytes, 0);
   std::vector<float> bb2(E * d);
   to_f32(b2, bias_dtype, E * d, bb2.data());
   for (uint64_t e = 0; e < E; ++e)
     for (uint64_t c = 0; c < d; ++c) {
       std::memcpy(&q2[(e * d + c) * (kp2 / 2)], &w2_blocks[(e * d + c) * bpr2], bpr2);
-      uint8_t* atoms = &s2[e * rb2 * kc2 * kSfAtomBytes];
+      uint8_t* atoms = &s2[e * rp2 * kc2 * kWSfPairBytes];
       for (uint64_t gi = 0; gi < gpr2; ++gi)
-        atoms[sf_offset(static_cast<uint32_t>(c), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc2))] =
+        atoms[w_sf_offset(static_cast<uint32_t>(c), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc2))] =
             sf_byte(w2_scales[(e * d + c) * gpr2 + gi], w2d->ue8_offset);
     }
 

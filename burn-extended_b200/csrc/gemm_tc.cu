@@ -40,8 +40,8 @@ namespace {
 // per TMEM sub-partition, one per 128-column half of the accumulator).  The
 // last warp copies each stage's scale factors into TMEM, off the MMA thread.
 __host__ __device__ constexpr int num_threads(bool tok) { return tok ? 352 : 224; }
-__host__ __device__ constexpr int num_epi_threads(bool tok) { return tok ? 256 : 128; }
 __host__ __device__ constexpr int sf_warp(bool tok) { return tok ? 10 : 6; }
+__host__ __device__ constexpr int num_epi_threads(bool tok) { return tok ? 256 : 128; }
 constexpr int kMaxStages = 8;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kSfTmemBase = 256;  // scale factors live in columns 256.. (32 per stage)
@@ -58,13 +58,19 @@ struct SmemPlan {
 // Tokens-as-A loads only the PT (= pair tile) rows of each activation term;
 // the MMA still reads 128 rows, the rows past PT falling into the next buffer
 // of the same stage and only feeding accumulator rows that are discarded.
-__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms, int PT) {
+// Stacked tokens-as-A tiles hold both terms of PT pairs in 2 * PT rows.
+__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms, int PT, bool stacked) {
   SmemPlan s;
   if (!tok) {
     s.a_terms = 1;
     s.b_terms = terms;
     s.a_bytes = 128 * kTileK;
     s.b_bytes = static_cast<uint32_t>(N) * kTileK;
+  } else if (stacked) {
+    s.a_terms = 1;
+    s.b_terms = 1;
+    s.a_bytes = 2u * static_cast<uint32_t>(PT) * kTileK;
+    s.b_bytes = 256 * kTileK;
   } else {
     s.a_terms = terms;
     s.b_terms = 1;
@@ -114,7 +120,7 @@ __device__ __forceinline__ float swiglu_clamp(float g, float l, float alpha, flo
 __device__ __forceinline__ uint64_t act_sf_offset(const TcParams& p, int pos, int t, int kb) {
   if (p.stacked)
     return stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(t), static_cast<uint32_t>(kb),
-                             static_cast<uint32_t>(p.act_kchunks));
+                             static_cast<uint32_t>(p.act_kchunks), static_cast<uint32_t>(p.sf_rows));
   return t * p.act_sf_term_stride + sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(kb),
                                               static_cast<uint32_t>(p.act_kchunks),
                                               static_cast<uint32_t>(p.sf_rows));
@@ -123,10 +129,14 @@ __device__ __forceinline__ uint64_t act_sf_offset(const TcParams& p, int pos, in
 __device__ __forceinline__ void store_block_terms(const TcParams& p, int pos, int j0,
                                                   const uint32_t (&words)[kMaxTerms][8],
                                                   const uint8_t (&sbyte)[kMaxTerms]) {
-  const uint64_t off = static_cast<uint64_t>(pos) * p.act_kp + j0;
 #pragma unroll
   for (int t = 0; t < 2; ++t) {
-    uint4* dst = reinterpret_cast<uint4*>(p.act_codes + t * p.act_term_stride + off);
+    const uint64_t off =
+        p.stacked ? static_cast<uint64_t>(stacked_code_row(static_cast<uint32_t>(pos), static_cast<uint32_t>(t),
+                                                                       static_cast<uint32_t>(p.sf_rows))) *
+                            p.act_kp + j0
+                  : t * p.act_term_stride + static_cast<uint64_t>(pos) * p.act_kp + j0;
+    uint4* dst = reinterpret_cast<uint4*>(p.act_codes + off);
     dst[0] = make_uint4(words[t][0], words[t][1], words[t][2], words[t][3]);
     dst[1] = make_uint4(words[t][4], words[t][5], words[t][6], words[t][7]);
     p.act_sf[act_sf_offset(p, pos, t, j0 / 32)] = sbyte[t];
@@ -139,7 +149,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
                        const TcParams p) {
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms, p.sf_rows);
+  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms, p.sf_rows, kTok && p.stacked);
   const int S = p.stages;
   float* epi = reinterpret_cast<float*>(smem + S * plan.stage_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi) + epi_smem_bytes(kTok));
@@ -214,29 +224,28 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
           break;
         }
         uint8_t* sb = smem + stage * plan.stage_bytes;
-        uint8_t* w_s = kTok ? sb + terms * plan.a_bytes : sb;
+        uint8_t* w_s = kTok ? sb + plan.a_terms * plan.a_bytes : sb;
         uint8_t* x_s = kTok ? sb : sb + plan.a_bytes;
         const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
         uint8_t* sf = sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes;
         mbar_arrive_expect_tx(&full_bar[stage], tx);
         tma_load_3d(w_s, &tmap_w, &full_bar[stage], kt * kTileK, wt * (kTok ? 256 : 128), e);
         if (kTok && p.stacked) {
-          // 16-row boxes: pairs 16g..16g+15 of term q go to smem rows 32g + 16q
-          for (int term = 0; term < 2; ++term)
-            for (int gq = 0; gq < 4; ++gq)
-              tma_load_3d(x_s + (gq * 32 + 16 * term) * kTileK, &tmap_x, &full_bar[stage], kt * kTileK,
-                          row0 + gq * 16, term);
+          // the tile's stacked code rows (stacked_code_row) are consecutive:
+          // one box of 2 * PT rows of the flat code map
+          tma_load_3d(x_s, &tmap_x, &full_bar[stage], kt * kTileK, (row0 / PT) * 2 * PT, 0);
         } else {
           for (int term = 0; term < terms; ++term)
             tma_load_3d(x_s + term * x_stride, &tmap_x, &full_bar[stage], kt * kTileK, row0, term);
         }
         // scale atoms in smem: [weights x natoms_w][term 0 x natoms_x][term 1 ...]
-        for (int a = 0; a < natoms_w; ++a) {
-          int wa = wt * natoms_w + a;
-          if (wa >= p.w_row_blocks) wa = p.w_row_blocks - 1;  // rows past the end carry zero codes
-          bulk_load(sf + kSfAtomBytes * a,
-                    p.a_sf + ((static_cast<uint64_t>(e) * p.w_row_blocks + wa) * p.k_tiles + kt) * kSfAtomBytes,
-                    kSfAtomBytes, &full_bar[stage]);
+        // weight atoms: the tile's pair of 128-row atoms is adjacent (w_sf_offset);
+        // a 128-row weights-as-A tile takes its half
+        {
+          const int wp = kTok ? wt : wt / 2;
+          const uint64_t src = ((static_cast<uint64_t>(e) * p.w_row_pairs + wp) * p.k_tiles + kt) * kWSfPairBytes +
+                               (kTok ? 0 : (wt & 1) * kSfAtomBytes);
+          bulk_load(sf, p.a_sf + src, kSfAtomBytes * natoms_w, &full_bar[stage]);
         }
         if (kTok && p.stacked) {
           bulk_load(sf + kSfAtomBytes * natoms_w, p.b_sf + (rbx * p.k_tiles + kt) * kSfAtomBytes, kSfAtomBytes,
@@ -284,7 +293,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         }
         tc_fence_after();
         uint8_t* sb = smem + stage * plan.stage_bytes;
-        const uint32_t w_addr = smem_u32(kTok ? sb + terms * plan.a_bytes : sb);
+        const uint32_t w_addr = smem_u32(kTok ? sb + plan.a_terms * plan.a_bytes : sb);
         const uint32_t x_addr = smem_u32(kTok ? sb : sb + plan.a_bytes);
         const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
         const uint32_t col0 = kSfTmemBase + stage * 32;
@@ -384,13 +393,73 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         tc_fence_before();
         mbar_arrive(&tmem_empty[acc]);
         if (++acc == nacc) acc = 0;
-        int jrow = m;  // pair index within the tile
         if (p.stacked) {
-          // lanes 16..31 hold the lo-term rows of the pairs in lanes 0..15
+          // Lane L < 16 holds the hi-term row of pair sp*16 + L, lane L + 16 its
+          // lo-term row.  The two lanes swap partial sums so that each ends
+          // with hi + lo for half of the columns and finishes that half:
+          // W1 lower lane GLU units [0, 32) of this half (columns 0..31 and
+          // 64..95), upper lane units [32, 64); W2 lower lane columns 0..63,
+          // upper lane 64..127.
+          const bool upper = lane >= 16;
+          float g[64];
+          if (p.mode == 2) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i) v[i] += __shfl_down_sync(0xFFFFFFFFu, v[i], 16);
-          jrow = lane < 16 ? sp * 16 + lane : PT;
+            for (int j = 0; j < 64; ++j) {
+              const float recv = __shfl_xor_sync(0xFFFFFFFFu, upper ? v[j] : v[64 + j], 16);
+              g[j] = (upper ? v[64 + j] : v[j]) + recv;
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const int cl = j < 32 ? j : j + 32, cu = cl + 32;
+              const float recv = __shfl_xor_sync(0xFFFFFFFFu, upper ? v[cl] : v[cu], 16);
+              g[j] = (upper ? v[cu] : v[cl]) + recv;
+            }
+          }
+          const int jr = sp * 16 + (lane & 15);
+          if (jr >= n_valid) continue;
+          const int pos = pos0 + jr;
+          const int pair = __ldg(p.perm + pos);
+          if (p.mode == 2) {
+            const float w = __ldg(p.topk_w + pair);
+            const int cf0 = wt * 256 + half * 128 + (upper ? 64 : 0);
+            const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + cf0);
+            uint2* dst = reinterpret_cast<uint2*>(p.y_pair_bf16 + static_cast<uint64_t>(pos) * p.d + cf0);
+#pragma unroll
+            for (int q = 0; q < 16; ++q) {
+              if (cf0 + 4 * q < p.rows_valid) {
+                const float4 b4 = __ldg(bb + q);
+                const __nv_bfloat162 lo = __floats2bfloat162_rn(fmaf(b4.x, p.bias_mult, g[4 * q + 0]) * w,
+                                                                 fmaf(b4.y, p.bias_mult, g[4 * q + 1]) * w);
+                const __nv_bfloat162 hi = __floats2bfloat162_rn(fmaf(b4.z, p.bias_mult, g[4 * q + 2]) * w,
+                                                                 fmaf(b4.w, p.bias_mult, g[4 * q + 3]) * w);
+                dst[q] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+              }
+            }
+          } else {
+            const int unit0 = wt * 128 + half * 64 + (upper ? 32 : 0);  // GLU unit of g[0]
+            if (unit0 >= p.units) continue;
+            const float r = __ldg(p.rscale + pair / p.k);
+            const float4* bb =
+                reinterpret_cast<const float4*>(p.bias + bias_e + wt * 256 + half * 128 + (upper ? 32 : 0));
+            float a[32];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+              const float4 bg = __ldg(bb + q);       // GLU biases
+              const float4 bl = __ldg(bb + 16 + q);  // linear biases (64 columns later)
+              a[4 * q + 0] = swiglu_clamp(fmaf(g[4 * q + 0], r, bg.x), fmaf(g[32 + 4 * q + 0], r, bl.x), p.alpha, p.limit);
+              a[4 * q + 1] = swiglu_clamp(fmaf(g[4 * q + 1], r, bg.y), fmaf(g[32 + 4 * q + 1], r, bl.y), p.alpha, p.limit);
+              a[4 * q + 2] = swiglu_clamp(fmaf(g[4 * q + 2], r, bg.z), fmaf(g[32 + 4 * q + 2], r, bl.z), p.alpha, p.limit);
+              a[4 * q + 3] = swiglu_clamp(fmaf(g[4 * q + 3], r, bg.w), fmaf(g[32 + 4 * q + 3], r, bl.w), p.alpha, p.limit);
+            }
+            uint32_t words[kMaxTerms][8];
+            uint8_t sbyte[kMaxTerms];
+            quantize_block32(a, 2, words, sbyte);
+            store_block_terms(p, pos, unit0, words, sbyte);
+          }
+          continue;
         }
+        const int jrow = m;  // pair index within the tile
         const bool valid = jrow < n_valid;
         const int pos = pos0 + jrow;
         if (!valid) continue;
@@ -520,21 +589,21 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile) {
-  const SmemPlan plan = smem_plan(tokens_as_a, N, terms, pair_tile);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked) {
+  const SmemPlan plan = smem_plan(tokens_as_a, N, terms, pair_tile, tokens_as_a && stacked);
   return 1024 + static_cast<size_t>(stages) * plan.stage_bytes + epi_smem_bytes(tokens_as_a) +
          (3 * kMaxStages + 10) * sizeof(uint64_t);
 }
 
-int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile) {
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile, bool stacked) {
   int s = kMaxStages - 1;  // 7 stages x 32 scale columns fit above column 256
-  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s, pair_tile) > smem_limit) --s;
+  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s, pair_tile, stacked) > smem_limit) --s;
   return s;
 }
 
 cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
                            const TcParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages, p.sf_rows);
+  const size_t smem = tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages, p.sf_rows, p.stacked != 0);
   if (tokens_as_a) {
     cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<true>), smem);
     if (st != cudaSuccess) return st;

@@ -763,13 +763,18 @@ __global__ void __launch_bounds__(256, 3)
       for (int q = 0; q < kMaxTerms; ++q) {
         if (q >= terms) break;
         if (active) {
-          uint4* dst = reinterpret_cast<uint4*>(codes + q * term_stride + off);
+          uint4* dst = reinterpret_cast<uint4*>(
+              codes + (stacked ? static_cast<uint64_t>(stacked_code_row(static_cast<uint32_t>(pos[s]),
+                                                                        static_cast<uint32_t>(q),
+                                                                        static_cast<uint32_t>(sf_rows))) * kp + b * 32
+                               : q * term_stride + off));
           dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
           dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
         }
         if ((lane & 3) == 0) {
           const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos[s]), static_cast<uint32_t>(q),
-                                                         static_cast<uint32_t>(b), static_cast<uint32_t>(kchunks))
+                                                         static_cast<uint32_t>(b), static_cast<uint32_t>(kchunks),
+                                                         static_cast<uint32_t>(sf_rows))
                                      : q * sf_term_stride + so;
           *reinterpret_cast<uint32_t*>(sf + o) = sword[q];
         }
@@ -880,7 +885,7 @@ __device__ __forceinline__ float w_value(const uint8_t* codes, const uint8_t* sf
                                          uint32_t row, uint32_t col) {
   const uint8_t byte = codes[row * row_bytes + (col >> 1)];
   const uint8_t nib = (col & 1) ? (byte >> 4) : (byte & 0x0F);
-  const int s = static_cast<int>(sfa[sf_offset(row, col / 32, kchunks)]) - 127;
+  const int s = static_cast<int>(sfa[w_sf_offset(row, col / 32, kchunks)]) - 127;
   return kFp4Lut[nib] * ldexpf(1.0f, s);
 }
 
@@ -897,7 +902,7 @@ __global__ void simt_w1_kernel(const void* __restrict__ x, int x_dtype, int d, i
   if (j >= fp) return;
   const uint64_t rows = 2ull * fp;
   const uint8_t* codes = w1q + static_cast<uint64_t>(e) * rows * (kp1 / 2);
-  const uint8_t* sfa = w1sf + static_cast<uint64_t>(e) * (rows / kRowBlock) * (kp1 / kTileK) * kSfAtomBytes;
+  const uint8_t* sfa = w1sf + static_cast<uint64_t>(e) * w_sf_row_pairs(static_cast<uint32_t>(rows)) * (kp1 / kTileK) * kWSfPairBytes;
   const uint32_t rg = w1_packed_row(j, 0), rl = w1_packed_row(j, 1);
   const float bg = b1[static_cast<uint64_t>(e) * rows + rg];
   const float bl = b1[static_cast<uint64_t>(e) * rows + rl];
@@ -932,9 +937,8 @@ __global__ void simt_w2_kernel(const float* __restrict__ act, int fp, int d, int
   const int c = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (c >= d) return;
-  const uint64_t row_blocks = (d + kRowBlock - 1) / kRowBlock;
   const uint8_t* codes = w2q + static_cast<uint64_t>(e) * d * (kp2 / 2);
-  const uint8_t* sfa = w2sf + static_cast<uint64_t>(e) * row_blocks * (kp2 / kTileK) * kSfAtomBytes;
+  const uint8_t* sfa = w2sf + static_cast<uint64_t>(e) * w_sf_row_pairs(static_cast<uint32_t>(d)) * (kp2 / kTileK) * kWSfPairBytes;
   const float bb = b2[static_cast<uint64_t>(e) * d + c] * bias_mult;
   const int p0 = poff[e], cnt = counts[e];
   for (int i = 0; i < cnt; ++i) {

@@ -11,10 +11,14 @@
 //   scales    E8M0 with the file offset removed, stored as 512-byte atoms that
 //             the MMA's scale-factor TMEM layout reads directly:
 //             atom (row block of 128, k chunk of 4 x 32 columns);
-//             byte (r % 32) * 16 + (r / 32 % 4) * 4 + (kb % 4).
+//             byte (r % 32) * 16 + (r / 32 % 4) * 4 + (kb % 4).  The two
+//             atoms of one 256-row tile and k chunk are adjacent
+//             (w_sf_offset), so a pipeline stage fetches them in one copy.
 // Activations (per forward, rows = routed (token, expert) pairs sorted by
 // expert, every expert segment padded to a multiple of 128 rows):
-//   codes     [2 terms][rows][Kp] E4M3 (value = hi + lo, two block-scaled terms)
+//   codes     [2 terms][rows][Kp] E4M3 (value = hi + lo, two block-scaled terms);
+//             stacked tiles keep both terms of a tile in consecutive rows
+//             instead (stacked_code_row)
 //   scales    [terms][rows/R][Kp/128] atoms, same byte order as weights, with
 //             R = min(N, 128) rows per atom for tile width N.
 #pragma once
@@ -49,14 +53,35 @@ __host__ __device__ inline uint64_t sf_offset(uint32_t row, uint32_t kb, uint32_
          sf_atom_byte(row % block_rows, kb % 4);
 }
 
-// Stacked activation scales (tiles of 64 pairs, two terms in one 128-row MMA
-// operand): one atom per 64 rows and k chunk holding both terms; pair j of
-// the tile at atom row (j / 16) * 32 + j % 16 + 16 * term, so every 32-lane
-// TMEM sub-partition carries 16 pairs' hi rows followed by their lo rows.
-__host__ __device__ inline uint64_t stacked_sf_offset(uint32_t row, uint32_t term, uint32_t kb, uint32_t k_chunks) {
-  const uint32_t j = row % 64u;
-  const uint32_t r = (j / 16u) * 32u + j % 16u + 16u * term;
-  return (static_cast<uint64_t>(row / 64u) * k_chunks + kb / 4) * kSfAtomBytes + sf_atom_byte(r, kb % 4);
+// Stacked activation tiles of PT pairs (PT = 16, 32 or 64), both terms in one
+// 128-row MMA operand: pair j of the tile, term t, is operand row
+// (j / 16) * 32 + 16 * t + j % 16, so every 32-lane TMEM sub-partition
+// carries 16 pairs' hi rows followed by their lo rows (rows from 2 * PT on
+// feed discarded accumulator rows).  Scales: one atom per tile and k chunk,
+// operand row r at sf_atom_byte(r, kb).
+__host__ __device__ inline uint32_t stacked_operand_row(uint32_t j, uint32_t term) {
+  return (j / 16u) * 32u + 16u * term + j % 16u;
+}
+__host__ __device__ inline uint64_t stacked_sf_offset(uint32_t row, uint32_t term, uint32_t kb, uint32_t k_chunks,
+                                                      uint32_t pt) {
+  return (static_cast<uint64_t>(row / pt) * k_chunks + kb / 4) * kSfAtomBytes +
+         sf_atom_byte(stacked_operand_row(row % pt, term), kb % 4);
+}
+
+// Weight scales: byte offset of (row, k block) in [row_pairs][k_chunks][2][512]
+// (row pair = 256 rows; the rows' 128-row block picks the atom of the pair).
+constexpr int kWSfPairBytes = 2 * kSfAtomBytes;
+__host__ __device__ inline uint32_t w_sf_row_pairs(uint32_t rows) { return (rows + 255u) / 256u; }
+__host__ __device__ inline uint64_t w_sf_offset(uint32_t row, uint32_t kb, uint32_t k_chunks) {
+  return (static_cast<uint64_t>(row / 256u) * k_chunks + kb / 4) * kWSfPairBytes + ((row / 128u) & 1u) * kSfAtomBytes +
+         sf_atom_byte(row % 128u, kb % 4);
+}
+
+// Stacked activation codes: pair pos, term t -> code row in one buffer of
+// 2 x rows rows: a PT-pair tile occupies 2 * PT consecutive rows in operand
+// order, so one TMA box of 2 * PT rows loads it.
+__host__ __device__ inline uint32_t stacked_code_row(uint32_t pos, uint32_t term, uint32_t pt) {
+  return (pos / pt) * (2u * pt) + stacked_operand_row(pos % pt, term);
 }
 
 }  // namespace mxmoe

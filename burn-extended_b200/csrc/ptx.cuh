@@ -10,6 +10,7 @@ namespace mxmoe {
 // Every device-side wait gives up after this long and raises an error code in
 // the layer's status word instead of spinning forever.
 constexpr unsigned long long kWaitTimeoutNs = 2000ull * 1000ull * 1000ull;  // 2 s
+constexpr unsigned long long kErrPollAfterNs = 20ull * 1000ull;  // waits older than 20 us also poll *err
 
 enum DeviceError : int {
   kDevOk = 0,
@@ -61,19 +62,23 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // unless another role already did) when the barrier did not flip within the
 // timeout, or when *err was already raised by someone else.  err may be null
 // (shutdown drains), in which case nothing is recorded.
+// The poll loop touches no global memory while the wait is young: a global
+// load there would delay noticing the flip by a memory round trip.  Only
+// waits older than kErrPollAfterNs also look at *err.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 32; ++i)
+    for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(addr, parity)) return true;
-    if (err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    const unsigned long long dt = global_timer_ns() - t0;
+    if (dt > kWaitTimeoutNs) {
       if (err != nullptr) atomicCAS(err, 0, code);
       return false;
     }
+    if (dt > kErrPollAfterNs && err != nullptr && *reinterpret_cast<volatile int*>(err) != 0) return false;
   }
 }
 

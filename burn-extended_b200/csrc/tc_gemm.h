@@ -12,7 +12,7 @@ struct TcParams {
   int mode;      // 1 = W1 + SwiGLU (writes act codes), 2 = W2 + bias + route weight (writes y_pair)
   int N;         // weights-as-A: routed pairs per tile (32, 64, 128); tokens-as-A: 256 weight rows
   int m_tiles;   // weight tiles per expert (128 rows weights-as-A, 256 rows tokens-as-A)
-  int w_row_blocks;  // 128-row scale atoms per expert of the weight operand
+  int w_row_pairs;   // 256-row scale-atom pairs per expert of the weight operand (w_sf_offset)
   int units;     // W1: GLU units written to the activation operand (f padded to 64)
   int k_tiles;   // K / 128
   int E;         // experts held by this layer
@@ -46,8 +46,8 @@ struct TcParams {
   int* err;                 // device status word (0 = ok)
 };
 
-size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile);
-int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked);
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile, bool stacked);
 // tmap_w: weight codes (box 128 rows weights-as-A, 256 rows tokens-as-A);
 // tmap_x: activation terms (box = pairs per tile rows).
 cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
