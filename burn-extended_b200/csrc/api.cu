@@ -164,6 +164,7 @@ struct Workspace {
   float* act_f32 = nullptr;// [rows][fp] (SIMT path only)
   int32_t* local_idx = nullptr; // [cap_pairs] local expert ids (expert-parallel receive side)
   int32_t* perm_scratch = nullptr; // multi-block permutation (permute_scratch_ints)
+  uint32_t* ret_slot = nullptr;    // [cap_pairs] expert-parallel return slots of received pairs
   int pair_dtype = MXMOE_F32;   // element type the last run_experts wrote y_pair in
   CUtensorMap tmap_x[kNumTileWidths];
   CUtensorMap tmap_act[kNumTileWidths];
@@ -206,6 +207,7 @@ void free_workspace(Workspace& w) {
   dfree(w.ntile_prefix); dfree(w.perm_p); dfree(w.inv_p);
   dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
   dfree(w.local_idx);
+  dfree(w.ret_slot);
   dfree(w.perm_scratch);
   w.cap_tokens = w.cap_pairs = w.rows = w.row_blocks = 0;
 }
@@ -246,6 +248,7 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   TRY(dalloc(&w.perm_p, w.rows));
   TRY(dalloc(&w.inv_p, cap_p));
   TRY(dalloc(&w.local_idx, cap_p));
+  TRY(dalloc(&w.ret_slot, cap_p));
   const size_t pscr = permute_scratch_ints(static_cast<int>(cap_p), static_cast<int>(Et));
   TRY(dalloc(&w.perm_scratch, pscr));
   CUDA_TRY(cudaMemset(w.perm_scratch, 0, pscr * sizeof(int32_t)));
@@ -314,7 +317,8 @@ int x_terms_for(const mxmoe_layer* L, int x_dtype) {
 // Expert FFN over already-routed pairs: quantize -> W1 -> W2 (or the SIMT
 // pair) -> y_pair.  Uses ws.poff / counts / ntile_prefix / perm_p / inv_p.
 int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
-                const float* route_w, const TilePlan& tp, int x_terms, cudaStream_t st) {
+                const float* route_w, const TilePlan& tp, int x_terms, cudaStream_t st,
+                void* const* ret_ptrs = nullptr, const uint32_t* ret_slot = nullptr) {
   Workspace& w = L->ws;
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
   const int N = tp.pair_tile;
@@ -396,6 +400,8 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.bias_mult = bias_mult;
   p.y_pair = w.y_pair;
   p.y_pair_bf16 = reinterpret_cast<__nv_bfloat16*>(w.y_pair);
+  p.ret_ptrs = ret_ptrs;
+  p.ret_slot = ret_slot;
   w.pair_dtype = MXMOE_BF16;
   grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
   CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tp.stacked ? w.tmap_act_stk[tp.tw] : w.tmap_act[tp.tw], p, grid,
@@ -920,6 +926,97 @@ int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_
     return fail(MXMOE_ERR_INVALID_ARG, "x, pair_out and y must be 16-byte aligned");
   CUDA_TRY(launch_combine(x, x_dtype, pair_out, pair_dtype, topk_idx, inv, n_tokens, d_model, k, residual, y, y_dtype,
                           as_stream(stream)));
+  return MXMOE_OK;
+}
+
+// ------------------------------------------------------------------ expert-parallel over peer memory
+int mxmoe_ipc_alloc(size_t bytes, int device, void** ptr, void* handle) {
+  if (!ptr || !handle || bytes == 0) return fail(MXMOE_ERR_INVALID_ARG, "bad ipc allocation request");
+  DeviceGuard g(device);
+  *ptr = nullptr;
+  CUDA_TRY(cudaMalloc(ptr, bytes));
+  CUDA_TRY(cudaMemset(*ptr, 0, bytes));
+  cudaIpcMemHandle_t h;
+  CUDA_TRY(cudaIpcGetMemHandle(&h, *ptr));
+  static_assert(sizeof(cudaIpcMemHandle_t) == MXMOE_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  return MXMOE_OK;
+}
+
+int mxmoe_ipc_free(void* ptr, int device) {
+  if (!ptr) return MXMOE_OK;
+  DeviceGuard g(device);
+  CUDA_TRY(cudaFree(ptr));
+  return MXMOE_OK;
+}
+
+int mxmoe_ipc_open(const void* handle, int device, void** peer_ptr) {
+  if (!handle || !peer_ptr) return fail(MXMOE_ERR_INVALID_ARG, "null ipc handle");
+  DeviceGuard g(device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  CUDA_TRY(cudaIpcOpenMemHandle(peer_ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return MXMOE_OK;
+}
+
+int mxmoe_ipc_close(void* peer_ptr, int device) {
+  if (!peer_ptr) return MXMOE_OK;
+  DeviceGuard g(device);
+  CUDA_TRY(cudaIpcCloseMemHandle(peer_ptr));
+  return MXMOE_OK;
+}
+
+int mxmoe_dispatch_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_t d_model, uint32_t k,
+                         const int32_t* perm, const float* rscale, const int32_t* topk_idx, const float* topk_w,
+                         const int32_t* offsets, uint32_t experts_per_rank, uint32_t world, uint32_t rank,
+                         const int32_t* counts, void* const* peer_x, uint32_t* const* peer_meta,
+                         uint32_t recv_cap, int* err, void* stream) {
+  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
+  if (P == 0) return MXMOE_OK;
+  if (!x || !perm || !rscale || !topk_idx || !topk_w || !offsets || !counts || !peer_x || !peer_meta)
+    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (world == 0 || rank >= world || world > 256 || experts_per_rank == 0)
+    return fail(MXMOE_ERR_INVALID_ARG, "bad world %u / rank %u", world, rank);
+  if (P >= (1u << 24)) return fail(MXMOE_ERR_TOO_LARGE, "too many pairs for return slots: %llu", (unsigned long long)P);
+  if (d_model % 32 != 0) return fail(MXMOE_ERR_UNSUPPORTED, "d_model must be a multiple of 32");
+  if (!aligned16(x)) return fail(MXMOE_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  CUDA_TRY(launch_dispatch_pairs(x, x_dtype, d_model, k, static_cast<int>(P), perm, rscale, topk_idx, topk_w, offsets,
+                                 experts_per_rank, world, rank, counts, peer_x, peer_meta, recv_cap, err,
+                                 as_stream(stream)));
+  return MXMOE_OK;
+}
+
+int mxmoe_forward_local_meta(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, const uint32_t* meta,
+                             uint32_t n_pairs, void* const* ret_ptrs, void* stream) {
+  TRY(check_layer(L));
+  if (!L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "experts not uploaded");
+  if (n_pairs == 0) return MXMOE_OK;
+  if (!xr || !meta || !ret_ptrs) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(xr) || !aligned16(meta)) return fail(MXMOE_ERR_INVALID_ARG, "xr and meta must be 16-byte aligned");
+  if (L->cfg.flags & MXMOE_FLAG_SIMT) return fail(MXMOE_ERR_UNSUPPORTED, "peer return needs the tensor-core path");
+  DeviceGuard g(L->cfg.device);
+  TRY(ensure_workspace(L, n_pairs, 1));
+  Workspace& w = L->ws;
+  cudaStream_t st = as_stream(stream);
+  const int xt = x_terms_for(L, xr_dtype);
+  const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt);
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  // profiled stages: split + localize in the "router" slot, no combine
+  L->profile_valid = false;
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
+  CUDA_TRY(launch_split_meta(meta, static_cast<int>(n_pairs), w.rscale, w.topk_idx, w.topk_w, w.ret_slot, st));
+  CUDA_TRY(launch_localize(w.topk_idx, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
+                           static_cast<int>(L->e_count), w.local_idx, L->err, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
+  CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, tp.pair_tile, nullptr,
+                          nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st,
+                          w.perm_scratch));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
+  TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, w.rscale, w.topk_w, tp, xt, st, ret_ptrs, w.ret_slot));
+  if (L->profiling) {
+    CUDA_TRY(cudaEventRecord(L->ev[6], st));
+    L->profile_valid = true;
+  }
   return MXMOE_OK;
 }
 

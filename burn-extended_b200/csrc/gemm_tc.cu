@@ -143,6 +143,28 @@ __device__ __forceinline__ void store_block_terms(const TcParams& p, int pos, in
   }
 }
 
+// W2 output row of a pair: this GPU's y_pair (row pos) or, for the
+// expert-parallel return, the source GPU's buffer at the pair's return slot.
+__device__ __forceinline__ __nv_bfloat16* w2_out_row(const TcParams& p, int pos, int pair) {
+  if (p.ret_ptrs != nullptr) {
+    const uint32_t slot = __ldg(p.ret_slot + pair);
+    return static_cast<__nv_bfloat16*>(p.ret_ptrs[slot >> 24]) + static_cast<uint64_t>(slot & 0xFFFFFFu) * p.d;
+  }
+  return p.y_pair_bf16 + static_cast<uint64_t>(pos) * p.d;
+}
+
+// 8 outputs (bias, route weight) -> 8 bf16 in one 16-byte store.
+__device__ __forceinline__ void store_w2_8(__nv_bfloat16* dst, const float* v, float4 b0, float4 b1, float bm,
+                                           float w) {
+  const __nv_bfloat162 a = __floats2bfloat162_rn(fmaf(b0.x, bm, v[0]) * w, fmaf(b0.y, bm, v[1]) * w);
+  const __nv_bfloat162 b = __floats2bfloat162_rn(fmaf(b0.z, bm, v[2]) * w, fmaf(b0.w, bm, v[3]) * w);
+  const __nv_bfloat162 c = __floats2bfloat162_rn(fmaf(b1.x, bm, v[4]) * w, fmaf(b1.y, bm, v[5]) * w);
+  const __nv_bfloat162 e = __floats2bfloat162_rn(fmaf(b1.z, bm, v[6]) * w, fmaf(b1.w, bm, v[7]) * w);
+  *reinterpret_cast<uint4*>(dst) =
+      make_uint4(*reinterpret_cast<const uint32_t*>(&a), *reinterpret_cast<const uint32_t*>(&b),
+                 *reinterpret_cast<const uint32_t*>(&c), *reinterpret_cast<const uint32_t*>(&e));
+}
+
 template <bool kTok>
 __global__ void __launch_bounds__(num_threads(kTok), 1)
     tc_moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
@@ -424,18 +446,11 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
             const float w = __ldg(p.topk_w + pair);
             const int cf0 = wt * 256 + half * 128 + (upper ? 64 : 0);
             const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + cf0);
-            uint2* dst = reinterpret_cast<uint2*>(p.y_pair_bf16 + static_cast<uint64_t>(pos) * p.d + cf0);
+            __nv_bfloat16* dst = w2_out_row(p, pos, pair) + cf0;
 #pragma unroll
-            for (int q = 0; q < 16; ++q) {
-              if (cf0 + 4 * q < p.rows_valid) {
-                const float4 b4 = __ldg(bb + q);
-                const __nv_bfloat162 lo = __floats2bfloat162_rn(fmaf(b4.x, p.bias_mult, g[4 * q + 0]) * w,
-                                                                 fmaf(b4.y, p.bias_mult, g[4 * q + 1]) * w);
-                const __nv_bfloat162 hi = __floats2bfloat162_rn(fmaf(b4.z, p.bias_mult, g[4 * q + 2]) * w,
-                                                                 fmaf(b4.w, p.bias_mult, g[4 * q + 3]) * w);
-                dst[q] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
-              }
-            }
+            for (int q = 0; q < 8; ++q)
+              if (cf0 + 8 * q < p.rows_valid)
+                store_w2_8(dst + 8 * q, g + 8 * q, __ldg(bb + 2 * q), __ldg(bb + 2 * q + 1), p.bias_mult, w);
           } else {
             const int unit0 = wt * 128 + half * 64 + (upper ? 32 : 0);  // GLU unit of g[0]
             if (unit0 >= p.units) continue;
@@ -468,18 +483,11 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
           const float w = __ldg(p.topk_w + pair);
           const int cf0 = wt * 256 + half * 128;  // output feature of v[0]
           const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + cf0);
-          uint2* dst = reinterpret_cast<uint2*>(p.y_pair_bf16 + static_cast<uint64_t>(pos) * p.d + cf0);
+          __nv_bfloat16* dst = w2_out_row(p, pos, pair) + cf0;
 #pragma unroll
-          for (int q = 0; q < 32; ++q) {
-            if (cf0 + 4 * q < p.rows_valid) {
-              const float4 b4 = __ldg(bb + q);
-              const __nv_bfloat162 lo = __floats2bfloat162_rn(fmaf(b4.x, p.bias_mult, v[4 * q + 0]) * w,
-                                                               fmaf(b4.y, p.bias_mult, v[4 * q + 1]) * w);
-              const __nv_bfloat162 hi = __floats2bfloat162_rn(fmaf(b4.z, p.bias_mult, v[4 * q + 2]) * w,
-                                                               fmaf(b4.w, p.bias_mult, v[4 * q + 3]) * w);
-              dst[q] = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
-            }
-          }
+          for (int q = 0; q < 16; ++q)
+            if (cf0 + 8 * q < p.rows_valid)
+              store_w2_8(dst + 8 * q, v + 8 * q, __ldg(bb + 2 * q), __ldg(bb + 2 * q + 1), p.bias_mult, w);
         } else {
           const int unit0 = wt * 128 + half * 64;  // GLU unit of v[0]
           if (unit0 >= p.units) continue;

@@ -679,103 +679,130 @@ __global__ void __launch_bounds__(kPermChunkThreads)
 // Gathers each routed pair's token row into its padded expert-sorted position
 // and writes it as `terms` block-scaled E4M3 terms (two reproduce bf16 input
 // with unit gain exactly; three are used for f32 input or a non-unit gain).
-// One thread per (token, 32-column block): reads 32 inputs, quantizes them on
-// its own once and writes the codes (16-byte stores) and scale bytes to the
-// positions of all k pairs of the token.
-__global__ void __launch_bounds__(256, 3)
+// Each token block is quantized once and written to the positions of all k
+// pairs of the token.
+// Warp per (token, octet of eight 32-column blocks); the four lanes of a
+// quad share one block, eight columns (16 bytes of bf16) each, so loads and
+// code stores are contiguous across the warp.  The block's per-term scale
+// comes from a max over the quad; the arithmetic per element is
+// quantize_block32's.  Lanes of blocks past d / 32 contribute zero scale
+// bytes (the K padding) and store no codes.
+__global__ void __launch_bounds__(256)
     quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                           const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
                           int terms, uint8_t* codes, uint64_t term_stride, int kp, uint8_t* sf,
                           uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked) {
-  // items (t, b) with b padded to a multiple of 4, so the four lanes of one
-  // aligned lane quad hold the four 32-blocks of one scale word; lanes with
-  // b >= d / 32 only contribute zero scale bytes (the K padding)
   const int nb = d / 32;
-  const int nbp = (nb + 3) & ~3;
-  const uint64_t items = static_cast<uint64_t>(n) * nbp;
+  const int noct = (nb + 7) / 8;
+  const uint64_t items = static_cast<uint64_t>(n) * noct;
   const int lane = threadIdx.x & 31;
-  const uint64_t stride = static_cast<uint64_t>(gridDim.x) * blockDim.x;
-  // every lane of a warp runs the same number of iterations (the shuffles
-  // below need the whole warp): the loop bound is rounded up to the stride
-  const uint64_t it_end = (items + stride - 1) / stride * stride;
-  for (uint64_t it = blockIdx.x * static_cast<uint64_t>(blockDim.x) + threadIdx.x; it < it_end; it += stride) {
-    const bool in = it < items;
-    const int t = in ? static_cast<int>(it / nbp) : 0;
-    const int b = in ? static_cast<int>(it - static_cast<uint64_t>(t) * nbp) : nb;
+  const int qtr = lane & 3, lb = lane >> 2;
+  const uint64_t wstride = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (uint64_t it = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += wstride) {
+    const int t = static_cast<int>(it / noct);
+    const int b = static_cast<int>(it - static_cast<uint64_t>(t) * noct) * 8 + lb;
     const bool active = b < nb;
-    int pos[kMaxTopK];
-#pragma unroll
-    for (int s = 0; s < kMaxTopK; ++s) pos[s] = in && s < k ? __ldg(inv_p + static_cast<uint64_t>(t) * k + s) : 0;
-    float v[32];
+    const int c0 = b * 32 + qtr * 8;
+    float v[8];
     if (!active) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = 0.0f;
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
     } else if (x_dtype == 1) {
-      const uint4* xs =
-          reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + static_cast<uint64_t>(t) * d + b * 32);
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
+                                                            static_cast<uint64_t>(t) * d + c0));
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const uint4 u = __ldg(xs + q);
-        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          v[q * 8 + 2 * h] = __uint_as_float(w4[h] << 16);
-          v[q * 8 + 2 * h + 1] = __uint_as_float(w4[h] & 0xFFFF0000u);
-        }
+      for (int h = 0; h < 4; ++h) {
+        v[2 * h] = __uint_as_float(w4[h] << 16);
+        v[2 * h + 1] = __uint_as_float(w4[h] & 0xFFFF0000u);
       }
     } else {
-      const float4* xs =
-          reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<uint64_t>(t) * d + b * 32);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const float4 u = __ldg(xs + q);
-        v[4 * q] = u.x; v[4 * q + 1] = u.y; v[4 * q + 2] = u.z; v[4 * q + 3] = u.w;
-      }
+      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<uint64_t>(t) * d + c0);
+      const float4 a = __ldg(xs), c = __ldg(xs + 1);
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
     }
     if (!gamma_is_one && active) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + b * 32 + i));
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
     }
-    uint32_t words[kMaxTerms][8];
-    uint8_t sbyte[kMaxTerms];
-    quantize_block32(v, terms, words, sbyte);
-    if (!active) {
-#pragma unroll
-      for (int q = 0; q < kMaxTerms; ++q) sbyte[q] = 0;
-    }
-    // the quad's four scale bytes as one word, stored by the quad's first lane
+    uint32_t words[kMaxTerms][2];
     uint32_t sword[kMaxTerms];
 #pragma unroll
     for (int q = 0; q < kMaxTerms; ++q) {
-      uint32_t w = static_cast<uint32_t>(sbyte[q]) << (8 * (lane & 3));
-      w |= __shfl_xor_sync(0xFFFFFFFFu, w, 1);
-      w |= __shfl_xor_sync(0xFFFFFFFFu, w, 2);
-      sword[q] = w;
+      words[q][0] = words[q][1] = 0;
+      sword[q] = 0;
+      if (q < terms) {
+        float amax = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+        const int s = e4m3_block_exp(amax);
+        const bool fast = (s > -126) && (s < 127);
+        const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
+        const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
+#pragma unroll
+        for (int w = 0; w < 2; ++w) {
+          uint32_t word = 0;
+#pragma unroll
+          for (int hp = 0; hp < 2; ++hp) {
+            const int i = w * 4 + hp * 2;
+            float a, bb;
+            if (fast) {
+              a = v[i] * inv;
+              bb = v[i + 1] * inv;
+            } else {
+              a = ldexpf(v[i], -s);
+              bb = ldexpf(v[i + 1], -s);
+            }
+            const uint32_t c = cvt_e4m3x2(a, bb);
+            float da, db;
+            dec_e4m3x2(c, da, db);
+            if (fast) {
+              v[i] = fmaf(-da, back, v[i]);
+              v[i + 1] = fmaf(-db, back, v[i + 1]);
+            } else {
+              v[i] = v[i] - ldexpf(da, s);
+              v[i + 1] = v[i + 1] - ldexpf(db, s);
+            }
+            word |= c << (16 * hp);
+          }
+          words[q][w] = word;
+        }
+        // the scale words of four consecutive blocks (quads lb & ~3 .. +3)
+        uint32_t sw = active ? static_cast<uint32_t>(s + 127) << (8 * (lb & 3)) : 0u;
+        sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 4);
+        sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 8);
+        sword[q] = sw;
+      }
     }
-    if (!in) continue;
+    // one lane per group of four blocks stores the group's scale word; a group
+    // wholly past d / 32 would land in the next row block's atom and stores nothing
+    const bool sf_lane = qtr == 0 && (lb & 3) == 0 && active;
 #pragma unroll
     for (int s = 0; s < kMaxTopK; ++s) {
       if (s >= k) break;
-      const uint64_t off = static_cast<uint64_t>(pos[s]) * kp + b * 32;
-      const uint64_t so = sf_offset(static_cast<uint32_t>(pos[s]), static_cast<uint32_t>(b),
-                                    static_cast<uint32_t>(kchunks), static_cast<uint32_t>(sf_rows));
+      const int pos = __ldg(inv_p + static_cast<uint64_t>(t) * k + s);
 #pragma unroll
       for (int q = 0; q < kMaxTerms; ++q) {
         if (q >= terms) break;
         if (active) {
-          uint4* dst = reinterpret_cast<uint4*>(
-              codes + (stacked ? static_cast<uint64_t>(stacked_code_row(static_cast<uint32_t>(pos[s]),
-                                                                        static_cast<uint32_t>(q),
-                                                                        static_cast<uint32_t>(sf_rows))) * kp + b * 32
-                               : q * term_stride + off));
-          dst[0] = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
-          dst[1] = make_uint4(words[q][4], words[q][5], words[q][6], words[q][7]);
+          const uint64_t row = stacked ? static_cast<uint64_t>(stacked_code_row(static_cast<uint32_t>(pos),
+                                                                                static_cast<uint32_t>(q),
+                                                                                static_cast<uint32_t>(sf_rows)))
+                                       : static_cast<uint64_t>(pos);
+          uint8_t* dst = codes + (stacked ? 0 : q * term_stride) + row * kp + c0;
+          *reinterpret_cast<uint2*>(dst) = make_uint2(words[q][0], words[q][1]);
         }
-        if ((lane & 3) == 0) {
-          const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos[s]), static_cast<uint32_t>(q),
+        if (sf_lane) {
+          const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
                                                          static_cast<uint32_t>(b), static_cast<uint32_t>(kchunks),
                                                          static_cast<uint32_t>(sf_rows))
-                                     : q * sf_term_stride + so;
+                                     : q * sf_term_stride + sf_offset(static_cast<uint32_t>(pos),
+                                                                      static_cast<uint32_t>(b),
+                                                                      static_cast<uint32_t>(kchunks),
+                                                                      static_cast<uint32_t>(sf_rows));
           *reinterpret_cast<uint32_t*>(sf + o) = sword[q];
         }
       }
@@ -878,6 +905,55 @@ __global__ void gather_pairs_kernel(const void* __restrict__ x, uint32_t row_byt
   const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + static_cast<uint64_t>(t) * row_bytes);
   uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(out_x) + static_cast<uint64_t>(q) * row_bytes);
   for (uint32_t i = lane; i < row_bytes / 16; i += 32) dst[i] = __ldg(src + i);
+}
+
+// Expert-parallel dispatch over peer memory (replaces gather + all-to-all):
+// warp per canonical position q (pairs sorted by expert, hence by owning
+// rank g = expert / experts_per_rank).  The pair's token row and its metadata
+// {bits of 1/rms, expert, bits of the route weight, return slot} go straight
+// into rank g's receive buffers at row base_g + (q - offsets[g * Epr]), where
+// base_g = pairs that lower ranks send to g (counts [src][dst]).  The return
+// slot (rank << 24 | q) tells the owner where to write the pair's output.
+__global__ void dispatch_pairs_kernel(const void* __restrict__ x, uint32_t row_bytes, int k, int P,
+                                      const int32_t* __restrict__ perm, const float* __restrict__ rscale,
+                                      const int32_t* __restrict__ topk_idx, const float* __restrict__ topk_w,
+                                      const int32_t* __restrict__ offsets, int epr, int world, int rank,
+                                      const int32_t* __restrict__ counts, void* const* __restrict__ peer_x,
+                                      uint32_t* const* __restrict__ peer_meta, uint32_t recv_cap, int* err) {
+  const int q = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (q >= P) return;
+  const int p = __ldg(perm + q);
+  const int t = p / k;
+  const int e = __ldg(topk_idx + p);
+  const int g = e / epr;
+  int base = 0;
+  for (int s = 0; s < rank; ++s) base += __ldg(counts + s * world + g);
+  const int row = base + (q - __ldg(offsets + g * epr));
+  if (g >= world || row < 0 || static_cast<uint32_t>(row) >= recv_cap) {  // inconsistent counts: write nothing
+    if (lane == 0 && err != nullptr) atomicCAS(err, 0, 8);
+    return;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(x) + static_cast<uint64_t>(t) * row_bytes);
+  uint4* dst = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_x[g]) + static_cast<uint64_t>(row) * row_bytes);
+  for (uint32_t i = lane; i < row_bytes / 16; i += 32) dst[i] = __ldg(src + i);
+  if (lane == 0)
+    reinterpret_cast<uint4*>(peer_meta[g])[row] =
+        make_uint4(__float_as_uint(__ldg(rscale + t)), static_cast<uint32_t>(e), __float_as_uint(__ldg(topk_w + p)),
+                   (static_cast<uint32_t>(rank) << 24) | static_cast<uint32_t>(q));
+  __threadfence_system();  // peer writes ordered before anything this thread's GPU does later
+}
+
+// Received metadata [R][4] -> per-pair arrays for the expert pipeline.
+__global__ void split_meta_kernel(const uint4* __restrict__ meta, int R, float* rscale, int32_t* expert,
+                                  float* weight, uint32_t* slot) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= R) return;
+  const uint4 m = __ldg(meta + i);
+  rscale[i] = __uint_as_float(m.x);
+  expert[i] = static_cast<int32_t>(m.y);
+  weight[i] = __uint_as_float(m.z);
+  slot[i] = m.w;
 }
 
 // ------------------------------------------------------------------ SIMT FFN
@@ -1062,10 +1138,10 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
                                   int sf_rows, int stacked, cudaStream_t st) {
-  const uint64_t items = static_cast<uint64_t>(n) * (((d / 32) + 3) & ~3);
+  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + 7) / 8);  // warps
   if (items == 0 || k == 0) return cudaSuccess;
-  const uint64_t blocks = (items + 255) / 256;
-  const int grid = static_cast<int>(blocks < 148 * 32 ? blocks : 148 * 32);
+  const uint64_t blocks = (items + 7) / 8;
+  const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
   quantize_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
                                               term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked);
   return cudaGetLastError();
@@ -1093,6 +1169,27 @@ cudaError_t launch_gather_pairs(const void* x, int x_dtype, int d, int k, int P,
   const uint32_t row_bytes = static_cast<uint32_t>(d) * (x_dtype == 0 ? 4u : 2u);
   gather_pairs_kernel<<<(P + 7) / 8, 256, 0, st>>>(x, row_bytes, k, P, perm, rscale, topk_idx, topk_w, out_x,
                                                    out_meta);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_dispatch_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
+                                  const float* rscale, const int32_t* topk_idx, const float* topk_w,
+                                  const int32_t* offsets, int experts_per_rank, int world, int rank,
+                                  const int32_t* counts, void* const* peer_x, uint32_t* const* peer_meta,
+                                  uint32_t recv_cap, int* err, cudaStream_t st) {
+  if (P == 0) return cudaSuccess;
+  const uint32_t row_bytes = static_cast<uint32_t>(d) * (x_dtype == 0 ? 4u : 2u);
+  dispatch_pairs_kernel<<<(P + 7) / 8, 256, 0, st>>>(x, row_bytes, k, P, perm, rscale, topk_idx, topk_w, offsets,
+                                                      experts_per_rank, world, rank, counts, peer_x, peer_meta,
+                                                      recv_cap, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
+                              uint32_t* slot, cudaStream_t st) {
+  if (R == 0) return cudaSuccess;
+  split_meta_kernel<<<(R + 255) / 256, 256, 0, st>>>(reinterpret_cast<const uint4*>(meta), R, rscale, expert, weight,
+                                                      slot);
   return cudaGetLastError();
 }
 

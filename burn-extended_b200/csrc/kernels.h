@@ -58,6 +58,13 @@ cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, 
 cudaError_t launch_gather_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
                                 const float* rscale, const int32_t* topk_idx, const float* topk_w, void* out_x,
                                 uint32_t* out_meta, cudaStream_t st);
+cudaError_t launch_dispatch_pairs(const void* x, int x_dtype, int d, int k, int P, const int32_t* perm,
+                                  const float* rscale, const int32_t* topk_idx, const float* topk_w,
+                                  const int32_t* offsets, int experts_per_rank, int world, int rank,
+                                  const int32_t* counts, void* const* peer_x, uint32_t* const* peer_meta,
+                                  uint32_t recv_cap, int* err, cudaStream_t st);
+cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
+                              uint32_t* slot, cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
                            const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
                            const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,

@@ -42,6 +42,12 @@ struct TcParams {
   int act_kchunks;
   float* y_pair;            // W2 output [rows][d] f32 (weights-as-A)
   __nv_bfloat16* y_pair_bf16;  // W2 output [rows][d] bf16 (tokens-as-A)
+  // Expert-parallel return (tokens-as-A W2): when set, the output of pair
+  // `pair` goes to row (ret_slot[pair] & 0xFFFFFF) of the bf16 buffer
+  // ret_ptrs[ret_slot[pair] >> 24] (a peer GPU's return buffer) instead of
+  // y_pair_bf16.
+  void* const* ret_ptrs;
+  const uint32_t* ret_slot;
   int d;
   int* err;                 // device status word (0 = ok)
 };

@@ -74,7 +74,16 @@ _SIGS = {
     "mxmoe_gather_pairs": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "mxmoe_forward_local": ([_vp, _vp, _i32, _vp, _vp, _vp, _u32, _vp, _i32, _vp], _i32),
     "mxmoe_combine": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _i32, _i32, _vp, _i32, _vp], _i32),
+    "mxmoe_ipc_alloc": ([ctypes.c_size_t, _i32, ctypes.POINTER(_vp), _vp], _i32),
+    "mxmoe_ipc_free": ([_vp, _i32], _i32),
+    "mxmoe_ipc_open": ([_vp, _i32, ctypes.POINTER(_vp)], _i32),
+    "mxmoe_ipc_close": ([_vp, _i32], _i32),
+    "mxmoe_dispatch_pairs": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp,
+                              _u32, _vp, _vp], _i32),
+    "mxmoe_forward_local_meta": ([_vp, _vp, _i32, _vp, _u32, _vp, _vp], _i32),
 }
+
+IPC_HANDLE_BYTES = 64
 
 _lib = None
 

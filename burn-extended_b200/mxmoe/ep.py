@@ -198,3 +198,215 @@ def build_cuda_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig]
     begin, count = shard_bounds(inp.E, world, rank)
     be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
     return ExpertParallelMoe(be, inp.E, world, rank, group)
+
+
+# ----------------------------------------------------------------------------
+# Expert parallelism over peer memory (NVLink / NVSwitch).  The source rank's
+# dispatch kernel writes every routed pair straight into the owning rank's
+# receive buffers; the owner's W2 epilogue writes each pair's output straight
+# into the source rank's return buffer (canonical order), so the step needs
+# no gather copy, no data all-to-all and no un-permute pass.  Two collective
+# barriers order the peer writes against their readers; the per-destination
+# pair counts travel in one small all-gather.
+
+class IpcBuffer:
+    """Device buffer of this rank that peers open through CUDA IPC."""
+
+    def __init__(self, nbytes: int, device: int):
+        import ctypes
+        from ._lib import IPC_HANDLE_BYTES, check, lib
+        self.device = device
+        self.nbytes = nbytes
+        self.ptr = ctypes.c_void_p()
+        self.handle = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+        check(lib().mxmoe_ipc_alloc(nbytes, device, ctypes.byref(self.ptr), self.handle))
+
+    def close(self):
+        from ._lib import lib
+        if self.ptr:
+            lib().mxmoe_ipc_free(self.ptr, self.device)
+            self.ptr = None
+
+
+def open_peer(handle: bytes, device: int) -> int:
+    import ctypes
+    from ._lib import check, lib
+    p = ctypes.c_void_p()
+    check(lib().mxmoe_ipc_open(ctypes.create_string_buffer(handle, len(handle)), device, ctypes.byref(p)))
+    return p.value
+
+
+def return_slot(rank: int, q: int) -> int:
+    """Return slot word of the pair at canonical position q of `rank`."""
+    return (rank << 24) | q
+
+
+def receive_rows(counts, world: int, src: int, dst: int, begin: int, end: int):
+    """Rows [row0, row1) of dst's receive buffer that src fills with its
+    canonical positions [begin, end) (its pairs for dst's experts);
+    counts[s][g] = pairs s sends to g."""
+    row0 = sum(counts[s][dst] for s in range(src))
+    return row0, row0 + (end - begin)
+
+
+class PeerExpertParallelMoe:
+    """One rank of the expert-parallel layer over peer memory."""
+
+    # rms, router logits, top-k, permute x2, dispatch, split meta, localize,
+    # permute x2, quantize, W1, W2, combine
+    launches_per_step = 14
+
+    def __init__(self, backend: CudaExpertBackend, world: int, rank: int, max_tokens: int, x_dtype=None,
+                 group=None, peers=None):
+        """peers: optional list of (recv_x, recv_meta, ret) device pointers
+        per rank, used instead of the IPC exchange (ranks emulated in one
+        process on one GPU)."""
+        import torch
+        self.torch = torch
+        self.backend = backend
+        self.world, self.rank, self.group = world, rank, group
+        cfg = backend.cfg
+        self.d, self.k, self.E = cfg.d_model, cfg.experts_per_token, cfg.num_experts
+        if self.E % world:
+            raise ValueError(f"{self.E} experts do not split over {world} ranks")
+        self.Eg = self.E // world
+        self.max_tokens = max_tokens
+        self.x_dtype = x_dtype or torch.bfloat16
+        elem = torch.tensor([], dtype=self.x_dtype).element_size()
+        dev = backend.device
+        self.dev_index = dev.index or 0
+        cap_local = max_tokens * self.k
+        self.recv_cap = world * cap_local  # every pair of every rank could target one rank
+        self.own = None
+        if peers is None:
+            import torch.distributed as dist
+            self.own = [IpcBuffer(self.recv_cap * self.d * elem, self.dev_index),
+                        IpcBuffer(self.recv_cap * 16, self.dev_index),
+                        IpcBuffer(cap_local * self.d * 2, self.dev_index)]
+            mine = [bytes(b.handle.raw) for b in self.own]
+            allh = [None] * world
+            dist.all_gather_object(allh, mine, group=group)
+            self.opened = []
+            peers = []
+            for r in range(world):
+                if r == rank:
+                    peers.append(tuple(b.ptr.value for b in self.own))
+                else:
+                    ptrs = tuple(open_peer(h, self.dev_index) for h in allh[r])
+                    self.opened.extend(ptrs)
+                    peers.append(ptrs)
+        self.peers = peers
+        self.recv_x, self.recv_meta, self.ret = peers[rank]
+        self.peer_x = torch.tensor([p[0] for p in peers], dtype=torch.int64, device=dev)
+        self.peer_meta = torch.tensor([p[1] for p in peers], dtype=torch.int64, device=dev)
+        self.peer_ret = torch.tensor([p[2] for p in peers], dtype=torch.int64, device=dev)
+        self.tick = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)  # dispatch bound violations (code 8)
+
+    # -- pieces of one step (the single-GPU emulation drives them directly)
+    def send_counts(self, r):
+        """Pairs this rank sends to each rank: [world] int32 on the device."""
+        o = r.offsets
+        return (o[self.Eg::self.Eg] - o[0:self.E:self.Eg]).to(self.torch.int32)
+
+    def dispatch(self, x, r, counts_dev):
+        from . import _dtype_code, _stream_ptr
+        from ._lib import check, lib
+        n = x.shape[0]
+        if n == 0:
+            return
+        check(lib().mxmoe_dispatch_pairs(x.data_ptr(), _dtype_code(x), n, self.d, self.k, r.perm.data_ptr(),
+                                         r.rscale.data_ptr(), r.topk_idx.data_ptr(), r.topk_w.data_ptr(),
+                                         r.offsets.data_ptr(), self.Eg, self.world, self.rank,
+                                         counts_dev.data_ptr(), self.peer_x.data_ptr(),
+                                         self.peer_meta.data_ptr(), self.recv_cap, self.err.data_ptr(),
+                                         _stream_ptr()))
+
+    def experts(self, n_recv: int):
+        from . import BF16, F32, _stream_ptr
+        from ._lib import check, lib
+        if n_recv == 0:
+            return
+        code = BF16 if self.x_dtype == self.torch.bfloat16 else F32
+        check(lib().mxmoe_forward_local_meta(self.backend.layer._h, self.recv_x, code, self.recv_meta, n_recv,
+                                             self.peer_ret.data_ptr(), _stream_ptr()))
+
+    def combine(self, x, r, out_dtype=None):
+        from . import BF16, _dtype_code, _stream_ptr
+        from ._lib import check, lib
+        t = self.torch
+        y = t.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+        n = x.shape[0]
+        if n:
+            check(lib().mxmoe_combine(x.data_ptr(), _dtype_code(x), n, self.d, self.k, r.topk_idx.data_ptr(),
+                                      r.inv.data_ptr(), self.ret, BF16, 1 if self.backend.cfg.residual else 0,
+                                      y.data_ptr(), _dtype_code(y), _stream_ptr()))
+        return y
+
+    def barrier(self):
+        self.torch.distributed.all_reduce(self.tick, group=self.group)
+
+    def exchange_counts(self, counts_dev):
+        """All ranks' send counts [world][world] on the device and on the host."""
+        t = self.torch
+        allc = t.empty(self.world * self.world, dtype=t.int32, device=counts_dev.device)
+        t.distributed.all_gather_into_tensor(allc, counts_dev, group=self.group)
+        host = allc.cpu().tolist()
+        return allc, [host[s * self.world:(s + 1) * self.world] for s in range(self.world)]
+
+    def forward(self, x, out_dtype=None):
+        if x.shape[0] > self.max_tokens:
+            raise ValueError(f"{x.shape[0]} tokens > max_tokens {self.max_tokens}")
+        if x.dtype != self.x_dtype:
+            raise ValueError(f"x dtype {x.dtype} != {self.x_dtype}")
+        r = self.backend.route(x)
+        allc, host = self.exchange_counts(self.send_counts(r))
+        n_recv = sum(host[s][self.rank] for s in range(self.world))
+        self.dispatch(x, r, allc)
+        self.barrier()  # every rank's pairs are in its owners' receive buffers
+        self.experts(n_recv)
+        self.barrier()  # every pair's output is back in its source's return buffer
+        return self.combine(x, r, out_dtype)
+
+    def profile(self, x, steps: int = 3):
+        """Per-phase device times in ms (CUDA events on the current stream)."""
+        t = self.torch
+        names = ["route", "counts", "dispatch", "experts", "combine"]
+        acc = {nm: 0.0 for nm in names}
+        for _ in range(steps):
+            ev = [t.cuda.Event(enable_timing=True) for _ in range(6)]
+            ev[0].record()
+            r = self.backend.route(x)
+            ev[1].record()
+            allc, host = self.exchange_counts(self.send_counts(r))
+            n_recv = sum(host[s][self.rank] for s in range(self.world))
+            ev[2].record()
+            self.dispatch(x, r, allc)
+            self.barrier()
+            ev[3].record()
+            self.experts(n_recv)
+            self.barrier()
+            ev[4].record()
+            self.combine(x, r)
+            ev[5].record()
+            t.cuda.synchronize()
+            for i, nm in enumerate(names):
+                acc[nm] += ev[i].elapsed_time(ev[i + 1]) / steps
+        return acc
+
+    def close(self):
+        from ._lib import lib
+        for p in getattr(self, "opened", []):
+            lib().mxmoe_ipc_close(p, self.dev_index)
+        self.opened = []
+        for b in self.own or []:
+            b.close()
+        self.own = None
+
+
+def build_peer_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig] = None, group=None):
+    """PeerExpertParallelMoe over libmxmoe for synthetic inputs `inp` (mxmoe.synth)."""
+    cfg = cfg or MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    begin, count = shard_bounds(inp.E, world, rank)
+    be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    return PeerExpertParallelMoe(be, world, rank, inp.n, group=group)

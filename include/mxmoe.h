@@ -263,6 +263,47 @@ MXMOE_API int mxmoe_forward_local(mxmoe_layer* layer, const void* xr, mxmoe_dtyp
                         const float* weight, uint32_t n_pairs, void* out,
                         mxmoe_dtype out_dtype, void* stream);
 
+/* ---- expert parallelism over peer memory (NVLink / NVSwitch) -------------
+ * Instead of a gather and two NCCL all-to-alls, the source GPU's dispatch
+ * kernel writes each routed pair straight into the owning GPU's receive
+ * buffers, and the owner's W2 epilogue writes each pair's output straight
+ * into the source GPU's return buffer.  Buffers are shared with CUDA IPC:
+ * every rank allocates with mxmoe_ipc_alloc, exchanges the handles on the
+ * host, and opens its peers' handles with mxmoe_ipc_open.  Ordering between
+ * the writes and their readers is the caller's (a collective barrier on the
+ * stream after mxmoe_dispatch_pairs and after mxmoe_forward_local_meta). */
+#define MXMOE_IPC_HANDLE_BYTES 64
+MXMOE_API int mxmoe_ipc_alloc(size_t bytes, int device, void** ptr, void* handle);
+MXMOE_API int mxmoe_ipc_free(void* ptr, int device);
+MXMOE_API int mxmoe_ipc_open(const void* handle, int device, void** peer_ptr);
+MXMOE_API int mxmoe_ipc_close(void* peer_ptr, int device);
+
+/* Source side.  perm / offsets: the canonical permutation of mxmoe_route;
+ * experts of rank g are [g * experts_per_rank, (g + 1) * experts_per_rank).
+ * counts [world][world] (device): pairs rank s sends to rank g at
+ * counts[s * world + g].  For every pair, writes the token row (x's dtype)
+ * to peer_x[g] and four 32-bit words {bits of rscale[t], expert, bits of
+ * topk_w[p], rank << 24 | canonical position} to peer_meta[g], at row
+ * (pairs lower ranks send to g) + (position within the pairs for g).
+ * peer_x / peer_meta: device arrays of world pointers; every receive buffer
+ * holds recv_cap rows.  A row at or past recv_cap is not written and sets
+ * *err (device int, may be null) to 8.  n_tokens * k < 2^24. */
+MXMOE_API int mxmoe_dispatch_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_t d_model,
+                         uint32_t k, const int32_t* perm, const float* rscale,
+                         const int32_t* topk_idx, const float* topk_w, const int32_t* offsets,
+                         uint32_t experts_per_rank, uint32_t world, uint32_t rank,
+                         const int32_t* counts, void* const* peer_x, uint32_t* const* peer_meta,
+                         uint32_t recv_cap, int* err, void* stream);
+
+/* Owner side: expert FFN of this layer's shard over n_pairs received rows
+ * xr [n_pairs][d] with metadata [n_pairs][4] as written by
+ * mxmoe_dispatch_pairs.  The bf16 output weight * (W2 act + b2) of each pair
+ * goes to row (slot & 0xFFFFFF) of ret_ptrs[slot >> 24] (device array of the
+ * ranks' return buffers, [n_tokens * k][d] bf16 each, canonical order). */
+MXMOE_API int mxmoe_forward_local_meta(mxmoe_layer* layer, const void* xr, mxmoe_dtype xr_dtype,
+                             const uint32_t* meta, uint32_t n_pairs, void* const* ret_ptrs,
+                             void* stream);
+
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
  * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers, each

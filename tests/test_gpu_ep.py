@@ -52,3 +52,43 @@ def test_forward_local_rejects_foreign_expert():
     be.local(to_device_x(inp), meta)
     with pytest.raises(mxmoe.MxMoeError):
         be.layer.sync_status()
+
+
+@pytest.mark.parametrize("world,n_per,E,k", [(2, 100, 8, 4), (4, 64, 8, 2), (4, 300, 16, 4)])
+def test_peer_dispatch_emulated_on_one_gpu(world, n_per, E, k):
+    """The peer-memory expert-parallel step with `world` ranks emulated on one
+    GPU: each rank's receive / return buffers are plain device buffers whose
+    pointers stand in for the IPC-opened peers; the ranks' dispatch, expert
+    and combine phases run in turn, as the two barriers order them across
+    GPUs.  Every rank's output must match the single-layer forward."""
+    import torch
+    from mxmoe.ep import PeerExpertParallelMoe
+    inp = synth.make_inputs(512, 384, E, k, world * n_per, True, seed=31 + world)
+    full = make_layer(inp)
+    x_all = to_device_x(inp)
+    cfg = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    bufs = [(torch.zeros(world * n_per * k, inp.d, dtype=torch.bfloat16, device="cuda:0"),
+             torch.zeros(world * n_per * k, 4, dtype=torch.int32, device="cuda:0"),
+             torch.zeros(n_per * k, inp.d, dtype=torch.bfloat16, device="cuda:0")) for _ in range(world)]
+    peers = [tuple(b.data_ptr() for b in bb) for bb in bufs]
+    ranks = []
+    for r in range(world):
+        b, c = shard_bounds(inp.E, world, r)
+        be = CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+        ranks.append(PeerExpertParallelMoe(be, world, r, n_per, peers=peers))
+    xs = [x_all[r * n_per:(r + 1) * n_per].contiguous() for r in range(world)]
+    routes = [m.backend.route(x) for m, x in zip(ranks, xs)]
+    allc = torch.cat([m.send_counts(rt) for m, rt in zip(ranks, routes)])
+    host = allc.cpu().tolist()
+    for m, x, rt in zip(ranks, xs, routes):
+        m.dispatch(x, rt, allc)
+    for r, m in enumerate(ranks):
+        m.experts(sum(host[s * world + r] for s in range(world)))
+    ys = [m.combine(x, rt, out_dtype=torch.float32) for m, x, rt in zip(ranks, xs, routes)]
+    torch.cuda.synchronize()
+    for r in range(world):
+        assert int(ranks[r].err.item()) == 0
+        ranks[r].backend.layer.sync_status()
+        want = full.forward(xs[r], out_dtype=torch.float32)
+        assert_close(ys[r].cpu().numpy(), want.cpu().numpy(), f"peer EP rank {r}/{world}")
+    full.close()
