@@ -318,7 +318,7 @@ int x_terms_for(const mxmoe_layer* L, int x_dtype) {
 // pair) -> y_pair.  Uses ws.poff / counts / ntile_prefix / perm_p / inv_p.
 int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
                 const float* route_w, const TilePlan& tp, int x_terms, cudaStream_t st,
-                void* const* ret_ptrs = nullptr, const uint32_t* ret_slot = nullptr) {
+                void* const* ret_ptrs = nullptr, const uint32_t* ret_slot = nullptr, bool y_by_pair = false) {
   Workspace& w = L->ws;
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
   const int N = tp.pair_tile;
@@ -402,6 +402,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.y_pair_bf16 = reinterpret_cast<__nv_bfloat16*>(w.y_pair);
   p.ret_ptrs = ret_ptrs;
   p.ret_slot = ret_slot;
+  p.y_by_pair = y_by_pair ? 1 : 0;
   w.pair_dtype = MXMOE_BF16;
   grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
   CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tp.stacked ? w.tmap_act_stk[tp.tw] : w.tmap_act[tp.tw], p, grid,
@@ -987,7 +988,8 @@ int mxmoe_dispatch_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, 
 }
 
 int mxmoe_forward_local_meta(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, const uint32_t* meta,
-                             uint32_t n_pairs, void* const* ret_ptrs, void* stream) {
+                             uint32_t n_pairs, void* const* ret_ptrs, uint32_t world, uint32_t ret_rows,
+                             uint32_t flags, void* stream) {
   TRY(check_layer(L));
   if (!L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "experts not uploaded");
   if (n_pairs == 0) return MXMOE_OK;
@@ -1012,7 +1014,15 @@ int mxmoe_forward_local_meta(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtyp
                           nullptr, nullptr, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st,
                           w.perm_scratch));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
-  TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, w.rscale, w.topk_w, tp, xt, st, ret_ptrs, w.ret_slot));
+  if (flags & MXMOE_RETURN_FROM_EPILOGUE) {
+    TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, w.rscale, w.topk_w, tp, xt, st, ret_ptrs, w.ret_slot));
+  } else {
+    // W2 writes this GPU's rows in received order, then one pass pushes each
+    // row to its source in 512-byte warp stores
+    TRY(run_experts(L, xr, xr_dtype, n_pairs, 1, w.rscale, w.topk_w, tp, xt, st, nullptr, nullptr, true));
+    CUDA_TRY(launch_return_pairs(w.y_pair, static_cast<int>(L->d), static_cast<int>(n_pairs), w.ret_slot,
+                                 static_cast<int>(world), ret_ptrs, ret_rows, L->err, st));
+  }
   if (L->profiling) {
     CUDA_TRY(cudaEventRecord(L->ev[6], st));
     L->profile_valid = true;

@@ -150,7 +150,7 @@ __device__ __forceinline__ __nv_bfloat16* w2_out_row(const TcParams& p, int pos,
     const uint32_t slot = __ldg(p.ret_slot + pair);
     return static_cast<__nv_bfloat16*>(p.ret_ptrs[slot >> 24]) + static_cast<uint64_t>(slot & 0xFFFFFFu) * p.d;
   }
-  return p.y_pair_bf16 + static_cast<uint64_t>(pos) * p.d;
+  return p.y_pair_bf16 + static_cast<uint64_t>(p.y_by_pair ? pair : pos) * p.d;
 }
 
 // 8 outputs (bias, route weight) -> 8 bf16 in one 16-byte store.

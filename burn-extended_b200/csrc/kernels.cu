@@ -944,6 +944,28 @@ __global__ void dispatch_pairs_kernel(const void* __restrict__ x, uint32_t row_b
   __threadfence_system();  // peer writes ordered before anything this thread's GPU does later
 }
 
+// Expert-parallel return: warp per received row r; its bf16 output row goes
+// to row (slot & 0xFFFFFF) of the source rank's return buffer
+// peer_ret[slot >> 24] in 16-byte lanes (512 contiguous bytes per store).
+__global__ void return_pairs_kernel(const __nv_bfloat16* __restrict__ y, uint32_t row_bytes, int R,
+                                    const uint32_t* __restrict__ slot, int world, void* const* __restrict__ peer_ret,
+                                    uint32_t ret_rows, int* err) {
+  const int r = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const uint32_t s = __ldg(slot + r);
+  const int src = static_cast<int>(s >> 24);
+  const uint32_t row = s & 0xFFFFFFu;
+  if (src >= world || row >= ret_rows) {  // corrupt slot: write nothing
+    if (lane == 0 && err != nullptr) atomicCAS(err, 0, 8);
+    return;
+  }
+  const uint4* from = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(y) + static_cast<uint64_t>(r) * row_bytes);
+  uint4* to = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_ret[src]) + static_cast<uint64_t>(row) * row_bytes);
+  for (uint32_t i = lane; i < row_bytes / 16; i += 32) to[i] = __ldg(from + i);
+  __threadfence_system();
+}
+
 // Received metadata [R][4] -> per-pair arrays for the expert pipeline.
 __global__ void split_meta_kernel(const uint4* __restrict__ meta, int R, float* rscale, int32_t* expert,
                                   float* weight, uint32_t* slot) {
@@ -1182,6 +1204,15 @@ cudaError_t launch_dispatch_pairs(const void* x, int x_dtype, int d, int k, int 
   dispatch_pairs_kernel<<<(P + 7) / 8, 256, 0, st>>>(x, row_bytes, k, P, perm, rscale, topk_idx, topk_w, offsets,
                                                       experts_per_rank, world, rank, counts, peer_x, peer_meta,
                                                       recv_cap, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_return_pairs(const void* y_bf16, int d, int R, const uint32_t* slot, int world,
+                                void* const* peer_ret, uint32_t ret_rows, int* err, cudaStream_t st) {
+  if (R == 0) return cudaSuccess;
+  return_pairs_kernel<<<(R + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
+                                                    static_cast<uint32_t>(d) * 2u, R, slot, world, peer_ret, ret_rows,
+                                                    err);
   return cudaGetLastError();
 }
 

@@ -63,6 +63,8 @@ cudaError_t launch_dispatch_pairs(const void* x, int x_dtype, int d, int k, int 
                                   const int32_t* offsets, int experts_per_rank, int world, int rank,
                                   const int32_t* counts, void* const* peer_x, uint32_t* const* peer_meta,
                                   uint32_t recv_cap, int* err, cudaStream_t st);
+cudaError_t launch_return_pairs(const void* y_bf16, int d, int R, const uint32_t* slot, int world,
+                                void* const* peer_ret, uint32_t ret_rows, int* err, cudaStream_t st);
 cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
                               uint32_t* slot, cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,

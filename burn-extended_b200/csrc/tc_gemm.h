@@ -48,6 +48,7 @@ struct TcParams {
   // y_pair_bf16.
   void* const* ret_ptrs;
   const uint32_t* ret_slot;
+  int y_by_pair;  // W2 output row = the pair's own index (received row) instead of its sorted position
   int d;
   int* err;                 // device status word (0 = ok)
 };

@@ -80,10 +80,11 @@ _SIGS = {
     "mxmoe_ipc_close": ([_vp, _i32], _i32),
     "mxmoe_dispatch_pairs": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp,
                               _u32, _vp, _vp], _i32),
-    "mxmoe_forward_local_meta": ([_vp, _vp, _i32, _vp, _u32, _vp, _vp], _i32),
+    "mxmoe_forward_local_meta": ([_vp, _vp, _i32, _vp, _u32, _vp, _u32, _u32, _u32, _vp], _i32),
 }
 
 IPC_HANDLE_BYTES = 64
+RETURN_FROM_EPILOGUE = 0x1
 
 _lib = None
 

@@ -302,6 +302,9 @@ class PeerExpertParallelMoe:
         self.peer_ret = torch.tensor([p[2] for p in peers], dtype=torch.int64, device=dev)
         self.tick = torch.zeros(1, dtype=torch.int32, device=dev)
         self.err = torch.zeros(1, dtype=torch.int32, device=dev)  # dispatch bound violations (code 8)
+        # 0: W2 writes locally, a copy pass pushes rows back; RETURN_FROM_EPILOGUE:
+        # the W2 epilogue stores to the source ranks directly
+        self.return_flags = 0
 
     # -- pieces of one step (the single-GPU emulation drives them directly)
     def send_counts(self, r):
@@ -329,7 +332,8 @@ class PeerExpertParallelMoe:
             return
         code = BF16 if self.x_dtype == self.torch.bfloat16 else F32
         check(lib().mxmoe_forward_local_meta(self.backend.layer._h, self.recv_x, code, self.recv_meta, n_recv,
-                                             self.peer_ret.data_ptr(), _stream_ptr()))
+                                             self.peer_ret.data_ptr(), self.world, self.max_tokens * self.k,
+                                             self.return_flags, _stream_ptr()))
 
     def combine(self, x, r, out_dtype=None):
         from . import BF16, _dtype_code, _stream_ptr

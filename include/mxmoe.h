@@ -299,10 +299,14 @@ MXMOE_API int mxmoe_dispatch_pairs(const void* x, mxmoe_dtype x_dtype, uint32_t 
  * xr [n_pairs][d] with metadata [n_pairs][4] as written by
  * mxmoe_dispatch_pairs.  The bf16 output weight * (W2 act + b2) of each pair
  * goes to row (slot & 0xFFFFFF) of ret_ptrs[slot >> 24] (device array of the
- * ranks' return buffers, [n_tokens * k][d] bf16 each, canonical order). */
+ * world ranks' return buffers, ret_rows x d bf16 each, canonical order).
+ * flags: MXMOE_RETURN_FROM_EPILOGUE makes the W2 epilogue store to the peers
+ * directly; by default W2 writes locally and a copy pass pushes whole rows.
+ * A slot outside (world, ret_rows) is not written and sets status 8. */
+#define MXMOE_RETURN_FROM_EPILOGUE 0x1u
 MXMOE_API int mxmoe_forward_local_meta(mxmoe_layer* layer, const void* xr, mxmoe_dtype xr_dtype,
                              const uint32_t* meta, uint32_t n_pairs, void* const* ret_ptrs,
-                             void* stream);
+                             uint32_t world, uint32_t ret_rows, uint32_t flags, void* stream);
 
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in

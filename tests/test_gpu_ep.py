@@ -54,8 +54,9 @@ def test_forward_local_rejects_foreign_expert():
         be.layer.sync_status()
 
 
-@pytest.mark.parametrize("world,n_per,E,k", [(2, 100, 8, 4), (4, 64, 8, 2), (4, 300, 16, 4)])
-def test_peer_dispatch_emulated_on_one_gpu(world, n_per, E, k):
+@pytest.mark.parametrize("world,n_per,E,k,flags", [(2, 100, 8, 4, 0), (4, 64, 8, 2, 0), (4, 300, 16, 4, 0),
+                                                    (2, 100, 8, 4, 1), (4, 300, 16, 4, 1)])
+def test_peer_dispatch_emulated_on_one_gpu(world, n_per, E, k, flags):
     """The peer-memory expert-parallel step with `world` ranks emulated on one
     GPU: each rank's receive / return buffers are plain device buffers whose
     pointers stand in for the IPC-opened peers; the ranks' dispatch, expert
@@ -76,6 +77,7 @@ def test_peer_dispatch_emulated_on_one_gpu(world, n_per, E, k):
         b, c = shard_bounds(inp.E, world, r)
         be = CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
         ranks.append(PeerExpertParallelMoe(be, world, r, n_per, peers=peers))
+        ranks[-1].return_flags = flags  # 1: the W2 epilogue stores to the source directly
     xs = [x_all[r * n_per:(r + 1) * n_per].contiguous() for r in range(world)]
     routes = [m.backend.route(x) for m, x in zip(ranks, xs)]
     allc = torch.cat([m.send_counts(rt) for m, rt in zip(ranks, routes)])
