@@ -212,7 +212,7 @@ def run_ours(args, world, rank, local):
     n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
     if world > 1:
         from mxmoe import ep
-        runner = ep.build_peer_rank(inp, world, rank, dev)
+        runner = ep.build_quantized_peer_rank(inp, world, rank, dev)
         step = lambda x: runner.forward(x)  # noqa: E731
         x = torch.from_numpy(inp.x).to(torch.bfloat16).to(dev)
     else:

@@ -165,6 +165,12 @@ struct Workspace {
   int32_t* local_idx = nullptr; // [cap_pairs] local expert ids (expert-parallel receive side)
   int32_t* perm_scratch = nullptr; // multi-block permutation (permute_scratch_ints)
   uint32_t* ret_slot = nullptr;    // [cap_pairs] expert-parallel return slots of received pairs
+  // expert-parallel rows written by the source ranks (mxmoe_ep_dispatch), per layout row
+  float* pos_rscale = nullptr;     // [rows]
+  float* pos_weight = nullptr;     // [rows]
+  uint32_t* pos_slot = nullptr;    // [rows]
+  int32_t* iota = nullptr;         // [rows] identity permutation
+  int32_t* ep_src_base = nullptr;  // [E_total]
   int pair_dtype = MXMOE_F32;   // element type the last run_experts wrote y_pair in
   CUtensorMap tmap_x[kNumTileWidths];
   CUtensorMap tmap_act[kNumTileWidths];
@@ -196,6 +202,9 @@ struct mxmoe_layer {
   uint32_t last_n = 0;
   bool profiling = false;
   bool profile_valid = false;
+  // expert parallelism over peer memory: the workspace is shared with peers and must not move
+  bool ep_reserved = false;
+  uint32_t ep_world = 0, ep_max_tokens = 0;
   cudaEvent_t ev[8] = {};
 };
 
@@ -208,6 +217,11 @@ void free_workspace(Workspace& w) {
   dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
   dfree(w.local_idx);
   dfree(w.ret_slot);
+  dfree(w.pos_rscale);
+  dfree(w.pos_weight);
+  dfree(w.pos_slot);
+  dfree(w.iota);
+  dfree(w.ep_src_base);
   dfree(w.perm_scratch);
   w.cap_tokens = w.cap_pairs = w.rows = w.row_blocks = 0;
 }
@@ -219,6 +233,9 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   const uint64_t pairs = static_cast<uint64_t>(n_tokens) * k;
   if (n_tokens <= w.cap_tokens && pairs <= w.cap_pairs && w.cap_tokens > 0) return MXMOE_OK;
   if (pairs > (1u << 28)) return fail(MXMOE_ERR_TOO_LARGE, "too many pairs: %llu", (unsigned long long)pairs);
+  if (L->ep_reserved)
+    return fail(MXMOE_ERR_TOO_LARGE, "workspace is shared with peer ranks and cannot grow to %llu pairs",
+                (unsigned long long)pairs);
   // Capacities only grow (the expert-parallel receive side alternates sizes
   // from step to step), with an eighth of headroom on the requested growth.
   const uint32_t old_t = w.cap_tokens, old_p = w.cap_pairs;
@@ -249,6 +266,12 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   TRY(dalloc(&w.inv_p, cap_p));
   TRY(dalloc(&w.local_idx, cap_p));
   TRY(dalloc(&w.ret_slot, cap_p));
+  TRY(dalloc(&w.pos_rscale, w.rows));
+  TRY(dalloc(&w.pos_weight, w.rows));
+  TRY(dalloc(&w.pos_slot, w.rows));
+  TRY(dalloc(&w.iota, w.rows));
+  TRY(dalloc(&w.ep_src_base, Et));
+  CUDA_TRY(launch_iota(w.iota, static_cast<int>(w.rows), 0));
   const size_t pscr = permute_scratch_ints(static_cast<int>(cap_p), static_cast<int>(Et));
   TRY(dalloc(&w.perm_scratch, pscr));
   CUDA_TRY(cudaMemset(w.perm_scratch, 0, pscr * sizeof(int32_t)));
@@ -318,7 +341,8 @@ int x_terms_for(const mxmoe_layer* L, int x_dtype) {
 // pair) -> y_pair.  Uses ws.poff / counts / ntile_prefix / perm_p / inv_p.
 int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
                 const float* route_w, const TilePlan& tp, int x_terms, cudaStream_t st,
-                void* const* ret_ptrs = nullptr, const uint32_t* ret_slot = nullptr, bool y_by_pair = false) {
+                void* const* ret_ptrs = nullptr, const uint32_t* ret_slot = nullptr, bool y_by_pair = false,
+                bool input_quantized = false, const int32_t* perm = nullptr) {
   Workspace& w = L->ws;
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
   const int N = tp.pair_tile;
@@ -336,10 +360,11 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
     return MXMOE_OK;
   }
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
-  CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
-                                 w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
-                                 static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), N,
-                                 tp.stacked ? 1 : 0, st));
+  if (!input_quantized)
+    CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
+                                   w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
+                                   static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1),
+                                   N, tp.stacked ? 1 : 0, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
   const uint64_t max_pair_tiles = (P + N - 1) / N + L->e_count;
   const bool tok = tp.tok;
@@ -355,7 +380,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.alpha = L->cfg.swiglu_alpha;
   p.limit = L->cfg.swiglu_limit;
   p.rscale = rscale;
-  p.perm = w.perm_p;
+  p.perm = perm ? perm : w.perm_p;
   p.k = static_cast<int>(k);
   p.topk_w = route_w;
   p.err = L->err;
@@ -1027,6 +1052,104 @@ int mxmoe_forward_local_meta(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtyp
     CUDA_TRY(cudaEventRecord(L->ev[6], st));
     L->profile_valid = true;
   }
+  return MXMOE_OK;
+}
+
+// ---- expert parallelism: quantized dispatch into the owners' layouts
+int mxmoe_ep_reserve(mxmoe_layer* L, uint32_t max_tokens, uint32_t world, void* handles) {
+  TRY(check_layer(L));
+  if (!handles || max_tokens == 0 || world == 0) return fail(MXMOE_ERR_INVALID_ARG, "bad ep reservation");
+  if (L->ep_reserved) return fail(MXMOE_ERR_INVALID_ARG, "ep workspace already reserved");
+  if (L->e_count * world != L->E_total)
+    return fail(MXMOE_ERR_INVALID_ARG, "shard of %u experts x %u ranks != %u experts", L->e_count, world, L->E_total);
+  if (static_cast<uint64_t>(max_tokens) * L->k >= (1u << 24))
+    return fail(MXMOE_ERR_TOO_LARGE, "max_tokens * k must stay below 2^24 (return slots)");
+  DeviceGuard g(L->cfg.device);
+  TRY(ensure_workspace(L, world * max_tokens, L->k));
+  CUDA_TRY(cudaDeviceSynchronize());
+  Workspace& w = L->ws;
+  void* bufs[5] = {w.xq, w.xsf, w.pos_rscale, w.pos_weight, w.pos_slot};
+  for (int i = 0; i < 5; ++i) {
+    cudaIpcMemHandle_t h;
+    CUDA_TRY(cudaIpcGetMemHandle(&h, bufs[i]));
+    std::memcpy(static_cast<uint8_t*>(handles) + i * MXMOE_IPC_HANDLE_BYTES, &h, sizeof(h));
+  }
+  L->ep_reserved = true;
+  L->ep_world = world;
+  L->ep_max_tokens = max_tokens;
+  return MXMOE_OK;
+}
+
+static TilePlan ep_tiles(const mxmoe_layer* L, int xt) {
+  // every rank derives the owners' tile plan from the same numbers
+  return pick_tiles(static_cast<uint64_t>(L->ep_max_tokens) * L->k, L->e_count, xt);
+}
+
+int mxmoe_ep_dispatch(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, const float* rscale,
+                      const int32_t* topk_idx, const float* topk_w, const int32_t* inv, const int32_t* offsets,
+                      const int32_t* counts, uint32_t rank, void* const* peer_bufs, void* stream) {
+  TRY(check_layer(L));
+  if (!L->ep_reserved) return fail(MXMOE_ERR_NOT_READY, "mxmoe_ep_reserve first");
+  if (n_tokens > L->ep_max_tokens) return fail(MXMOE_ERR_TOO_LARGE, "%u tokens > reserved %u", n_tokens, L->ep_max_tokens);
+  if (rank >= L->ep_world) return fail(MXMOE_ERR_INVALID_ARG, "rank %u of %u", rank, L->ep_world);
+  if (!counts || !peer_bufs || (n_tokens > 0 && (!x || !rscale || !topk_idx || !topk_w || !inv || !offsets)))
+    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(x)) return fail(MXMOE_ERR_INVALID_ARG, "x must be 16-byte aligned");
+  if (L->cfg.flags & MXMOE_FLAG_SIMT) return fail(MXMOE_ERR_UNSUPPORTED, "ep dispatch needs the tensor-core path");
+  DeviceGuard g(L->cfg.device);
+  Workspace& w = L->ws;
+  cudaStream_t st = as_stream(stream);
+  const int xt = x_terms_for(L, x_dtype);
+  const TilePlan tp = ep_tiles(L, xt);
+  const int world = static_cast<int>(L->ep_world);
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  CUDA_TRY(launch_ep_layout(counts, world, static_cast<int>(rank), static_cast<int>(L->E_total),
+                            static_cast<int>(L->e_count), kRowBlock, tp.pair_tile, w.ep_src_base, w.poff, w.counts,
+                            w.ntile_prefix, st));
+  if (n_tokens == 0) return MXMOE_OK;
+  const uint64_t kc1 = L->kp1 / kTileK;
+  void* const* pb = peer_bufs;
+  CUDA_TRY(launch_ep_quantize_dispatch(
+      x, x_dtype, static_cast<int>(n_tokens), static_cast<int>(L->d), static_cast<int>(L->k), L->gamma,
+      L->gamma_is_one ? 1 : 0, inv, xt, static_cast<uint64_t>(w.rows) * L->kp1, static_cast<int>(L->kp1),
+      static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), tp.pair_tile,
+      tp.stacked ? 1 : 0, w.ep_src_base, offsets, topk_idx, topk_w, rscale, static_cast<int>(L->e_count),
+      static_cast<int>(rank), w.rows, reinterpret_cast<uint8_t* const*>(pb), reinterpret_cast<uint8_t* const*>(pb + world),
+      reinterpret_cast<float* const*>(pb + 2 * world), reinterpret_cast<float* const*>(pb + 3 * world),
+      reinterpret_cast<uint32_t* const*>(pb + 4 * world), L->err, st));
+  return MXMOE_OK;
+}
+
+int mxmoe_ep_experts(mxmoe_layer* L, mxmoe_dtype x_dtype, void* const* peer_ret, uint32_t ret_rows, void* stream) {
+  TRY(check_layer(L));
+  if (!L->ep_reserved) return fail(MXMOE_ERR_NOT_READY, "mxmoe_ep_reserve first");
+  if (!L->experts_ready) return fail(MXMOE_ERR_NOT_READY, "experts not uploaded");
+  if (!peer_ret) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  DeviceGuard g(L->cfg.device);
+  Workspace& w = L->ws;
+  cudaStream_t st = as_stream(stream);
+  const int xt = x_terms_for(L, x_dtype);
+  const TilePlan tp = ep_tiles(L, xt);
+  L->profile_valid = false;
+  // rows are their own pairs (identity permutation, one pair per row)
+  TRY(run_experts(L, nullptr, x_dtype, L->ep_world * L->ep_max_tokens * L->k, 1, w.pos_rscale, w.pos_weight, tp, xt,
+                  st, nullptr, nullptr, false, true, w.iota));
+  CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff, w.counts,
+                            static_cast<int>(L->e_count), w.pos_slot, static_cast<int>(L->ep_world), peer_ret,
+                            ret_rows, L->err, st));
+  return MXMOE_OK;
+}
+
+int mxmoe_ep_buffers(mxmoe_layer* L, void** ptrs) {
+  TRY(check_layer(L));
+  if (!L->ep_reserved) return fail(MXMOE_ERR_NOT_READY, "mxmoe_ep_reserve first");
+  if (!ptrs) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  Workspace& w = L->ws;
+  ptrs[0] = w.xq;
+  ptrs[1] = w.xsf;
+  ptrs[2] = w.pos_rscale;
+  ptrs[3] = w.pos_weight;
+  ptrs[4] = w.pos_slot;
   return MXMOE_OK;
 }
 

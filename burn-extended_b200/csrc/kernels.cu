@@ -675,6 +675,26 @@ __global__ void __launch_bounds__(kPermChunkThreads)
   }
 }
 
+// Expert-parallel dispatch of quantized pairs (quantize_pairs_kernel<true>):
+// the codes, scale words and per-row metadata of a pair go to its owner
+// rank g's buffers (peer pointers) at row src_base[e] + (canonical position -
+// offsets[e]), the pair's row in g's expert-sorted, padded layout.
+struct EpDispatch {
+  const int32_t* src_base;  // [E] this rank's first row per expert at the owner
+  const int32_t* offsets;   // [E + 1] canonical offsets of this rank's pairs
+  const int32_t* topk_idx;
+  const float* topk_w;
+  const float* rscale;
+  int epr, rank;
+  uint32_t dst_rows;        // rows of every owner's layout
+  uint8_t* const* xq;       // [world] code buffers
+  uint8_t* const* xsf;      // [world] scale-atom buffers
+  float* const* rs;         // [world] per-row 1 / rms
+  float* const* wt;         // [world] per-row route weight
+  uint32_t* const* slot;    // [world] per-row return slot (rank << 24 | canonical position)
+  int* err;
+};
+
 // ------------------------------------------------------------------ quantize
 // Gathers each routed pair's token row into its padded expert-sorted position
 // and writes it as `terms` block-scaled E4M3 terms (two reproduce bf16 input
@@ -687,11 +707,12 @@ __global__ void __launch_bounds__(kPermChunkThreads)
 // comes from a max over the quad; the arithmetic per element is
 // quantize_block32's.  Lanes of blocks past d / 32 contribute zero scale
 // bytes (the K padding) and store no codes.
+template <bool kDispatch>
 __global__ void __launch_bounds__(256)
     quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                           const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
                           int terms, uint8_t* codes, uint64_t term_stride, int kp, uint8_t* sf,
-                          uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked) {
+                          uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked, const EpDispatch ep) {
   const int nb = d / 32;
   const int noct = (nb + 7) / 8;
   const uint64_t items = static_cast<uint64_t>(n) * noct;
@@ -783,7 +804,29 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int s = 0; s < kMaxTopK; ++s) {
       if (s >= k) break;
-      const int pos = __ldg(inv_p + static_cast<uint64_t>(t) * k + s);
+      int pos = __ldg(inv_p + static_cast<uint64_t>(t) * k + s);
+      uint8_t* codes_d = codes;
+      uint8_t* sf_d = sf;
+      if constexpr (kDispatch) {
+        // pos is the pair's canonical position; its row at the owner follows
+        // from the owner's segment layout (ep.src_base)
+        const int p = t * k + s;
+        const int e = __ldg(ep.topk_idx + p);
+        const int g = e / ep.epr;
+        const int q0 = pos;
+        pos = __ldg(ep.src_base + e) + (q0 - __ldg(ep.offsets + e));
+        if (pos < 0 || static_cast<uint32_t>(pos) >= ep.dst_rows) {  // inconsistent counts: write nothing
+          if (lane == 0 && ep.err != nullptr) atomicCAS(ep.err, 0, 8);
+          continue;
+        }
+        codes_d = ep.xq[g];
+        sf_d = ep.xsf[g];
+        if (lane == 0 && static_cast<int>(it % noct) == 0) {
+          ep.rs[g][pos] = __ldg(ep.rscale + t);
+          ep.wt[g][pos] = __ldg(ep.topk_w + p);
+          ep.slot[g][pos] = (static_cast<uint32_t>(ep.rank) << 24) | static_cast<uint32_t>(q0);
+        }
+      }
 #pragma unroll
       for (int q = 0; q < kMaxTerms; ++q) {
         if (q >= terms) break;
@@ -792,7 +835,7 @@ __global__ void __launch_bounds__(256)
                                                                                 static_cast<uint32_t>(q),
                                                                                 static_cast<uint32_t>(sf_rows)))
                                        : static_cast<uint64_t>(pos);
-          uint8_t* dst = codes + (stacked ? 0 : q * term_stride) + row * kp + c0;
+          uint8_t* dst = codes_d + (stacked ? 0 : q * term_stride) + row * kp + c0;
           *reinterpret_cast<uint2*>(dst) = make_uint2(words[q][0], words[q][1]);
         }
         if (sf_lane) {
@@ -803,11 +846,12 @@ __global__ void __launch_bounds__(256)
                                                                       static_cast<uint32_t>(b),
                                                                       static_cast<uint32_t>(kchunks),
                                                                       static_cast<uint32_t>(sf_rows));
-          *reinterpret_cast<uint32_t*>(sf + o) = sword[q];
+          *reinterpret_cast<uint32_t*>(sf_d + o) = sword[q];
         }
       }
     }
   }
+  if constexpr (kDispatch) __threadfence_system();  // peer writes ordered before this GPU's later work
 }
 
 // ------------------------------------------------------------------ combine
@@ -964,6 +1008,89 @@ __global__ void return_pairs_kernel(const __nv_bfloat16* __restrict__ y, uint32_
   uint4* to = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_ret[src]) + static_cast<uint64_t>(row) * row_bytes);
   for (uint32_t i = lane; i < row_bytes / 16; i += 32) to[i] = __ldg(from + i);
   __threadfence_system();
+}
+
+// Expert-parallel layout from the all-gathered pair counts [world][E]
+// (counts[s * E + e] = pairs rank s routes to expert e).  Every owner g lays
+// its experts [g * epr, (g + 1) * epr) out as consecutive segments, each
+// padded to `pad` rows, pairs in (source rank, canonical position) order.
+// Outputs: src_base[e] = this rank's first row for expert e at its owner;
+// for the experts this rank owns, the padded starts poff[epr + 1], counts
+// [epr] and the tile prefix (tiles of n_tile pairs) [epr + 1].
+__global__ void ep_layout_kernel(const int32_t* __restrict__ counts, int world, int rank, int E, int epr, int pad,
+                                 int n_tile, int32_t* src_base, int32_t* poff, int32_t* seg_counts,
+                                 int32_t* ntile_prefix) {
+  extern __shared__ int32_t lay[];  // tot[E], below[E], start[E]
+  int32_t* tot = lay;
+  int32_t* below = lay + E;
+  int32_t* start = lay + 2 * E;
+  for (int e = threadIdx.x; e < E; e += blockDim.x) {
+    int t = 0, b = 0;
+    for (int s = 0; s < world; ++s) {
+      const int c = counts[s * E + e];
+      t += c;
+      if (s < rank) b += c;
+    }
+    tot[e] = t;
+    below[e] = b;
+  }
+  __syncthreads();
+  for (int g = threadIdx.x; g < world; g += blockDim.x) {
+    int run = 0;
+    for (int el = 0; el < epr; ++el) {
+      start[g * epr + el] = run;
+      run += (tot[g * epr + el] + pad - 1) / pad * pad;
+    }
+    if (g == rank) poff[epr] = run;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += blockDim.x) src_base[e] = start[e] + below[e];
+  if (threadIdx.x == 0) {
+    int tiles = 0;
+    for (int el = 0; el < epr; ++el) {
+      const int e = rank * epr + el;
+      poff[el] = start[e];
+      seg_counts[el] = tot[e];
+      ntile_prefix[el] = tiles;
+      tiles += (tot[e] + n_tile - 1) / n_tile;
+    }
+    ntile_prefix[epr] = tiles;
+  }
+}
+
+// Expert-parallel return from the owner's layout: warp per row pos of the
+// segments (poff / seg_counts); a row holding a pair sends its bf16 output
+// y[pos] to row (slot & 0xFFFFFF) of peer_ret[slot >> 24] in 16-byte lanes.
+__global__ void ep_return_kernel(const __nv_bfloat16* __restrict__ y, uint32_t row_bytes, int rows,
+                                 const int32_t* __restrict__ poff, const int32_t* __restrict__ seg_counts, int epr,
+                                 const uint32_t* __restrict__ slot, int world, void* const* __restrict__ peer_ret,
+                                 uint32_t ret_rows, int* err) {
+  extern __shared__ int32_t seg[];  // poff[epr + 1], counts[epr]
+  for (int i = threadIdx.x; i <= epr; i += blockDim.x) seg[i] = poff[i];
+  for (int i = threadIdx.x; i < epr; i += blockDim.x) seg[epr + 1 + i] = seg_counts[i];
+  __syncthreads();
+  const int pos = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (pos >= rows || pos >= seg[epr]) return;
+  int el = 0;
+  while (el + 1 < epr && seg[el + 1] <= pos) ++el;
+  if (pos - seg[el] >= seg[epr + 1 + el]) return;  // padding row
+  const uint32_t s = __ldg(slot + pos);
+  const int src = static_cast<int>(s >> 24);
+  const uint32_t row = s & 0xFFFFFFu;
+  if (src >= world || row >= ret_rows) {
+    if (lane == 0 && err != nullptr) atomicCAS(err, 0, 8);
+    return;
+  }
+  const uint4* from = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(y) + static_cast<uint64_t>(pos) * row_bytes);
+  uint4* to = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_ret[src]) + static_cast<uint64_t>(row) * row_bytes);
+  for (uint32_t i = lane; i < row_bytes / 16; i += 32) to[i] = __ldg(from + i);
+  __threadfence_system();
+}
+
+__global__ void iota_kernel(int32_t* a, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) a[i] = i;
 }
 
 // Received metadata [R][4] -> per-pair arrays for the expert pipeline.
@@ -1164,8 +1291,9 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
-  quantize_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
-                                              term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked);
+  quantize_pairs_kernel<false><<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
+                                                     term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked,
+                                                     EpDispatch{});
   return cudaGetLastError();
 }
 
@@ -1213,6 +1341,52 @@ cudaError_t launch_return_pairs(const void* y_bf16, int d, int R, const uint32_t
   return_pairs_kernel<<<(R + 7) / 8, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
                                                     static_cast<uint32_t>(d) * 2u, R, slot, world, peer_ret, ret_rows,
                                                     err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, int epr, int pad, int n_tile,
+                             int32_t* src_base, int32_t* poff, int32_t* seg_counts, int32_t* ntile_prefix,
+                             cudaStream_t st) {
+  const size_t smem = 3ull * E * sizeof(int32_t);
+  ensure_dynamic_smem(reinterpret_cast<const void*>(ep_layout_kernel), smem);
+  ep_layout_kernel<<<1, 256, smem, st>>>(counts, world, rank, E, epr, pad, n_tile, src_base, poff, seg_counts,
+                                         ntile_prefix);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_quantize_dispatch(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
+                                        int gamma_is_one, const int32_t* inv_c, int terms, uint64_t term_stride,
+                                        int kp, uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked,
+                                        const int32_t* src_base, const int32_t* offsets, const int32_t* topk_idx,
+                                        const float* topk_w, const float* rscale, int epr, int rank,
+                                        uint32_t dst_rows, uint8_t* const* xq, uint8_t* const* xsf, float* const* rs,
+                                        float* const* wt, uint32_t* const* slot, int* err, cudaStream_t st) {
+  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + 7) / 8);
+  if (items == 0 || k == 0) return cudaSuccess;
+  const uint64_t blocks = (items + 7) / 8;
+  const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
+  const EpDispatch ep{src_base, offsets, topk_idx, topk_w, rscale, epr, rank, dst_rows, xq, xsf, rs, wt, slot, err};
+  quantize_pairs_kernel<true><<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_c, terms, nullptr,
+                                                    term_stride, kp, nullptr, sf_term_stride, kchunks, sf_rows,
+                                                    stacked, ep);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t* poff, const int32_t* seg_counts,
+                             int epr, const uint32_t* slot, int world, void* const* peer_ret, uint32_t ret_rows,
+                             int* err, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  const size_t smem = (2ull * epr + 1) * sizeof(int32_t);
+  ensure_dynamic_smem(reinterpret_cast<const void*>(ep_return_kernel), smem);
+  ep_return_kernel<<<(rows + 7) / 8, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
+                                                       static_cast<uint32_t>(d) * 2u, rows, poff, seg_counts, epr,
+                                                       slot, world, peer_ret, ret_rows, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_iota(int32_t* a, int n, cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  iota_kernel<<<(n + 255) / 256, 256, 0, st>>>(a, n);
   return cudaGetLastError();
 }
 

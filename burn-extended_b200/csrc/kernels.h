@@ -65,6 +65,20 @@ cudaError_t launch_dispatch_pairs(const void* x, int x_dtype, int d, int k, int 
                                   uint32_t recv_cap, int* err, cudaStream_t st);
 cudaError_t launch_return_pairs(const void* y_bf16, int d, int R, const uint32_t* slot, int world,
                                 void* const* peer_ret, uint32_t ret_rows, int* err, cudaStream_t st);
+cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, int epr, int pad, int n_tile,
+                             int32_t* src_base, int32_t* poff, int32_t* seg_counts, int32_t* ntile_prefix,
+                             cudaStream_t st);
+cudaError_t launch_ep_quantize_dispatch(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
+                                        int gamma_is_one, const int32_t* inv_c, int terms, uint64_t term_stride,
+                                        int kp, uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked,
+                                        const int32_t* src_base, const int32_t* offsets, const int32_t* topk_idx,
+                                        const float* topk_w, const float* rscale, int epr, int rank,
+                                        uint32_t dst_rows, uint8_t* const* xq, uint8_t* const* xsf, float* const* rs,
+                                        float* const* wt, uint32_t* const* slot, int* err, cudaStream_t st);
+cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t* poff, const int32_t* seg_counts,
+                             int epr, const uint32_t* slot, int world, void* const* peer_ret, uint32_t ret_rows,
+                             int* err, cudaStream_t st);
+cudaError_t launch_iota(int32_t* a, int n, cudaStream_t st);
 cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
                               uint32_t* slot, cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,

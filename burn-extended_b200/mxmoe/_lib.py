@@ -81,6 +81,10 @@ _SIGS = {
     "mxmoe_dispatch_pairs": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _u32, _u32, _u32, _vp, _vp, _vp,
                               _u32, _vp, _vp], _i32),
     "mxmoe_forward_local_meta": ([_vp, _vp, _i32, _vp, _u32, _vp, _u32, _u32, _u32, _vp], _i32),
+    "mxmoe_ep_reserve": ([_vp, _u32, _u32, _vp], _i32),
+    "mxmoe_ep_dispatch": ([_vp, _vp, _i32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _vp, _vp], _i32),
+    "mxmoe_ep_experts": ([_vp, _i32, _vp, _u32, _vp], _i32),
+    "mxmoe_ep_buffers": ([_vp, _vp], _i32),
 }
 
 IPC_HANDLE_BYTES = 64

@@ -414,3 +414,170 @@ def build_peer_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig]
     begin, count = shard_bounds(inp.E, world, rank)
     be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
     return PeerExpertParallelMoe(be, world, rank, inp.n, group=group)
+
+
+class QuantizedPeerMoe:
+    """One rank of the expert-parallel layer with quantized dispatch: this
+    rank quantizes its own tokens once and writes every pair's codes, scales
+    and row metadata straight into the owner's GEMM operand layout (peer
+    memory); the owner runs W1/W2 on it and pushes the outputs back.  The
+    pair counts travel in one all-gather on the device, so a step never
+    waits on the host."""
+
+    # rms, router logits, top-k, permute x2, layout, quantize-dispatch, W1, W2, return, combine
+    launches_per_step = 11
+    BUFS = 5  # codes, scale atoms, 1/rms, route weight, return slot (mxmoe_ep_reserve order)
+
+    def __init__(self, backend: CudaExpertBackend, world: int, rank: int, max_tokens: int, x_dtype=None,
+                 group=None, peers=None):
+        """peers: for ranks emulated in one process, a list per rank of
+        (5 layout buffer pointers, return buffer pointer) used instead of the
+        IPC exchange; this rank's buffers are then exposed by .local_peers()
+        before the list is complete (see the tests)."""
+        import ctypes
+        import torch
+        from ._lib import IPC_HANDLE_BYTES, check, lib
+        self.torch = torch
+        self.backend = backend
+        self.world, self.rank, self.group = world, rank, group
+        cfg = backend.cfg
+        self.d, self.k, self.E = cfg.d_model, cfg.experts_per_token, cfg.num_experts
+        self.max_tokens = max_tokens
+        self.x_dtype = x_dtype or torch.bfloat16
+        self.dev = backend.device
+        self.dev_index = self.dev.index or 0
+        self.ret_rows = max_tokens * self.k
+        handles = ctypes.create_string_buffer(self.BUFS * IPC_HANDLE_BYTES)
+        check(lib().mxmoe_ep_reserve(backend.layer._h, max_tokens, world, handles))
+        self.opened = []
+        self.own_ret = None
+        if peers is None:
+            import torch.distributed as dist
+            self.own_ret = IpcBuffer(self.ret_rows * self.d * 2, self.dev_index)
+            mine = (bytes(handles.raw), bytes(self.own_ret.handle.raw))
+            allh = [None] * world
+            dist.all_gather_object(allh, mine, group=group)
+            own = self.local_peers()[0]
+            table = []
+            for r in range(world):
+                if r == rank:
+                    table.append((own, self.own_ret.ptr.value))
+                    continue
+                hb, hr = allh[r]
+                bufs = [open_peer(hb[i * IPC_HANDLE_BYTES:(i + 1) * IPC_HANDLE_BYTES], self.dev_index)
+                        for i in range(self.BUFS)]
+                ret = open_peer(hr, self.dev_index)
+                self.opened.extend(bufs + [ret])
+                table.append((bufs, ret))
+            self.set_peers(table)
+
+    def local_peers(self):
+        """This rank's 5 layout buffers as device pointers."""
+        import ctypes
+        from ._lib import check, lib
+        arr = (ctypes.c_void_p * self.BUFS)()
+        check(lib().mxmoe_ep_buffers(self.backend.layer._h, arr))
+        return [int(arr[i]) for i in range(self.BUFS)], None
+
+    def set_peers(self, table):
+        """table[r] = (5 layout buffer pointers of rank r, its return buffer pointer)."""
+        t = self.torch
+        flat = [table[r][0][b] for b in range(self.BUFS) for r in range(self.world)]
+        self.peer_bufs = t.tensor(flat, dtype=t.int64, device=self.dev)
+        self.peer_ret = t.tensor([table[r][1] for r in range(self.world)], dtype=t.int64, device=self.dev)
+        self.ret = table[self.rank][1]
+
+    def counts(self, r):
+        o = r.offsets
+        return (o[1:] - o[:-1]).to(self.torch.int32)
+
+    def all_counts(self, counts_dev):
+        t = self.torch
+        allc = t.empty(self.world * self.E, dtype=t.int32, device=counts_dev.device)
+        t.distributed.all_gather_into_tensor(allc, counts_dev, group=self.group)
+        return allc
+
+    def dispatch(self, x, r, allc):
+        from . import _dtype_code, _stream_ptr
+        from ._lib import check, lib
+        check(lib().mxmoe_ep_dispatch(self.backend.layer._h, x.data_ptr(), _dtype_code(x), x.shape[0],
+                                      r.rscale.data_ptr(), r.topk_idx.data_ptr(), r.topk_w.data_ptr(),
+                                      r.inv.data_ptr(), r.offsets.data_ptr(), allc.data_ptr(), self.rank,
+                                      self.peer_bufs.data_ptr(), _stream_ptr()))
+
+    def experts(self):
+        from . import BF16, F32, _stream_ptr
+        from ._lib import check, lib
+        code = BF16 if self.x_dtype == self.torch.bfloat16 else F32
+        check(lib().mxmoe_ep_experts(self.backend.layer._h, code, self.peer_ret.data_ptr(), self.ret_rows,
+                                     _stream_ptr()))
+
+    def combine(self, x, r, out_dtype=None):
+        from . import BF16, _dtype_code, _stream_ptr
+        from ._lib import check, lib
+        y = self.torch.empty(x.shape, dtype=out_dtype or x.dtype, device=x.device)
+        if x.shape[0]:
+            check(lib().mxmoe_combine(x.data_ptr(), _dtype_code(x), x.shape[0], self.d, self.k,
+                                      r.topk_idx.data_ptr(), r.inv.data_ptr(), self.ret, BF16,
+                                      1 if self.backend.cfg.residual else 0, y.data_ptr(), _dtype_code(y),
+                                      _stream_ptr()))
+        return y
+
+    def barrier(self):
+        if not hasattr(self, "tick"):
+            self.tick = self.torch.zeros(1, dtype=self.torch.int32, device=self.dev)
+        self.torch.distributed.all_reduce(self.tick, group=self.group)
+
+    def forward(self, x, out_dtype=None):
+        if x.shape[0] > self.max_tokens:
+            raise ValueError(f"{x.shape[0]} tokens > max_tokens {self.max_tokens}")
+        if x.dtype != self.x_dtype:
+            raise ValueError(f"x dtype {x.dtype} != {self.x_dtype}")
+        r = self.backend.route(x)
+        allc = self.all_counts(self.counts(r))
+        self.dispatch(x, r, allc)
+        self.barrier()  # every pair is in its owner's layout
+        self.experts()
+        self.barrier()  # every output is back at its source
+        return self.combine(x, r, out_dtype)
+
+    def profile(self, x, steps: int = 3):
+        t = self.torch
+        names = ["route", "counts", "dispatch", "experts", "combine"]
+        acc = {nm: 0.0 for nm in names}
+        for _ in range(steps):
+            ev = [t.cuda.Event(enable_timing=True) for _ in range(6)]
+            ev[0].record()
+            r = self.backend.route(x)
+            ev[1].record()
+            allc = self.all_counts(self.counts(r))
+            ev[2].record()
+            self.dispatch(x, r, allc)
+            self.barrier()
+            ev[3].record()
+            self.experts()
+            self.barrier()
+            ev[4].record()
+            self.combine(x, r)
+            ev[5].record()
+            t.cuda.synchronize()
+            for i, nm in enumerate(names):
+                acc[nm] += ev[i].elapsed_time(ev[i + 1]) / steps
+        return acc
+
+    def close(self):
+        from ._lib import lib
+        for p in self.opened:
+            lib().mxmoe_ipc_close(p, self.dev_index)
+        self.opened = []
+        if self.own_ret is not None:
+            self.own_ret.close()
+            self.own_ret = None
+
+
+def build_quantized_peer_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig] = None, group=None):
+    """QuantizedPeerMoe over libmxmoe for synthetic inputs `inp` (mxmoe.synth)."""
+    cfg = cfg or MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    begin, count = shard_bounds(inp.E, world, rank)
+    be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    return QuantizedPeerMoe(be, world, rank, inp.n, group=group)

@@ -308,6 +308,45 @@ MXMOE_API int mxmoe_forward_local_meta(mxmoe_layer* layer, const void* xr, mxmoe
                              const uint32_t* meta, uint32_t n_pairs, void* const* ret_ptrs,
                              uint32_t world, uint32_t ret_rows, uint32_t flags, void* stream);
 
+/* ---- expert parallelism, quantized dispatch into the owners' layouts ----
+ * The source rank quantizes its own tokens once and writes each pair's E4M3
+ * codes, scale words and row metadata straight into the owning rank's GEMM
+ * operand buffers, at the pair's row in the owner's expert-sorted layout,
+ * which every rank derives from the all-gathered pair counts.  The owner
+ * then runs W1/W2 with no permutation or quantization of its own and pushes
+ * each output row back to the source's return buffer.  No host
+ * synchronisation is needed within a step.
+ *
+ * mxmoe_ep_reserve: sizes this layer's workspace for world ranks of up to
+ * max_tokens tokens each (it cannot grow afterwards) and returns 5 IPC
+ * handles (5 x MXMOE_IPC_HANDLE_BYTES): codes, scale atoms, per-row 1/rms,
+ * per-row route weight, per-row return slot.  Ranks exchange them and open
+ * the peers' with mxmoe_ipc_open.  The layer's shard must be E / world
+ * experts. */
+MXMOE_API int mxmoe_ep_reserve(mxmoe_layer* layer, uint32_t max_tokens, uint32_t world, void* handles);
+/* The same 5 buffers as device pointers of this process (ranks emulated on
+ * one GPU use them in place of opened handles). */
+MXMOE_API int mxmoe_ep_buffers(mxmoe_layer* layer, void** ptrs);
+
+/* Source side, after mxmoe_route: counts [world][E] (device) = every rank's
+ * pairs per expert (offsets[e + 1] - offsets[e], all-gathered); inv and
+ * offsets are this rank's canonical maps.  peer_bufs: device array of
+ * 5 x world pointers, grouped by buffer in the mxmoe_ep_reserve order
+ * ([codes of ranks 0..world-1][scales ...]...).  Also records, for this
+ * rank's own experts, the layout mxmoe_ep_experts runs on.  Every rank must
+ * pass the same counts and x dtype. */
+MXMOE_API int mxmoe_ep_dispatch(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
+                      const float* rscale, const int32_t* topk_idx, const float* topk_w,
+                      const int32_t* inv, const int32_t* offsets, const int32_t* counts,
+                      uint32_t rank, void* const* peer_bufs, void* stream);
+
+/* Owner side, once every rank's dispatch has completed: the expert FFN over
+ * the rows the sources wrote, each output weight * (W2 act + b2) pushed to
+ * row (slot & 0xFFFFFF) of peer_ret[slot >> 24] (bf16 return buffers of
+ * ret_rows rows, canonical order at the source). */
+MXMOE_API int mxmoe_ep_experts(mxmoe_layer* layer, mxmoe_dtype x_dtype, void* const* peer_ret, uint32_t ret_rows,
+                     void* stream);
+
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
  * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers, each

@@ -94,3 +94,41 @@ def test_peer_dispatch_emulated_on_one_gpu(world, n_per, E, k, flags):
         want = full.forward(xs[r], out_dtype=torch.float32)
         assert_close(ys[r].cpu().numpy(), want.cpu().numpy(), f"peer EP rank {r}/{world}")
     full.close()
+
+
+@pytest.mark.parametrize("world,n_per,E,k", [(2, 100, 8, 4), (4, 64, 8, 2), (4, 300, 16, 4), (2, 40, 4, 2)])
+def test_quantized_dispatch_emulated_on_one_gpu(world, n_per, E, k):
+    """Quantized dispatch into the owners' layouts with `world` ranks emulated
+    on one GPU (each rank its own layer and workspace; the pointer tables
+    stand in for the IPC-opened peers).  Every rank's output must match the
+    single-layer forward."""
+    import torch
+    from mxmoe.ep import QuantizedPeerMoe
+    inp = synth.make_inputs(512, 384, E, k, world * n_per, True, seed=41 + world + E)
+    full = make_layer(inp)
+    x_all = to_device_x(inp)
+    cfg = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    rets = [torch.zeros(n_per * k, inp.d, dtype=torch.bfloat16, device="cuda:0") for _ in range(world)]
+    ranks = []
+    for r in range(world):
+        b, c = shard_bounds(inp.E, world, r)
+        be = CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+        ranks.append(QuantizedPeerMoe(be, world, r, n_per, peers=[]))
+    table = [(m.local_peers()[0], rets[r].data_ptr()) for r, m in enumerate(ranks)]
+    for m in ranks:
+        m.set_peers(table)
+    xs = [x_all[r * n_per:(r + 1) * n_per].contiguous() for r in range(world)]
+    for _ in range(2):  # a second step reuses the layouts
+        routes = [m.backend.route(x) for m, x in zip(ranks, xs)]
+        allc = torch.cat([m.counts(rt) for m, rt in zip(ranks, routes)])
+        for m, x, rt in zip(ranks, xs, routes):
+            m.dispatch(x, rt, allc)
+        for m in ranks:
+            m.experts()
+        ys = [m.combine(x, rt, out_dtype=torch.float32) for m, x, rt in zip(ranks, xs, routes)]
+        torch.cuda.synchronize()
+        for r in range(world):
+            ranks[r].backend.layer.sync_status()
+            want = full.forward(xs[r], out_dtype=torch.float32)
+            assert_close(ys[r].cpu().numpy(), want.cpu().numpy(), f"quantized EP rank {r}/{world}")
+    full.close()
