@@ -19,9 +19,7 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -51,53 +49,61 @@ def load_peaks():
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """SM clock and throttle-reason sampling during the timed region, from
+    NVML in a background thread (every ~2 ms, so that short timed regions
+    still get samples).  Only reads: no clock or setting is changed."""
+    # NVML clocks-event reason bits
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
 
     def __init__(self, gpu_index):
         self.gpu = gpu_index
-        self.proc = None
-        self.tmp = None
+        self.samples = []
+        self.thread = None
+        self.stop = False
+        self.err = None
+
+    def _handle(self, nv):
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(self.gpu)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId(bus.encode())
+        except Exception:
+            return nv.nvmlDeviceGetHandleByIndex(self.gpu)
+
+    def _run(self):
+        try:
+            import pynvml as nv
+            nv.nvmlInit()
+            h = self._handle(nv)
+            smax = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+            get_reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                nv.nvmlDeviceGetCurrentClocksThrottleReasons
+            while not self.stop:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), smax, get_reasons(h)))
+                time.sleep(0.002)
+        except Exception as exc:  # noqa: BLE001
+            self.err = f"nvml: {exc}"
 
     def __enter__(self):
-        try:
-            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+        import threading
+        self.thread = threading.Thread(target=self._run, daemon=True)
+        self.thread.start()
+        time.sleep(0.01)  # first samples precede the timed region's start
         return self
 
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop = True
+        if self.thread is not None:
+            self.thread.join(timeout=5)
 
     def summary(self):
-        if self.proc is None or self.tmp is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.tmp.flush()
-        rows = []
-        with open(self.tmp.name) as f:
-            for line in f:
-                parts = [p.strip() for p in line.split(",")]
-                if len(parts) >= 9:
-                    rows.append(parts)
-        os.unlink(self.tmp.name)
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(rows)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.err or "no samples"]}
+        sm = [s[0] for s in self.samples]
+        reasons = sorted({name for s in self.samples for bit, name in self.REASONS.items() if s[2] & bit})
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(s[1] for s in self.samples), "reasons": reasons,
+                "samples": len(self.samples), "source": "nvml"}
 
 
 def dist_setup(n_gpus):
@@ -255,7 +261,29 @@ def run_ours(args, world, rank, local):
     clocks = clk.summary()
 
     if world > 1:
-        stages, e2e = runner.profile(x, args.steps), None
+        stages = runner.profile(x, args.steps)
+        # end to end through the layer's Python API: each step copies its
+        # tokens from pinned host memory, runs the expert-parallel forward and
+        # reads the output back to pinned host memory; wall clock, max over ranks
+        xh = x.cpu().pin_memory()
+        yh = torch.empty_like(xh).pin_memory()
+        xd = torch.empty_like(x)
+
+        def e2e_step():
+            xd.copy_(xh, non_blocking=True)
+            yh.copy_(runner.forward(xd), non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        e2e_step()
+        torch.distributed.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_step()
+        e2e_s = torch.tensor([(time.perf_counter() - t0) / args.steps], device=dev)
+        torch.distributed.all_reduce(e2e_s, op=torch.distributed.ReduceOp.MAX)
+        e2e = {"value": n * world / float(e2e_s.item()), "unit": UNIT,
+               "h2d_bytes_per_step": xh.numel() * xh.element_size(),
+               "d2h_bytes_per_step": yh.numel() * yh.element_size(), "per": "rank"}
         if rank == 0:
             line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
@@ -264,7 +292,8 @@ def run_ours(args, world, rank, local):
                     "config": {"workload": "gptoss20b_moe_prefill", "tokens_per_gpu": n, "experts": E,
                                "experts_per_gpu": E // world, "top_k": k, "parallelism": f"ep{world}",
                                "l2": "working set > 126 MB L2 (expert weights alone 423 MB)"},
-                    "clocks": clocks, "stages_ms": stages, "gpu_launches": runner.launches_per_step * args.steps}
+                    "e2e": e2e, "clocks": clocks, "stages_ms": stages,
+                    "gpu_launches": runner.launches_per_step * args.steps}
             print(json.dumps(line), flush=True)
         torch.distributed.destroy_process_group()
         return

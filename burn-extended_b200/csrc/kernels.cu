@@ -701,12 +701,13 @@ struct EpDispatch {
 // with unit gain exactly; three are used for f32 input or a non-unit gain).
 // Each token block is quantized once and written to the positions of all k
 // pairs of the token.
-// Warp per (token, octet of eight 32-column blocks); the four lanes of a
-// quad share one block, eight columns (16 bytes of bf16) each, so loads and
-// code stores are contiguous across the warp.  The block's per-term scale
-// comes from a max over the quad; the arithmetic per element is
-// quantize_block32's.  Lanes of blocks past d / 32 contribute zero scale
-// bytes (the K padding) and store no codes.
+// Warp per (token, group of sixteen 32-column blocks); the two lanes of a
+// lane pair share one block, sixteen columns (32 bytes of bf16) each, so a
+// warp's loads and 16-byte code stores cover 1 KB / 512 B contiguous.  The
+// block's per-term scale comes from a max over the lane pair; the arithmetic
+// per element is quantize_block32's.  Lanes of blocks past d / 32 store no
+// codes and add zero scale bytes (the K padding).
+constexpr int kQBlocksPerWarp = 16;
 template <bool kDispatch>
 __global__ void __launch_bounds__(256)
     quantize_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
@@ -714,57 +715,61 @@ __global__ void __launch_bounds__(256)
                           int terms, uint8_t* codes, uint64_t term_stride, int kp, uint8_t* sf,
                           uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked, const EpDispatch ep) {
   const int nb = d / 32;
-  const int noct = (nb + 7) / 8;
-  const uint64_t items = static_cast<uint64_t>(n) * noct;
+  const int ngrp = (nb + kQBlocksPerWarp - 1) / kQBlocksPerWarp;
+  const uint64_t items = static_cast<uint64_t>(n) * ngrp;
   const int lane = threadIdx.x & 31;
-  const int qtr = lane & 3, lb = lane >> 2;
+  const int hf = lane & 1, lb = lane >> 1;  // half of the block, block within the group
   const uint64_t wstride = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
   for (uint64_t it = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
        it += wstride) {
-    const int t = static_cast<int>(it / noct);
-    const int b = static_cast<int>(it - static_cast<uint64_t>(t) * noct) * 8 + lb;
+    const int t = static_cast<int>(it / ngrp);
+    const int grp = static_cast<int>(it - static_cast<uint64_t>(t) * ngrp);
+    const int b = grp * kQBlocksPerWarp + lb;
     const bool active = b < nb;
-    const int c0 = b * 32 + qtr * 8;
-    float v[8];
+    const int c0 = b * 32 + hf * 16;
+    float v[16];
     if (!active) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+      for (int i = 0; i < 16; ++i) v[i] = 0.0f;
     } else if (x_dtype == 1) {
-      const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
-                                                            static_cast<uint64_t>(t) * d + c0));
-      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+      const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
+                                                        static_cast<uint64_t>(t) * d + c0);
+      const uint4 u0 = __ldg(xs), u1 = __ldg(xs + 1);
+      const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        v[2 * h] = __uint_as_float(w4[h] << 16);
-        v[2 * h + 1] = __uint_as_float(w4[h] & 0xFFFF0000u);
+      for (int h = 0; h < 8; ++h) {
+        v[2 * h] = __uint_as_float(w8[h] << 16);
+        v[2 * h + 1] = __uint_as_float(w8[h] & 0xFFFF0000u);
       }
     } else {
       const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<uint64_t>(t) * d + c0);
-      const float4 a = __ldg(xs), c = __ldg(xs + 1);
-      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = c.x; v[5] = c.y; v[6] = c.z; v[7] = c.w;
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float4 a = __ldg(xs + h);
+        v[4 * h] = a.x; v[4 * h + 1] = a.y; v[4 * h + 2] = a.z; v[4 * h + 3] = a.w;
+      }
     }
     if (!gamma_is_one && active) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
+      for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
     }
-    uint32_t words[kMaxTerms][2];
+    uint32_t words[kMaxTerms][4];
     uint32_t sword[kMaxTerms];
 #pragma unroll
     for (int q = 0; q < kMaxTerms; ++q) {
-      words[q][0] = words[q][1] = 0;
+      words[q][0] = words[q][1] = words[q][2] = words[q][3] = 0;
       sword[q] = 0;
       if (q < terms) {
         float amax = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+        for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
         amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
-        amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
         const int s = e4m3_block_exp(amax);
         const bool fast = (s > -126) && (s < 127);
         const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
         const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
 #pragma unroll
-        for (int w = 0; w < 2; ++w) {
+        for (int w = 0; w < 4; ++w) {
           uint32_t word = 0;
 #pragma unroll
           for (int hp = 0; hp < 2; ++hp) {
@@ -791,16 +796,16 @@ __global__ void __launch_bounds__(256)
           }
           words[q][w] = word;
         }
-        // the scale words of four consecutive blocks (quads lb & ~3 .. +3)
+        // the scale word of four consecutive blocks (lane pairs lb & ~3 .. +3)
         uint32_t sw = active ? static_cast<uint32_t>(s + 127) << (8 * (lb & 3)) : 0u;
+        sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 2);
         sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 4);
-        sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 8);
         sword[q] = sw;
       }
     }
     // one lane per group of four blocks stores the group's scale word; a group
     // wholly past d / 32 would land in the next row block's atom and stores nothing
-    const bool sf_lane = qtr == 0 && (lb & 3) == 0 && active;
+    const bool sf_lane = hf == 0 && (lb & 3) == 0 && active;
 #pragma unroll
     for (int s = 0; s < kMaxTopK; ++s) {
       if (s >= k) break;
@@ -821,7 +826,7 @@ __global__ void __launch_bounds__(256)
         }
         codes_d = ep.xq[g];
         sf_d = ep.xsf[g];
-        if (lane == 0 && static_cast<int>(it % noct) == 0) {
+        if (lane == 0 && grp == 0) {
           ep.rs[g][pos] = __ldg(ep.rscale + t);
           ep.wt[g][pos] = __ldg(ep.topk_w + p);
           ep.slot[g][pos] = (static_cast<uint32_t>(ep.rank) << 24) | static_cast<uint32_t>(q0);
@@ -836,7 +841,7 @@ __global__ void __launch_bounds__(256)
                                                                                 static_cast<uint32_t>(sf_rows)))
                                        : static_cast<uint64_t>(pos);
           uint8_t* dst = codes_d + (stacked ? 0 : q * term_stride) + row * kp + c0;
-          *reinterpret_cast<uint2*>(dst) = make_uint2(words[q][0], words[q][1]);
+          *reinterpret_cast<uint4*>(dst) = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
         }
         if (sf_lane) {
           const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
@@ -1287,7 +1292,7 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,
                                   int sf_rows, int stacked, cudaStream_t st) {
-  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + 7) / 8);  // warps
+  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQBlocksPerWarp - 1) / kQBlocksPerWarp);  // warps
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
@@ -1361,7 +1366,7 @@ cudaError_t launch_ep_quantize_dispatch(const void* x, int x_dtype, int n, int d
                                         const float* topk_w, const float* rscale, int epr, int rank,
                                         uint32_t dst_rows, uint8_t* const* xq, uint8_t* const* xsf, float* const* rs,
                                         float* const* wt, uint32_t* const* slot, int* err, cudaStream_t st) {
-  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + 7) / 8);
+  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQBlocksPerWarp - 1) / kQBlocksPerWarp);
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
