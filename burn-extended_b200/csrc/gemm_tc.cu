@@ -391,16 +391,24 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
     float* xl = epi;                   // [64][kXPitch] linear half (weights-as-A)
     float* as = epi + 64 * kXPitch;    // [kChunk][kAPitch] activations (weights-as-A)
     float* rs = as + kChunk * kAPitch; // [kChunk] 1/rms per column
-    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
-      int e, wt, pt;
-      decode_tile(p, t, e, wt, pt);
-      if (!mbar_wait(&tmem_full[acc], acc_phase[acc], err, kDevTimeoutTmemFull)) break;
-      acc_phase[acc] ^= 1u;
-      tc_fence_after();
+    // Tokens-as-A: the first pass (t < 0) is dry -- zeros instead of an
+    // accumulator, no stores -- and runs while the first tile's MMAs do, so
+    // the epilogue's long straight-line code is in the instruction cache
+    // before the first real accumulator arrives.
+    for (int t = static_cast<int>(blockIdx.x) - (kTok ? static_cast<int>(gridDim.x) : 0); t < total_tiles;
+         t += gridDim.x) {
+      const bool dry = kTok && t < 0;
+      int e = 0, wt = 0, pt = 0;
+      if (!dry) {
+        decode_tile(p, t, e, wt, pt);
+        if (!mbar_wait(&tmem_full[acc], acc_phase[acc], err, kDevTimeoutTmemFull)) break;
+        acc_phase[acc] ^= 1u;
+        tc_fence_after();
+      }
       const uint32_t trow = tmem_base + static_cast<uint32_t>(acc * 128) + (static_cast<uint32_t>(sp * 32) << 16);
-      const int cnt = __ldg(p.counts + e);
+      const int cnt = dry ? PT : __ldg(p.counts + e);
       const int n_valid = min(PT, cnt - pt * PT);
-      const int pos0 = __ldg(p.poff + e) + pt * PT;
+      const int pos0 = dry ? 0 : __ldg(p.poff + e) + pt * PT;
       const uint64_t bias_e = static_cast<uint64_t>(e) * p.bias_stride;
       if (kTok) {
         // Thread = pair row m; this warp owns columns [half*128, half*128 + 128)
@@ -409,12 +417,17 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         // overlap this epilogue.
         const int half = (warp - 2) >> 2;
         float v[128];
+        if (dry) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(trow + half * 128 + q * 32, v + q * 32);
-        tmem_wait_ld();
-        tc_fence_before();
-        mbar_arrive(&tmem_empty[acc]);
-        if (++acc == nacc) acc = 0;
+          for (int i = 0; i < 128; ++i) v[i] = 0.0f;
+        } else {
+#pragma unroll
+          for (int q = 0; q < 4; ++q) tmem_ld_32x32b_x32(trow + half * 128 + q * 32, v + q * 32);
+          tmem_wait_ld();
+          tc_fence_before();
+          mbar_arrive(&tmem_empty[acc]);
+          if (++acc == nacc) acc = 0;
+        }
         if (p.stacked) {
           // Lane L < 16 holds the hi-term row of pair sp*16 + L, lane L + 16 its
           // lo-term row.  The two lanes swap partial sums so that each ends
@@ -449,7 +462,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
             __nv_bfloat16* dst = w2_out_row(p, pos, pair) + cf0;
 #pragma unroll
             for (int q = 0; q < 8; ++q)
-              if (cf0 + 8 * q < p.rows_valid)
+              if (!dry && cf0 + 8 * q < p.rows_valid)
                 store_w2_8(dst + 8 * q, g + 8 * q, __ldg(bb + 2 * q), __ldg(bb + 2 * q + 1), p.bias_mult, w);
           } else {
             const int unit0 = wt * 128 + half * 64 + (upper ? 32 : 0);  // GLU unit of g[0]
@@ -470,7 +483,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
             uint32_t words[kMaxTerms][8];
             uint8_t sbyte[kMaxTerms];
             quantize_block32(a, 2, words, sbyte);
-            store_block_terms(p, pos, unit0, words, sbyte);
+            if (!dry) store_block_terms(p, pos, unit0, words, sbyte);
           }
           continue;
         }
@@ -486,7 +499,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
           __nv_bfloat16* dst = w2_out_row(p, pos, pair) + cf0;
 #pragma unroll
           for (int q = 0; q < 16; ++q)
-            if (cf0 + 8 * q < p.rows_valid)
+            if (!dry && cf0 + 8 * q < p.rows_valid)
               store_w2_8(dst + 8 * q, v + 8 * q, __ldg(bb + 2 * q), __ldg(bb + 2 * q + 1), p.bias_mult, w);
         } else {
           const int unit0 = wt * 128 + half * 64;  // GLU unit of v[0]
@@ -510,7 +523,7 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
             uint32_t words[kMaxTerms][8];
             uint8_t sbyte[kMaxTerms];
             quantize_block32(a, 2, words, sbyte);
-            store_block_terms(p, pos, unit0 + sb * 32, words, sbyte);
+            if (!dry) store_block_terms(p, pos, unit0 + sb * 32, words, sbyte);
           }
         }
         continue;
