@@ -199,6 +199,92 @@ def measure_decode(args, local, dev, hbm_peak):
             "l2": "weights of the 32 experts (423 MB) exceed the 126 MB L2; no flush"}
 
 
+def measure_microbench(args, local, dev, hbm_peak):
+    """Single-expert fused dequant + GEMV: W1 [5760, 2880]
+    and W2 [2880, 2880] MXFP4, bf16 activations at T = 1, 2, 4, 8 tokens.
+    Independent copies of the expert (one layer each) are used in rotation,
+    together 4x the 126 MB L2, so every call streams its weights from HBM.
+    GB/s = algorithmic bytes (the expert's codes, scales and biases plus the
+    activations in and out) / time, for the whole layer call and for its two
+    GEMM launches alone (CUDA events on the call's stream)."""
+    import torch
+    import mxmoe
+    from mxmoe import synth
+    d = f = 2880
+    per_expert = 2 * f * d // 2 + 2 * f * d // 32 + d * f // 2 + d * f // 32
+    copies = int(np.ceil(4 * 126e6 / per_expert)) + 1
+    base = synth.make_inputs(d, f, 1, 1, 8, True, seed=args.seed + 7)
+    layers = []
+    for _ in range(copies):
+        L = mxmoe.MoeConfig(d, f, 1, 1).init(local)
+        L.set_router(base.gamma, base.gate_w, base.gate_b)
+        L.set_resident(base.host, base.b1, base.b2)
+        L.reserve(8)  # the rotation never resizes a workspace inside the timed loop
+        layers.append(L)
+    out = {}
+    for T in (1, 2, 4, 8):
+        x = torch.from_numpy(base.x[:T]).to(torch.bfloat16).to(dev)
+        for L in layers:
+            L.forward(x)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        calls = max(args.steps, 1) * copies
+        s.record()
+        for i in range(calls):
+            layers[i % copies].forward(x)
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / calls
+        gemm = []
+        for i in range(copies):
+            layers[i].set_profiling(True)
+            layers[i].forward(x)
+            pr = layers[i].last_profile()
+            gemm.append(pr["w1_gemm"] + pr["w2_gemm"])
+            layers[i].set_profiling(False)
+        gemm_ms = statistics.median(gemm)
+        nbytes = per_expert + 2 * (2 * f + d) + 2 * T * d * 2
+        out[f"T{T}"] = {"us_per_call": ms * 1e3, "gbs": nbytes / (ms / 1e3) / 1e9,
+                        "hbm_frac": nbytes / (ms / 1e3) / 1e9 / hbm_peak, "gemm_us": gemm_ms * 1e3,
+                        "gemm_gbs": nbytes / (gemm_ms / 1e3) / 1e9,
+                        "gemm_hbm_frac": nbytes / (gemm_ms / 1e3) / 1e9 / hbm_peak}
+    for L in layers:
+        L.close()
+    return {"config": "single-expert MXFP4 dequant+GEMV, W1 [5760,2880] + W2 [2880,2880], bf16 x",
+            "rotation": f"{copies} expert copies ({copies * per_expert / 1e6:.0f} MB, >= 4x L2)",
+            "algorithmic_bytes_per_call": "codes + scales + biases + 2*T*d*2 activation bytes", **out}
+
+
+def measure_120b(args, local, dev):
+    """GPT-OSS-120B-shaped layer on one GPU: 4096 tokens,
+    128 experts, top-4, router bias giving a Zipf(1.1)-like expert load."""
+    import torch
+    import mxmoe
+    from mxmoe import synth
+    inp = synth.make_config("gptoss120b", seed=args.seed)
+    L = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k).init(local)
+    L.set_router(inp.gamma, inp.gate_w, inp.gate_b)
+    L.set_resident(inp.host, inp.b1, inp.b2)
+    x = torch.from_numpy(inp.x).to(torch.bfloat16).to(dev)
+    for _ in range(3):
+        L.forward(x)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        L.forward(x)
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    load = np.diff(L.routing_results(inp.n)["offsets"].cpu().numpy())
+    flops = 2.0 * inp.n * inp.k * (2 * inp.f * inp.d + inp.f * inp.d) + 2.0 * inp.n * inp.d * inp.E
+    L.close()
+    return {"config": "gptoss120b_moe (4096 tokens, 128 experts, top-4, Zipf(1.1) router bias), 1 GPU",
+            "tokens_per_s": inp.n / (ms / 1e3), "ms_per_step": ms, "useful_tflops": flops / (ms / 1e3) / 1e12,
+            "expert_load_max": int(load.max()), "expert_load_mean": float(load.mean()),
+            "expert_load_max_over_mean": float(load.max() / load.mean()), "experts_unused": int((load == 0).sum())}
+
+
 def run_ours(args, world, rank, local):
     import torch
     import mxmoe
@@ -212,6 +298,12 @@ def run_ours(args, world, rank, local):
     hbm_peak, tc_burst, tc_sust, peak_src = load_peaks()
     if args.only == "decode":
         print(json.dumps({"decode": measure_decode(args, local, dev, hbm_peak)}), flush=True)
+        return
+    if args.only == "microbench":
+        print(json.dumps({"microbench": measure_microbench(args, local, dev, hbm_peak)}), flush=True)
+        return
+    if args.only == "gptoss120b":
+        print(json.dumps({"gptoss120b": measure_120b(args, local, dev)}), flush=True)
         return
 
     inp = synth.make_config("prefill", seed=args.seed + rank)
@@ -338,6 +430,9 @@ def run_ours(args, world, rank, local):
            "d2h_bytes_per_step": yh.numel() * yh.element_size()}
 
     extra["decode"] = measure_decode(args, local, dev, hbm_peak)
+    if args.only == "all":
+        extra["microbench"] = measure_microbench(args, local, dev, hbm_peak)
+        extra["gptoss120b"] = measure_120b(args, local, dev)
 
     cpu = None
     if not args.no_cpu_baseline:
@@ -373,8 +468,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=24)
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["all", "prefill", "decode"], default="all",
-                    help="prefill / decode: run only that leg (profiling runs)")
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "microbench", "gptoss120b"], default="all",
+                    help="run only that leg (profiling runs); 'all' adds decode, microbench and gptoss120b as extras")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)
     if args.impl == "reference":

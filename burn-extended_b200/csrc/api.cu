@@ -317,9 +317,16 @@ struct TilePlan {
   int pair_tile;
   int tw;
   bool stacked;
+  bool gemv = false;  // fused dequant-GEMV on CUDA cores instead of tensor-core tiles
 };
 
-TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms) {
+// Tiny batches (at most kGemvMaxPairs routed pairs in all) go to the fused
+// dequant-GEMV kernels, which spread the weights over every SM; tensor-core
+// tiles would leave most SMs idle there.
+constexpr uint64_t kGemvMaxPairs = 64;
+
+TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_gemv = false) {
+  if (allow_gemv && pairs <= kGemvMaxPairs) return {true, 8, 0, false, true};  // callers check kGemvMaxK
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
   // two-term activations: stacked tiles (tw indexes tmap_x_stk / tmap_act_stk)
   if (x_terms == 2 && avg <= 12) return {true, 16, 0, true};
@@ -356,6 +363,19 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
     if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
     CUDA_TRY(launch_simt_w2(w.act_f32, L->fp, L->d, k, L->w2q, L->w2sf, L->b2, bias_mult, L->kp2, L->e_count, w.poff,
                             w.counts, w.perm_p, route_w, w.y_pair, st));
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
+    return MXMOE_OK;
+  }
+  if (tp.gemv) {
+    if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
+    w.pair_dtype = MXMOE_F32;
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
+    CUDA_TRY(launch_gemv_w1(x, x_dtype, L->d, k, L->gamma, rscale, L->w1q, L->w1sf, L->b1, L->fp, L->kp1, L->e_count,
+                            w.poff, w.counts, perm ? perm : w.perm_p, L->cfg.swiglu_alpha, L->cfg.swiglu_limit,
+                            w.act_f32, static_cast<int>(P), st));
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
+    CUDA_TRY(launch_gemv_w2(w.act_f32, L->fp, L->d, L->w2q, L->w2sf, L->b2, bias_mult, L->kp2, L->e_count, w.poff,
+                            w.counts, perm ? perm : w.perm_p, route_w, w.y_pair, static_cast<int>(P), st));
     if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
     return MXMOE_OK;
   }
@@ -685,7 +705,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   const uint32_t k = L->k, E = L->e_count;
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
   const int xt = x_terms_for(L, x_dtype);
-  const TilePlan tp = pick_tiles(P, E, xt);
+  const TilePlan tp = pick_tiles(P, E, xt, L->d <= kGemvMaxK && L->fp <= kGemvMaxK);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   L->profile_valid = false;
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
@@ -929,7 +949,7 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   Workspace& w = L->ws;
   cudaStream_t st = as_stream(stream);
   const int xt = x_terms_for(L, xr_dtype);
-  const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt);
+  const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt, L->d <= kGemvMaxK && L->fp <= kGemvMaxK);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   CUDA_TRY(launch_localize(expert, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
                            static_cast<int>(L->e_count), w.local_idx, L->err, st));

@@ -81,6 +81,16 @@ cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t*
 cudaError_t launch_iota(int32_t* a, int n, cudaStream_t st);
 cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
                               uint32_t* slot, cudaStream_t st);
+// Fused dequant-GEMV expert FFN for a few pairs per expert (f32 act / y_pair);
+// d and the padded ffn width must be at most kGemvMaxK.
+constexpr int kGemvMaxK = 4096;
+cudaError_t launch_gemv_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
+                           const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
+                           const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
+                           float* act, int max_pairs, cudaStream_t st);
+cudaError_t launch_gemv_w2(const float* act, int fp, int d, const uint8_t* w2q, const uint8_t* w2sf, const float* b2,
+                           float bias_mult, int kp2, int E, const int32_t* poff, const int32_t* counts,
+                           const int32_t* perm_p, const float* topk_w, float* y_pair, int max_pairs, cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
                            const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
                            const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
