@@ -171,6 +171,9 @@ struct Workspace {
   uint32_t* pos_slot = nullptr;    // [rows]
   int32_t* iota = nullptr;         // [rows] identity permutation
   int32_t* ep_src_base = nullptr;  // [E_total]
+  uint8_t* ep_sf_rows = nullptr;   // [rows][kMaxTerms][ep_sf_row_bytes] scale bytes written by the sources
+  uint32_t* ep_meta = nullptr;     // [rows][4] {1/rms, route weight, return slot, 0} written by the sources
+  uint32_t ep_sf_row_bytes = 0;
   int pair_dtype = MXMOE_F32;   // element type the last run_experts wrote y_pair in
   CUtensorMap tmap_x[kNumTileWidths];
   CUtensorMap tmap_act[kNumTileWidths];
@@ -222,6 +225,8 @@ void free_workspace(Workspace& w) {
   dfree(w.pos_slot);
   dfree(w.iota);
   dfree(w.ep_src_base);
+  dfree(w.ep_sf_rows);
+  dfree(w.ep_meta);
   dfree(w.perm_scratch);
   w.cap_tokens = w.cap_pairs = w.rows = w.row_blocks = 0;
 }
@@ -271,6 +276,9 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   TRY(dalloc(&w.pos_slot, w.rows));
   TRY(dalloc(&w.iota, w.rows));
   TRY(dalloc(&w.ep_src_base, Et));
+  w.ep_sf_row_bytes = round_up(L->d / 32, 16);
+  TRY(dalloc(&w.ep_sf_rows, static_cast<size_t>(w.rows) * 3 * w.ep_sf_row_bytes));  // up to 3 terms
+  TRY(dalloc(&w.ep_meta, static_cast<size_t>(w.rows) * 4));
   CUDA_TRY(launch_iota(w.iota, static_cast<int>(w.rows), 0));
   const size_t pscr = permute_scratch_ints(static_cast<int>(cap_p), static_cast<int>(Et));
   TRY(dalloc(&w.perm_scratch, pscr));
@@ -1076,6 +1084,8 @@ int mxmoe_forward_local_meta(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtyp
 }
 
 // ---- expert parallelism: quantized dispatch into the owners' layouts
+constexpr int kEpBuffers = 3;  // codes, row-major scales, row metadata (mxmoe_ep_reserve order)
+
 int mxmoe_ep_reserve(mxmoe_layer* L, uint32_t max_tokens, uint32_t world, void* handles) {
   TRY(check_layer(L));
   if (!handles || max_tokens == 0 || world == 0) return fail(MXMOE_ERR_INVALID_ARG, "bad ep reservation");
@@ -1088,8 +1098,8 @@ int mxmoe_ep_reserve(mxmoe_layer* L, uint32_t max_tokens, uint32_t world, void* 
   TRY(ensure_workspace(L, world * max_tokens, L->k));
   CUDA_TRY(cudaDeviceSynchronize());
   Workspace& w = L->ws;
-  void* bufs[5] = {w.xq, w.xsf, w.pos_rscale, w.pos_weight, w.pos_slot};
-  for (int i = 0; i < 5; ++i) {
+  void* bufs[kEpBuffers] = {w.xq, w.ep_sf_rows, w.ep_meta};
+  for (int i = 0; i < kEpBuffers; ++i) {
     cudaIpcMemHandle_t h;
     CUDA_TRY(cudaIpcGetMemHandle(&h, bufs[i]));
     std::memcpy(static_cast<uint8_t*>(handles) + i * MXMOE_IPC_HANDLE_BYTES, &h, sizeof(h));
@@ -1127,16 +1137,14 @@ int mxmoe_ep_dispatch(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32
                             static_cast<int>(L->e_count), kRowBlock, tp.pair_tile, w.ep_src_base, w.poff, w.counts,
                             w.ntile_prefix, st));
   if (n_tokens == 0) return MXMOE_OK;
-  const uint64_t kc1 = L->kp1 / kTileK;
   void* const* pb = peer_bufs;
   CUDA_TRY(launch_ep_quantize_dispatch(
       x, x_dtype, static_cast<int>(n_tokens), static_cast<int>(L->d), static_cast<int>(L->k), L->gamma,
       L->gamma_is_one ? 1 : 0, inv, xt, static_cast<uint64_t>(w.rows) * L->kp1, static_cast<int>(L->kp1),
-      static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes, static_cast<int>(kc1), tp.pair_tile,
-      tp.stacked ? 1 : 0, w.ep_src_base, offsets, topk_idx, topk_w, rscale, static_cast<int>(L->e_count),
-      static_cast<int>(rank), w.rows, reinterpret_cast<uint8_t* const*>(pb), reinterpret_cast<uint8_t* const*>(pb + world),
-      reinterpret_cast<float* const*>(pb + 2 * world), reinterpret_cast<float* const*>(pb + 3 * world),
-      reinterpret_cast<uint32_t* const*>(pb + 4 * world), L->err, st));
+      tp.pair_tile, tp.stacked ? 1 : 0, w.ep_src_base, offsets, topk_idx, topk_w, rscale,
+      static_cast<int>(L->e_count), static_cast<int>(rank), w.rows, w.ep_sf_row_bytes,
+      reinterpret_cast<uint8_t* const*>(pb), reinterpret_cast<uint8_t* const*>(pb + world), pb + 2 * world, L->err,
+      st));
   return MXMOE_OK;
 }
 
@@ -1151,6 +1159,11 @@ int mxmoe_ep_experts(mxmoe_layer* L, mxmoe_dtype x_dtype, void* const* peer_ret,
   const int xt = x_terms_for(L, x_dtype);
   const TilePlan tp = ep_tiles(L, xt);
   L->profile_valid = false;
+  const uint64_t kc1 = L->kp1 / kTileK;
+  CUDA_TRY(launch_ep_unpack(w.ep_meta, w.ep_sf_rows, w.ep_sf_row_bytes, xt, static_cast<int>(L->d / 32),
+                            static_cast<int>(w.rows), w.poff, w.counts, static_cast<int>(L->e_count), w.pos_rscale,
+                            w.pos_weight, w.pos_slot, w.xsf, static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes,
+                            static_cast<int>(kc1), tp.pair_tile, tp.stacked ? 1 : 0, st));
   // rows are their own pairs (identity permutation, one pair per row)
   TRY(run_experts(L, nullptr, x_dtype, L->ep_world * L->ep_max_tokens * L->k, 1, w.pos_rscale, w.pos_weight, tp, xt,
                   st, nullptr, nullptr, false, true, w.iota));
@@ -1166,10 +1179,8 @@ int mxmoe_ep_buffers(mxmoe_layer* L, void** ptrs) {
   if (!ptrs) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   Workspace& w = L->ws;
   ptrs[0] = w.xq;
-  ptrs[1] = w.xsf;
-  ptrs[2] = w.pos_rscale;
-  ptrs[3] = w.pos_weight;
-  ptrs[4] = w.pos_slot;
+  ptrs[1] = w.ep_sf_rows;
+  ptrs[2] = w.ep_meta;
   return MXMOE_OK;
 }
 

@@ -688,11 +688,10 @@ struct EpDispatch {
   const float* rscale;
   int epr, rank;
   uint32_t dst_rows;        // rows of every owner's layout
+  uint32_t sf_row_bytes;    // scale bytes per row and term in sf_rows (a multiple of 16)
   uint8_t* const* xq;       // [world] code buffers
-  uint8_t* const* xsf;      // [world] scale-atom buffers
-  float* const* rs;         // [world] per-row 1 / rms
-  float* const* wt;         // [world] per-row route weight
-  uint32_t* const* slot;    // [world] per-row return slot (rank << 24 | canonical position)
+  uint8_t* const* sf_rows;  // [world] row-major scale bytes [rows][terms][sf_row_bytes]
+  uint4* const* meta;       // [world] per-row {bits of 1/rms, bits of route weight, return slot, 0}
   int* err;
 };
 
@@ -826,11 +825,19 @@ __global__ void __launch_bounds__(256)
           continue;
         }
         codes_d = ep.xq[g];
-        sf_d = ep.xsf[g];
-        if (lane == 0 && grp == 0) {
-          ep.rs[g][pos] = __ldg(ep.rscale + t);
-          ep.wt[g][pos] = __ldg(ep.topk_w + p);
-          ep.slot[g][pos] = (static_cast<uint32_t>(ep.rank) << 24) | static_cast<uint32_t>(q0);
+        if (lane == 0 && grp == 0)
+          ep.meta[g][pos] = make_uint4(__float_as_uint(__ldg(ep.rscale + t)), __float_as_uint(__ldg(ep.topk_w + p)),
+                                       (static_cast<uint32_t>(ep.rank) << 24) | static_cast<uint32_t>(q0), 0u);
+        // the warp's 16 scale bytes per term go out as one 16-byte store
+        // (row-major; the owner moves them into its atom layout)
+#pragma unroll
+        for (int q = 0; q < kMaxTerms; ++q) {
+          if (q >= terms) break;
+          const uint32_t s0 = __shfl_sync(0xFFFFFFFFu, sword[q], 0), s1 = __shfl_sync(0xFFFFFFFFu, sword[q], 8);
+          const uint32_t s2 = __shfl_sync(0xFFFFFFFFu, sword[q], 16), s3 = __shfl_sync(0xFFFFFFFFu, sword[q], 24);
+          if (lane == 0)
+            *reinterpret_cast<uint4*>(ep.sf_rows[g] + (static_cast<uint64_t>(pos) * terms + q) * ep.sf_row_bytes +
+                                      grp * kQBlocksPerWarp) = make_uint4(s0, s1, s2, s3);
         }
       }
 #pragma unroll
@@ -844,7 +851,7 @@ __global__ void __launch_bounds__(256)
           uint8_t* dst = codes_d + (stacked ? 0 : q * term_stride) + row * kp + c0;
           *reinterpret_cast<uint4*>(dst) = make_uint4(words[q][0], words[q][1], words[q][2], words[q][3]);
         }
-        if (sf_lane) {
+        if (!kDispatch && sf_lane) {
           const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
                                                          static_cast<uint32_t>(b), static_cast<uint32_t>(kchunks),
                                                          static_cast<uint32_t>(sf_rows))
@@ -1092,6 +1099,45 @@ __global__ void ep_return_kernel(const __nv_bfloat16* __restrict__ y, uint32_t r
   uint4* to = reinterpret_cast<uint4*>(static_cast<uint8_t*>(peer_ret[src]) + static_cast<uint64_t>(row) * row_bytes);
   for (uint32_t i = lane; i < row_bytes / 16; i += 32) to[i] = __ldg(from + i);
   __threadfence_system();
+}
+
+// Owner side of the quantized dispatch, before W1: warp per row pos of the
+// segments (poff / seg_counts); the row's metadata record becomes the per-row
+// 1/rms, route weight and return slot, and its row-major scale bytes move
+// into the scale-atom layout the MMA reads (plain or stacked tiles of pt).
+__global__ void ep_unpack_kernel(const uint4* __restrict__ meta, const uint8_t* __restrict__ sf_rows,
+                                 uint32_t sf_row_bytes, int terms, int nb, int rows, const int32_t* __restrict__ poff,
+                                 const int32_t* __restrict__ seg_counts, int epr, float* rs, float* wt,
+                                 uint32_t* slot, uint8_t* xsf, uint64_t sf_term_stride, int kchunks, int pt,
+                                 int stacked) {
+  extern __shared__ int32_t useg[];  // poff[epr + 1], counts[epr]
+  for (int i = threadIdx.x; i <= epr; i += blockDim.x) useg[i] = poff[i];
+  for (int i = threadIdx.x; i < epr; i += blockDim.x) useg[epr + 1 + i] = seg_counts[i];
+  __syncthreads();
+  const int pos = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (pos >= rows || pos >= useg[epr]) return;
+  int el = 0;
+  while (el + 1 < epr && useg[el + 1] <= pos) ++el;
+  if (pos - useg[el] >= useg[epr + 1 + el]) return;  // padding row
+  if (lane == 0) {
+    const uint4 m = __ldg(meta + pos);
+    rs[pos] = __uint_as_float(m.x);
+    wt[pos] = __uint_as_float(m.y);
+    slot[pos] = m.z;
+  }
+  const int ngroups = (nb + 3) / 4;  // 4-block scale words per term
+  for (int i = lane; i < terms * ngroups; i += 32) {
+    const int q = i / ngroups, g4 = i - q * ngroups;
+    const uint32_t word = __ldg(reinterpret_cast<const uint32_t*>(
+        sf_rows + (static_cast<uint64_t>(pos) * terms + q) * sf_row_bytes + 4 * g4));
+    const uint64_t o = stacked ? stacked_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
+                                                   static_cast<uint32_t>(4 * g4), static_cast<uint32_t>(kchunks),
+                                                   static_cast<uint32_t>(pt))
+                               : q * sf_term_stride + sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(4 * g4),
+                                                                static_cast<uint32_t>(kchunks), static_cast<uint32_t>(pt));
+    *reinterpret_cast<uint32_t*>(xsf + o) = word;
+  }
 }
 
 __global__ void iota_kernel(int32_t* a, int n) {
@@ -1670,19 +1716,19 @@ cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, 
 
 cudaError_t launch_ep_quantize_dispatch(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                         int gamma_is_one, const int32_t* inv_c, int terms, uint64_t term_stride,
-                                        int kp, uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked,
-                                        const int32_t* src_base, const int32_t* offsets, const int32_t* topk_idx,
-                                        const float* topk_w, const float* rscale, int epr, int rank,
-                                        uint32_t dst_rows, uint8_t* const* xq, uint8_t* const* xsf, float* const* rs,
-                                        float* const* wt, uint32_t* const* slot, int* err, cudaStream_t st) {
+                                        int kp, int sf_rows_n, int stacked, const int32_t* src_base,
+                                        const int32_t* offsets, const int32_t* topk_idx, const float* topk_w,
+                                        const float* rscale, int epr, int rank, uint32_t dst_rows,
+                                        uint32_t sf_row_bytes, uint8_t* const* xq, uint8_t* const* sf_rows,
+                                        void* const* meta, int* err, cudaStream_t st) {
   const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQBlocksPerWarp - 1) / kQBlocksPerWarp);
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
-  const EpDispatch ep{src_base, offsets, topk_idx, topk_w, rscale, epr, rank, dst_rows, xq, xsf, rs, wt, slot, err};
+  const EpDispatch ep{src_base, offsets, topk_idx, topk_w, rscale, epr, rank, dst_rows, sf_row_bytes, xq, sf_rows,
+                      reinterpret_cast<uint4* const*>(meta), err};
   quantize_pairs_kernel<true><<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_c, terms, nullptr,
-                                                    term_stride, kp, nullptr, sf_term_stride, kchunks, sf_rows,
-                                                    stacked, ep);
+                                                    term_stride, kp, nullptr, 0, 0, sf_rows_n, stacked, ep);
   return cudaGetLastError();
 }
 
@@ -1695,6 +1741,19 @@ cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t*
   ep_return_kernel<<<(rows + 7) / 8, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
                                                        static_cast<uint32_t>(d) * 2u, rows, poff, seg_counts, epr,
                                                        slot, world, peer_ret, ret_rows, err);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_ep_unpack(const void* meta, const uint8_t* sf_rows, uint32_t sf_row_bytes, int terms, int nb,
+                             int rows, const int32_t* poff, const int32_t* seg_counts, int epr, float* rs, float* wt,
+                             uint32_t* slot, uint8_t* xsf, uint64_t sf_term_stride, int kchunks, int pt, int stacked,
+                             cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  const size_t smem = (2ull * epr + 1) * sizeof(int32_t);
+  ensure_dynamic_smem(reinterpret_cast<const void*>(ep_unpack_kernel), smem);
+  ep_unpack_kernel<<<(rows + 7) / 8, 256, smem, st>>>(static_cast<const uint4*>(meta), sf_rows, sf_row_bytes, terms, nb,
+                                                       rows, poff, seg_counts, epr, rs, wt, slot, xsf, sf_term_stride,
+                                                       kchunks, pt, stacked);
   return cudaGetLastError();
 }
 

@@ -70,11 +70,15 @@ cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, 
                              cudaStream_t st);
 cudaError_t launch_ep_quantize_dispatch(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                         int gamma_is_one, const int32_t* inv_c, int terms, uint64_t term_stride,
-                                        int kp, uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked,
-                                        const int32_t* src_base, const int32_t* offsets, const int32_t* topk_idx,
-                                        const float* topk_w, const float* rscale, int epr, int rank,
-                                        uint32_t dst_rows, uint8_t* const* xq, uint8_t* const* xsf, float* const* rs,
-                                        float* const* wt, uint32_t* const* slot, int* err, cudaStream_t st);
+                                        int kp, int sf_rows_n, int stacked, const int32_t* src_base,
+                                        const int32_t* offsets, const int32_t* topk_idx, const float* topk_w,
+                                        const float* rscale, int epr, int rank, uint32_t dst_rows,
+                                        uint32_t sf_row_bytes, uint8_t* const* xq, uint8_t* const* sf_rows,
+                                        void* const* meta, int* err, cudaStream_t st);
+cudaError_t launch_ep_unpack(const void* meta, const uint8_t* sf_rows, uint32_t sf_row_bytes, int terms, int nb,
+                             int rows, const int32_t* poff, const int32_t* seg_counts, int epr, float* rs, float* wt,
+                             uint32_t* slot, uint8_t* xsf, uint64_t sf_term_stride, int kchunks, int pt, int stacked,
+                             cudaStream_t st);
 cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t* poff, const int32_t* seg_counts,
                              int epr, const uint32_t* slot, int world, void* const* peer_ret, uint32_t ret_rows,
                              int* err, cudaStream_t st);

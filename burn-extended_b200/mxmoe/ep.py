@@ -426,12 +426,12 @@ class QuantizedPeerMoe:
 
     # rms, router logits, top-k, permute x2, layout, quantize-dispatch, W1, W2, return, combine
     launches_per_step = 11
-    BUFS = 5  # codes, scale atoms, 1/rms, route weight, return slot (mxmoe_ep_reserve order)
+    BUFS = 3  # activation codes, row-major scale bytes, row metadata (mxmoe_ep_reserve order)
 
     def __init__(self, backend: CudaExpertBackend, world: int, rank: int, max_tokens: int, x_dtype=None,
                  group=None, peers=None):
         """peers: for ranks emulated in one process, a list per rank of
-        (5 layout buffer pointers, return buffer pointer) used instead of the
+        (3 layout buffer pointers, return buffer pointer) used instead of the
         IPC exchange; this rank's buffers are then exposed by .local_peers()
         before the list is complete (see the tests)."""
         import ctypes
@@ -472,7 +472,7 @@ class QuantizedPeerMoe:
             self.set_peers(table)
 
     def local_peers(self):
-        """This rank's 5 layout buffers as device pointers."""
+        """This rank's layout buffers as device pointers."""
         import ctypes
         from ._lib import check, lib
         arr = (ctypes.c_void_p * self.BUFS)()
@@ -480,7 +480,7 @@ class QuantizedPeerMoe:
         return [int(arr[i]) for i in range(self.BUFS)], None
 
     def set_peers(self, table):
-        """table[r] = (5 layout buffer pointers of rank r, its return buffer pointer)."""
+        """table[r] = (layout buffer pointers of rank r, its return buffer pointer)."""
         t = self.torch
         flat = [table[r][0][b] for b in range(self.BUFS) for r in range(self.world)]
         self.peer_bufs = t.tensor(flat, dtype=t.int64, device=self.dev)

@@ -318,21 +318,20 @@ MXMOE_API int mxmoe_forward_local_meta(mxmoe_layer* layer, const void* xr, mxmoe
  * synchronisation is needed within a step.
  *
  * mxmoe_ep_reserve: sizes this layer's workspace for world ranks of up to
- * max_tokens tokens each (it cannot grow afterwards) and returns 5 IPC
- * handles (5 x MXMOE_IPC_HANDLE_BYTES): codes, scale atoms, per-row 1/rms,
- * per-row route weight, per-row return slot.  Ranks exchange them and open
- * the peers' with mxmoe_ipc_open.  The layer's shard must be E / world
- * experts. */
+ * max_tokens tokens each (it cannot grow afterwards) and returns 3 IPC
+ * handles (3 x MXMOE_IPC_HANDLE_BYTES): activation codes, row-major scale
+ * bytes, row metadata.  Ranks exchange them and open the peers' with
+ * mxmoe_ipc_open.  The layer's shard must be E / world experts. */
 MXMOE_API int mxmoe_ep_reserve(mxmoe_layer* layer, uint32_t max_tokens, uint32_t world, void* handles);
-/* The same 5 buffers as device pointers of this process (ranks emulated on
+/* The same 3 buffers as device pointers of this process (ranks emulated on
  * one GPU use them in place of opened handles). */
 MXMOE_API int mxmoe_ep_buffers(mxmoe_layer* layer, void** ptrs);
 
 /* Source side, after mxmoe_route: counts [world][E] (device) = every rank's
  * pairs per expert (offsets[e + 1] - offsets[e], all-gathered); inv and
  * offsets are this rank's canonical maps.  peer_bufs: device array of
- * 5 x world pointers, grouped by buffer in the mxmoe_ep_reserve order
- * ([codes of ranks 0..world-1][scales ...]...).  Also records, for this
+ * 3 x world pointers, grouped by buffer in the mxmoe_ep_reserve order
+ * ([codes of ranks 0..world-1][scales ...][metadata ...]).  Also records, for this
  * rank's own experts, the layout mxmoe_ep_experts runs on.  Every rank must
  * pass the same counts and x dtype. */
 MXMOE_API int mxmoe_ep_dispatch(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
