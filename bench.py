@@ -306,7 +306,10 @@ def run_ours(args, world, rank, local):
         print(json.dumps({"gptoss120b": measure_120b(args, local, dev)}), flush=True)
         return
 
-    inp = synth.make_config("prefill", seed=args.seed + rank)
+    # one model on every rank (seeded once); each rank routes its own tokens
+    inp = synth.make_config("prefill", seed=args.seed)
+    if world > 1:
+        inp = synth.rank_tokens(inp, rank, args.seed)
     n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
     if world > 1:
         from mxmoe import ep

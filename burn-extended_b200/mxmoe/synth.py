@@ -82,6 +82,15 @@ def make_inputs(d: int, f: int, E: int, k: int, n: int, bf16: bool, seed: int = 
     return MoeInputs(d, f, E, k, n, x, np.ones(d, dtype=np.float32), gate_w, gate_b, host, b1, b2, bf16)
 
 
+def rank_tokens(inp: MoeInputs, rank: int, seed: int = 0) -> MoeInputs:
+    """The same layer (router, experts, biases) with this rank's own tokens:
+    every expert-parallel rank must hold one shared model, only x differs."""
+    from dataclasses import replace
+    rng = np.random.default_rng(10_000 + 7919 * rank + seed)
+    x = rng.standard_normal(inp.x.shape, dtype=np.float32)
+    return replace(inp, x=bf16_round(x) if inp.bf16 else x)
+
+
 def make_config(name: str, seed: int = 0, n: Optional[int] = None) -> MoeInputs:
     d, f, E, k, n0, bf16 = CONFIGS[name]
     zipf = 1.1 if name == "gptoss120b" else None

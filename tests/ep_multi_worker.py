@@ -32,7 +32,8 @@ def main():
     dev = torch.device(f"cuda:{local}")
     dist.init_process_group("nccl", device_id=dev)
     n, E, k = int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3])
-    inp = synth.make_inputs(512, 384, E, k, n, True, seed=100 + rank, zipf_router_bias=0.7)
+    # one model on every rank; each rank routes its own tokens
+    inp = synth.rank_tokens(synth.make_inputs(512, 384, E, k, n, True, seed=100, zipf_router_bias=0.7), rank)
     m = ep.build_quantized_peer_rank(inp, world, rank, dev)
     full = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k).init(local)
     full.set_router(inp.gamma, inp.gate_w, inp.gate_b)
