@@ -224,8 +224,9 @@ def measure_microbench(args, local, dev, hbm_peak):
     out = {}
     for T in (1, 2, 4, 8):
         x = torch.from_numpy(base.x[:T]).to(torch.bfloat16).to(dev)
-        for L in layers:
-            L.forward(x)
+        for _ in range(2):  # the second call per layer captures its CUDA graph
+            for L in layers:
+                L.forward(x)
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         calls = max(args.steps, 1) * copies

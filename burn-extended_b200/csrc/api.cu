@@ -205,6 +205,19 @@ struct mxmoe_layer {
   uint32_t last_n = 0;
   bool profiling = false;
   bool profile_valid = false;
+  // CUDA-graph replay of mxmoe_forward: bumped by anything that moves a buffer
+  // or changes a launch (uploads, workspace growth, shard changes)
+  uint64_t generation = 0;
+  struct FwdGraph {
+    const void* x = nullptr;
+    void* y = nullptr;
+    uint32_t n = 0;
+    int xd = -1, yd = -1;
+    uint64_t gen = ~0ull;
+    cudaGraphExec_t exec = nullptr;
+    bool failed = false;  // capture failed for this key: run directly
+  } graph;
+  cudaStream_t cap_stream = nullptr;  // capture happens here; replays go to the caller's stream
   // expert parallelism over peer memory: the workspace is shared with peers and must not move
   bool ep_reserved = false;
   uint32_t ep_world = 0, ep_max_tokens = 0;
@@ -246,6 +259,7 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   const uint32_t old_t = w.cap_tokens, old_p = w.cap_pairs;
   CUDA_TRY(cudaDeviceSynchronize());
   free_workspace(w);
+  ++L->generation;
   const uint32_t E = L->e_count, Et = L->E_total;
   auto grow = [](uint32_t old, uint64_t want) -> uint32_t {
     if (want <= old) return old;
@@ -552,6 +566,8 @@ int mxmoe_destroy(mxmoe_layer* L) {
   dfree(L->err);
   for (auto& e : L->ev)
     if (e) cudaEventDestroy(e);
+  if (L->graph.exec) cudaGraphExecDestroy(L->graph.exec);
+  if (L->cap_stream) cudaStreamDestroy(L->cap_stream);
   delete L;
   return MXMOE_OK;
 }
@@ -568,6 +584,7 @@ int mxmoe_set_router(mxmoe_layer* L, const void* norm_gamma, const void* gate_w,
   to_f32(gate_w, dtype, E * d, w.data());
   to_f32(gate_b, dtype, E, b.data());
   L->gamma_is_one = std::all_of(gm.begin(), gm.end(), [](float v) { return v == 1.0f; });
+  ++L->generation;
   if (!L->gamma) TRY(dalloc(&L->gamma, d));
   std::vector<float> wp(router_gate_packed_floats(static_cast<int>(E), static_cast<int>(d)));
   pack_router_gate(w.data(), static_cast<int>(E), static_cast<int>(d), wp.data());
@@ -592,6 +609,7 @@ int mxmoe_set_expert_shard(mxmoe_layer* L, uint32_t expert_begin, uint32_t exper
   free_workspace(L->ws);
   L->e_begin = expert_begin;
   L->e_count = expert_count;
+  ++L->generation;
   return MXMOE_OK;
 }
 
@@ -653,6 +671,7 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
     }
 
   dfree(L->w1q); dfree(L->w1sf); dfree(L->b1); dfree(L->w2q); dfree(L->w2sf); dfree(L->b2);
+  ++L->generation;
   TRY(dalloc(&L->w1q, q1.size()));
   TRY(dalloc(&L->w1sf, s1.size()));
   TRY(dalloc(&L->b1, bb1.size()));
@@ -684,6 +703,51 @@ int mxmoe_reserve(mxmoe_layer* L, uint32_t max_tokens) {
   return ensure_workspace(L, max_tokens, L->k);
 }
 
+// The kernel chain of mxmoe_forward (router, permutation, experts, combine)
+// on stream st; everything that can allocate or resize ran before.
+static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, mxmoe_dtype y_dtype,
+                         uint32_t n_tokens, cudaStream_t st) {
+  Workspace& w = L->ws;
+  const uint32_t k = L->k, E = L->e_count;
+  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
+  const int xt = x_terms_for(L, x_dtype);
+  const TilePlan tp = pick_tiles(P, E, xt, L->d <= kGemvMaxK && L->fp <= kGemvMaxK);
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
+  CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
+                         w.logits, w.topk_idx, w.topk_w, w.rscale, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
+  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, tp.pair_tile, w.offsets, w.perm_c,
+                          w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
+  TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
+  const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
+  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, w.pair_dtype, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y,
+                          y_dtype, st));
+  return MXMOE_OK;
+}
+
+// Capture the chain for this key into L->graph (on the layer's capture stream).
+static int capture_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, mxmoe_dtype y_dtype,
+                           uint32_t n_tokens) {
+  if (!L->cap_stream) CUDA_TRY(cudaStreamCreateWithFlags(&L->cap_stream, cudaStreamNonBlocking));
+  CUDA_TRY(cudaStreamBeginCapture(L->cap_stream, cudaStreamCaptureModeThreadLocal));
+  const int rc = forward_chain(L, x, x_dtype, y, y_dtype, n_tokens, L->cap_stream);
+  cudaGraph_t graph = nullptr;
+  const cudaError_t ce = cudaStreamEndCapture(L->cap_stream, &graph);
+  if (rc != MXMOE_OK || ce != cudaSuccess || !graph) {
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    return rc != MXMOE_OK ? rc : fail(MXMOE_ERR_CUDA, "forward capture failed: %s", cudaGetErrorString(ce));
+  }
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+  cudaGraphDestroy(graph);
+  if (ie != cudaSuccess) return fail(MXMOE_ERR_CUDA, "graph instantiate failed: %s", cudaGetErrorString(ie));
+  L->graph.exec = exec;
+  return MXMOE_OK;
+}
+
 int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, mxmoe_dtype y_dtype,
                   uint32_t n_tokens, void* stream) {
   TRY(check_layer(L));
@@ -709,23 +773,29 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   if (L->e_count != L->E_total)
     return fail(MXMOE_ERR_INVALID_ARG, "layer holds an expert shard; use the expert-parallel entry points");
   TRY(ensure_workspace(L, n_tokens, L->k));
-  Workspace& w = L->ws;
-  const uint32_t k = L->k, E = L->e_count;
-  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
-  const int xt = x_terms_for(L, x_dtype);
-  const TilePlan tp = pick_tiles(P, E, xt, L->d <= kGemvMaxK && L->fp <= kGemvMaxK);
-  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   L->profile_valid = false;
-  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
-  CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
-                         w.logits, w.topk_idx, w.topk_w, w.rscale, st));
-  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
-  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, tp.pair_tile, w.offsets, w.perm_c,
-                          w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
-  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
-  TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
-  const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
-  CUDA_TRY(launch_combine(x, x_dtype, w.y_pair, w.pair_dtype, w.topk_idx, w.inv_p, n_tokens, L->d, k, residual, y, y_dtype, st));
+  if (!L->profiling && !(L->cfg.flags & MXMOE_FLAG_NO_GRAPHS)) {
+    auto& gr = L->graph;
+    const bool same = gr.x == x && gr.y == y && gr.n == n_tokens && gr.xd == x_dtype && gr.yd == y_dtype &&
+                      gr.gen == L->generation;
+    if (same && !gr.exec && !gr.failed)  // second call with this key: capture
+      gr.failed = capture_forward(L, x, x_dtype, y, y_dtype, n_tokens) != MXMOE_OK;
+    if (same && gr.exec) {
+      CUDA_TRY(cudaGraphLaunch(gr.exec, st));
+      return MXMOE_OK;
+    }
+    if (!same) {  // a new key: run directly and remember it
+      if (gr.exec) cudaGraphExecDestroy(gr.exec);
+      gr = mxmoe_layer::FwdGraph{};
+      gr.x = x;
+      gr.y = y;
+      gr.n = n_tokens;
+      gr.xd = x_dtype;
+      gr.yd = y_dtype;
+      gr.gen = L->generation;
+    }
+  }
+  TRY(forward_chain(L, x, x_dtype, y, y_dtype, n_tokens, st));
   if (L->profiling) {
     CUDA_TRY(cudaEventRecord(L->ev[6], st));
     L->profile_valid = true;

@@ -62,6 +62,10 @@ typedef enum mxmoe_dtype {
                                             kernels instead of tcgen05 (a second,
                                             independent GPU implementation used to
                                             cross-check the tensor-core path) */
+#define MXMOE_FLAG_NO_GRAPHS       0x20u /* never replay mxmoe_forward as a CUDA
+                                            graph (by default the second call with
+                                            the same x, y, n and dtypes is captured
+                                            and later ones replay it) */
 
 /* Mirrors moe::MoeConfig (src/moe/mod.rs:22-33).  `initializer` and `verbose`
  * have no device meaning; swiglu_alpha / swiglu_limit are honoured (the
