@@ -158,15 +158,22 @@ class MoeGatedSwiGLU:
         check(lib().mxmoe_reserve(self._h, max_tokens))
 
     # -- forward -----------------------------------------------------------
-    def forward(self, x, out_dtype=None, stream=None):
+    def forward(self, x, out_dtype=None, stream=None, out=None):
         """MoeGatedSwiGLU::forward (src/moe/mod.rs:99-115) on a CUDA tensor
-        [..., d] (float32 or bfloat16); returns y of the same shape."""
+        [..., d] (float32 or bfloat16); returns y of the same shape (written
+        into `out` when given: repeated calls on the same x and out buffers
+        replay a captured CUDA graph)."""
         torch = _torch()
         if not x.is_cuda:
             raise MxMoeError(1, "forward takes a CUDA tensor; use forward_host for host buffers")
         xc = x.contiguous()
         n = xc.numel() // self.cfg.d_model
-        y = torch.empty(xc.shape, dtype=out_dtype or xc.dtype, device=xc.device)
+        if out is not None:
+            if out.shape != xc.shape or not out.is_contiguous():
+                raise MxMoeError(1, "out must be a contiguous tensor of x's shape")
+            y = out
+        else:
+            y = torch.empty(xc.shape, dtype=out_dtype or xc.dtype, device=xc.device)
         check(lib().mxmoe_forward(self._h, xc.data_ptr(), _dtype_code(xc), y.data_ptr(), _dtype_code(y), n,
                                   _stream_ptr(stream)))
         return y

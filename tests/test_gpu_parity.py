@@ -299,3 +299,21 @@ def test_errors_are_reported(torch):
     with pytest.raises(mxmoe.MxMoeError):
         layer.set_resident(bad.host, bad.b1, bad.b2)
     layer.close()
+
+
+@pytest.mark.parametrize("name,n", [("decode", 64), ("tiny", 16)])
+def test_forward_graph_replay(torch, name, n):
+    """Repeated forwards on the same x / out buffers: the first runs directly,
+    the second is captured as a CUDA graph, later ones replay it.  New token
+    values in x every call must give the oracle's output every call."""
+    base = synth.make_config(name, seed=0, n=n)
+    layer = make_layer(base)
+    x = to_device_x(base)
+    y = torch.empty(x.shape, dtype=torch.float32, device=x.device)
+    for i in range(4):
+        inp = synth.rank_tokens(base, i)
+        x.copy_(torch.from_numpy(inp.x).to(x.dtype))
+        layer.forward(x, out=y)
+        want, _, _ = oracle_forward(inp)
+        assert_close(y.cpu().numpy(), want, f"{name} call {i}")
+    layer.close()
