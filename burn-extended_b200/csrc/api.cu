@@ -36,6 +36,19 @@ int fail(int code, const char* fmt, ...) {
   return code;
 }
 
+}  // namespace
+
+namespace mxmoe {
+// Lets the other translation units of the library (the model.bin reader)
+// report through mxmoe_last_error().
+int set_last_error(int code, const char* msg) {
+  g_last_error = msg;
+  return code;
+}
+}  // namespace mxmoe
+
+namespace {
+
 #define CUDA_TRY(expr)                                                                        \
   do {                                                                                        \
     cudaError_t _e = (expr);                                                                  \

@@ -127,6 +127,13 @@ class MoeGatedSwiGLU:
         self._h = h
         self._keep = []
 
+    @classmethod
+    def _adopt(cls, cfg: MoeConfig, device: int, handle: ctypes.c_void_p) -> "MoeGatedSwiGLU":
+        """Wraps a layer the library already created (the model.bin loader)."""
+        self = cls.__new__(cls)
+        self.cfg, self.device, self._h, self._keep = cfg, device, handle, []
+        return self
+
     # -- parameters --------------------------------------------------------
     def set_router(self, norm_gamma: np.ndarray, gate_w: np.ndarray, gate_b: np.ndarray):
         """RmsNorm gain [d] and gate Linear weight [E, d] / bias [E] (f32)."""

@@ -37,6 +37,21 @@ class Config(ctypes.Structure):
     ]
 
 
+class ModelBinHeader(ctypes.Structure):
+    """mxmoe_modelbin_header: model.bin header fields and derived offsets."""
+    _fields_ = [
+        ("context_length", ctypes.c_uint32), ("num_blocks", ctypes.c_uint32),
+        ("num_experts", ctypes.c_uint32), ("num_active_experts", ctypes.c_uint32),
+        ("embedding_dim", ctypes.c_uint32), ("mlp_dim", ctypes.c_uint32),
+        ("swiglu_limit", ctypes.c_float), ("head_dim", ctypes.c_uint32),
+        ("num_heads", ctypes.c_uint32), ("num_kv_heads", ctypes.c_uint32),
+        ("attention_window", ctypes.c_uint32), ("rms_eps", ctypes.c_float),
+        ("num_text_tokens", ctypes.c_uint32), ("num_special_tokens", ctypes.c_uint32),
+        ("dense_offset", ctypes.c_uint64), ("moe_offset", ctypes.c_uint64),
+        ("moe_layer_stride", ctypes.c_uint64), ("file_bytes", ctypes.c_uint64),
+    ]
+
+
 class QuantDesc(ctypes.Structure):
     _fields_ = [
         ("experts", ctypes.c_uint64), ("rows", ctypes.c_uint64), ("cols", ctypes.c_uint64),
@@ -85,6 +100,8 @@ _SIGS = {
     "mxmoe_ep_dispatch": ([_vp, _vp, _i32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _u32, _vp, _vp], _i32),
     "mxmoe_ep_experts": ([_vp, _i32, _vp, _u32, _vp], _i32),
     "mxmoe_ep_buffers": ([_vp, _vp], _i32),
+    "mxmoe_modelbin_info": ([ctypes.c_char_p, ctypes.POINTER(ModelBinHeader)], _i32),
+    "mxmoe_modelbin_load_layer": ([ctypes.c_char_p, _u32, _i32, _u32, _u32, _u32, _vp, ctypes.POINTER(_vp)], _i32),
 }
 
 IPC_HANDLE_BYTES = 64

@@ -360,6 +360,56 @@ MXMOE_API int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_token
                   mxmoe_dtype pair_dtype, int residual, void* y,
                   mxmoe_dtype y_dtype, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * model.bin reader (src/loader/modelbin.rs).  The file is the GPT-OSS v1.0
+ * container that src/bin/gptoss_export.rs writes: a header, a tokenizer
+ * section padded to 16 KiB, the bf16 dense tensors (embedding, per-layer
+ * attention / MoE norm / gate, final norm, unembedding, each segment 16-byte
+ * aligned), then one 16 KiB-aligned MXFP4 expert payload per layer.  Only the
+ * MoE part is loaded here; the reader checks the magic and that every section
+ * it touches lies inside the file (MXMOE_ERR_INVALID_ARG otherwise).
+ * ------------------------------------------------------------------------- */
+
+/* Header fields parse_headers reads (src/loader/modelbin.rs:75-151), plus the
+ * byte offsets this reader derives. */
+typedef struct mxmoe_modelbin_header {
+  uint32_t context_length;
+  uint32_t num_blocks;          /* layers */
+  uint32_t num_experts;
+  uint32_t num_active_experts;  /* experts per token */
+  uint32_t embedding_dim;       /* d_model */
+  uint32_t mlp_dim;             /* ffn_hidden */
+  float swiglu_limit;
+  uint32_t head_dim;
+  uint32_t num_heads;
+  uint32_t num_kv_heads;
+  uint32_t attention_window;
+  float rms_eps;
+  uint32_t num_text_tokens;
+  uint32_t num_special_tokens;
+  uint64_t dense_offset;        /* first byte of the embedding table (16 KiB aligned) */
+  uint64_t moe_offset;          /* first byte of layer 0's expert payload */
+  uint64_t moe_layer_stride;    /* bytes from one layer's expert payload to the next */
+  uint64_t file_bytes;
+} mxmoe_modelbin_header;
+
+/* Parses the header of the model.bin at `path` (a host file). */
+MXMOE_API int mxmoe_modelbin_info(const char* path, mxmoe_modelbin_header* out);
+
+/* Creates the MoE layer `layer` of the model.bin at `path` on `device`, the
+ * part of load_modelbin_into (src/loader/modelbin.rs:158-462) that feeds
+ * MoeGatedSwiGLU: config from the header (d_model, ffn_hidden, num_experts,
+ * num_active_experts, swiglu_limit, rms_eps; alpha 1.702), the router from
+ * layers.{layer}.mlp.norm.scale and mlp.gate (bf16, :273-291), the experts
+ * from the layer's MXFP4 payload with ue8_offset 14 (:452-453) and the bf16
+ * mlp1/mlp2 biases (:362-406).  flags are MXMOE_FLAG_*.  expert_count == 0
+ * loads every expert; otherwise only [expert_begin, expert_begin +
+ * expert_count) is read and uploaded (mxmoe_set_expert_shard), so each
+ * expert-parallel rank reads its own share of the file. */
+MXMOE_API int mxmoe_modelbin_load_layer(const char* path, uint32_t layer, int32_t device, uint32_t flags,
+                              uint32_t expert_begin, uint32_t expert_count, void* stream,
+                              mxmoe_layer** out);
+
 #ifdef __cplusplus
 }
 #endif

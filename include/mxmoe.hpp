@@ -87,6 +87,8 @@ class MoeGatedSwiGLU {
                    cfg.swiglu_limit, cfg.rms_eps, cfg.flags | (cfg.disabled ? MXMOE_FLAG_DISABLED : 0u), device};
     check(mxmoe_create(&c, &layer_));
   }
+  // Takes ownership of a layer the library created (the model.bin loader).
+  MoeGatedSwiGLU(const MoeConfig& cfg, mxmoe_layer* adopted) : cfg_(cfg), layer_(adopted) {}
   MoeGatedSwiGLU(const MoeGatedSwiGLU&) = delete;
   MoeGatedSwiGLU& operator=(const MoeGatedSwiGLU&) = delete;
   MoeGatedSwiGLU(MoeGatedSwiGLU&& o) noexcept : cfg_(o.cfg_), layer_(std::exchange(o.layer_, nullptr)) {}
@@ -131,6 +133,35 @@ inline MoeGatedSwiGLU MoeConfig::init(int device) const { return MoeGatedSwiGLU(
 }  // namespace moe
 
 namespace loader {
+namespace modelbin {
+
+// parse_modelbin (src/loader/modelbin.rs:153-156).
+inline mxmoe_modelbin_header parse_modelbin(const char* path) {
+  mxmoe_modelbin_header h{};
+  check(mxmoe_modelbin_info(path, &h));
+  return h;
+}
+
+// The MoE part of load_modelbin_into (src/loader/modelbin.rs:158-462) for one
+// layer; expert_count == 0 loads every expert.
+inline moe::MoeGatedSwiGLU load_moe_layer(const char* path, uint32_t layer, int device = 0, uint32_t flags = 0,
+                                          uint32_t expert_begin = 0, uint32_t expert_count = 0) {
+  const mxmoe_modelbin_header h = parse_modelbin(path);
+  mxmoe_layer* raw = nullptr;
+  check(mxmoe_modelbin_load_layer(path, layer, device, flags, expert_begin, expert_count, nullptr, &raw));
+  moe::MoeConfig cfg;
+  cfg.d_model = h.embedding_dim;
+  cfg.ffn_hidden = h.mlp_dim;
+  cfg.num_experts = h.num_experts;
+  cfg.experts_per_token = h.num_active_experts;
+  cfg.swiglu_limit = h.swiglu_limit;
+  cfg.rms_eps = h.rms_eps;
+  cfg.flags = flags;
+  return moe::MoeGatedSwiGLU(cfg, raw);
+}
+
+}  // namespace modelbin
+
 namespace mxfp4 {
 
 // Device-side dequant_mxfp4_bytes: blocks [rows][b], scales [rows], out [rows][2b].
