@@ -11,6 +11,12 @@ from mxmoe import modelbin, synth
 from moe_testutil import assert_close, oracle_forward
 
 
+@pytest.fixture
+def torch():
+    import torch
+    return torch
+
+
 def layer_tensors(inp: synth.MoeInputs, seed: int) -> modelbin.MoeLayerTensors:
     rng = np.random.default_rng(1000 + seed)
     norm = synth.bf16_round(1.0 + 0.1 * rng.standard_normal(inp.d).astype(np.float32))
