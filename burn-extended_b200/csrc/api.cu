@@ -569,6 +569,12 @@ int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out) {
   return MXMOE_OK;
 }
 
+int mxmoe_get_config(const mxmoe_layer* L, mxmoe_config* out) {
+  if (!L || !out) return fail(MXMOE_ERR_INVALID_ARG, "mxmoe_get_config: null argument");
+  *out = L->cfg;
+  return MXMOE_OK;
+}
+
 int mxmoe_destroy(mxmoe_layer* L) {
   if (!L) return MXMOE_OK;
   DeviceGuard g(L->cfg.device);

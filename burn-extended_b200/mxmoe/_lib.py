@@ -69,6 +69,7 @@ _SIGS = {
     "mxmoe_last_error": ([ctypes.c_char_p, ctypes.c_size_t], _i32),
     "mxmoe_create": ([ctypes.POINTER(Config), ctypes.POINTER(_vp)], _i32),
     "mxmoe_destroy": ([_vp], _i32),
+    "mxmoe_get_config": ([_vp, ctypes.POINTER(Config)], _i32),
     "mxmoe_set_router": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "mxmoe_upload_experts": ([_vp, ctypes.POINTER(QuantDesc), _vp, _vp, ctypes.POINTER(QuantDesc), _vp, _vp,
                               _vp, _vp, _i32, _vp], _i32),
@@ -101,6 +102,8 @@ _SIGS = {
     "mxmoe_ep_experts": ([_vp, _i32, _vp, _u32, _vp], _i32),
     "mxmoe_ep_buffers": ([_vp, _vp], _i32),
     "mxmoe_modelbin_info": ([ctypes.c_char_p, ctypes.POINTER(ModelBinHeader)], _i32),
+    "mxmoe_safetensors_load_layer": ([ctypes.POINTER(ctypes.c_char_p), _u32, _u32, ctypes.POINTER(Config), _u32, _u32,
+                                      _vp, ctypes.POINTER(_vp)], _i32),
     "mxmoe_modelbin_load_layer": ([ctypes.c_char_p, _u32, _i32, _u32, _u32, _u32, _vp, ctypes.POINTER(_vp)], _i32),
 }
 

@@ -109,6 +109,10 @@ MXMOE_API int mxmoe_last_error(char* buf, size_t cap);
  * creates an empty layer on cfg->device. */
 MXMOE_API int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out);
 
+/* The layer's config as created (the loaders fill in the shapes and flags
+ * from the file). */
+MXMOE_API int mxmoe_get_config(const mxmoe_layer* layer, mxmoe_config* out);
+
 /* Frees every device buffer the layer owns. */
 MXMOE_API int mxmoe_destroy(mxmoe_layer* layer);
 
@@ -409,6 +413,24 @@ MXMOE_API int mxmoe_modelbin_info(const char* path, mxmoe_modelbin_header* out);
 MXMOE_API int mxmoe_modelbin_load_layer(const char* path, uint32_t layer, int32_t device, uint32_t flags,
                               uint32_t expert_begin, uint32_t expert_count, void* stream,
                               mxmoe_layer** out);
+
+/* Replaces load_gptoss_moe (src/loader/gpt_oss.rs:369-423) for one layer:
+ * creates MoE layer `layer` from a GPT-OSS safetensors checkpoint split over
+ * paths[0..n_paths) (tensors block.{layer}.mlp.{norm.scale, gate.weight,
+ * gate.bias, mlp1_weight.blocks, mlp1_weight.scales, mlp1_bias,
+ * mlp2_weight.blocks, mlp2_weight.scales, mlp2_bias}).  The MXFP4 bytes are
+ * uploaded packed (scales E8M0 with bias 127, ue8_offset 0), not dequantized
+ * on the host as src/loader/mxfp4.rs:82-125 does, and land in the layer
+ * itself rather than the stale `layers.{l}.mlp.mlp1_weight` path.  cfg gives
+ * experts_per_token, swiglu_alpha / limit, rms_eps, flags and device;
+ * d_model / ffn_hidden / num_experts are taken from the tensor shapes (a
+ * non-zero value in cfg must agree).  MXMOE_FLAG_INTERLEAVED_GLU is always
+ * set: checkpoint W1 rows are [glu0, lin0, glu1, lin1, ...]
+ * (src/activation/mod.rs:8-13).  expert_count == 0 loads every expert,
+ * otherwise [expert_begin, expert_begin + expert_count) only. */
+MXMOE_API int mxmoe_safetensors_load_layer(const char* const* paths, uint32_t n_paths, uint32_t layer,
+                                 const mxmoe_config* cfg, uint32_t expert_begin, uint32_t expert_count,
+                                 void* stream, mxmoe_layer** out);
 
 #ifdef __cplusplus
 }
