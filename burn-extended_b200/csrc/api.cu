@@ -192,6 +192,16 @@ struct Workspace {
   CUtensorMap tmap_act[kNumTileWidths];
   // stacked tiles of 16 / 32 / 64 pairs: boxes of 32 / 64 / 128 rows over 2 x rows code rows
   CUtensorMap tmap_x_stk[3], tmap_act_stk[3];
+  // FP4 decode tiles (allocated on first use, sized for the at most
+  // kF4MaxAvgPairs pairs per expert that select them): four E2M1 terms per
+  // pair, rows4 pair rows, packed codes [4 * rows4][kp / 2], scale atoms
+  // [rows4 / 32][kp / 128][512]
+  uint32_t rows4 = 0;
+  uint8_t* xq4 = nullptr;
+  uint8_t* xsf4 = nullptr;
+  uint8_t* aq4 = nullptr;
+  uint8_t* asf4 = nullptr;
+  CUtensorMap tmap_x4, tmap_act4;
 };
 
 struct mxmoe_layer {
@@ -214,6 +224,7 @@ struct mxmoe_layer {
   float* b2 = nullptr;
   int* err = nullptr;
   CUtensorMap tmap_w1[2] = {}, tmap_w2[2] = {};  // box rows 128 (weights-as-A) / 256 (tokens-as-A)
+  CUtensorMap tmap_w1_f4 = {}, tmap_w2_f4 = {};  // packed bytes, 256-row boxes of K 256 (FP4 tiles)
   Workspace ws;
   uint32_t last_n = 0;
   bool profiling = false;
@@ -244,6 +255,8 @@ void free_workspace(Workspace& w) {
   dfree(w.offsets); dfree(w.perm_c); dfree(w.inv_c); dfree(w.poff); dfree(w.counts);
   dfree(w.ntile_prefix); dfree(w.perm_p); dfree(w.inv_p);
   dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
+  dfree(w.xq4); dfree(w.xsf4); dfree(w.aq4); dfree(w.asf4);
+  w.rows4 = 0;
   dfree(w.local_idx);
   dfree(w.ret_slot);
   dfree(w.pos_rscale);
@@ -340,6 +353,40 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   return MXMOE_OK;
 }
 
+// FP4 decode tiles serve up to this many routed pairs per expert on average
+// (beyond it the E4M3 64-pair stacked tiles issue no more MMAs per weight
+// byte and read each weight tile once).
+constexpr int kF4MaxAvgPairs = 24;
+
+// FP4 decode buffers: fp4 plans keep at most kF4MaxAvgPairs * E pairs, and
+// their expert segments are padded to kF4PairTile rows.
+int ensure_f4(mxmoe_layer* L) {
+  Workspace& w = L->ws;
+  if (w.xq4) return MXMOE_OK;
+  const uint32_t E = L->e_count;
+  const uint32_t rows4 = round_up((kF4MaxAvgPairs + kF4PairTile) * E + 64, kF4PairTile);
+  const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
+  const uint64_t tiles = rows4 / kF4PairTile;
+  const size_t xq_bytes = static_cast<size_t>(kF4Terms) * rows4 * (L->kp1 / 2);
+  const size_t aq_bytes = static_cast<size_t>(kF4Terms) * rows4 * (L->kp2 / 2);
+  TRY(dalloc(&w.xq4, xq_bytes));
+  TRY(dalloc(&w.aq4, aq_bytes));
+  TRY(dalloc(&w.xsf4, tiles * kc1 * kSfAtomBytes));
+  TRY(dalloc(&w.asf4, tiles * kc2 * kSfAtomBytes));
+  // K padding and rows of absent pairs read as zero codes and finite scales
+  CUDA_TRY(cudaMemset(w.xq4, 0, xq_bytes));
+  CUDA_TRY(cudaMemset(w.aq4, 0, aq_bytes));
+  CUDA_TRY(cudaMemset(w.xsf4, 0, tiles * kc1 * kSfAtomBytes));
+  CUDA_TRY(cudaMemset(w.asf4, 0, tiles * kc2 * kSfAtomBytes));
+  const uint32_t box = kF4Terms * kF4PairTile;
+  TRY(make_tmap(&w.tmap_x4, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.xq4, L->kp1 / 2, uint64_t(kF4Terms) * rows4, 1,
+                L->kp1 / 2, xq_bytes, box));
+  TRY(make_tmap(&w.tmap_act4, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.aq4, L->kp2 / 2, uint64_t(kF4Terms) * rows4, 1,
+                L->kp2 / 2, aq_bytes, box));
+  w.rows4 = rows4;
+  return MXMOE_OK;
+}
+
 // Tile plan from the average routed pairs per expert:
 //   few pairs  -> weights-as-A, pair tiles of 32 / 64 / 128 (HBM-bound decode);
 //   many pairs -> tokens-as-A, pair tiles of 128 x weight tiles of 256 rows.
@@ -353,16 +400,19 @@ struct TilePlan {
   int tw;
   bool stacked;
   bool gemv = false;  // fused dequant-GEMV on CUDA cores instead of tensor-core tiles
+  bool fp4 = false;   // kind::mxf4 stacked tiles of kF4PairTile pairs, four E2M1 activation terms
 };
+
 
 // Tiny batches (at most kGemvMaxPairs routed pairs in all) go to the fused
 // dequant-GEMV kernels, which spread the weights over every SM; tensor-core
 // tiles would leave most SMs idle there.
 constexpr uint64_t kGemvMaxPairs = 64;
 
-TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_gemv = false) {
+TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_gemv = false, bool allow_fp4 = false) {
   if (allow_gemv && pairs <= kGemvMaxPairs) return {true, 8, 0, false, true};  // callers check kGemvMaxK
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
+  if (allow_fp4 && avg <= kF4MaxAvgPairs) return {true, kF4PairTile, 0, true, false, true};
   // two-term activations: stacked tiles (tw indexes tmap_x_stk / tmap_act_stk)
   if (x_terms == 2 && avg <= 12) return {true, 16, 0, true};
   if (x_terms == 2 && avg <= 24) return {true, 32, 1, true};
@@ -377,6 +427,88 @@ TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_ge
 // otherwise three terms keep the operand error near 2^-13.
 int x_terms_for(const mxmoe_layer* L, int x_dtype) {
   return (x_dtype == MXMOE_BF16 && L->gamma_is_one) ? 2 : 3;
+}
+
+// The FP4 decode variant of run_experts: four-term E2M1 quantization into
+// the stacked 32-pair layout, then W1 and W2 on kind::mxf4 tiles (K = 256
+// per stage; the last stage issues only the MMAs that reach real K).
+int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
+                   const float* route_w, cudaStream_t st, void* const* ret_ptrs, const uint32_t* ret_slot,
+                   bool y_by_pair, const int32_t* perm) {
+  Workspace& w = L->ws;
+  if (!w.xq4) return fail(MXMOE_ERR_INVALID_ARG, "FP4 decode buffers were not reserved");
+  const uint64_t P = static_cast<uint64_t>(n_tok) * k;
+  const int PT = kF4PairTile;
+  const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
+  const float bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
+  CUDA_TRY(launch_quantize_f4_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, w.xq4,
+                                    static_cast<int>(L->kp1 / 2), w.xsf4, static_cast<int>(kc1), PT, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
+  const uint64_t max_pair_tiles = (P + PT - 1) / PT + L->e_count;
+  TcParams p{};
+  p.N = 256;
+  p.sf_rows = PT;
+  p.stacked = 1;
+  p.fp4 = 1;
+  p.b_terms = 1;
+  p.E = L->e_count;
+  p.poff = w.poff;
+  p.counts = w.counts;
+  p.ntile_prefix = w.ntile_prefix;
+  p.alpha = L->cfg.swiglu_alpha;
+  p.limit = L->cfg.swiglu_limit;
+  p.rscale = rscale;
+  p.perm = perm ? perm : w.perm_p;
+  p.k = static_cast<int>(k);
+  p.topk_w = route_w;
+  p.err = L->err;
+  p.d = L->d;
+  p.units = static_cast<int>(L->fp);
+  p.stages = tc_gemm_max_stages(true, 256, 1, L->smem_limit, PT, true, true);
+  auto stage_plan = [&](uint64_t kc, uint32_t k_real) {
+    p.k_chunks = static_cast<int>(kc);
+    p.k_tiles = static_cast<int>((kc + 1) / 2);
+    p.last_mmas = static_cast<int>((k_real - static_cast<uint32_t>(p.k_tiles - 1) * 256u + 63u) / 64u);
+  };
+  // W1 + SwiGLU
+  p.mode = 1;
+  stage_plan(kc1, L->d);
+  p.m_tiles = static_cast<int>((2 * L->fp + 255) / 256);
+  p.w_row_pairs = static_cast<int>(w_sf_row_pairs(2 * L->fp));
+  p.a_sf = L->w1sf;
+  p.b_sf = w.xsf4;
+  p.bias = L->b1;
+  p.bias_stride = static_cast<int>(2 * L->fp);
+  p.rows_valid = static_cast<int>(2 * L->fp);
+  p.bias_mult = 1.0f;
+  p.act_codes = w.aq4;
+  p.act_kp = static_cast<int>(L->kp2 / 2);
+  p.act_sf = w.asf4;
+  p.act_kchunks = static_cast<int>(kc2);
+  int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
+  CUDA_TRY(tc_gemm_launch(true, L->tmap_w1_f4, w.tmap_x4, p, grid, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
+  // W2 + bias + route weight
+  p.mode = 2;
+  stage_plan(kc2, L->fp);
+  p.m_tiles = static_cast<int>((L->d + 255) / 256);
+  p.w_row_pairs = static_cast<int>(w_sf_row_pairs(L->d));
+  p.a_sf = L->w2sf;
+  p.b_sf = w.asf4;
+  p.bias = L->b2;
+  p.bias_stride = static_cast<int>(L->d);
+  p.rows_valid = static_cast<int>(L->d);
+  p.bias_mult = bias_mult;
+  p.y_pair = w.y_pair;
+  p.y_pair_bf16 = reinterpret_cast<__nv_bfloat16*>(w.y_pair);
+  p.ret_ptrs = ret_ptrs;
+  p.ret_slot = ret_slot;
+  p.y_by_pair = y_by_pair ? 1 : 0;
+  w.pair_dtype = MXMOE_BF16;
+  grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
+  CUDA_TRY(tc_gemm_launch(true, L->tmap_w2_f4, w.tmap_act4, p, grid, st));
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
+  return MXMOE_OK;
 }
 
 // Expert FFN over already-routed pairs: quantize -> W1 -> W2 (or the SIMT
@@ -415,6 +547,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
     return MXMOE_OK;
   }
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
+  if (tp.fp4) return run_experts_f4(L, x, x_dtype, n_tok, k, rscale, route_w, st, ret_ptrs, ret_slot, y_by_pair, perm);
   if (!input_quantized)
     CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
                                    w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
@@ -569,6 +702,17 @@ int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out) {
   return MXMOE_OK;
 }
 
+int mxmoe_fp4_operands(mxmoe_layer* L, void** ptrs, uint32_t* rows4) {
+  if (!L || !ptrs || !rows4) return fail(MXMOE_ERR_INVALID_ARG, "mxmoe_fp4_operands: null argument");
+  const Workspace& w = L->ws;
+  ptrs[0] = w.xq4;
+  ptrs[1] = w.xsf4;
+  ptrs[2] = w.aq4;
+  ptrs[3] = w.asf4;
+  *rows4 = w.rows4;
+  return MXMOE_OK;
+}
+
 int mxmoe_get_config(const mxmoe_layer* L, mxmoe_config* out) {
   if (!L || !out) return fail(MXMOE_ERR_INVALID_ARG, "mxmoe_get_config: null argument");
   *out = L->cfg;
@@ -712,6 +856,10 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
     TRY(make_tmap(&L->tmap_w2[i], CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B, L->w2q, kp2, d, E, kp2 / 2, d * (kp2 / 2),
                   box));
   }
+  // the same codes as packed bytes for the kind::mxf4 tiles (128-byte rows = K 256)
+  TRY(make_tmap(&L->tmap_w1_f4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->w1q, kp1 / 2, rows1, E, kp1 / 2, rows1 * (kp1 / 2),
+                256));
+  TRY(make_tmap(&L->tmap_w2_f4, CU_TENSOR_MAP_DATA_TYPE_UINT8, L->w2q, kp2 / 2, d, E, kp2 / 2, d * (kp2 / 2), 256));
   L->experts_ready = true;
   return MXMOE_OK;
 }
@@ -722,6 +870,13 @@ int mxmoe_reserve(mxmoe_layer* L, uint32_t max_tokens) {
   return ensure_workspace(L, max_tokens, L->k);
 }
 
+// Tile plan of mxmoe_forward for P routed pairs.
+static TilePlan forward_plan(const mxmoe_layer* L, uint64_t P, int x_terms) {
+  const bool simt = (L->cfg.flags & MXMOE_FLAG_SIMT) != 0;
+  return pick_tiles(P, L->e_count, x_terms, L->d <= kGemvMaxK && L->fp <= kGemvMaxK,
+                    !simt && !(L->cfg.flags & MXMOE_FLAG_NO_FP4));
+}
+
 // The kernel chain of mxmoe_forward (router, permutation, experts, combine)
 // on stream st; everything that can allocate or resize ran before.
 static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, mxmoe_dtype y_dtype,
@@ -730,13 +885,14 @@ static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, voi
   const uint32_t k = L->k, E = L->e_count;
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
   const int xt = x_terms_for(L, x_dtype);
-  const TilePlan tp = pick_tiles(P, E, xt, L->d <= kGemvMaxK && L->fp <= kGemvMaxK);
+  const TilePlan tp = forward_plan(L, P, xt);
   CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
   CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
                          w.logits, w.topk_idx, w.topk_w, w.rscale, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
-  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, kRowBlock, tp.pair_tile, w.offsets, w.perm_c,
+  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, tp.fp4 ? kF4PairTile : kRowBlock, tp.pair_tile,
+                          w.offsets, w.perm_c,
                           w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
   TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
@@ -792,6 +948,7 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   if (L->e_count != L->E_total)
     return fail(MXMOE_ERR_INVALID_ARG, "layer holds an expert shard; use the expert-parallel entry points");
   TRY(ensure_workspace(L, n_tokens, L->k));
+  if (forward_plan(L, static_cast<uint64_t>(n_tokens) * L->k, x_terms_for(L, x_dtype)).fp4) TRY(ensure_f4(L));
   L->profile_valid = false;
   if (!L->profiling && !(L->cfg.flags & MXMOE_FLAG_NO_GRAPHS)) {
     auto& gr = L->graph;

@@ -12,11 +12,16 @@
 // sum of block-scaled E4M3 terms, so one k-step issues one
 // kind::mxf8f6f4.block_scale MMA per term into the same fp32 TMEM accumulator.
 //
-// Two tile shapes:
+// Three tile shapes:
 //   weights-as-A (decode, few pairs per expert): 128 weight rows x N pairs,
 //     N = 32..128, double-buffered accumulator;
 //   tokens-as-A (prefill): 128 pairs x 256 weight rows, so that each epilogue
-//     thread owns one pair's row and quantizes 32-wide blocks on its own.
+//     thread owns one pair's row and quantizes 32-wide blocks on its own;
+//   FP4 tokens-as-A (decode, few pairs per expert): kind::mxf4 with packed
+//     E2M1 weights and a four-term E2M1 activation, the four terms of 32
+//     pairs stacked in one 128-row operand.  One instruction covers K = 64
+//     at the cycle cost of a K = 32 mxf8f6f4 one, which halves the tensor
+//     time per weight byte where decode would otherwise be MMA-bound.
 // Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, then the
 // epilogue warps (TMEM -> registers -> global: 2..5 for weights-as-A, 2..9 for
 // tokens-as-A) and one warp that moves each stage's scale factors from shared
@@ -59,9 +64,15 @@ struct SmemPlan {
 // the MMA still reads 128 rows, the rows past PT falling into the next buffer
 // of the same stage and only feeding accumulator rows that are discarded.
 // Stacked tokens-as-A tiles hold both terms of PT pairs in 2 * PT rows.
-__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms, int PT, bool stacked) {
+__host__ __device__ inline SmemPlan smem_plan(bool tok, int N, int terms, int PT, bool stacked, bool fp4 = false) {
   SmemPlan s;
-  if (!tok) {
+  if (fp4) {
+    // packed E2M1 rows of K = 256 (128 bytes): 4 * PT activation rows, 256 weight rows
+    s.a_terms = 1;
+    s.b_terms = 1;
+    s.a_bytes = static_cast<uint32_t>(kF4Terms) * static_cast<uint32_t>(PT) * 128u;
+    s.b_bytes = 256u * 128u;
+  } else if (!tok) {
     s.a_terms = 1;
     s.b_terms = terms;
     s.a_bytes = 128 * kTileK;
@@ -165,13 +176,16 @@ __device__ __forceinline__ void store_w2_8(__nv_bfloat16* dst, const float* v, f
                  *reinterpret_cast<const uint32_t*>(&c), *reinterpret_cast<const uint32_t*>(&e));
 }
 
-template <bool kTok>
-__global__ void __launch_bounds__(num_threads(kTok), 1)
+// kKind: 0 = weights-as-A, 1 = tokens-as-A, 2 = FP4 tokens-as-A (stacked).
+template <int kKind>
+__global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     tc_moe_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_x,
                        const TcParams p) {
+  constexpr bool kTok = kKind != 0;
+  constexpr bool kF4 = kKind == 2;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms, p.sf_rows, kTok && p.stacked);
+  const SmemPlan plan = smem_plan(kTok, p.N, p.b_terms, p.sf_rows, kTok && p.stacked, kF4);
   const int S = p.stages;
   float* epi = reinterpret_cast<float*>(smem + S * plan.stage_bytes);
   uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(epi) + epi_smem_bytes(kTok));
@@ -250,6 +264,30 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         uint8_t* x_s = kTok ? sb : sb + plan.a_bytes;
         const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
         uint8_t* sf = sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes;
+        if constexpr (kF4) {
+          // one stage = K 256: the weight tile's packed rows, the tile's 4 * PT
+          // stacked activation rows, and the scale atoms of the stage's one or
+          // two 128-K chunks (weights: the 256-row atom pair per chunk,
+          // adjacent chunks contiguous; activation: one atom per chunk)
+          const int nch = min(2, p.k_chunks - 2 * kt);
+          const uint64_t tile = static_cast<uint64_t>(row0 / PT);
+          mbar_arrive_expect_tx(&full_bar[stage], plan.a_bytes + plan.b_bytes +
+                                                      static_cast<uint32_t>(nch) * (kWSfPairBytes + kSfAtomBytes));
+          tma_load_3d(w_s, &tmap_w, &full_bar[stage], kt * 128, wt * 256, e);
+          tma_load_3d(x_s, &tmap_x, &full_bar[stage], kt * 128, static_cast<int>(tile) * kF4Terms * PT, 0);
+          bulk_load(sf,
+                    p.a_sf + ((static_cast<uint64_t>(e) * p.w_row_pairs + wt) * p.k_chunks + 2 * kt) * kWSfPairBytes,
+                    static_cast<uint32_t>(nch) * kWSfPairBytes, &full_bar[stage]);
+          bulk_load(sf + 2 * kWSfPairBytes, p.b_sf + (tile * p.k_chunks + 2 * kt) * kSfAtomBytes,
+                    static_cast<uint32_t>(nch) * kSfAtomBytes, &full_bar[stage]);
+          issued[stage] = true;
+          issued_parity[stage] = phase;
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          continue;
+        }
         mbar_arrive_expect_tx(&full_bar[stage], tx);
         tma_load_3d(w_s, &tmap_w, &full_bar[stage], kt * kTileK, wt * (kTok ? 256 : 128), e);
         if (kTok && p.stacked) {
@@ -320,19 +358,37 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         const uint32_t x_stride = kTok ? plan.a_bytes : plan.b_bytes;
         const uint32_t col0 = kSfTmemBase + stage * 32;
         const int mma_terms = (kTok && p.stacked) ? 1 : terms;
+        if constexpr (kF4) {
+          // A = stacked activation terms, B = weights; scale columns: weights
+          // col0 + 8 * chunk (+4 for rows 128..255), activation col0 + 16 + 4 * chunk
+          const int nk = kt == p.k_tiles - 1 ? p.last_mmas : 4;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint64_t w_desc = make_smem_desc(w_addr + kk * 32, 16, 1024, 2);
-          for (int term = 0; term < mma_terms; ++term) {
-            const uint64_t x_desc = make_smem_desc(x_addr + term * x_stride + kk * 32, 16, 1024, 2);
-            const uint32_t idesc = make_idesc_mxf8f6f4(a_fmt, b_fmt, 128u, mma_n, kk, kk);
-            const uint32_t sf_w = (tmem_base + col0) | (static_cast<uint32_t>(kk) << 30);
-            const uint32_t sf_x = (tmem_base + col0 + 8 + term * 8) | (static_cast<uint32_t>(kk) << 30);
-            const uint32_t accum = (kt | kk | term) != 0 ? 1u : 0u;
-            if (kTok)
-              tc_mma_mxf8f6f4(d_tmem, x_desc, w_desc, idesc, sf_x, sf_w, accum);
-            else
-              tc_mma_mxf8f6f4(d_tmem, w_desc, x_desc, idesc, sf_w, sf_x, accum);
+          for (int kk = 0; kk < 4; ++kk) {
+            if (kk < nk) {
+              const uint32_t sid = static_cast<uint32_t>(kk & 1) * 2u;
+              const uint64_t w_desc = make_smem_desc(w_addr + kk * 32, 16, 1024, 2);
+              const uint64_t x_desc = make_smem_desc(x_addr + kk * 32, 16, 1024, 2);
+              const uint32_t sf_w = (tmem_base + col0 + static_cast<uint32_t>(kk >> 1) * 8u) | (sid << 30);
+              const uint32_t sf_x = (tmem_base + col0 + 16u + static_cast<uint32_t>(kk >> 1) * 4u) | (sid << 30);
+              tc_mma_mxf4(d_tmem, x_desc, w_desc, make_idesc_mxf4(128u, 256u, sid, sid), sf_x, sf_w,
+                          (kt | kk) != 0 ? 1u : 0u);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t w_desc = make_smem_desc(w_addr + kk * 32, 16, 1024, 2);
+            for (int term = 0; term < mma_terms; ++term) {
+              const uint64_t x_desc = make_smem_desc(x_addr + term * x_stride + kk * 32, 16, 1024, 2);
+              const uint32_t idesc = make_idesc_mxf8f6f4(a_fmt, b_fmt, 128u, mma_n, kk, kk);
+              const uint32_t sf_w = (tmem_base + col0) | (static_cast<uint32_t>(kk) << 30);
+              const uint32_t sf_x = (tmem_base + col0 + 8 + term * 8) | (static_cast<uint32_t>(kk) << 30);
+              const uint32_t accum = (kt | kk | term) != 0 ? 1u : 0u;
+              if (kTok)
+                tc_mma_mxf8f6f4(d_tmem, x_desc, w_desc, idesc, sf_x, sf_w, accum);
+              else
+                tc_mma_mxf8f6f4(d_tmem, w_desc, x_desc, idesc, sf_w, sf_x, accum);
+            }
           }
         }
         tc_commit(&empty_bar[stage]);
@@ -364,14 +420,25 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
         uint8_t* sb = smem + stage * plan.stage_bytes;
         const uint32_t sf_addr = smem_u32(sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes);
         const uint32_t col0 = kSfTmemBase + stage * 32;
-        // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
-        // activation term q at col0 + 8 + 8q (4 per 128 rows).
-        for (int a = 0; a < natoms_w; ++a)
-          tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
-        for (int term = 0; term < mma_terms; ++term)
-          for (int a = 0; a < natoms_x; ++a)
-            tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
-                                 make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
+        if constexpr (kF4) {
+          const int nch = min(2, p.k_chunks - 2 * kt);
+          for (int c = 0; c < nch; ++c) {
+            for (int ra = 0; ra < 2; ++ra)
+              tc_cp_32x128b_warpx4(tmem_base + col0 + c * 8 + ra * 4,
+                                   make_smem_desc(sf_addr + c * kWSfPairBytes + ra * kSfAtomBytes, 0, 128, 0));
+            tc_cp_32x128b_warpx4(tmem_base + col0 + 16 + c * 4,
+                                 make_smem_desc(sf_addr + 2 * kWSfPairBytes + c * kSfAtomBytes, 0, 128, 0));
+          }
+        } else {
+          // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
+          // activation term q at col0 + 8 + 8q (4 per 128 rows).
+          for (int a = 0; a < natoms_w; ++a)
+            tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
+          for (int term = 0; term < mma_terms; ++term)
+            for (int a = 0; a < natoms_x; ++a)
+              tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
+                                   make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
+        }
         tc_commit(&sf_full[stage]);
         if (++stage == S) {
           stage = 0;
@@ -427,6 +494,94 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
           tc_fence_before();
           mbar_arrive(&tmem_empty[acc]);
           if (++acc == nacc) acc = 0;
+        }
+        if constexpr (kF4) {
+          // Lane L holds term L / 8 of pair sp * 8 + L % 8.  Two butterfly
+          // steps (lane ^ 16, lane ^ 8) sum the four terms and leave each lane
+          // a quarter of the warp's 128 columns: W2 columns 32 * (L / 8) ..
+          // + 31; W1 the GLU units 16 * (L / 8) .. + 15 with their linear
+          // partners 64 columns later.
+          const int tq = lane >> 3;
+          const bool up1 = (tq >> 1) != 0, up2 = (tq & 1) != 0;
+          const int jr = sp * 8 + (lane & 7);
+          if (p.mode == 2) {
+            float g1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const float recv = __shfl_xor_sync(0xFFFFFFFFu, up1 ? v[j] : v[64 + j], 16);
+              g1[j] = (up1 ? v[64 + j] : v[j]) + recv;
+            }
+            float g2[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const float recv = __shfl_xor_sync(0xFFFFFFFFu, up2 ? g1[j] : g1[32 + j], 8);
+              g2[j] = (up2 ? g1[32 + j] : g1[j]) + recv;
+            }
+            if (jr >= n_valid) continue;
+            const int pos = pos0 + jr;
+            const int pair = __ldg(p.perm + pos);
+            const float w = __ldg(p.topk_w + pair);
+            const int cf0 = wt * 256 + half * 128 + 32 * tq;
+            const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + cf0);
+            __nv_bfloat16* dst = w2_out_row(p, pos, pair) + cf0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              if (!dry && cf0 + 8 * q < p.rows_valid)
+                store_w2_8(dst + 8 * q, g2 + 8 * q, __ldg(bb + 2 * q), __ldg(bb + 2 * q + 1), p.bias_mult, w);
+          } else {
+            float g1[64];
+#pragma unroll
+            for (int j = 0; j < 64; ++j) {
+              const int cl = j < 32 ? j : j + 32;
+              const float recv = __shfl_xor_sync(0xFFFFFFFFu, up1 ? v[cl] : v[cl + 32], 16);
+              g1[j] = (up1 ? v[cl + 32] : v[cl]) + recv;
+            }
+            float g2[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int cl = j < 16 ? j : j + 16;
+              const float recv = __shfl_xor_sync(0xFFFFFFFFu, up2 ? g1[cl] : g1[cl + 16], 8);
+              g2[j] = (up2 ? g1[cl + 16] : g1[cl]) + recv;
+            }
+            const int unit0 = wt * 128 + half * 64 + 16 * tq;  // GLU unit of g2[0]
+            const bool valid = jr < n_valid && unit0 < p.units;
+            const int pos = pos0 + jr;
+            float a[16];
+            if (valid) {
+              const int pair = __ldg(p.perm + pos);
+              const float r = __ldg(p.rscale + pair / p.k);
+              const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + wt * 256 + half * 128 + 16 * tq);
+#pragma unroll
+              for (int q = 0; q < 4; ++q) {
+                const float4 bg = __ldg(bb + q);       // GLU biases
+                const float4 bl = __ldg(bb + 16 + q);  // linear biases (64 columns later)
+                a[4 * q + 0] = swiglu_clamp(fmaf(g2[4 * q + 0], r, bg.x), fmaf(g2[16 + 4 * q + 0], r, bl.x), p.alpha, p.limit);
+                a[4 * q + 1] = swiglu_clamp(fmaf(g2[4 * q + 1], r, bg.y), fmaf(g2[16 + 4 * q + 1], r, bl.y), p.alpha, p.limit);
+                a[4 * q + 2] = swiglu_clamp(fmaf(g2[4 * q + 2], r, bg.z), fmaf(g2[16 + 4 * q + 2], r, bl.z), p.alpha, p.limit);
+                a[4 * q + 3] = swiglu_clamp(fmaf(g2[4 * q + 3], r, bg.w), fmaf(g2[16 + 4 * q + 3], r, bl.w), p.alpha, p.limit);
+              }
+            } else {
+#pragma unroll
+              for (int i = 0; i < 16; ++i) a[i] = 0.0f;
+            }
+            // a 32-unit block spans this lane and lane ^ 8
+            uint32_t words[kF4Terms][2];
+            uint8_t sbyte[kF4Terms];
+            quantize16_e2m1_terms(a, 8, words, sbyte);
+            if (valid && !dry) {
+#pragma unroll
+              for (int q = 0; q < kF4Terms; ++q) {
+                const uint64_t row = stacked4_code_row(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
+                                                       static_cast<uint32_t>(PT));
+                *reinterpret_cast<uint2*>(p.act_codes + row * p.act_kp + unit0 / 2) = make_uint2(words[q][0], words[q][1]);
+                if (!up2)
+                  p.act_sf[stacked4_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
+                                              static_cast<uint32_t>(unit0 / 32), static_cast<uint32_t>(p.act_kchunks),
+                                              static_cast<uint32_t>(PT))] = sbyte[q];
+              }
+            }
+          }
+          continue;
         }
         if (p.stacked) {
           // Lane L < 16 holds the hi-term row of pair sp*16 + L, lane L + 16 its
@@ -610,29 +765,35 @@ __global__ void __launch_bounds__(num_threads(kTok), 1)
 
 }  // namespace
 
-size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked) {
-  const SmemPlan plan = smem_plan(tokens_as_a, N, terms, pair_tile, tokens_as_a && stacked);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked, bool fp4) {
+  const SmemPlan plan = smem_plan(tokens_as_a, N, terms, pair_tile, tokens_as_a && stacked, fp4);
   return 1024 + static_cast<size_t>(stages) * plan.stage_bytes + epi_smem_bytes(tokens_as_a) +
          (3 * kMaxStages + 10) * sizeof(uint64_t);
 }
 
-int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile, bool stacked) {
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile, bool stacked,
+                       bool fp4) {
   int s = kMaxStages - 1;  // 7 stages x 32 scale columns fit above column 256
-  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s, pair_tile, stacked) > smem_limit) --s;
+  while (s > 1 && tc_gemm_smem_bytes(tokens_as_a, N, terms, s, pair_tile, stacked, fp4) > smem_limit) --s;
   return s;
 }
 
 cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,
                            const TcParams& p, int grid, cudaStream_t stream) {
-  const size_t smem = tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages, p.sf_rows, p.stacked != 0);
-  if (tokens_as_a) {
-    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<true>), smem);
+  const size_t smem =
+      tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages, p.sf_rows, p.stacked != 0, p.fp4 != 0);
+  if (tokens_as_a && p.fp4) {
+    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<2>), smem);
     if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<true><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
+    tc_moe_gemm_kernel<2><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
+  } else if (tokens_as_a) {
+    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<1>), smem);
+    if (st != cudaSuccess) return st;
+    tc_moe_gemm_kernel<1><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
   } else {
-    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<false>), smem);
+    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<0>), smem);
     if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<false><<<grid, num_threads(false), smem, stream>>>(tmap_w, tmap_x, p);
+    tc_moe_gemm_kernel<0><<<grid, num_threads(false), smem, stream>>>(tmap_w, tmap_x, p);
   }
   return cudaGetLastError();
 }

@@ -867,6 +867,85 @@ __global__ void __launch_bounds__(256)
   if constexpr (kDispatch) __threadfence_system();  // peer writes ordered before this GPU's later work
 }
 
+// FP4 decode operand (kind::mxf4 tiles): each routed pair's token row as four
+// block-scaled E2M1 terms in the stacked 32-pair layout (stacked4_code_row,
+// stacked4_sf_offset).  Same warp organisation as quantize_pairs_kernel: warp
+// per (token, sixteen 32-column blocks), a lane pair per block, sixteen
+// columns per lane, so each lane stores 8 code bytes per term.
+__global__ void __launch_bounds__(256)
+    quantize_f4_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
+                             const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
+                             uint8_t* codes, int row_bytes, uint8_t* sf, int kchunks, int pt) {
+  const int nb = d / 32;
+  const int ngrp = (nb + kQBlocksPerWarp - 1) / kQBlocksPerWarp;
+  const uint64_t items = static_cast<uint64_t>(n) * ngrp;
+  const int lane = threadIdx.x & 31;
+  const int hf = lane & 1, lb = lane >> 1;
+  const uint64_t wstride = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (uint64_t it = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
+       it += wstride) {
+    const int t = static_cast<int>(it / ngrp);
+    const int grp = static_cast<int>(it - static_cast<uint64_t>(t) * ngrp);
+    const int b = grp * kQBlocksPerWarp + lb;
+    const bool active = b < nb;
+    const int c0 = b * 32 + hf * 16;
+    float v[16];
+    if (!active) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = 0.0f;
+    } else if (x_dtype == 1) {
+      const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
+                                                        static_cast<uint64_t>(t) * d + c0);
+      const uint4 u0 = __ldg(xs), u1 = __ldg(xs + 1);
+      const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int h = 0; h < 8; ++h) {
+        v[2 * h] = __uint_as_float(w8[h] << 16);
+        v[2 * h + 1] = __uint_as_float(w8[h] & 0xFFFF0000u);
+      }
+    } else {
+      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<uint64_t>(t) * d + c0);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float4 a = __ldg(xs + h);
+        v[4 * h] = a.x; v[4 * h + 1] = a.y; v[4 * h + 2] = a.z; v[4 * h + 3] = a.w;
+      }
+    }
+    if (!gamma_is_one && active) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
+    }
+    uint32_t words[kF4Terms][2];
+    uint8_t sbyte[kF4Terms];
+    quantize16_e2m1_terms(v, 1, words, sbyte);
+    uint32_t sword[kF4Terms];
+#pragma unroll
+    for (int q = 0; q < kF4Terms; ++q) {
+      uint32_t sw = active ? static_cast<uint32_t>(sbyte[q]) << (8 * (lb & 3)) : 0u;
+      sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 2);
+      sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 4);
+      sword[q] = sw;
+    }
+    const bool sf_lane = hf == 0 && (lb & 3) == 0 && active;
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s) {
+      if (s >= k) break;
+      const uint32_t pos = static_cast<uint32_t>(__ldg(inv_p + static_cast<uint64_t>(t) * k + s));
+#pragma unroll
+      for (int q = 0; q < kF4Terms; ++q) {
+        if (active) {
+          const uint64_t row = stacked4_code_row(pos, static_cast<uint32_t>(q), static_cast<uint32_t>(pt));
+          *reinterpret_cast<uint2*>(codes + row * row_bytes + c0 / 2) = make_uint2(words[q][0], words[q][1]);
+        }
+        if (sf_lane)
+          *reinterpret_cast<uint32_t*>(sf + stacked4_sf_offset(pos, static_cast<uint32_t>(q), static_cast<uint32_t>(b),
+                                                               static_cast<uint32_t>(kchunks),
+                                                               static_cast<uint32_t>(pt))) = sword[q];
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ combine
 // y[t] = x[t] + sum over the token's experts in increasing expert index of
 // y_pair (src/moe/mod.rs:279, :405, :411).  One block per token, four
@@ -1654,6 +1733,18 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
   quantize_pairs_kernel<false><<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
                                                      term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked,
                                                      EpDispatch{});
+  return cudaGetLastError();
+}
+
+cudaError_t launch_quantize_f4_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
+                                     int gamma_is_one, const int32_t* inv_p, uint8_t* codes, int row_bytes,
+                                     uint8_t* sf, int kchunks, int pt, cudaStream_t st) {
+  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQBlocksPerWarp - 1) / kQBlocksPerWarp);  // warps
+  if (items == 0 || k == 0) return cudaSuccess;
+  const uint64_t blocks = (items + 7) / 8;
+  const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
+  quantize_f4_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, codes, row_bytes,
+                                                 sf, kchunks, pt);
   return cudaGetLastError();
 }
 

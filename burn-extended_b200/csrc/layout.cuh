@@ -21,6 +21,9 @@
 //             instead (stacked_code_row)
 //   scales    [terms][rows/R][Kp/128] atoms, same byte order as weights, with
 //             R = min(N, 128) rows per atom for tile width N.
+// FP4 decode tiles (kind::mxf4): the activation is a sum of four block-scaled
+// E2M1 terms, packed two codes per byte like the weights, and the four terms
+// of a 32-pair tile fill one 128-row operand (stacked4_code_row).
 #pragma once
 #include <cstdint>
 
@@ -82,6 +85,28 @@ __host__ __device__ inline uint64_t w_sf_offset(uint32_t row, uint32_t kb, uint3
 // order, so one TMA box of 2 * PT rows loads it.
 __host__ __device__ inline uint32_t stacked_code_row(uint32_t pos, uint32_t term, uint32_t pt) {
   return (pos / pt) * (2u * pt) + stacked_operand_row(pos % pt, term);
+}
+
+// FP4 stacked tiles of PT <= 32 pairs, four E2M1 terms in one 128-row MMA
+// operand: pair j, term t is operand row (j / 8) * 32 + 8 * t + j % 8, so
+// every 32-lane TMEM sub-partition carries 8 pairs with their four terms in
+// lanes L, L + 8, L + 16, L + 24.
+constexpr int kF4Terms = 4;
+constexpr int kF4PairTile = 32;
+__host__ __device__ inline uint32_t stacked4_operand_row(uint32_t j, uint32_t term) {
+  return (j / 8u) * 32u + 8u * term + j % 8u;
+}
+// Code row of (pair pos, term t) in a buffer of 4 x rows rows of Kp/2 bytes:
+// a tile's 4 * PT rows are consecutive, in operand order.
+__host__ __device__ inline uint32_t stacked4_code_row(uint32_t pos, uint32_t term, uint32_t pt) {
+  return (pos / pt) * (4u * pt) + stacked4_operand_row(pos % pt, term);
+}
+// Scale byte of (pair pos, term t, k block kb): one atom per tile and 128-K
+// chunk, [tiles][k_chunks][512], so a stage's two chunks are adjacent.
+__host__ __device__ inline uint64_t stacked4_sf_offset(uint32_t pos, uint32_t term, uint32_t kb, uint32_t k_chunks,
+                                                       uint32_t pt) {
+  return (static_cast<uint64_t>(pos / pt) * k_chunks + kb / 4) * kSfAtomBytes +
+         sf_atom_byte(stacked4_operand_row(pos % pt, term), kb % 4);
 }
 
 }  // namespace mxmoe

@@ -143,6 +143,19 @@ __device__ __forceinline__ void tc_mma_mxf8f6f4(uint32_t d_tmem, uint64_t a_desc
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
       : "memory");
 }
+// D(tmem) (+)= A(smem) x B(smem)^T, both packed E2M1 (two codes per byte),
+// K = 64 per instruction, one E8M0 scale per 32 K (two per row per
+// instruction, picked by the scale id 0 or 2 of the TMEM scale column).
+__device__ __forceinline__ void tc_mma_mxf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4.block_scale.scale_vec::2X [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(
+          d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
+      : "memory");
+}
 // 32 lanes x 32 bit, 16 consecutive columns per thread.
 __device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, float (&v)[16]) {
   uint32_t r[16];
@@ -191,6 +204,14 @@ __host__ __device__ constexpr uint32_t make_idesc_mxf8f6f4(uint32_t a_fmt, uint3
                                                            uint32_t sfa_id, uint32_t sfb_id) {
   return ((sfb_id & 3u) << 4) | ((a_fmt & 7u) << 7) | ((b_fmt & 7u) << 10) | (((n >> 3) & 0x3Fu) << 17) |
          (1u << 23) /* E8M0 */ | (((m >> 4) & 0x1Fu) << 24) | ((sfa_id & 3u) << 29);
+}
+
+// Instruction descriptor of kind::mxf4.block_scale: A and B packed E2M1
+// (format 1), both K-major, E8M0 scales; scale ids 0 or 2 select the byte
+// pair of the 32-bit scale column.
+__host__ __device__ constexpr uint32_t make_idesc_mxf4(uint32_t m, uint32_t n, uint32_t sfa_id, uint32_t sfb_id) {
+  return ((sfb_id & 3u) << 4) | (1u << 7) | (1u << 10) | (((n >> 3) & 0x3Fu) << 17) | (1u << 23) |
+         (((m >> 4) & 0x1Fu) << 24) | ((sfa_id & 3u) << 29);
 }
 
 }  // namespace mxmoe

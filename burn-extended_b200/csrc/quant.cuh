@@ -7,8 +7,11 @@
 // so n terms carry about 4n significant bits: two terms reproduce a bf16 value
 // exactly, three cover f32 inputs to ~2^-13.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <cstdint>
+
+#include "layout.cuh"
 
 namespace mxmoe {
 
@@ -116,6 +119,86 @@ __device__ __forceinline__ void quantize_block32(float (&v)[32], int terms, uint
       }
       sbyte[t] = static_cast<uint8_t>(s + 127);
     }
+  }
+}
+
+}  // namespace mxmoe
+
+namespace mxmoe {
+
+// ---------------------------------------------------------------- E2M1 terms
+// The FP4 decode operand: a sum of four block-scaled E2M1 terms (kind::mxf4).
+// Term t of a 32-block is code_t * 2^s_t with s_t the smallest exponent that
+// keeps the block's largest remaining magnitude within E2M1 range (<= 6); the
+// residual after each term is exact in f32.  Each term removes two to three
+// bits of the block's error, so four terms leave ~2^-9 of the block maximum.
+
+// E8M0 exponent s (value 2^s) such that amax * 2^-s <= 6 (E2M1 max).
+__device__ __forceinline__ int e2m1_block_exp(float amax) {
+  const uint32_t bits = __float_as_uint(amax);
+  const int ef = static_cast<int>((bits >> 23) & 0xFF);
+  if (ef == 0) return -127;  // zero or subnormal block
+  const uint32_t mant = bits & 0x7FFFFFu;
+  const int s = (ef - 127) - (mant <= 0x400000u ? 2 : 1);  // 1.5 * 2^2 == 6
+  return s < -127 ? -127 : (s > 127 ? 127 : s);
+}
+
+// Eight f32 -> eight E2M1 codes, element 2i in the low nibble of byte i.
+__device__ __forceinline__ uint32_t cvt_e2m1x8(const float* a) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b0, %2, %1;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b1, %4, %3;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b2, %6, %5;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 b3, %8, %7;\n\t"
+      "mov.b32 %0, {b0, b1, b2, b3};\n\t}"
+      : "=r"(r)
+      : "f"(a[0]), "f"(a[1]), "f"(a[2]), "f"(a[3]), "f"(a[4]), "f"(a[5]), "f"(a[6]), "f"(a[7]));
+  return r;
+}
+
+// Exact value of one E2M1 code (sign bit 3, exponent bits 2..1, mantissa
+// bit 0), built as f32 bits with integer operations.  The residual update
+// decodes the codes it just packed this way rather than with the
+// e2m1x2 -> f16x2 conversion, whose byte-register inputs did not survive
+// being packed and unpacked within one function.
+__device__ __forceinline__ float e2m1_value(uint32_t c) {
+  const uint32_t e = (c >> 1) & 3u, m = c & 1u;
+  uint32_t bits = e ? (((e + 126u) << 23) | (m << 22)) : (m ? 0x3F000000u : 0u);
+  bits |= (c & 8u) << 28;
+  return __uint_as_float(bits);
+}
+
+// Lane-pair cooperative: this lane holds 16 elements of a 32-block whose
+// other half sits in lane ^ xor_mask.  Writes the four terms' codes (16
+// nibbles = two words per term) and E8M0 bytes (equal in both lanes).  Every
+// lane of the warp must call it (the block maximum is a shuffle).
+__device__ __forceinline__ void quantize16_e2m1_terms(float (&v)[16], int xor_mask, uint32_t (&words)[kF4Terms][2],
+                                                      uint8_t (&sbyte)[kF4Terms]) {
+#pragma unroll
+  for (int t = 0; t < kF4Terms; ++t) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, xor_mask));
+    const int s = e2m1_block_exp(amax);
+    const bool fast = (s > -127) && (s < 127);
+    const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
+    const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
+#pragma unroll
+    for (int w = 0; w < 2; ++w) {
+      float sc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sc[i] = fast ? v[8 * w + i] * inv : ldexpf(v[8 * w + i], -s);
+      const uint32_t c = cvt_e2m1x8(sc);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float dq = e2m1_value(c >> (4 * i));
+        v[8 * w + i] = fast ? fmaf(-dq, back, v[8 * w + i]) : v[8 * w + i] - ldexpf(dq, s);
+      }
+      words[t][w] = c;
+    }
+    sbyte[t] = static_cast<uint8_t>(s + 127);
   }
 }
 

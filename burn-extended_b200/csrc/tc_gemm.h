@@ -20,6 +20,9 @@ struct TcParams {
   int b_terms;   // E4M3 terms of the activation operand (2 or 3)
   int sf_rows;   // rows per activation scale atom (= pairs per tile, <= 128)
   int stacked;   // tokens-as-A tiles of 64 pairs with both activation terms in one 128-row operand
+  int fp4;       // kind::mxf4 stacked tiles: four E2M1 activation terms, K = 256 per stage
+  int k_chunks;  // 128-K scale chunks of the operands (= k_tiles except in fp4 tiles)
+  int last_mmas; // fp4: MMAs of K = 64 issued in the last stage (the rest is K padding)
   const int* poff;          // [E+1] padded segment starts (multiples of 128)
   const int* counts;        // [E] pairs per expert
   const int* ntile_prefix;  // [E+1] prefix sums of ceil(count / N)
@@ -36,7 +39,7 @@ struct TcParams {
   const float* topk_w;      // [n*k]
   uint8_t* act_codes;       // W1 output [2][rows][act_kp]
   uint64_t act_term_stride;
-  int act_kp;
+  int act_kp;    // bytes per activation code row
   uint8_t* act_sf;          // W1 output atoms [2][row_blocks][act_kchunks][512]
   uint64_t act_sf_term_stride;
   int act_kchunks;
@@ -53,8 +56,10 @@ struct TcParams {
   int* err;                 // device status word (0 = ok)
 };
 
-size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked);
-int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile, bool stacked);
+size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked,
+                          bool fp4 = false);
+int tc_gemm_max_stages(bool tokens_as_a, int N, int terms, size_t smem_limit, int pair_tile, bool stacked,
+                       bool fp4 = false);
 // tmap_w: weight codes (box 128 rows weights-as-A, 256 rows tokens-as-A);
 // tmap_x: activation terms (box = pairs per tile rows).
 cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CUtensorMap& tmap_x,

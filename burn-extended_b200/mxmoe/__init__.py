@@ -18,8 +18,8 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (BF16, F32, FLAG_BIAS_PER_FTILE, FLAG_DISABLED, FLAG_INTERLEAVED_GLU, FLAG_NO_RESIDUAL,
-                   FLAG_SIMT, Config, MxMoeError, QuantDesc, check, exported_symbols, last_error, lib)
+from ._lib import (BF16, F32, FLAG_BIAS_PER_FTILE, FLAG_DISABLED, FLAG_INTERLEAVED_GLU, FLAG_NO_FP4,
+                   FLAG_NO_RESIDUAL, FLAG_SIMT, Config, MxMoeError, QuantDesc, check, exported_symbols, last_error, lib)
 
 __all__ = [
     "MoeConfig", "MoeGatedSwiGLU", "QuantLinearMxFp4Desc", "MoeQuantLayerHost", "dequant_mxfp4_bytes",
@@ -94,6 +94,7 @@ class MoeConfig:
     bias_per_ftile: bool = False
     residual: bool = True
     simt: bool = False
+    fp4_decode: bool = True  # kind::mxf4 tiles for decode batches (FLAG_NO_FP4 when False)
 
     def flags(self) -> int:
         f = 0
@@ -107,6 +108,8 @@ class MoeConfig:
             f |= FLAG_DISABLED
         if self.simt:
             f |= FLAG_SIMT
+        if not self.fp4_decode:
+            f |= FLAG_NO_FP4
         return f
 
     def init(self, device: int = 0) -> "MoeGatedSwiGLU":

@@ -20,6 +20,8 @@ FLAG_BIAS_PER_FTILE = 0x2
 FLAG_NO_RESIDUAL = 0x4
 FLAG_DISABLED = 0x8
 FLAG_SIMT = 0x10
+FLAG_NO_GRAPHS = 0x20
+FLAG_NO_FP4 = 0x40
 
 
 class MxMoeError(RuntimeError):
@@ -70,6 +72,7 @@ _SIGS = {
     "mxmoe_create": ([ctypes.POINTER(Config), ctypes.POINTER(_vp)], _i32),
     "mxmoe_destroy": ([_vp], _i32),
     "mxmoe_get_config": ([_vp, ctypes.POINTER(Config)], _i32),
+    "mxmoe_fp4_operands": ([_vp, _vp, ctypes.POINTER(_u32)], _i32),
     "mxmoe_set_router": ([_vp, _vp, _vp, _vp, _i32, _vp], _i32),
     "mxmoe_upload_experts": ([_vp, ctypes.POINTER(QuantDesc), _vp, _vp, ctypes.POINTER(QuantDesc), _vp, _vp,
                               _vp, _vp, _i32, _vp], _i32),

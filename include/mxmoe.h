@@ -66,6 +66,11 @@ typedef enum mxmoe_dtype {
                                             graph (by default the second call with
                                             the same x, y, n and dtypes is captured
                                             and later ones replay it) */
+#define MXMOE_FLAG_NO_FP4          0x40u /* keep decode batches (at most 24 routed
+                                            pairs per expert) on the E4M3
+                                            tensor-core tiles instead of the
+                                            kind::mxf4 tiles with a four-term
+                                            E2M1 activation */
 
 /* Mirrors moe::MoeConfig (src/moe/mod.rs:22-33).  `initializer` and `verbose`
  * have no device meaning; swiglu_alpha / swiglu_limit are honoured (the
@@ -108,6 +113,14 @@ MXMOE_API int mxmoe_last_error(char* buf, size_t cap);
 /* Replaces MoeConfig::init (src/moe/mod.rs:60-91): validates the config and
  * creates an empty layer on cfg->device. */
 MXMOE_API int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out);
+
+/* Device buffers of the FP4 decode operands of the last forward that used
+ * them (for inspection): ptrs[0] W1 input codes [4 * rows4][kp1 / 2],
+ * ptrs[1] their scale atoms [rows4 / 32][kp1 / 128][512], ptrs[2] / ptrs[3]
+ * the same for the W2 input (kp2 = f padded); pair pos, term t sits at
+ * code row (pos / 32) * 128 + (pos % 32 / 8) * 32 + 8 t + pos % 8.  NULL and
+ * rows4 = 0 before the first FP4 forward. */
+MXMOE_API int mxmoe_fp4_operands(mxmoe_layer* layer, void** ptrs, uint32_t* rows4);
 
 /* The layer's config as created (the loaders fill in the shapes and flags
  * from the file). */

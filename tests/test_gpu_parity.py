@@ -215,6 +215,30 @@ def test_decode_config_against_oracle(torch, simt):
     layer.close()
 
 
+@pytest.mark.parametrize("fp4", [True, False])
+@pytest.mark.parametrize("shape", [
+    (2880, 2880, 32, 4, 64, True, False),    # decode config: 8 pairs per expert
+    (2880, 2880, 32, 4, 190, True, False),   # 23.75 pairs per expert: the last FP4 plan
+    (512, 384, 4, 2, 40, False, True),       # f32 input, non-unit RmsNorm gain, 20 pairs per expert
+    (1024, 320, 8, 4, 48, True, True),       # K not a multiple of 256 (last stage partial)
+])
+def test_decode_tile_paths(torch, shape, fp4):
+    """Decode-sized batches on the kind::mxf4 tiles (four E2M1 activation
+    terms) and on the E4M3 stacked tiles they replace."""
+    d, f, E, k, n, bf16, gain = shape
+    inp = synth.make_inputs(d, f, E, k, n, bf16, seed=n + E)
+    if gain:
+        inp.gamma = synth.bf16_round(1.0 + 0.25 * np.random.default_rng(7).standard_normal(d).astype(np.float32))
+    want, idx, _ = oracle_forward(inp)
+    layer = make_layer(inp, fp4_decode=fp4)
+    y = layer.forward(to_device_x(inp), out_dtype=torch.float32)
+    layer.sync_status()
+    r = layer.routing_results(n)
+    np.testing.assert_array_equal(r["topk_idx"].cpu().numpy().reshape(n, k), idx)
+    assert_close(y.cpu().numpy(), want, f"{shape} fp4={fp4}")
+    layer.close()
+
+
 @pytest.mark.parametrize("T", [1, 2, 4, 8])
 def test_microbench_single_expert(torch, T):
     inp = synth.make_inputs(2880, 2880, 1, 1, T, True, seed=T)
