@@ -201,6 +201,7 @@ struct Workspace {
   uint8_t* xsf4 = nullptr;
   uint8_t* aq4 = nullptr;
   uint8_t* asf4 = nullptr;
+  float* act4_f32 = nullptr;  // [rows4][fp] W1 output before quantization
   CUtensorMap tmap_x4, tmap_act4;
 };
 
@@ -255,7 +256,7 @@ void free_workspace(Workspace& w) {
   dfree(w.offsets); dfree(w.perm_c); dfree(w.inv_c); dfree(w.poff); dfree(w.counts);
   dfree(w.ntile_prefix); dfree(w.perm_p); dfree(w.inv_p);
   dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
-  dfree(w.xq4); dfree(w.xsf4); dfree(w.aq4); dfree(w.asf4);
+  dfree(w.xq4); dfree(w.xsf4); dfree(w.aq4); dfree(w.asf4); dfree(w.act4_f32);
   w.rows4 = 0;
   dfree(w.local_idx);
   dfree(w.ret_slot);
@@ -373,6 +374,7 @@ int ensure_f4(mxmoe_layer* L) {
   TRY(dalloc(&w.aq4, aq_bytes));
   TRY(dalloc(&w.xsf4, tiles * kc1 * kSfAtomBytes));
   TRY(dalloc(&w.asf4, tiles * kc2 * kSfAtomBytes));
+  TRY(dalloc(&w.act4_f32, static_cast<size_t>(rows4) * L->fp));
   // K padding and rows of absent pairs read as zero codes and finite scales
   CUDA_TRY(cudaMemset(w.xq4, 0, xq_bytes));
   CUDA_TRY(cudaMemset(w.aq4, 0, aq_bytes));
@@ -442,7 +444,7 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   const float bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
   CUDA_TRY(launch_quantize_f4_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, w.xq4,
-                                    static_cast<int>(L->kp1 / 2), w.xsf4, static_cast<int>(kc1), PT, st));
+                                    static_cast<int>(L->kp1 / 2), w.xsf4, static_cast<int>(kc1), PT, 0, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
   const uint64_t max_pair_tiles = (P + PT - 1) / PT + L->e_count;
   TcParams p{};
@@ -481,12 +483,13 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
   p.bias_stride = static_cast<int>(2 * L->fp);
   p.rows_valid = static_cast<int>(2 * L->fp);
   p.bias_mult = 1.0f;
-  p.act_codes = w.aq4;
-  p.act_kp = static_cast<int>(L->kp2 / 2);
-  p.act_sf = w.asf4;
-  p.act_kchunks = static_cast<int>(kc2);
+  p.act_f32 = w.act4_f32;
   int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
   CUDA_TRY(tc_gemm_launch(true, L->tmap_w1_f4, w.tmap_x4, p, grid, st));
+  // the f32 activation rows of the routed pairs -> four-term E2M1 operand of W2
+  CUDA_TRY(launch_quantize_f4_pairs(w.act4_f32, MXMOE_F32, static_cast<int>(P), static_cast<int>(L->fp), 1, nullptr, 1,
+                                    w.inv_p, w.aq4, static_cast<int>(L->kp2 / 2), w.asf4, static_cast<int>(kc2), PT,
+                                    1, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
   // W2 + bias + route weight
   p.mode = 2;

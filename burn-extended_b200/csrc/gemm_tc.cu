@@ -19,7 +19,8 @@
 //     thread owns one pair's row and quantizes 32-wide blocks on its own;
 //   FP4 tokens-as-A (decode, few pairs per expert): kind::mxf4 with packed
 //     E2M1 weights and a four-term E2M1 activation, the four terms of 32
-//     pairs stacked in one 128-row operand.  One instruction covers K = 64
+//     pairs stacked in one 128-row operand; W1 writes its activation in f32
+//     for a separate quantization pass.  One instruction covers K = 64
 //     at the cycle cost of a K = 32 mxf8f6f4 one, which halves the tensor
 //     time per weight byte where decode would otherwise be MMA-bound.
 // Warp roles: warp 0 = TMA producer, warp 1 = TMEM owner + MMA issuer, then the
@@ -543,41 +544,26 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
               const float recv = __shfl_xor_sync(0xFFFFFFFFu, up2 ? g1[cl] : g1[cl + 16], 8);
               g2[j] = (up2 ? g1[cl + 16] : g1[cl]) + recv;
             }
+            // SwiGLU in f32 to the activation rows [pos][units]; a separate
+            // pass splits them into the four-term E2M1 operand of W2 (doing
+            // that here would make this epilogue slower than the tile's MMAs)
             const int unit0 = wt * 128 + half * 64 + 16 * tq;  // GLU unit of g2[0]
-            const bool valid = jr < n_valid && unit0 < p.units;
-            const int pos = pos0 + jr;
-            float a[16];
-            if (valid) {
+            if (jr < n_valid && unit0 < p.units && !dry) {
+              const int pos = pos0 + jr;
               const int pair = __ldg(p.perm + pos);
               const float r = __ldg(p.rscale + pair / p.k);
               const float4* bb = reinterpret_cast<const float4*>(p.bias + bias_e + wt * 256 + half * 128 + 16 * tq);
+              float4* dst = reinterpret_cast<float4*>(p.act_f32 + static_cast<uint64_t>(pos) * p.units + unit0);
 #pragma unroll
               for (int q = 0; q < 4; ++q) {
                 const float4 bg = __ldg(bb + q);       // GLU biases
                 const float4 bl = __ldg(bb + 16 + q);  // linear biases (64 columns later)
-                a[4 * q + 0] = swiglu_clamp(fmaf(g2[4 * q + 0], r, bg.x), fmaf(g2[16 + 4 * q + 0], r, bl.x), p.alpha, p.limit);
-                a[4 * q + 1] = swiglu_clamp(fmaf(g2[4 * q + 1], r, bg.y), fmaf(g2[16 + 4 * q + 1], r, bl.y), p.alpha, p.limit);
-                a[4 * q + 2] = swiglu_clamp(fmaf(g2[4 * q + 2], r, bg.z), fmaf(g2[16 + 4 * q + 2], r, bl.z), p.alpha, p.limit);
-                a[4 * q + 3] = swiglu_clamp(fmaf(g2[4 * q + 3], r, bg.w), fmaf(g2[16 + 4 * q + 3], r, bl.w), p.alpha, p.limit);
-              }
-            } else {
-#pragma unroll
-              for (int i = 0; i < 16; ++i) a[i] = 0.0f;
-            }
-            // a 32-unit block spans this lane and lane ^ 8
-            uint32_t words[kF4Terms][2];
-            uint8_t sbyte[kF4Terms];
-            quantize16_e2m1_terms(a, 8, words, sbyte);
-            if (valid && !dry) {
-#pragma unroll
-              for (int q = 0; q < kF4Terms; ++q) {
-                const uint64_t row = stacked4_code_row(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
-                                                       static_cast<uint32_t>(PT));
-                *reinterpret_cast<uint2*>(p.act_codes + row * p.act_kp + unit0 / 2) = make_uint2(words[q][0], words[q][1]);
-                if (!up2)
-                  p.act_sf[stacked4_sf_offset(static_cast<uint32_t>(pos), static_cast<uint32_t>(q),
-                                              static_cast<uint32_t>(unit0 / 32), static_cast<uint32_t>(p.act_kchunks),
-                                              static_cast<uint32_t>(PT))] = sbyte[q];
+                float4 o;
+                o.x = swiglu_clamp(fmaf(g2[4 * q + 0], r, bg.x), fmaf(g2[16 + 4 * q + 0], r, bl.x), p.alpha, p.limit);
+                o.y = swiglu_clamp(fmaf(g2[4 * q + 1], r, bg.y), fmaf(g2[16 + 4 * q + 1], r, bl.y), p.alpha, p.limit);
+                o.z = swiglu_clamp(fmaf(g2[4 * q + 2], r, bg.z), fmaf(g2[16 + 4 * q + 2], r, bl.z), p.alpha, p.limit);
+                o.w = swiglu_clamp(fmaf(g2[4 * q + 3], r, bg.w), fmaf(g2[16 + 4 * q + 3], r, bl.w), p.alpha, p.limit);
+                dst[q] = o;
               }
             }
           }

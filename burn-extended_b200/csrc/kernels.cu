@@ -875,7 +875,7 @@ __global__ void __launch_bounds__(256)
 __global__ void __launch_bounds__(256)
     quantize_f4_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                              const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
-                             uint8_t* codes, int row_bytes, uint8_t* sf, int kchunks, int pt) {
+                             uint8_t* codes, int row_bytes, uint8_t* sf, int kchunks, int pt, int src_by_pos) {
   const int nb = d / 32;
   const int ngrp = (nb + kQBlocksPerWarp - 1) / kQBlocksPerWarp;
   const uint64_t items = static_cast<uint64_t>(n) * ngrp;
@@ -889,13 +889,15 @@ __global__ void __launch_bounds__(256)
     const int b = grp * kQBlocksPerWarp + lb;
     const bool active = b < nb;
     const int c0 = b * 32 + hf * 16;
+    // source row: token t, or (activation rows, k = 1) the pair's own position
+    const uint64_t src = src_by_pos ? static_cast<uint64_t>(__ldg(inv_p + t)) : static_cast<uint64_t>(t);
     float v[16];
     if (!active) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = 0.0f;
     } else if (x_dtype == 1) {
       const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
-                                                        static_cast<uint64_t>(t) * d + c0);
+                                                        src * d + c0);
       const uint4 u0 = __ldg(xs), u1 = __ldg(xs + 1);
       const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
 #pragma unroll
@@ -904,7 +906,7 @@ __global__ void __launch_bounds__(256)
         v[2 * h + 1] = __uint_as_float(w8[h] & 0xFFFF0000u);
       }
     } else {
-      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + static_cast<uint64_t>(t) * d + c0);
+      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + src * d + c0);
 #pragma unroll
       for (int h = 0; h < 4; ++h) {
         const float4 a = __ldg(xs + h);
@@ -1738,13 +1740,13 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
 
 cudaError_t launch_quantize_f4_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                      int gamma_is_one, const int32_t* inv_p, uint8_t* codes, int row_bytes,
-                                     uint8_t* sf, int kchunks, int pt, cudaStream_t st) {
+                                     uint8_t* sf, int kchunks, int pt, int src_by_pos, cudaStream_t st) {
   const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQBlocksPerWarp - 1) / kQBlocksPerWarp);  // warps
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
   quantize_f4_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, codes, row_bytes,
-                                                 sf, kchunks, pt);
+                                                 sf, kchunks, pt, src_by_pos);
   return cudaGetLastError();
 }
 

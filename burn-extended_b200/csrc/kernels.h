@@ -47,9 +47,11 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
                            int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix, int32_t* perm_p,
                            int32_t* inv_p, cudaStream_t st, int32_t* scratch = nullptr);
 // Four-term E2M1 stacked decode operand (kind::mxf4 tiles of pt <= 32 pairs).
+// src_by_pos: x holds one row per padded pair position (k = 1, row
+// inv_p[t]) instead of one row per token.
 cudaError_t launch_quantize_f4_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                      int gamma_is_one, const int32_t* inv_p, uint8_t* codes, int row_bytes,
-                                     uint8_t* sf, int kchunks, int pt, cudaStream_t st);
+                                     uint8_t* sf, int kchunks, int pt, int src_by_pos, cudaStream_t st);
 cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                   int gamma_is_one, const int32_t* inv_p, int terms, uint8_t* codes,
                                   uint64_t term_stride, int kp, uint8_t* sf, uint64_t sf_term_stride, int kchunks,

@@ -41,6 +41,7 @@ struct TcParams {
   uint64_t act_term_stride;
   int act_kp;    // bytes per activation code row
   uint8_t* act_sf;          // W1 output atoms [2][row_blocks][act_kchunks][512]
+  float* act_f32;           // fp4 W1 output [rows][units] f32 (SwiGLU, before quantization)
   uint64_t act_sf_term_stride;
   int act_kchunks;
   float* y_pair;            // W2 output [rows][d] f32 (weights-as-A)
