@@ -176,6 +176,12 @@ def measure_decode(args, local, dev, hbm_peak):
     e2_.record()
     torch.cuda.synchronize()
     dec_ms = s2.elapsed_time(e2_) / args.steps
+    # SM clock under this load (a longer loop so that the sampler sees it)
+    with ClockSampler(local) as clk:
+        for _ in range(400):
+            dl.forward(xd)
+        torch.cuda.synchronize()
+    dec_clocks = clk.summary()
     rr = dl.routing_results(dec.n)
     used = int((np.diff(rr["offsets"].cpu().numpy()) > 0).sum())
     per_expert = 2 * f * d // 2 + 2 * f * d // 32 + d * f // 2 + d * f // 32 + 2 * (2 * f + d)
@@ -196,6 +202,7 @@ def measure_decode(args, local, dev, hbm_peak):
                             "peak": hbm_peak, "unit": "GB/s",
                             "frac": used * (8294400 + 518400 + 23040) / (dstages["w1_gemm"] / 1e3) / 1e9 / hbm_peak,
                             "traffic": W1_DECODE_TRAFFIC},
+            "clocks": dec_clocks,
             "l2": "weights of the 32 experts (423 MB) exceed the 126 MB L2; no flush"}
 
 

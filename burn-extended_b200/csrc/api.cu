@@ -202,7 +202,7 @@ struct Workspace {
   uint8_t* aq4 = nullptr;
   uint8_t* asf4 = nullptr;
   float* act4_f32 = nullptr;  // [rows4][fp] W1 output before quantization
-  CUtensorMap tmap_x4, tmap_act4;
+  CUtensorMap tmap_x4[2], tmap_act4[2];  // boxes of 4 x 16 and 4 x 32 rows
 };
 
 struct mxmoe_layer {
@@ -360,14 +360,14 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
 constexpr int kF4MaxAvgPairs = 24;
 
 // FP4 decode buffers: fp4 plans keep at most kF4MaxAvgPairs * E pairs, and
-// their expert segments are padded to kF4PairTile rows.
+// their expert segments are padded to the pair tile (at most kF4PairTile).
 int ensure_f4(mxmoe_layer* L) {
   Workspace& w = L->ws;
   if (w.xq4) return MXMOE_OK;
   const uint32_t E = L->e_count;
   const uint32_t rows4 = round_up((kF4MaxAvgPairs + kF4PairTile) * E + 64, kF4PairTile);
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
-  const uint64_t tiles = rows4 / kF4PairTile;
+  const uint64_t tiles = rows4 / kF4PairTileSmall;  // scale atoms per 128-K chunk, smallest tile
   const size_t xq_bytes = static_cast<size_t>(kF4Terms) * rows4 * (L->kp1 / 2);
   const size_t aq_bytes = static_cast<size_t>(kF4Terms) * rows4 * (L->kp2 / 2);
   TRY(dalloc(&w.xq4, xq_bytes));
@@ -380,11 +380,13 @@ int ensure_f4(mxmoe_layer* L) {
   CUDA_TRY(cudaMemset(w.aq4, 0, aq_bytes));
   CUDA_TRY(cudaMemset(w.xsf4, 0, tiles * kc1 * kSfAtomBytes));
   CUDA_TRY(cudaMemset(w.asf4, 0, tiles * kc2 * kSfAtomBytes));
-  const uint32_t box = kF4Terms * kF4PairTile;
-  TRY(make_tmap(&w.tmap_x4, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.xq4, L->kp1 / 2, uint64_t(kF4Terms) * rows4, 1,
-                L->kp1 / 2, xq_bytes, box));
-  TRY(make_tmap(&w.tmap_act4, CU_TENSOR_MAP_DATA_TYPE_UINT8, w.aq4, L->kp2 / 2, uint64_t(kF4Terms) * rows4, 1,
-                L->kp2 / 2, aq_bytes, box));
+  for (int i = 0; i < 2; ++i) {
+    const uint32_t box = kF4Terms * (i ? kF4PairTile : kF4PairTileSmall);
+    TRY(make_tmap(&w.tmap_x4[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.xq4, L->kp1 / 2, uint64_t(kF4Terms) * rows4, 1,
+                  L->kp1 / 2, xq_bytes, box));
+    TRY(make_tmap(&w.tmap_act4[i], CU_TENSOR_MAP_DATA_TYPE_UINT8, w.aq4, L->kp2 / 2, uint64_t(kF4Terms) * rows4, 1,
+                  L->kp2 / 2, aq_bytes, box));
+  }
   w.rows4 = rows4;
   return MXMOE_OK;
 }
@@ -402,7 +404,7 @@ struct TilePlan {
   int tw;
   bool stacked;
   bool gemv = false;  // fused dequant-GEMV on CUDA cores instead of tensor-core tiles
-  bool fp4 = false;   // kind::mxf4 stacked tiles of kF4PairTile pairs, four E2M1 activation terms
+  bool fp4 = false;   // kind::mxf4 stacked tiles of 16 / 32 pairs (tw 0 / 1), four E2M1 activation terms
 };
 
 
@@ -414,7 +416,10 @@ constexpr uint64_t kGemvMaxPairs = 64;
 TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_gemv = false, bool allow_fp4 = false) {
   if (allow_gemv && pairs <= kGemvMaxPairs) return {true, 8, 0, false, true};  // callers check kGemvMaxK
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
-  if (allow_fp4 && avg <= kF4MaxAvgPairs) return {true, kF4PairTile, 0, true, false, true};
+  // FP4: 16-pair tiles (8 KB of activation per stage, so five stages fit)
+  // while few experts overflow them, else 32-pair tiles
+  if (allow_fp4 && avg <= kF4MaxAvgPairs / 2) return {true, kF4PairTileSmall, 0, true, false, true};
+  if (allow_fp4 && avg <= kF4MaxAvgPairs) return {true, kF4PairTile, 1, true, false, true};
   // two-term activations: stacked tiles (tw indexes tmap_x_stk / tmap_act_stk)
   if (x_terms == 2 && avg <= 12) return {true, 16, 0, true};
   if (x_terms == 2 && avg <= 24) return {true, 32, 1, true};
@@ -435,12 +440,12 @@ int x_terms_for(const mxmoe_layer* L, int x_dtype) {
 // the stacked 32-pair layout, then W1 and W2 on kind::mxf4 tiles (K = 256
 // per stage; the last stage issues only the MMAs that reach real K).
 int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
-                   const float* route_w, cudaStream_t st, void* const* ret_ptrs, const uint32_t* ret_slot,
-                   bool y_by_pair, const int32_t* perm) {
+                   const float* route_w, const TilePlan& tp, cudaStream_t st, void* const* ret_ptrs,
+                   const uint32_t* ret_slot, bool y_by_pair, const int32_t* perm) {
   Workspace& w = L->ws;
   if (!w.xq4) return fail(MXMOE_ERR_INVALID_ARG, "FP4 decode buffers were not reserved");
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
-  const int PT = kF4PairTile;
+  const int PT = tp.pair_tile;
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   const float bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
   CUDA_TRY(launch_quantize_f4_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, w.xq4,
@@ -485,7 +490,7 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
   p.bias_mult = 1.0f;
   p.act_f32 = w.act4_f32;
   int grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
-  CUDA_TRY(tc_gemm_launch(true, L->tmap_w1_f4, w.tmap_x4, p, grid, st));
+  CUDA_TRY(tc_gemm_launch(true, L->tmap_w1_f4, w.tmap_x4[tp.tw], p, grid, st));
   // the f32 activation rows of the routed pairs -> four-term E2M1 operand of W2
   CUDA_TRY(launch_quantize_f4_pairs(w.act4_f32, MXMOE_F32, static_cast<int>(P), static_cast<int>(L->fp), 1, nullptr, 1,
                                     w.inv_p, w.aq4, static_cast<int>(L->kp2 / 2), w.asf4, static_cast<int>(kc2), PT,
@@ -509,7 +514,7 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
   p.y_by_pair = y_by_pair ? 1 : 0;
   w.pair_dtype = MXMOE_BF16;
   grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
-  CUDA_TRY(tc_gemm_launch(true, L->tmap_w2_f4, w.tmap_act4, p, grid, st));
+  CUDA_TRY(tc_gemm_launch(true, L->tmap_w2_f4, w.tmap_act4[tp.tw], p, grid, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
   return MXMOE_OK;
 }
@@ -550,7 +555,8 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
     return MXMOE_OK;
   }
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
-  if (tp.fp4) return run_experts_f4(L, x, x_dtype, n_tok, k, rscale, route_w, st, ret_ptrs, ret_slot, y_by_pair, perm);
+  if (tp.fp4)
+    return run_experts_f4(L, x, x_dtype, n_tok, k, rscale, route_w, tp, st, ret_ptrs, ret_slot, y_by_pair, perm);
   if (!input_quantized)
     CUDA_TRY(launch_quantize_pairs(x, x_dtype, n_tok, L->d, k, L->gamma, L->gamma_is_one ? 1 : 0, w.inv_p, x_terms,
                                    w.xq, static_cast<uint64_t>(w.rows) * L->kp1, L->kp1, w.xsf,
@@ -894,7 +900,7 @@ static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, voi
   CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
                          w.logits, w.topk_idx, w.topk_w, w.rscale, st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
-  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, tp.fp4 ? kF4PairTile : kRowBlock, tp.pair_tile,
+  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, tp.fp4 ? tp.pair_tile : kRowBlock, tp.pair_tile,
                           w.offsets, w.perm_c,
                           w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));

@@ -347,8 +347,11 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 128);
       for (int kt = 0; kt < p.k_tiles; ++kt) {
         // the scale-factor warp waits for the stage's TMA data, copies the
-        // scales into TMEM and commits sf_full: data and scales are then ready
-        if (!mbar_wait(&sf_full[stage], phase, err, kDevTimeoutFull)) {
+        // scales into TMEM and commits sf_full: data and scales are then ready.
+        // FP4 tiles copy their scales from this thread instead (below): a copy
+        // issued by another thread queues behind this thread's MMAs, and
+        // waiting for its commit would drain the tensor pipe every stage.
+        if (!mbar_wait(kF4 ? &full_bar[stage] : &sf_full[stage], phase, err, kDevTimeoutFull)) {
           ok = false;
           break;
         }
@@ -363,6 +366,21 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
           // A = stacked activation terms, B = weights; scale columns: weights
           // col0 + 8 * chunk (+4 for rows 128..255), activation col0 + 16 + 4 * chunk
           const int nk = kt == p.k_tiles - 1 ? p.last_mmas : 4;
+          {
+            // scale atoms of the stage's one or two 128-K chunks -> TMEM; the
+            // tcgen05 ops of one thread run in issue order, so the MMAs below
+            // read them, and a later stage's copies into these columns wait
+            // for these MMAs
+            const uint32_t sf_addr = smem_u32(sb + plan.a_bytes + plan.b_bytes);
+            const int nch = min(2, p.k_chunks - 2 * kt);
+            for (int c = 0; c < nch; ++c) {
+              for (int ra = 0; ra < 2; ++ra)
+                tc_cp_32x128b_warpx4(tmem_base + col0 + c * 8 + ra * 4,
+                                     make_smem_desc(sf_addr + c * kWSfPairBytes + ra * kSfAtomBytes, 0, 128, 0));
+              tc_cp_32x128b_warpx4(tmem_base + col0 + 16 + c * 4,
+                                   make_smem_desc(sf_addr + 2 * kWSfPairBytes + c * kSfAtomBytes, 0, 128, 0));
+            }
+          }
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
             if (kk < nk) {
@@ -405,7 +423,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     // Drain: every MMA issued by this thread has finished before TMEM is freed.
     tc_commit(drain_bar);
     mbar_wait(drain_bar, 0, nullptr, kDevTimeoutDrain);
-  } else if (warp == sf_warp(kTok) && lane == 0) {
+  } else if (!kF4 && warp == sf_warp(kTok) && lane == 0) {
     // ------------------------------------------------------------ scale factors -> TMEM
     int stage = 0;
     uint32_t phase = 0;
@@ -421,25 +439,14 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
         uint8_t* sb = smem + stage * plan.stage_bytes;
         const uint32_t sf_addr = smem_u32(sb + plan.a_terms * plan.a_bytes + plan.b_terms * plan.b_bytes);
         const uint32_t col0 = kSfTmemBase + stage * 32;
-        if constexpr (kF4) {
-          const int nch = min(2, p.k_chunks - 2 * kt);
-          for (int c = 0; c < nch; ++c) {
-            for (int ra = 0; ra < 2; ++ra)
-              tc_cp_32x128b_warpx4(tmem_base + col0 + c * 8 + ra * 4,
-                                   make_smem_desc(sf_addr + c * kWSfPairBytes + ra * kSfAtomBytes, 0, 128, 0));
-            tc_cp_32x128b_warpx4(tmem_base + col0 + 16 + c * 4,
-                                 make_smem_desc(sf_addr + 2 * kWSfPairBytes + c * kSfAtomBytes, 0, 128, 0));
-          }
-        } else {
-          // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
-          // activation term q at col0 + 8 + 8q (4 per 128 rows).
-          for (int a = 0; a < natoms_w; ++a)
-            tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
-          for (int term = 0; term < mma_terms; ++term)
-            for (int a = 0; a < natoms_x; ++a)
-              tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
-                                   make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
-        }
+        // TMEM scale columns of this stage: weights at col0 (4 per 128 rows),
+        // activation term q at col0 + 8 + 8q (4 per 128 rows).
+        for (int a = 0; a < natoms_w; ++a)
+          tc_cp_32x128b_warpx4(tmem_base + col0 + a * 4, make_smem_desc(sf_addr + kSfAtomBytes * a, 0, 128, 0));
+        for (int term = 0; term < mma_terms; ++term)
+          for (int a = 0; a < natoms_x; ++a)
+            tc_cp_32x128b_warpx4(tmem_base + col0 + 8 + term * 8 + a * 4,
+                                 make_smem_desc(sf_addr + kSfAtomBytes * (natoms_w + term * natoms_x + a), 0, 128, 0));
         tc_commit(&sf_full[stage]);
         if (++stage == S) {
           stage = 0;

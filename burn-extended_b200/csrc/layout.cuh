@@ -92,7 +92,8 @@ __host__ __device__ inline uint32_t stacked_code_row(uint32_t pos, uint32_t term
 // every 32-lane TMEM sub-partition carries 8 pairs with their four terms in
 // lanes L, L + 8, L + 16, L + 24.
 constexpr int kF4Terms = 4;
-constexpr int kF4PairTile = 32;
+constexpr int kF4PairTile = 32;       // widest FP4 tile (4 x 32 = 128 operand rows)
+constexpr int kF4PairTileSmall = 16;  // 64 operand rows: half the activation bytes per stage
 __host__ __device__ inline uint32_t stacked4_operand_row(uint32_t j, uint32_t term) {
   return (j / 8u) * 32u + 8u * term + j % 8u;
 }

@@ -217,7 +217,8 @@ def test_decode_config_against_oracle(torch, simt):
 
 @pytest.mark.parametrize("fp4", [True, False])
 @pytest.mark.parametrize("shape", [
-    (2880, 2880, 32, 4, 64, True, False),    # decode config: 8 pairs per expert
+    (2880, 2880, 32, 4, 64, True, False),    # decode config: 8 pairs per expert (16-pair tiles)
+    (2880, 2880, 32, 4, 96, True, False),    # 12 per expert: 16-pair tiles, some experts need two
     (2880, 2880, 32, 4, 190, True, False),   # 23.75 pairs per expert: the last FP4 plan
     (512, 384, 4, 2, 40, False, True),       # f32 input, non-unit RmsNorm gain, 20 pairs per expert
     (1024, 320, 8, 4, 48, True, True),       # K not a multiple of 256 (last stage partial)
