@@ -249,6 +249,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     const uint32_t x_tx = PT * kTileK;                      // E4M3 bytes per term
     const int nsf_x = (kTok && p.stacked) ? 1 : terms * natoms_x;  // activation scale atoms per stage
     const uint32_t tx = w_tx + terms * x_tx + kSfAtomBytes * (natoms_w + nsf_x);
+    const uint64_t w_policy = kF4 ? l2_evict_first_policy() : 0;
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       int e, wt, pt;
@@ -274,11 +275,13 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
           const uint64_t tile = static_cast<uint64_t>(row0 / PT);
           mbar_arrive_expect_tx(&full_bar[stage], plan.a_bytes + plan.b_bytes +
                                                       static_cast<uint32_t>(nch) * (kWSfPairBytes + kSfAtomBytes));
-          tma_load_3d(w_s, &tmap_w, &full_bar[stage], kt * 128, wt * 256, e);
+          // weights and their scales are read once per step: evict them first
+          tma_load_3d_hint(w_s, &tmap_w, &full_bar[stage], kt * 128, wt * 256, e, w_policy);
           tma_load_3d(x_s, &tmap_x, &full_bar[stage], kt * 128, static_cast<int>(tile) * kF4Terms * PT, 0);
-          bulk_load(sf,
-                    p.a_sf + ((static_cast<uint64_t>(e) * p.w_row_pairs + wt) * p.k_chunks + 2 * kt) * kWSfPairBytes,
-                    static_cast<uint32_t>(nch) * kWSfPairBytes, &full_bar[stage]);
+          bulk_load_hint(sf,
+                         p.a_sf + ((static_cast<uint64_t>(e) * p.w_row_pairs + wt) * p.k_chunks + 2 * kt) *
+                                      kWSfPairBytes,
+                         static_cast<uint32_t>(nch) * kWSfPairBytes, &full_bar[stage], w_policy);
           bulk_load(sf + 2 * kWSfPairBytes, p.b_sf + (tile * p.k_chunks + 2 * kt) * kSfAtomBytes,
                     static_cast<uint32_t>(nch) * kSfAtomBytes, &full_bar[stage]);
           issued[stage] = true;

@@ -388,6 +388,90 @@ __global__ void __launch_bounds__(kRouterThreads)
   }
 }
 
+// Small batches (decode): RmsNorm, gate logits and top-k + softmax of one
+// token per block in one launch (E <= 32, one packed gate group).  Every
+// warp computes 1/rms with the lane chain c = lane, lane + 32, ... and a
+// butterfly, as rms_kernel does; the block then writes the normalized token,
+// (x * 1/rms) * gamma, to shared memory in the packed gate's order, and warp
+// w accumulates experts 4w .. 4w + 3: per 128-column chunk one float4 of the
+// token and one of each expert's packed row hold a lane's four chain values
+// in increasing column order.  The fused multiply-adds therefore run in the
+// order of router_logits_kernel and the logits are bit-identical to it; the
+// gate comes straight from L2 with a whole chunk row per warp load.
+constexpr int kRouterSmallMaxN = 512;
+constexpr int kRouterSmallMaxD = 8192;
+template <typename XT>
+__global__ void __launch_bounds__(256)
+    router_small_kernel(const XT* __restrict__ x, int n, int d, int E, int k, const float* __restrict__ gamma,
+                        const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
+                        float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                        float* __restrict__ rscale) {
+  extern __shared__ __align__(16) float xn_s[];  // [nch][128] normalized token, packed order
+  __shared__ float lg_s[32];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x;
+  const int C = kRouterChunk;
+  const int nch = (d + C - 1) / C;
+  const XT* xr = x + static_cast<uint64_t>(t) * d;
+  float ss = 0.0f;
+#pragma unroll 8
+  for (int c = lane; c < d; c += 32) {
+    const float f = load_f32(xr, c);
+    ss = __fmaf_rn(f, f, ss);
+  }
+  ss = warp_sum_butterfly(ss);
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
+  for (int i = threadIdx.x; i < nch * C; i += blockDim.x) {
+    const int ch = i / C, cc = i % C, l = cc % 32, j = cc / 32;
+    const int c = ch * C + cc;
+    xn_s[ch * C + l * 4 + j] = c < d ? __fmul_rn(__fmul_rn(load_f32(xr, c), r), __ldg(gamma + c)) : 0.0f;
+  }
+  __syncthreads();
+  const int e0 = warp * 4;
+  if (e0 < E) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+    const int full = d / C;  // chunks with all 128 columns
+#pragma unroll 4
+    for (int ch = 0; ch < full; ++ch) {
+      const float4 xv = *reinterpret_cast<const float4*>(xn_s + ch * C + lane * 4);
+      const float* wrow = gate_packed + (static_cast<uint64_t>(ch) * kRouterGroup + e0) * C + lane * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + e * C));
+        acc[e] = __fmaf_rn(xv.x, wv.x, acc[e]);
+        acc[e] = __fmaf_rn(xv.y, wv.y, acc[e]);
+        acc[e] = __fmaf_rn(xv.z, wv.z, acc[e]);
+        acc[e] = __fmaf_rn(xv.w, wv.w, acc[e]);
+      }
+    }
+    if (full < nch) {
+      // ragged last chunk: only the lane's columns below d join its chain
+      const float* wrow = gate_packed + (static_cast<uint64_t>(full) * kRouterGroup + e0) * C + lane * 4;
+      for (int j = 0; j < 4; ++j) {
+        if (full * C + lane + 32 * j >= d) break;
+        const float xv = xn_s[full * C + lane * 4 + j];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[e] = __fmaf_rn(xv, __ldg(wrow + e * C + j), acc[e]);
+      }
+    }
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float sum = warp_sum_butterfly(acc[e]);
+      if (lane == 0 && e0 + e < E) {
+        const float l = __fadd_rn(sum, __ldg(gate_b + e0 + e));
+        logits_out[static_cast<uint64_t>(t) * E + e0 + e] = l;
+        lg_s[e0 + e] = l;
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 0) {
+    if (lane == 0) rscale[t] = r;
+    const float v[1] = {lane < E ? lg_s[lane] : 0.0f};
+    warp_topk_softmax<1>(v, E, k, lane, topk_idx + static_cast<uint64_t>(t) * k, topk_w + static_cast<uint64_t>(t) * k);
+  }
+}
+
 // ------------------------------------------------------------------ permute
 // Canonical permutation (replaces src/moe/mod.rs:279-288): pairs p = t*k+s are
 // stably sorted by expert id.  One block of 1024 threads; warp w owns a
@@ -765,33 +849,21 @@ __global__ void __launch_bounds__(256)
         for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
         amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
         const int s = e4m3_block_exp(amax);
-        const bool fast = (s > -126) && (s < 127);
-        const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
-        const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
+        // a finite block has s <= 120; s = -127 (amax below 2^-118) is written as zero codes
+        const bool live = s > -127;
+        const float inv = live ? __int_as_float((127 - s) << 23) : 0.0f;
+        const float back = live ? __int_as_float((127 + s) << 23) : 0.0f;
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
           uint32_t word = 0;
 #pragma unroll
           for (int hp = 0; hp < 2; ++hp) {
             const int i = w * 4 + hp * 2;
-            float a, bb;
-            if (fast) {
-              a = v[i] * inv;
-              bb = v[i + 1] * inv;
-            } else {
-              a = ldexpf(v[i], -s);
-              bb = ldexpf(v[i + 1], -s);
-            }
-            const uint32_t c = cvt_e4m3x2(a, bb);
+            const uint32_t c = cvt_e4m3x2(v[i] * inv, v[i + 1] * inv);
             float da, db;
             dec_e4m3x2(c, da, db);
-            if (fast) {
-              v[i] = fmaf(-da, back, v[i]);
-              v[i + 1] = fmaf(-db, back, v[i + 1]);
-            } else {
-              v[i] = v[i] - ldexpf(da, s);
-              v[i + 1] = v[i + 1] - ldexpf(db, s);
-            }
+            v[i] = fmaf(-da, back, v[i]);
+            v[i + 1] = fmaf(-db, back, v[i + 1]);
             word |= c << (16 * hp);
           }
           words[q][w] = word;
@@ -985,26 +1057,49 @@ __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const vo
       int tmp = ex[b]; ex[b] = ex[b - 1]; ex[b - 1] = tmp;
       tmp = ord[b]; ord[b] = ord[b - 1]; ord[b - 1] = tmp;
     }
-  for (int c = 4 * threadIdx.x; c < d; c += 4 * blockDim.x) {
-    const uint64_t xi = static_cast<uint64_t>(t) * d + c;
-    float4 v;
-    if (k == 0) {
-      v = load4(x, x_dtype, xi);
-    } else {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int s = 0; s < k; ++s) {
-        const float4 q = load4(y_pair, pair_dtype, static_cast<uint64_t>(ord[s]) * d + c);
-        acc.x = __fadd_rn(acc.x, q.x); acc.y = __fadd_rn(acc.y, q.y);
-        acc.z = __fadd_rn(acc.z, q.z); acc.w = __fadd_rn(acc.w, q.w);
-      }
-      if (residual) {
-        const float4 xv = load4(x, x_dtype, xi);
-        acc.x = __fadd_rn(xv.x, acc.x); acc.y = __fadd_rn(xv.y, acc.y);
-        acc.z = __fadd_rn(xv.z, acc.z); acc.w = __fadd_rn(xv.w, acc.w);
-      }
-      v = acc;
+  // kCombineVec column groups per thread per round, all their loads in
+  // flight together; the sums keep the order of the expert ids, then x
+  constexpr int kCombineVec = 4;
+  const int stride = 4 * blockDim.x;
+  for (int c0 = 4 * threadIdx.x; c0 < d; c0 += stride * kCombineVec) {
+    float4 acc[kCombineVec];
+    float4 xv[kCombineVec];
+#pragma unroll
+    for (int v = 0; v < kCombineVec; ++v) {
+      const int c = c0 + v * stride;
+      acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+      xv[v] = (c < d && (residual || k == 0)) ? load4(x, x_dtype, static_cast<uint64_t>(t) * d + c)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
     }
-    store4(y, y_dtype, xi, v);
+#pragma unroll
+    for (int s = 0; s < kMaxTopK; ++s) {
+      if (s < k) {
+#pragma unroll
+        for (int v = 0; v < kCombineVec; ++v) {
+          const int c = c0 + v * stride;
+          if (c < d) {
+            const float4 q = load4(y_pair, pair_dtype, static_cast<uint64_t>(ord[s]) * d + c);
+            acc[v].x = __fadd_rn(acc[v].x, q.x); acc[v].y = __fadd_rn(acc[v].y, q.y);
+            acc[v].z = __fadd_rn(acc[v].z, q.z); acc[v].w = __fadd_rn(acc[v].w, q.w);
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < kCombineVec; ++v) {
+      const int c = c0 + v * stride;
+      if (c >= d) continue;
+      float4 o;
+      if (k == 0) {
+        o = xv[v];
+      } else if (residual) {
+        o.x = __fadd_rn(xv[v].x, acc[v].x); o.y = __fadd_rn(xv[v].y, acc[v].y);
+        o.z = __fadd_rn(xv[v].z, acc[v].z); o.w = __fadd_rn(xv[v].w, acc[v].w);
+      } else {
+        o = acc[v];
+      }
+      store4(y, y_dtype, static_cast<uint64_t>(t) * d + c, o);
+    }
   }
 }
 
@@ -1672,6 +1767,12 @@ template <typename XT>
 static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, const float* gamma,
                                    const float* gate_packed, const float* gate_b, float eps, float* logits,
                                    int32_t* topk_idx, float* topk_w, float* rscale, cudaStream_t st) {
+  if (n <= kRouterSmallMaxN && E <= kRouterGroup && d <= kRouterSmallMaxD) {
+    const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float);
+    router_small_kernel<XT><<<n, 256, smem, st>>>(x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx,
+                                                  topk_w, rscale);
+    return cudaGetLastError();
+  }
   const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
   rms_kernel<XT><<<(n + 7) / 8, 256, 0, st>>>(x, n, d, eps, rscale, aligned);
   const bool fuse = E <= kRouterGroup;

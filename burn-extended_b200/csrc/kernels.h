@@ -34,7 +34,8 @@ inline void pack_router_gate(const float* w, int E, int d, float* out) {
     }
 }
 
-// gate_packed: pack_router_gate layout.
+// gate_packed: pack_router_gate layout.  Small batches (n <= 512, E <= 32)
+// run as one launch (RmsNorm + logits + top-k), larger ones as two or three.
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st);

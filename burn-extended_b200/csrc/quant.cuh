@@ -84,35 +84,22 @@ __device__ __forceinline__ void quantize_block32(float (&v)[32], int terms, uint
 #pragma unroll
       for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
       const int s = e4m3_block_exp(amax);
-      // 2^-s and 2^s as normal floats when both exist; the extreme exponents
-      // take the exact ldexpf path.
-      const bool fast = (s > -126) && (s < 127);
-      const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
-      const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
+      // 2^-s and 2^s as normal floats: a finite block has s <= 120, and a
+      // block with s = -127 (amax below 2^-118) is written as zero codes
+      const bool live = s > -127;
+      const float inv = live ? __int_as_float((127 - s) << 23) : 0.0f;
+      const float back = live ? __int_as_float((127 + s) << 23) : 0.0f;
 #pragma unroll
       for (int w = 0; w < 8; ++w) {
         uint32_t word = 0;
 #pragma unroll
         for (int hp = 0; hp < 2; ++hp) {
           const int i = w * 4 + hp * 2;
-          float a, b;
-          if (fast) {
-            a = v[i] * inv;
-            b = v[i + 1] * inv;
-          } else {
-            a = ldexpf(v[i], -s);
-            b = ldexpf(v[i + 1], -s);
-          }
-          const uint32_t c = cvt_e4m3x2(a, b);
+          const uint32_t c = cvt_e4m3x2(v[i] * inv, v[i + 1] * inv);
           float da, db;
           dec_e4m3x2(c, da, db);
-          if (fast) {
-            v[i] = fmaf(-da, back, v[i]);
-            v[i + 1] = fmaf(-db, back, v[i + 1]);
-          } else {
-            v[i] = v[i] - ldexpf(da, s);
-            v[i + 1] = v[i + 1] - ldexpf(db, s);
-          }
+          v[i] = fmaf(-da, back, v[i]);
+          v[i + 1] = fmaf(-db, back, v[i + 1]);
           word |= c << (16 * hp);
         }
         words[t][w] = word;
@@ -181,21 +168,20 @@ __device__ __forceinline__ void quantize16_e2m1_terms(float (&v)[16], int xor_ma
 #pragma unroll
     for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
     amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, xor_mask));
+    // A finite block never needs s > 126; s = -127 (amax below 2^-125) is
+    // written as zero codes with the smallest scale, leaving the residual as is.
     const int s = e2m1_block_exp(amax);
-    const bool fast = (s > -127) && (s < 127);
-    const float inv = fast ? __int_as_float((127 - s) << 23) : 0.0f;
-    const float back = fast ? __int_as_float((127 + s) << 23) : 0.0f;
+    const bool live = s > -127;
+    const float inv = live ? __int_as_float((127 - s) << 23) : 0.0f;
+    const float back = live ? __int_as_float((127 + s) << 23) : 0.0f;
 #pragma unroll
     for (int w = 0; w < 2; ++w) {
       float sc[8];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) sc[i] = fast ? v[8 * w + i] * inv : ldexpf(v[8 * w + i], -s);
+      for (int i = 0; i < 8; ++i) sc[i] = v[8 * w + i] * inv;
       const uint32_t c = cvt_e2m1x8(sc);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const float dq = e2m1_value(c >> (4 * i));
-        v[8 * w + i] = fast ? fmaf(-dq, back, v[8 * w + i]) : v[8 * w + i] - ldexpf(dq, s);
-      }
+      for (int i = 0; i < 8; ++i) v[8 * w + i] = fmaf(-e2m1_value(c >> (4 * i)), back, v[8 * w + i]);
       words[t][w] = c;
     }
     sbyte[t] = static_cast<uint8_t>(s + 127);

@@ -123,7 +123,9 @@ def _check_routing(layer, inp, x, n):
 # expert count off the 32-expert groups, E = 1, f32 and bf16 activations, and
 # both router tilings (n >= 2048 and below)
 @pytest.mark.parametrize("d,E,k,n,bf16", [(2880, 32, 4, 2500, True), (96, 40, 2, 2100, False),
-                                          (96, 1, 1, 37, True), (352, 72, 8, 300, False)])
+                                          (96, 1, 1, 37, True), (352, 72, 8, 300, False),
+                                          (2880, 32, 4, 512, True), (2880, 20, 3, 300, False),
+                                          (160, 7, 2, 5, False)])
 def test_router_bit_exact_shapes(torch, d, E, k, n, bf16):
     inp = synth.make_inputs(d, 128, E, k, n, bf16, seed=d + E + n, zipf_router_bias=0.5)
     layer = make_layer(inp)
