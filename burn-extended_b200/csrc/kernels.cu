@@ -389,34 +389,46 @@ __global__ void __launch_bounds__(kRouterThreads)
 }
 
 // Small batches (decode): RmsNorm, gate logits and top-k + softmax of one
-// token per block in one launch (E <= 32, one packed gate group).  Every
-// warp computes 1/rms with the lane chain c = lane, lane + 32, ... and a
-// butterfly, as rms_kernel does; the block then writes the normalized token,
-// (x * 1/rms) * gamma, to shared memory in the packed gate's order, and warp
-// w accumulates experts 4w .. 4w + 3: per 128-column chunk one float4 of the
-// token and one of each expert's packed row hold a lane's four chain values
-// in increasing column order.  The fused multiply-adds therefore run in the
-// order of router_logits_kernel and the logits are bit-identical to it; the
-// gate comes straight from L2 with a whole chunk row per warp load.
+// token per block in one launch (E <= 32, one packed gate group, one warp
+// per expert).  The block stages the token row in shared memory with
+// 16-byte loads; every warp computes 1/rms from it with the lane chain c =
+// lane, lane + 32, ... and a butterfly, as rms_kernel does; the block writes
+// the normalized token, (x * 1/rms) * gamma, in the packed gate's order, and
+// warp e accumulates expert e: per 128-column chunk one float4 of the token
+// and one of the expert's packed row hold a lane's four chain values in
+// increasing column order.  The fused multiply-adds therefore run in the
+// order of router_logits_kernel and the logits are bit-identical to it.
+// Everything a warp reads from global memory is issued in a few rounds of
+// independent loads: the step is latency-bound at these sizes.
 constexpr int kRouterSmallMaxN = 512;
 constexpr int kRouterSmallMaxD = 8192;
 template <typename XT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(1024)
     router_small_kernel(const XT* __restrict__ x, int n, int d, int E, int k, const float* __restrict__ gamma,
                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
                         float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
-                        float* __restrict__ rscale) {
-  extern __shared__ __align__(16) float xn_s[];  // [nch][128] normalized token, packed order
+                        float* __restrict__ rscale, int x_aligned) {
+  extern __shared__ __align__(16) float router_small_smem[];
+  const int C = kRouterChunk;
+  const int nch = (d + C - 1) / C;
+  float* xn_s = router_small_smem;                                           // [nch][128] packed order
+  XT* xr_s = reinterpret_cast<XT*>(router_small_smem + nch * C);             // [d] raw row
   __shared__ float lg_s[32];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x;
-  const int C = kRouterChunk;
-  const int nch = (d + C - 1) / C;
   const XT* xr = x + static_cast<uint64_t>(t) * d;
+  constexpr int kEpv = 16 / static_cast<int>(sizeof(XT));
+  if (x_aligned) {
+    for (int i = threadIdx.x; i < d / kEpv; i += blockDim.x)
+      reinterpret_cast<uint4*>(xr_s)[i] = __ldg(reinterpret_cast<const uint4*>(xr) + i);
+  } else {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) xr_s[i] = xr[i];
+  }
+  __syncthreads();
   float ss = 0.0f;
 #pragma unroll 8
   for (int c = lane; c < d; c += 32) {
-    const float f = load_f32(xr, c);
+    const float f = load_f32(xr_s, c);
     ss = __fmaf_rn(f, f, ss);
   }
   ss = warp_sum_butterfly(ss);
@@ -424,44 +436,36 @@ __global__ void __launch_bounds__(256)
   for (int i = threadIdx.x; i < nch * C; i += blockDim.x) {
     const int ch = i / C, cc = i % C, l = cc % 32, j = cc / 32;
     const int c = ch * C + cc;
-    xn_s[ch * C + l * 4 + j] = c < d ? __fmul_rn(__fmul_rn(load_f32(xr, c), r), __ldg(gamma + c)) : 0.0f;
+    xn_s[ch * C + l * 4 + j] = c < d ? __fmul_rn(__fmul_rn(load_f32(xr_s, c), r), __ldg(gamma + c)) : 0.0f;
   }
   __syncthreads();
-  const int e0 = warp * 4;
-  if (e0 < E) {
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  const int e = warp;
+  if (e < E) {
+    float acc = 0.0f;
     const int full = d / C;  // chunks with all 128 columns
-#pragma unroll 4
+    const float* wrow = gate_packed + static_cast<uint64_t>(e) * C + lane * 4;
+#pragma unroll 8
     for (int ch = 0; ch < full; ++ch) {
       const float4 xv = *reinterpret_cast<const float4*>(xn_s + ch * C + lane * 4);
-      const float* wrow = gate_packed + (static_cast<uint64_t>(ch) * kRouterGroup + e0) * C + lane * 4;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + e * C));
-        acc[e] = __fmaf_rn(xv.x, wv.x, acc[e]);
-        acc[e] = __fmaf_rn(xv.y, wv.y, acc[e]);
-        acc[e] = __fmaf_rn(xv.z, wv.z, acc[e]);
-        acc[e] = __fmaf_rn(xv.w, wv.w, acc[e]);
-      }
+      const float4 wv = __ldg(reinterpret_cast<const float4*>(wrow + static_cast<uint64_t>(ch) * kRouterGroup * C));
+      acc = __fmaf_rn(xv.x, wv.x, acc);
+      acc = __fmaf_rn(xv.y, wv.y, acc);
+      acc = __fmaf_rn(xv.z, wv.z, acc);
+      acc = __fmaf_rn(xv.w, wv.w, acc);
     }
     if (full < nch) {
       // ragged last chunk: only the lane's columns below d join its chain
-      const float* wrow = gate_packed + (static_cast<uint64_t>(full) * kRouterGroup + e0) * C + lane * 4;
+      const float* wl = wrow + static_cast<uint64_t>(full) * kRouterGroup * C;
       for (int j = 0; j < 4; ++j) {
         if (full * C + lane + 32 * j >= d) break;
-        const float xv = xn_s[full * C + lane * 4 + j];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[e] = __fmaf_rn(xv, __ldg(wrow + e * C + j), acc[e]);
+        acc = __fmaf_rn(xn_s[full * C + lane * 4 + j], __ldg(wl + j), acc);
       }
     }
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float sum = warp_sum_butterfly(acc[e]);
-      if (lane == 0 && e0 + e < E) {
-        const float l = __fadd_rn(sum, __ldg(gate_b + e0 + e));
-        logits_out[static_cast<uint64_t>(t) * E + e0 + e] = l;
-        lg_s[e0 + e] = l;
-      }
+    const float sum = warp_sum_butterfly(acc);
+    if (lane == 0) {
+      const float l = __fadd_rn(sum, __ldg(gate_b + e));
+      logits_out[static_cast<uint64_t>(t) * E + e] = l;
+      lg_s[e] = l;
     }
   }
   __syncthreads();
@@ -989,6 +993,12 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
       for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
     }
+    // the pair positions are loaded before the arithmetic so that their
+    // latency overlaps it
+    uint32_t pos_k[kMaxTopK];
+#pragma unroll
+    for (int q = 0; q < kMaxTopK; ++q)
+      pos_k[q] = q < k ? static_cast<uint32_t>(__ldg(inv_p + static_cast<uint64_t>(t) * k + q)) : 0u;
     uint32_t words[kF4Terms][2];
     uint8_t sbyte[kF4Terms];
     quantize16_e2m1_terms(v, 1, words, sbyte);
@@ -1004,7 +1014,7 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int s = 0; s < kMaxTopK; ++s) {
       if (s >= k) break;
-      const uint32_t pos = static_cast<uint32_t>(__ldg(inv_p + static_cast<uint64_t>(t) * k + s));
+      const uint32_t pos = pos_k[s];
 #pragma unroll
       for (int q = 0; q < kF4Terms; ++q) {
         if (active) {
@@ -1767,13 +1777,15 @@ template <typename XT>
 static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, const float* gamma,
                                    const float* gate_packed, const float* gate_b, float eps, float* logits,
                                    int32_t* topk_idx, float* topk_w, float* rscale, cudaStream_t st) {
+  const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
   if (n <= kRouterSmallMaxN && E <= kRouterGroup && d <= kRouterSmallMaxD) {
-    const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float);
-    router_small_kernel<XT><<<n, 256, smem, st>>>(x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx,
-                                                  topk_w, rscale);
+    const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float) +
+                        (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16;
+    ensure_dynamic_smem(reinterpret_cast<const void*>(router_small_kernel<XT>), smem);
+    router_small_kernel<XT><<<n, 32 * E, smem, st>>>(  // one warp per expert
+        x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx, topk_w, rscale, aligned);
     return cudaGetLastError();
   }
-  const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
   rms_kernel<XT><<<(n + 7) / 8, 256, 0, st>>>(x, n, d, eps, rscale, aligned);
   const bool fuse = E <= kRouterGroup;
   int32_t* fi = fuse ? topk_idx : nullptr;
