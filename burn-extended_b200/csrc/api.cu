@@ -19,6 +19,7 @@
 #include "kernels.h"
 #include "layout.cuh"
 #include "tc_gemm.h"
+#include "launch_util.h"
 
 using namespace mxmoe;
 
@@ -416,9 +417,11 @@ constexpr uint64_t kGemvMaxPairs = 64;
 TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_gemv = false, bool allow_fp4 = false) {
   if (allow_gemv && pairs <= kGemvMaxPairs) return {true, 8, 0, false, true};  // callers check kGemvMaxK
   const double avg = experts ? static_cast<double>(pairs) / experts : 0.0;
-  // FP4: 16-pair tiles (8 KB of activation per stage, so five stages fit)
-  // while few experts overflow them, else 32-pair tiles
-  if (allow_fp4 && avg <= kF4MaxAvgPairs / 2) return {true, kF4PairTileSmall, 0, true, false, true};
+  // FP4: 32-pair tiles.  16-pair tiles (half the activation bytes per
+  // stage, five stages instead of four) measured no faster, and their extra
+  // tiles for experts past 16 pairs break the even waves of 148 CTAs (GPT-OSS
+  // decode: 23 x 32 = 736 W1 tiles, 5 per CTA, against 759).  They stay
+  // selectable through the tile table for experiments.
   if (allow_fp4 && avg <= kF4MaxAvgPairs) return {true, kF4PairTile, 1, true, false, true};
   // two-term activations: stacked tiles (tw indexes tmap_x_stk / tmap_act_stk)
   if (x_terms == 2 && avg <= 12) return {true, 16, 0, true};
@@ -890,6 +893,9 @@ static TilePlan forward_plan(const mxmoe_layer* L, uint64_t P, int x_terms) {
 // on stream st; everything that can allocate or resize ran before.
 static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, mxmoe_dtype y_dtype,
                          uint32_t n_tokens, cudaStream_t st) {
+  // kernels of the chain start while their predecessor finishes (the event
+  // records of profiling mode break that overlap, so it stays off there)
+  PdlScope pdl(!L->profiling);
   Workspace& w = L->ws;
   const uint32_t k = L->k, E = L->e_count;
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;

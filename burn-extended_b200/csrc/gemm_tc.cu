@@ -232,6 +232,18 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int total_tiles = p.m_tiles * __ldg(p.ntile_prefix + p.E);
+  // With a programmatic launch the setup above overlapped the previous
+  // kernel.  So can the first weight boxes: the tile list comes from the
+  // permutation, which completed before the previous kernel started its
+  // work, and the weights never change -- prefetch them into L2, then wait
+  // for the previous kernel's output (the activation operand).
+  if (kTok && warp == 0 && lane == 0 && static_cast<int>(blockIdx.x) < total_tiles) {
+    int e, wt, pt;
+    decode_tile(p, blockIdx.x, e, wt, pt);
+    const int nk = min(p.stages, p.k_tiles);
+    for (int kt = 0; kt < nk; ++kt) tma_prefetch_3d(&tmap_w, kt * (kF4 ? 128 : kTileK), wt * 256, e);
+  }
+  griddep_wait();
   const int natoms_x = kTok ? 1 : (N + p.sf_rows - 1) / p.sf_rows;  // activation atoms per term
   const int natoms_w = kTok ? 2 : 1;                                 // weight atoms
 
@@ -778,20 +790,10 @@ cudaError_t tc_gemm_launch(bool tokens_as_a, const CUtensorMap& tmap_w, const CU
                            const TcParams& p, int grid, cudaStream_t stream) {
   const size_t smem =
       tc_gemm_smem_bytes(tokens_as_a, p.N, p.b_terms, p.stages, p.sf_rows, p.stacked != 0, p.fp4 != 0);
-  if (tokens_as_a && p.fp4) {
-    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<2>), smem);
-    if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<2><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
-  } else if (tokens_as_a) {
-    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<1>), smem);
-    if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<1><<<grid, num_threads(true), smem, stream>>>(tmap_w, tmap_x, p);
-  } else {
-    cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(tc_moe_gemm_kernel<0>), smem);
-    if (st != cudaSuccess) return st;
-    tc_moe_gemm_kernel<0><<<grid, num_threads(false), smem, stream>>>(tmap_w, tmap_x, p);
-  }
-  return cudaGetLastError();
+  const auto fn = tokens_as_a ? (p.fp4 ? tc_moe_gemm_kernel<2> : tc_moe_gemm_kernel<1>) : tc_moe_gemm_kernel<0>;
+  cudaError_t st = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+  if (st != cudaSuccess) return st;
+  return launch_kernel(fn, dim3(grid), dim3(num_threads(tokens_as_a)), smem, stream, tmap_w, tmap_x, p);
 }
 
 }  // namespace mxmoe

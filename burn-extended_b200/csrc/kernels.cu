@@ -125,6 +125,7 @@ __device__ __forceinline__ void warp_topk_softmax(const float (&v)[PL], int E, i
 template <int PL>
 __global__ void topk_softmax_kernel(const float* __restrict__ logits, int n, int E, int k, int32_t* topk_idx,
                                     float* topk_w) {
+  griddep_wait();
   const int t = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
@@ -160,6 +161,7 @@ constexpr int kRmsVec = 4;  // 16-byte vectors per lane per segment
 template <typename XT>
 __global__ void __launch_bounds__(256) rms_kernel(const XT* __restrict__ x, int n, int d, float eps,
                                                   float* __restrict__ rscale, int aligned) {
+  griddep_wait();
   constexpr int kEpv = 16 / static_cast<int>(sizeof(XT));  // elements per vector
   constexpr int kSeg = 32 * kRmsVec * kEpv;                  // elements per segment
   __shared__ __align__(16) XT buf[8][kSeg];
@@ -240,6 +242,7 @@ __global__ void __launch_bounds__(kRouterThreads)
                          const float* __restrict__ gate_packed, const float* __restrict__ gate_b,
                          const float* __restrict__ rscale, float* __restrict__ logits_out, int x_aligned,
                          int k, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w) {
+  griddep_wait();
   constexpr int WE = kRouterGroup / TE;       // warps along experts
   constexpr int WT = kRouterWarps / WE;       // warps along tokens
   constexpr int BT = WT * TT;                 // tokens per block
@@ -408,6 +411,7 @@ __global__ void __launch_bounds__(1024)
                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
                         float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
                         float* __restrict__ rscale, int x_aligned) {
+  griddep_wait();
   extern __shared__ __align__(16) float router_small_smem[];
   const int C = kRouterChunk;
   const int nch = (d + C - 1) / C;
@@ -519,6 +523,7 @@ __global__ void __launch_bounds__(kPermThreads)
     permute_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
                    int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
                    int32_t* perm_p, int32_t* inv_p) {
+  griddep_wait();
   extern __shared__ int32_t cnt[];  // [32 warps][E], canonical and padded starts [E] each, staging
   int32_t* cstart = cnt + 32 * E;
   int32_t* pstart = cstart + E;
@@ -652,6 +657,7 @@ __device__ int block_exclusive_scan(int* a, int len, int* warp_tot) {
 __global__ void __launch_bounds__(kPermChunkThreads)
     perm_hist_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* scratch,
                      int32_t* offsets, int32_t* poff, int32_t* counts, int32_t* ntile_prefix) {
+  griddep_wait();
   extern __shared__ int32_t sh[];  // [E] counts, then 3 x [E] scan arrays
   __shared__ int warp_tot[kPermChunkThreads / 32 + 1];
   __shared__ bool last;
@@ -710,6 +716,7 @@ __global__ void __launch_bounds__(kPermChunkThreads)
 __global__ void __launch_bounds__(kPermChunkThreads)
     perm_scatter_kernel(const int32_t* __restrict__ topk_idx, int P, int E, const int32_t* __restrict__ scratch,
                         int32_t* perm_c, int32_t* inv_c, int32_t* perm_p, int32_t* inv_p) {
+  griddep_wait();
   constexpr int kWarps = kPermChunkThreads / 32;
   constexpr int kRows = kPermChunk / kPermChunkThreads;
   extern __shared__ int32_t wcnt[];  // [kWarps][E]
@@ -802,6 +809,7 @@ __global__ void __launch_bounds__(256)
                           const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
                           int terms, uint8_t* codes, uint64_t term_stride, int kp, uint8_t* sf,
                           uint64_t sf_term_stride, int kchunks, int sf_rows, int stacked, const EpDispatch ep) {
+  griddep_wait();
   const int nb = d / 32;
   const int ngrp = (nb + kQBlocksPerWarp - 1) / kQBlocksPerWarp;
   const uint64_t items = static_cast<uint64_t>(n) * ngrp;
@@ -952,6 +960,7 @@ __global__ void __launch_bounds__(256)
     quantize_f4_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                              const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
                              uint8_t* codes, int row_bytes, uint8_t* sf, int kchunks, int pt, int src_by_pos) {
+  griddep_wait();
   const int nb = d / 32;
   const int ngrp = (nb + kQBlocksPerWarp - 1) / kQBlocksPerWarp;
   const uint64_t items = static_cast<uint64_t>(n) * ngrp;
@@ -1054,6 +1063,7 @@ __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const vo
                                int pair_dtype, const int32_t* __restrict__ topk_idx,
                                const int32_t* __restrict__ inv_p, int n, int d, int k, int residual, void* y,
                                int y_dtype) {
+  griddep_wait();
   const int t = blockIdx.x;
   if (t >= n) return;
   int ord[kMaxTopK];
@@ -1765,9 +1775,8 @@ static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, int k, c
                       2 * static_cast<size_t>(BT) * kRouterChunk * sizeof(float);
   const auto fn = router_logits_kernel<XT, TT, TE>;
   ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
-  fn<<<grid, kRouterThreads, smem, st>>>(x, n, d, E, gamma, gate_packed, gate_b, rscale, logits, aligned, k, topk_idx,
-                                         topk_w);
-  return cudaGetLastError();
+  return launch_kernel(fn, grid, dim3(kRouterThreads), smem, st, x, n, d, E, gamma, gate_packed, gate_b, rscale, logits,
+                       aligned, k, topk_idx, topk_w);
 }
 
 // rms_kernel, then the logits; with E <= 32 the logits blocks hold every
@@ -1782,11 +1791,14 @@ static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, cons
     const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float) +
                         (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16;
     ensure_dynamic_smem(reinterpret_cast<const void*>(router_small_kernel<XT>), smem);
-    router_small_kernel<XT><<<n, 32 * E, smem, st>>>(  // one warp per expert
-        x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx, topk_w, rscale, aligned);
-    return cudaGetLastError();
+    return launch_kernel(router_small_kernel<XT>, dim3(n), dim3(32 * E), smem, st,  // one warp per expert
+                         x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx, topk_w, rscale, aligned);
   }
-  rms_kernel<XT><<<(n + 7) / 8, 256, 0, st>>>(x, n, d, eps, rscale, aligned);
+  {
+    const cudaError_t re = launch_kernel(rms_kernel<XT>, dim3((n + 7) / 8), dim3(256), 0, st, x, n, d, eps, rscale,
+                                         aligned);
+    if (re != cudaSuccess) return re;
+  }
   const bool fuse = E <= kRouterGroup;
   int32_t* fi = fuse ? topk_idx : nullptr;
   float* fw = fuse ? topk_w : nullptr;
@@ -1822,19 +1834,18 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
     const int nch = (P + kPermChunk - 1) / kPermChunk;
     const size_t hsmem = 4 * static_cast<size_t>(E) * sizeof(int32_t);
     ensure_dynamic_smem(reinterpret_cast<const void*>(perm_hist_kernel), hsmem);
-    perm_hist_kernel<<<nch, kPermChunkThreads, hsmem, st>>>(topk_idx, P, E, pad, N, scratch, offsets, poff, counts,
-                                                             ntile_prefix);
+    cudaError_t pe = launch_kernel(perm_hist_kernel, dim3(nch), dim3(kPermChunkThreads), hsmem, st, topk_idx, P, E, pad,
+                                   N, scratch, offsets, poff, counts, ntile_prefix);
+    if (pe != cudaSuccess) return pe;
     const size_t ssmem = (kPermChunkThreads / 32) * static_cast<size_t>(E) * sizeof(int32_t);
     ensure_dynamic_smem(reinterpret_cast<const void*>(perm_scatter_kernel), ssmem);
-    perm_scatter_kernel<<<nch, kPermChunkThreads, ssmem, st>>>(topk_idx, P, E, scratch, perm_c, inv_c, perm_p,
-                                                                inv_p);
-    return cudaGetLastError();
+    return launch_kernel(perm_scatter_kernel, dim3(nch), dim3(kPermChunkThreads), ssmem, st, topk_idx, P, E, scratch,
+                         perm_c, inv_c, perm_p, inv_p);
   }
   const size_t smem = (static_cast<size_t>(34) * E + 32 * 32 * kPermBatch) * sizeof(int32_t);
   ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
-  permute_kernel<<<1, kPermThreads, smem, st>>>(topk_idx, P, E, pad, N, offsets, perm_c, inv_c, poff, counts,
-                                                ntile_prefix, perm_p, inv_p);
-  return cudaGetLastError();
+  return launch_kernel(permute_kernel, dim3(1), dim3(kPermThreads), smem, st, topk_idx, P, E, pad, N, offsets, perm_c,
+                       inv_c, poff, counts, ntile_prefix, perm_p, inv_p);
 }
 
 cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
@@ -1845,10 +1856,9 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
-  quantize_pairs_kernel<false><<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, terms, codes,
-                                                     term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked,
-                                                     EpDispatch{});
-  return cudaGetLastError();
+  return launch_kernel(quantize_pairs_kernel<false>, dim3(grid), dim3(256), 0, st, x, x_dtype, n, d, k, gamma,
+                       gamma_is_one, inv_p, terms, codes, term_stride, kp, sf, sf_term_stride, kchunks, sf_rows, stacked,
+                       EpDispatch{});
 }
 
 cudaError_t launch_quantize_f4_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
@@ -1858,17 +1868,16 @@ cudaError_t launch_quantize_f4_pairs(const void* x, int x_dtype, int n, int d, i
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);
-  quantize_f4_pairs_kernel<<<grid, 256, 0, st>>>(x, x_dtype, n, d, k, gamma, gamma_is_one, inv_p, codes, row_bytes,
-                                                 sf, kchunks, pt, src_by_pos);
-  return cudaGetLastError();
+  return launch_kernel(quantize_f4_pairs_kernel, dim3(grid), dim3(256), 0, st, x, x_dtype, n, d, k, gamma,
+                       gamma_is_one, inv_p, codes, row_bytes, sf, kchunks, pt, src_by_pos);
 }
 
 cudaError_t launch_combine(const void* x, int x_dtype, const void* y_pair, int pair_dtype, const int32_t* topk_idx,
                            const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
                            cudaStream_t st) {
   if (n == 0) return cudaSuccess;
-  combine_kernel<<<n, 256, 0, st>>>(x, x_dtype, y_pair, pair_dtype, topk_idx, inv_p, n, d, k, residual, y, y_dtype);
-  return cudaGetLastError();
+  return launch_kernel(combine_kernel, dim3(n), dim3(256), 0, st, x, x_dtype, y_pair, pair_dtype, topk_idx, inv_p, n, d,
+                       k, residual, y, y_dtype);
 }
 
 cudaError_t launch_localize(const int32_t* expert, int P, int begin, int count, int32_t* local, int* err,

@@ -24,4 +24,43 @@ inline cudaError_t ensure_dynamic_smem(const void* func, size_t bytes) {
   return e;
 }
 
+// Programmatic dependent launch for the kernels of one forward chain: with
+// it enabled (PdlScope on the launching thread), a kernel may start while
+// the previous one in the stream finishes, so its prologue overlaps that
+// tail.  Every kernel launched this way calls griddep_wait() before it reads
+// anything an earlier kernel of the chain wrote.
+inline bool& pdl_enabled() {
+  static thread_local bool on = false;
+  return on;
+}
+struct PdlScope {
+  bool prev;
+  explicit PdlScope(bool on) : prev(pdl_enabled()) { pdl_enabled() = on; }
+  ~PdlScope() { pdl_enabled() = prev; }
+  PdlScope(const PdlScope&) = delete;
+  PdlScope& operator=(const PdlScope&) = delete;
+};
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                                 Args... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr{};
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl_enabled() ? &attr : nullptr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
+#ifdef __CUDACC__
+// Waits until the kernels this one depends on have completed and their
+// writes are visible (returns at once for a plain launch).
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+#endif
+
 }  // namespace mxmoe
