@@ -548,34 +548,80 @@ __global__ void __launch_bounds__(kPermThreads)
     }
   }
   __syncthreads();
-  // per expert: totals, and each warp's base within the expert
-  for (int e = threadIdx.x; e < E; e += blockDim.x) {
-    int run = 0;
-    for (int w = 0; w < 32; ++w) {
-      const int c = cnt[w * E + e];
-      cnt[w * E + e] = run;
-      run += c;
+  if (E <= 32) {
+    // warp e scans expert e's per-warp counts across its lanes; then warp 0
+    // scans the expert totals (exclusive scans by shuffles, no serial loops)
+    if (warp < E) {
+      const int c = cnt[lane * E + warp];
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int u = __shfl_up_sync(0xFFFFFFFFu, inc, o);
+        if (lane >= o) inc += u;
+      }
+      cnt[lane * E + warp] = inc - c;
+      if (lane == 31) cstart[warp] = inc;  // total
     }
-    cstart[e] = run;  // total, turned into the start below
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, prun = 0, trun = 0;
-    for (int e = 0; e < E; ++e) {
-      const int tot = cstart[e];
-      cstart[e] = run;
-      pstart[e] = prun;
-      if (offsets) offsets[e] = run;
-      poff[e] = prun;
-      counts[e] = tot;
-      if (ntile_prefix) ntile_prefix[e] = trun;
-      run += tot;
-      prun += (tot + pad - 1) / pad * pad;
-      trun += (tot + N - 1) / N;
+    __syncthreads();
+    if (warp == 0) {
+      const int tot = lane < E ? cstart[lane] : 0;
+      int a = tot, b2 = (tot + pad - 1) / pad * pad, c = (tot + N - 1) / N;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int ua = __shfl_up_sync(0xFFFFFFFFu, a, o);
+        const int ub = __shfl_up_sync(0xFFFFFFFFu, b2, o);
+        const int uc = __shfl_up_sync(0xFFFFFFFFu, c, o);
+        if (lane >= o) {
+          a += ua;
+          b2 += ub;
+          c += uc;
+        }
+      }
+      const int run = a - tot, prun = b2 - (tot + pad - 1) / pad * pad, trun = c - (tot + N - 1) / N;
+      if (lane < E) {
+        cstart[lane] = run;
+        pstart[lane] = prun;
+        if (offsets) offsets[lane] = run;
+        poff[lane] = prun;
+        counts[lane] = tot;
+        if (ntile_prefix) ntile_prefix[lane] = trun;
+      }
+      if (lane == 31) {
+        if (offsets) offsets[E] = a;
+        poff[E] = b2;
+        if (ntile_prefix) ntile_prefix[E] = c;
+      }
     }
-    if (offsets) offsets[E] = run;
-    poff[E] = prun;
-    if (ntile_prefix) ntile_prefix[E] = trun;
+  } else {
+    // per expert: totals, and each warp's base within the expert
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      int run = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int c = cnt[w * E + e];
+        cnt[w * E + e] = run;
+        run += c;
+      }
+      cstart[e] = run;  // total, turned into the start below
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int run = 0, prun = 0, trun = 0;
+      for (int e = 0; e < E; ++e) {
+        const int tot = cstart[e];
+        cstart[e] = run;
+        pstart[e] = prun;
+        if (offsets) offsets[e] = run;
+        poff[e] = prun;
+        counts[e] = tot;
+        if (ntile_prefix) ntile_prefix[e] = trun;
+        run += tot;
+        prun += (tot + pad - 1) / pad * pad;
+        trun += (tot + N - 1) / N;
+      }
+      if (offsets) offsets[E] = run;
+      poff[E] = prun;
+      if (ntile_prefix) ntile_prefix[E] = trun;
+    }
   }
   __syncthreads();
   // pass 2: stable ranks within each expert, (token, slot) order
@@ -952,74 +998,71 @@ __global__ void __launch_bounds__(256)
 }
 
 // FP4 decode operand (kind::mxf4 tiles): each routed pair's token row as four
-// block-scaled E2M1 terms in the stacked 32-pair layout (stacked4_code_row,
-// stacked4_sf_offset).  Same warp organisation as quantize_pairs_kernel: warp
-// per (token, sixteen 32-column blocks), a lane pair per block, sixteen
-// columns per lane, so each lane stores 8 code bytes per term.
+// block-scaled E2M1 terms in the stacked layout (stacked4_code_row,
+// stacked4_sf_offset).  Warp per (row, group of eight 32-column blocks), a
+// lane quad per block, eight columns per lane: the step is latency-bound at
+// decode sizes, so the work is spread over many short warps.  Each lane
+// stores one code word per term and pair position; the first lane of each
+// quad's group of four blocks stores the 4-byte scale word.
+constexpr int kQ4BlocksPerWarp = 8;
 __global__ void __launch_bounds__(256)
     quantize_f4_pairs_kernel(const void* __restrict__ x, int x_dtype, int n, int d, int k,
                              const float* __restrict__ gamma, int gamma_is_one, const int32_t* __restrict__ inv_p,
                              uint8_t* codes, int row_bytes, uint8_t* sf, int kchunks, int pt, int src_by_pos) {
   griddep_wait();
   const int nb = d / 32;
-  const int ngrp = (nb + kQBlocksPerWarp - 1) / kQBlocksPerWarp;
+  const int ngrp = (nb + kQ4BlocksPerWarp - 1) / kQ4BlocksPerWarp;
   const uint64_t items = static_cast<uint64_t>(n) * ngrp;
   const int lane = threadIdx.x & 31;
-  const int hf = lane & 1, lb = lane >> 1;
+  const int qd = lane & 3, lb = lane >> 2;  // eighth of the block, block within the group
   const uint64_t wstride = static_cast<uint64_t>(gridDim.x) * (blockDim.x >> 5);
   for (uint64_t it = static_cast<uint64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items;
        it += wstride) {
     const int t = static_cast<int>(it / ngrp);
     const int grp = static_cast<int>(it - static_cast<uint64_t>(t) * ngrp);
-    const int b = grp * kQBlocksPerWarp + lb;
+    const int b = grp * kQ4BlocksPerWarp + lb;
     const bool active = b < nb;
-    const int c0 = b * 32 + hf * 16;
+    const int c0 = b * 32 + qd * 8;
     // source row: token t, or (activation rows, k = 1) the pair's own position
     const uint64_t src = src_by_pos ? static_cast<uint64_t>(__ldg(inv_p + t)) : static_cast<uint64_t>(t);
-    float v[16];
-    if (!active) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = 0.0f;
-    } else if (x_dtype == 1) {
-      const uint4* xs = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) +
-                                                        src * d + c0);
-      const uint4 u0 = __ldg(xs), u1 = __ldg(xs + 1);
-      const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
-#pragma unroll
-      for (int h = 0; h < 8; ++h) {
-        v[2 * h] = __uint_as_float(w8[h] << 16);
-        v[2 * h + 1] = __uint_as_float(w8[h] & 0xFFFF0000u);
-      }
-    } else {
-      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + src * d + c0);
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const float4 a = __ldg(xs + h);
-        v[4 * h] = a.x; v[4 * h + 1] = a.y; v[4 * h + 2] = a.z; v[4 * h + 3] = a.w;
-      }
-    }
-    if (!gamma_is_one && active) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
-    }
-    // the pair positions are loaded before the arithmetic so that their
-    // latency overlaps it
     uint32_t pos_k[kMaxTopK];
 #pragma unroll
     for (int q = 0; q < kMaxTopK; ++q)
       pos_k[q] = q < k ? static_cast<uint32_t>(__ldg(inv_p + static_cast<uint64_t>(t) * k + q)) : 0u;
-    uint32_t words[kF4Terms][2];
+    float v[8];
+    if (!active) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = 0.0f;
+    } else if (x_dtype == 1) {
+      const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + src * d + c0));
+      const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        v[2 * h] = __uint_as_float(w4[h] << 16);
+        v[2 * h + 1] = __uint_as_float(w4[h] & 0xFFFF0000u);
+      }
+    } else {
+      const float4* xs = reinterpret_cast<const float4*>(static_cast<const float*>(x) + src * d + c0);
+      const float4 a0 = __ldg(xs), a1 = __ldg(xs + 1);
+      v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w; v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+    }
+    if (!gamma_is_one && active) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fmul_rn(v[i], __ldg(gamma + c0 + i));
+    }
+    uint32_t words[kF4Terms];
     uint8_t sbyte[kF4Terms];
-    quantize16_e2m1_terms(v, 1, words, sbyte);
+    quantize8_e2m1_terms(v, words, sbyte);
     uint32_t sword[kF4Terms];
 #pragma unroll
     for (int q = 0; q < kF4Terms; ++q) {
+      // blocks lb & ~3 .. +3 are lanes 16 * (lb >> 2) .. + 15 (quads 4 apart)
       uint32_t sw = active ? static_cast<uint32_t>(sbyte[q]) << (8 * (lb & 3)) : 0u;
-      sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 2);
       sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 4);
+      sw |= __shfl_xor_sync(0xFFFFFFFFu, sw, 8);
       sword[q] = sw;
     }
-    const bool sf_lane = hf == 0 && (lb & 3) == 0 && active;
+    const bool sf_lane = qd == 0 && (lb & 3) == 0 && active;
 #pragma unroll
     for (int s = 0; s < kMaxTopK; ++s) {
       if (s >= k) break;
@@ -1028,7 +1071,7 @@ __global__ void __launch_bounds__(256)
       for (int q = 0; q < kF4Terms; ++q) {
         if (active) {
           const uint64_t row = stacked4_code_row(pos, static_cast<uint32_t>(q), static_cast<uint32_t>(pt));
-          *reinterpret_cast<uint2*>(codes + row * row_bytes + c0 / 2) = make_uint2(words[q][0], words[q][1]);
+          *reinterpret_cast<uint32_t*>(codes + row * row_bytes + c0 / 2) = words[q];
         }
         if (sf_lane)
           *reinterpret_cast<uint32_t*>(sf + stacked4_sf_offset(pos, static_cast<uint32_t>(q), static_cast<uint32_t>(b),
@@ -1864,7 +1907,7 @@ cudaError_t launch_quantize_pairs(const void* x, int x_dtype, int n, int d, int 
 cudaError_t launch_quantize_f4_pairs(const void* x, int x_dtype, int n, int d, int k, const float* gamma,
                                      int gamma_is_one, const int32_t* inv_p, uint8_t* codes, int row_bytes,
                                      uint8_t* sf, int kchunks, int pt, int src_by_pos, cudaStream_t st) {
-  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQBlocksPerWarp - 1) / kQBlocksPerWarp);  // warps
+  const uint64_t items = static_cast<uint64_t>(n) * ((d / 32 + kQ4BlocksPerWarp - 1) / kQ4BlocksPerWarp);  // warps
   if (items == 0 || k == 0) return cudaSuccess;
   const uint64_t blocks = (items + 7) / 8;
   const int grid = static_cast<int>(blocks < 148 * 64 ? blocks : 148 * 64);

@@ -189,3 +189,34 @@ __device__ __forceinline__ void quantize16_e2m1_terms(float (&v)[16], int xor_ma
 }
 
 }  // namespace mxmoe
+
+namespace mxmoe {
+
+// Lane-quad variant of quantize16_e2m1_terms: this lane holds 8 elements of
+// a 32-block spread over lanes l, l ^ 1, l ^ 2, l ^ 3 (one code word per
+// term).  Same arithmetic; every lane of the warp must call it.
+__device__ __forceinline__ void quantize8_e2m1_terms(float (&v)[8], uint32_t (&words)[kF4Terms],
+                                                     uint8_t (&sbyte)[kF4Terms]) {
+#pragma unroll
+  for (int t = 0; t < kF4Terms; ++t) {
+    float m0 = fmaxf(fabsf(v[0]), fabsf(v[1])), m1 = fmaxf(fabsf(v[2]), fabsf(v[3]));
+    float m2 = fmaxf(fabsf(v[4]), fabsf(v[5])), m3 = fmaxf(fabsf(v[6]), fabsf(v[7]));
+    float amax = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 1));
+    amax = fmaxf(amax, __shfl_xor_sync(0xFFFFFFFFu, amax, 2));
+    const int s = e2m1_block_exp(amax);
+    const bool live = s > -127;
+    const float inv = live ? __int_as_float((127 - s) << 23) : 0.0f;
+    const float back = live ? __int_as_float((127 + s) << 23) : 0.0f;
+    float sc[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) sc[i] = v[i] * inv;
+    const uint32_t c = cvt_e2m1x8(sc);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = fmaf(-e2m1_value(c >> (4 * i)), back, v[i]);
+    words[t] = c;
+    sbyte[t] = static_cast<uint8_t>(s + 127);
+  }
+}
+
+}  // namespace mxmoe
