@@ -30,7 +30,7 @@ import numpy as np  # noqa: E402
 # DRAM bytes (read + write) of one launch, from the ncu captures summarised in
 # profiles/tc_moe_gemm_prefill_gptoss20b.txt and profiles/tc_moe_gemm_decode_gptoss20b.txt.
 W1_PREFILL_TRAFFIC = 500.8e6 + 174.2e6
-W1_DECODE_TRAFFIC = 302.0e6 + 5.6e6
+W1_DECODE_TRAFFIC = 297.2e6 + 4.4e6  # ncu dram read + write of one FP4 W1 launch (profiles/tc_moe_gemm_decode_gptoss20b.txt)
 
 METRIC = "MoE layer tokens/s (GPT-OSS-20B-shaped MXFP4 layer, prefill 8192 tokens/GPU)"
 UNIT = "tokens/s"

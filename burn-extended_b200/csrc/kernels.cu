@@ -437,6 +437,7 @@ __global__ void __launch_bounds__(1024)
   }
   ss = warp_sum_butterfly(ss);
   const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
+#pragma unroll 4
   for (int i = threadIdx.x; i < nch * C; i += blockDim.x) {
     const int ch = i / C, cc = i % C, l = cc % 32, j = cc / 32;
     const int c = ch * C + cc;
@@ -1834,7 +1835,8 @@ static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, cons
     const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float) +
                         (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16;
     ensure_dynamic_smem(reinterpret_cast<const void*>(router_small_kernel<XT>), smem);
-    return launch_kernel(router_small_kernel<XT>, dim3(n), dim3(32 * E), smem, st,  // one warp per expert
+    // one warp per expert, and at least 8 warps to stage and normalize the row
+    return launch_kernel(router_small_kernel<XT>, dim3(n), dim3(32 * (E < 8 ? 8 : E)), smem, st,
                          x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx, topk_w, rscale, aligned);
   }
   {
