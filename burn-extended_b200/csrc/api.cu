@@ -4,9 +4,11 @@
 //   router -> permute -> quantize -> W1 GEMM -> W2 GEMM -> combine.
 #include <cuda.h>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -115,6 +117,21 @@ void dfree(T*& p) {
   p = nullptr;
 }
 
+// Row-major weight scale rows for the dequant-GEMV: kp / 32 bytes rounded up
+// to 16, so that a row range is one bulk copy.
+uint32_t dq_scale_row_bytes(uint32_t kp) { return round_up(kp / 32u, 16u); }
+
+// Status block: word 0 is the status code; from kStatusSyncOffset on, one
+// arrival counter per local expert (dequant-GEMV W1 -> W2 handoff).  Zeroed
+// before every forward.
+constexpr int kStatusSyncOffset = 16;
+constexpr int kStatusDoneWord = 1;  // dequant-GEMV fused mode: finished-block counter
+
+// The dequant-GEMV takes forwards of at most this many routed pairs (so at
+// most this many tokens); the router then also writes their normalized f16
+// rows for it.
+constexpr uint32_t kGemvMaxTokens = 64;
+
 float bf16_to_f32(uint16_t h) {
   uint32_t u = static_cast<uint32_t>(h) << 16;
   float f;
@@ -203,6 +220,8 @@ struct Workspace {
   uint8_t* aq4 = nullptr;
   uint8_t* asf4 = nullptr;
   float* act4_f32 = nullptr;  // [rows4][fp] W1 output before quantization
+  __half* xh = nullptr;       // [kGemvMaxTokens][d] router-normalized f16 token rows (dequant-GEMV input)
+  int* tok_ctr = nullptr;     // [8] per-token block counters of the small-batch router (kept zero)
   CUtensorMap tmap_x4[2], tmap_act4[2];  // boxes of 4 x 16 and 4 x 32 rows
 };
 
@@ -215,6 +234,10 @@ struct mxmoe_layer {
   size_t smem_limit = 227 * 1024;
   bool router_ready = false, experts_ready = false;
   bool gamma_is_one = true;
+  // powers of two that keep the dequant-GEMV's f16 operands in range:
+  // normalized rows |x * gamma / rms| <= sqrt(d) * max|gamma|, and SwiGLU
+  // outputs |act| <= max(limit, 0.28 / alpha) * (limit + 1)
+  float dq_x_scale = 1.0f, dq_act_scale = 1.0f;
   float* gamma = nullptr;
   float* gate_w = nullptr;  // packed for the router kernel (pack_router_gate)
   float* gate_b = nullptr;
@@ -224,7 +247,9 @@ struct mxmoe_layer {
   uint8_t* w2q = nullptr;
   uint8_t* w2sf = nullptr;
   float* b2 = nullptr;
-  int* err = nullptr;
+  uint8_t* w1sr = nullptr;  // row-major scale copies for the dequant-GEMV (dq_scale_row_bytes per row)
+  uint8_t* w2sr = nullptr;
+  int* err = nullptr;       // status block (kStatusSyncOffset + E_total words)
   CUtensorMap tmap_w1[2] = {}, tmap_w2[2] = {};  // box rows 128 (weights-as-A) / 256 (tokens-as-A)
   CUtensorMap tmap_w1_f4 = {}, tmap_w2_f4 = {};  // packed bytes, 256-row boxes of K 256 (FP4 tiles)
   Workspace ws;
@@ -257,7 +282,7 @@ void free_workspace(Workspace& w) {
   dfree(w.offsets); dfree(w.perm_c); dfree(w.inv_c); dfree(w.poff); dfree(w.counts);
   dfree(w.ntile_prefix); dfree(w.perm_p); dfree(w.inv_p);
   dfree(w.xq); dfree(w.xsf); dfree(w.aq); dfree(w.asf); dfree(w.y_pair); dfree(w.act_f32);
-  dfree(w.xq4); dfree(w.xsf4); dfree(w.aq4); dfree(w.asf4); dfree(w.act4_f32);
+  dfree(w.xq4); dfree(w.xsf4); dfree(w.aq4); dfree(w.asf4); dfree(w.act4_f32); dfree(w.xh); dfree(w.tok_ctr);
   w.rows4 = 0;
   dfree(w.local_idx);
   dfree(w.ret_slot);
@@ -330,6 +355,9 @@ int ensure_workspace(mxmoe_layer* L, uint32_t n_tokens, uint32_t k) {
   TRY(dalloc(&w.aq, 2ull * w.rows * L->kp2));
   TRY(dalloc(&w.asf, 2ull * w.row_blocks * kc2 * kSfAtomBytes));
   TRY(dalloc(&w.y_pair, static_cast<size_t>(w.rows) * L->d));
+  TRY(dalloc(&w.xh, static_cast<size_t>(std::min<uint32_t>(cap_t, kGemvMaxTokens)) * L->d));
+  TRY(dalloc(&w.tok_ctr, 8));
+  CUDA_TRY(cudaMemset(w.tok_ctr, 0, 8 * sizeof(int)));
   // Padding columns (K beyond d or f) and never-written scale bytes must read
   // as zero codes / finite scales for every later forward.
   CUDA_TRY(cudaMemset(w.xq, 0, 3ull * w.rows * L->kp1));
@@ -392,6 +420,22 @@ int ensure_f4(mxmoe_layer* L) {
   return MXMOE_OK;
 }
 
+// Power of two p with bound * p <= 2^14 (f16 keeps 11 significant bits up to
+// 65504, so the scaled operand stays normal and well inside the range).
+float f16_range_scale(float bound) {
+  if (!(bound > 0.0f) || !std::isfinite(bound)) return 1.0f;
+  const int ex = static_cast<int>(std::floor(std::log2(16384.0f / bound)));
+  return std::ldexp(1.0f, std::max(-60, std::min(60, ex)));
+}
+
+// The dequant-GEMV stores SwiGLU outputs as f16, which needs the clamp to
+// bound them: a finite limit of at most 128 and a positive alpha.
+bool gemv_ok(const mxmoe_layer* L) {
+  const float lim = L->cfg.swiglu_limit, al = L->cfg.swiglu_alpha;
+  return !(L->cfg.flags & MXMOE_FLAG_NO_GEMV) && L->d <= static_cast<uint32_t>(kDqMaxK) && L->fp <= static_cast<uint32_t>(kDqMaxK) &&
+         std::isfinite(lim) && lim > 0.0f && lim <= 128.0f && al > 0.0f && std::isfinite(al);
+}
+
 // Tile plan from the average routed pairs per expert:
 //   few pairs  -> weights-as-A, pair tiles of 32 / 64 / 128 (HBM-bound decode);
 //   many pairs -> tokens-as-A, pair tiles of 128 x weight tiles of 256 rows.
@@ -412,7 +456,10 @@ struct TilePlan {
 // Tiny batches (at most kGemvMaxPairs routed pairs in all) go to the fused
 // dequant-GEMV kernels, which spread the weights over every SM; tensor-core
 // tiles would leave most SMs idle there.
-constexpr uint64_t kGemvMaxPairs = 64;
+// Measured on B200 (layer forward, 20B / 120B shapes): the GEMV wins up to
+// 4 routed pairs (batch 1 at top-4, or up to 4 tokens on one expert); from
+// 8 pairs on, the kind::mxf4 tensor-core tiles are faster.
+constexpr uint64_t kGemvMaxPairs = 4;
 
 TilePlan pick_tiles(uint64_t pairs, uint32_t experts, int x_terms, bool allow_gemv = false, bool allow_fp4 = false) {
   if (allow_gemv && pairs <= kGemvMaxPairs) return {true, 8, 0, false, true};  // callers check kGemvMaxK
@@ -522,6 +569,82 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
   return MXMOE_OK;
 }
 
+// The dequant-GEMV expert FFN (dqgemv.cu) for at most kGemvMaxPairs routed
+// pairs.  With y (fused mode, mxmoe_forward) it also combines into y and
+// writes the canonical routing maps, and needs no permutation kernel before
+// it: its pairs come from the top-k ids and the router's f16 rows xh.
+// Without y it reads the permutation's counts / offsets / perm and writes
+// y_pair rows for mxmoe_combine.
+int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
+               const float* route_w, const int32_t* perm, cudaStream_t st, const __half* xh = nullptr,
+               void* y = nullptr, int y_dtype = MXMOE_F32) {
+  Workspace& w = L->ws;
+  const uint64_t P = static_cast<uint64_t>(n_tok) * k;
+  // SwiGLU rows as f16 in the f32 activation buffer (half its bytes)
+  if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
+  w.pair_dtype = MXMOE_F32;
+  if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
+  // a token's k experts are distinct, so no expert gets more than n_tok pairs
+  const int max_pe = static_cast<int>(std::min<uint64_t>(n_tok, P));
+  const int max_ex = static_cast<int>(std::min<uint64_t>(P, L->e_count));
+  DqParams a{};
+  a.d = static_cast<int>(L->d);
+  a.fp = static_cast<int>(L->fp);
+  a.kp1 = static_cast<int>(L->kp1);
+  a.kp2 = static_cast<int>(L->kp2);
+  a.w1q = L->w1q;
+  a.w1sr = L->w1sr;
+  a.sr1 = dq_scale_row_bytes(L->kp1);
+  a.b1 = L->b1;
+  a.w2q = L->w2q;
+  a.w2sr = L->w2sr;
+  a.sr2 = dq_scale_row_bytes(L->kp2);
+  a.b2 = L->b2;
+  a.bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
+  a.E = static_cast<int>(L->e_count);
+  a.poff = w.poff;
+  a.counts = w.counts;
+  a.perm = perm ? perm : w.perm_p;
+  a.pair_k = static_cast<int>(k);
+  a.xh = xh;
+  a.x = x;
+  a.x_dtype = x_dtype == MXMOE_F32 ? kDqSrcF32 : kDqSrcBf16;
+  a.gamma = L->gamma;
+  a.rscale = rscale;
+  a.x_scale = L->dq_x_scale;
+  a.inv_x_scale = 1.0f / L->dq_x_scale;
+  a.alpha = L->cfg.swiglu_alpha;
+  a.limit = L->cfg.swiglu_limit;
+  a.act_scale = L->dq_act_scale;
+  a.inv_act_scale = 1.0f / L->dq_act_scale;
+  a.act = reinterpret_cast<__half*>(w.act_f32);
+  a.y_pair = w.y_pair;
+  a.topk_w = route_w;
+  a.err = L->err;
+  a.sync = L->err + kStatusSyncOffset;
+  if (y) {
+    a.fused = 1;
+    a.topk_idx = w.topk_idx;
+    a.P = static_cast<int>(P);
+    a.n_tok = static_cast<int>(n_tok);
+    a.residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
+    a.y = y;
+    a.y_dtype = y_dtype == MXMOE_F32 ? kDqSrcF32 : kDqSrcBf16;
+    a.offsets = w.offsets;
+    a.perm_c = w.perm_c;
+    a.inv_c = w.inv_c;
+    a.done = L->err + kStatusDoneWord;
+  }
+  // pairs staged per pass: up to 16 (several passes only for skewed batches)
+  a.ps = max_pe <= 1 ? 1 : max_pe <= 2 ? 2 : max_pe <= 4 ? 4 : max_pe <= 8 ? 8 : 16;
+  CUDA_TRY(launch_dqgemv_ffn(a, max_pe, max_ex, L->num_sms, L->smem_limit, st));
+  if (L->profiling) {
+    CUDA_TRY(cudaEventRecord(L->ev[4], st));  // W1, W2 (and in fused mode the combine) are one launch
+    CUDA_TRY(cudaEventRecord(L->ev[5], st));
+  }
+  return MXMOE_OK;
+}
+
 // Expert FFN over already-routed pairs: quantize -> W1 -> W2 (or the SIMT
 // pair) -> y_pair.  Uses ws.poff / counts / ntile_prefix / perm_p / inv_p.
 int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
@@ -544,19 +667,7 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
     if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
     return MXMOE_OK;
   }
-  if (tp.gemv) {
-    if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
-    w.pair_dtype = MXMOE_F32;
-    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
-    CUDA_TRY(launch_gemv_w1(x, x_dtype, L->d, k, L->gamma, rscale, L->w1q, L->w1sf, L->b1, L->fp, L->kp1, L->e_count,
-                            w.poff, w.counts, perm ? perm : w.perm_p, L->cfg.swiglu_alpha, L->cfg.swiglu_limit,
-                            w.act_f32, static_cast<int>(P), st));
-    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[4], st));
-    CUDA_TRY(launch_gemv_w2(w.act_f32, L->fp, L->d, L->w2q, L->w2sf, L->b2, bias_mult, L->kp2, L->e_count, w.poff,
-                            w.counts, perm ? perm : w.perm_p, route_w, w.y_pair, static_cast<int>(P), st));
-    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
-    return MXMOE_OK;
-  }
+  if (tp.gemv) return run_dqgemv(L, x, x_dtype, n_tok, k, rscale, route_w, perm, st);
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   if (tp.fp4)
     return run_experts_f4(L, x, x_dtype, n_tok, k, rscale, route_w, tp, st, ret_ptrs, ret_slot, y_by_pair, perm);
@@ -699,13 +810,17 @@ int mxmoe_create(const mxmoe_config* cfg, mxmoe_layer** out) {
   L->kp2 = round_up(L->fp, kTileK);
   L->m_tiles1 = 2 * L->fp / 128;
   L->m_tiles2 = (L->d + 127) / 128;
+  if (gemv_ok(L))
+    L->dq_act_scale = f16_range_scale(std::max(cfg->swiglu_limit, 0.28f / cfg->swiglu_alpha) *
+                                      (cfg->swiglu_limit + 1.0f));
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, cfg->device) == cudaSuccess) {
     L->num_sms = prop.multiProcessorCount;
     L->smem_limit = prop.sharedMemPerBlockOptin;
   }
-  int rc = dalloc(&L->err, 1);
-  if (rc == MXMOE_OK && cudaMemset(L->err, 0, sizeof(int)) != cudaSuccess) rc = MXMOE_ERR_CUDA;
+  const size_t status_words = kStatusSyncOffset + static_cast<size_t>(L->E_total);
+  int rc = dalloc(&L->err, status_words);
+  if (rc == MXMOE_OK && cudaMemset(L->err, 0, status_words * sizeof(int)) != cudaSuccess) rc = MXMOE_ERR_CUDA;
   if (rc != MXMOE_OK) {
     delete L;
     return rc;
@@ -738,6 +853,7 @@ int mxmoe_destroy(mxmoe_layer* L) {
   free_workspace(L->ws);
   dfree(L->gamma); dfree(L->gate_w); dfree(L->gate_b);
   dfree(L->w1q); dfree(L->w1sf); dfree(L->b1); dfree(L->w2q); dfree(L->w2sf); dfree(L->b2);
+  dfree(L->w1sr); dfree(L->w2sr);
   dfree(L->err);
   for (auto& e : L->ev)
     if (e) cudaEventDestroy(e);
@@ -759,6 +875,9 @@ int mxmoe_set_router(mxmoe_layer* L, const void* norm_gamma, const void* gate_w,
   to_f32(gate_w, dtype, E * d, w.data());
   to_f32(gate_b, dtype, E, b.data());
   L->gamma_is_one = std::all_of(gm.begin(), gm.end(), [](float v) { return v == 1.0f; });
+  float gmax = 0.0f;
+  for (float v : gm) gmax = std::max(gmax, std::fabs(v));
+  L->dq_x_scale = f16_range_scale(std::sqrt(static_cast<float>(d)) * gmax);
   ++L->generation;
   if (!L->gamma) TRY(dalloc(&L->gamma, d));
   std::vector<float> wp(router_gate_packed_floats(static_cast<int>(E), static_cast<int>(d)));
@@ -819,6 +938,8 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
 
   const uint64_t rp1 = w_sf_row_pairs(static_cast<uint32_t>(rows1)), rp2 = w_sf_row_pairs(static_cast<uint32_t>(d));
   std::vector<uint8_t> q1(E * rows1 * (kp1 / 2), 0), s1(E * rp1 * kc1 * kWSfPairBytes, 0);
+  const uint64_t sr1 = dq_scale_row_bytes(static_cast<uint32_t>(kp1)), sr2 = dq_scale_row_bytes(static_cast<uint32_t>(kp2));
+  std::vector<uint8_t> r1(E * rows1 * sr1, 0), r2(E * d * sr2, 0);  // row-major scales (dequant-GEMV)
   std::vector<float> bb1(E * rows1, 0.0f), src_b1(E * 2 * f);
   to_f32(b1, bias_dtype, E * 2 * f, src_b1.data());
   for (uint64_t e = 0; e < E; ++e)
@@ -828,9 +949,11 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
         const uint64_t dst = w1_packed_row(static_cast<uint32_t>(j), half);
         std::memcpy(&q1[(e * rows1 + dst) * (kp1 / 2)], &w1_blocks[(e * 2 * f + src) * bpr1], bpr1);
         uint8_t* atoms = &s1[e * rp1 * kc1 * kWSfPairBytes];
-        for (uint64_t gi = 0; gi < gpr1; ++gi)
-          atoms[w_sf_offset(static_cast<uint32_t>(dst), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc1))] =
-              sf_byte(w1_scales[(e * 2 * f + src) * gpr1 + gi], w1d->ue8_offset);
+        for (uint64_t gi = 0; gi < gpr1; ++gi) {
+          const uint8_t v = sf_byte(w1_scales[(e * 2 * f + src) * gpr1 + gi], w1d->ue8_offset);
+          atoms[w_sf_offset(static_cast<uint32_t>(dst), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc1))] = v;
+          r1[(e * rows1 + dst) * sr1 + gi] = v;
+        }
         bb1[e * rows1 + dst] = src_b1[e * 2 * f + src];
       }
   std::vector<uint8_t> q2(E * d * (kp2 / 2), 0), s2(E * rp2 * kc2 * kWSfPairBytes, 0);
@@ -840,13 +963,18 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
     for (uint64_t c = 0; c < d; ++c) {
       std::memcpy(&q2[(e * d + c) * (kp2 / 2)], &w2_blocks[(e * d + c) * bpr2], bpr2);
       uint8_t* atoms = &s2[e * rp2 * kc2 * kWSfPairBytes];
-      for (uint64_t gi = 0; gi < gpr2; ++gi)
-        atoms[w_sf_offset(static_cast<uint32_t>(c), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc2))] =
-            sf_byte(w2_scales[(e * d + c) * gpr2 + gi], w2d->ue8_offset);
+      for (uint64_t gi = 0; gi < gpr2; ++gi) {
+        const uint8_t v = sf_byte(w2_scales[(e * d + c) * gpr2 + gi], w2d->ue8_offset);
+        atoms[w_sf_offset(static_cast<uint32_t>(c), static_cast<uint32_t>(gi), static_cast<uint32_t>(kc2))] = v;
+        r2[(e * d + c) * sr2 + gi] = v;
+      }
     }
 
   dfree(L->w1q); dfree(L->w1sf); dfree(L->b1); dfree(L->w2q); dfree(L->w2sf); dfree(L->b2);
+  dfree(L->w1sr); dfree(L->w2sr);
   ++L->generation;
+  TRY(dalloc(&L->w1sr, r1.size()));
+  TRY(dalloc(&L->w2sr, r2.size()));
   TRY(dalloc(&L->w1q, q1.size()));
   TRY(dalloc(&L->w1sf, s1.size()));
   TRY(dalloc(&L->b1, bb1.size()));
@@ -860,6 +988,8 @@ int mxmoe_upload_experts(mxmoe_layer* L, const mxmoe_quant_desc* w1d, const uint
   CUDA_TRY(cudaMemcpyAsync(L->w2q, q2.data(), q2.size(), cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(L->w2sf, s2.data(), s2.size(), cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaMemcpyAsync(L->b2, bb2.data(), bb2.size() * 4, cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->w1sr, r1.data(), r1.size(), cudaMemcpyHostToDevice, st));
+  CUDA_TRY(cudaMemcpyAsync(L->w2sr, r2.data(), r2.size(), cudaMemcpyHostToDevice, st));
   CUDA_TRY(cudaStreamSynchronize(st));
   for (int i = 0; i < 2; ++i) {
     const uint32_t box = i == 0 ? 128 : 256;
@@ -885,7 +1015,7 @@ int mxmoe_reserve(mxmoe_layer* L, uint32_t max_tokens) {
 // Tile plan of mxmoe_forward for P routed pairs.
 static TilePlan forward_plan(const mxmoe_layer* L, uint64_t P, int x_terms) {
   const bool simt = (L->cfg.flags & MXMOE_FLAG_SIMT) != 0;
-  return pick_tiles(P, L->e_count, x_terms, L->d <= kGemvMaxK && L->fp <= kGemvMaxK,
+  return pick_tiles(P, L->e_count, x_terms, gemv_ok(L),
                     !simt && !(L->cfg.flags & MXMOE_FLAG_NO_FP4));
 }
 
@@ -901,11 +1031,22 @@ static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, voi
   const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
   const int xt = x_terms_for(L, x_dtype);
   const TilePlan tp = forward_plan(L, P, xt);
-  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  const int status_words = static_cast<int>(kStatusSyncOffset + L->E_total);
+  // the small-batch router zeroes the status words itself (one graph node less)
+  if (!tp.gemv) CUDA_TRY(cudaMemsetAsync(L->err, 0, status_words * sizeof(int), st));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
+  // the dequant-GEMV stages the router's normalized f16 token rows
+  __half* xh = tp.gemv ? w.xh : nullptr;
   CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
-                         w.logits, w.topk_idx, w.topk_w, w.rscale, st));
+                         w.logits, w.topk_idx, w.topk_w, w.rscale, st, xh, L->dq_x_scale, w.tok_ctr,
+                         tp.gemv ? L->err : nullptr, status_words));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
+  if (tp.gemv) {
+    // router -> one fused kernel (expert FFN, combine, routing maps)
+    if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
+    TRY(run_dqgemv(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, nullptr, st, xh, y, y_dtype));
+    return MXMOE_OK;
+  }
   CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, tp.fp4 ? tp.pair_tile : kRowBlock, tp.pair_tile,
                           w.offsets, w.perm_c,
                           w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
@@ -1218,8 +1359,8 @@ int mxmoe_forward_local(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtype, co
   Workspace& w = L->ws;
   cudaStream_t st = as_stream(stream);
   const int xt = x_terms_for(L, xr_dtype);
-  const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt, L->d <= kGemvMaxK && L->fp <= kGemvMaxK);
-  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt, gemv_ok(L));
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, (kStatusSyncOffset + L->E_total) * sizeof(int), st));
   CUDA_TRY(launch_localize(expert, static_cast<int>(n_pairs), static_cast<int>(L->e_begin),
                            static_cast<int>(L->e_count), w.local_idx, L->err, st));
   CUDA_TRY(launch_permute(w.local_idx, static_cast<int>(n_pairs), L->e_count, kRowBlock, tp.pair_tile, nullptr,
@@ -1316,7 +1457,7 @@ int mxmoe_forward_local_meta(mxmoe_layer* L, const void* xr, mxmoe_dtype xr_dtyp
   cudaStream_t st = as_stream(stream);
   const int xt = x_terms_for(L, xr_dtype);
   const TilePlan tp = pick_tiles(n_pairs, L->e_count, xt);
-  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, (kStatusSyncOffset + L->E_total) * sizeof(int), st));
   // profiled stages: split + localize in the "router" slot, no combine
   L->profile_valid = false;
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
@@ -1393,7 +1534,7 @@ int mxmoe_ep_dispatch(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32
   const int xt = x_terms_for(L, x_dtype);
   const TilePlan tp = ep_tiles(L, xt);
   const int world = static_cast<int>(L->ep_world);
-  CUDA_TRY(cudaMemsetAsync(L->err, 0, sizeof(int), st));
+  CUDA_TRY(cudaMemsetAsync(L->err, 0, (kStatusSyncOffset + L->E_total) * sizeof(int), st));
   CUDA_TRY(launch_ep_layout(counts, world, static_cast<int>(rank), static_cast<int>(L->E_total),
                             static_cast<int>(L->e_count), kRowBlock, tp.pair_tile, w.ep_src_base, w.poff, w.counts,
                             w.ntile_prefix, st));

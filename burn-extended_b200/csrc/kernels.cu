@@ -7,6 +7,8 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <type_traits>
+
 #include "kernels.h"
 #include "launch_util.h"
 #include "layout.cuh"
@@ -158,6 +160,20 @@ __device__ __forceinline__ void cp_async_wait() {
 // next segment's loads in flight while the current one is summed) through a
 // shared-memory buffer from which each lane reads its own chain values.
 constexpr int kRmsVec = 4;  // 16-byte vectors per lane per segment
+
+// The normalized token row ((x * 1/rms) * gamma, times a power of two) as
+// f16, for the decode dequant-GEMV to stage without recomputing it; d is a
+// multiple of 32; xr and gamma are shared-memory copies.  Threads tid,
+// tid + nthreads, ... each write two columns.
+template <typename XT>
+__device__ __forceinline__ void write_xh_row(const XT* xr, int d, float r, const float* gamma, float scale,
+                                             __half* dst, int tid, int nthreads) {
+  for (int c = 2 * tid; c < d; c += 2 * nthreads) {
+    const float v0 = __fmul_rn(__fmul_rn(load_f32(xr, c), r), gamma[c]);
+    const float v1 = __fmul_rn(__fmul_rn(load_f32(xr, c + 1), r), gamma[c + 1]);
+    *reinterpret_cast<__half2*>(dst + c) = __floats2half2_rn(v0 * scale, v1 * scale);
+  }
+}
 template <typename XT>
 __global__ void __launch_bounds__(256) rms_kernel(const XT* __restrict__ x, int n, int d, float eps,
                                                   float* __restrict__ rscale, int aligned) {
@@ -411,10 +427,25 @@ __global__ void __launch_bounds__(1024)
                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
                         float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
                         float* __restrict__ rscale, int x_aligned) {
-  griddep_wait();
-  extern __shared__ __align__(16) float router_small_smem[];
   const int C = kRouterChunk;
   const int nch = (d + C - 1) / C;
+  extern __shared__ __align__(16) float router_small_smem[];
+  float* g_s = router_small_smem + nch * C + (d * static_cast<int>(sizeof(XT)) + 15) / 16 * 4;  // [d] gamma
+  // gamma is a constant: copied in while the previous kernel finishes (d % 32 == 0)
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) cp_async16(g_s + 4 * i, gamma + 4 * i, 16);
+  cp_async_commit();
+  {
+    // the gate rows do not depend on earlier kernels: pull this warp's
+    // expert row into L2 while the previous kernel finishes
+    const int e = threadIdx.x >> 5, l = threadIdx.x & 31;
+    if (e < E)
+      for (int ch = l; ch < nch; ch += 32) {
+        const float* p = gate_packed + (static_cast<uint64_t>(ch) * kRouterGroup + e) * C;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) asm volatile("prefetch.global.L2 [%0];" ::"l"(p + 32 * q));
+      }
+  }
+  griddep_wait();
   float* xn_s = router_small_smem;                                           // [nch][128] packed order
   XT* xr_s = reinterpret_cast<XT*>(router_small_smem + nch * C);             // [d] raw row
   __shared__ float lg_s[32];
@@ -428,6 +459,7 @@ __global__ void __launch_bounds__(1024)
   } else {
     for (int i = threadIdx.x; i < d; i += blockDim.x) xr_s[i] = xr[i];
   }
+  cp_async_wait<0>();
   __syncthreads();
   float ss = 0.0f;
 #pragma unroll 8
@@ -441,7 +473,7 @@ __global__ void __launch_bounds__(1024)
   for (int i = threadIdx.x; i < nch * C; i += blockDim.x) {
     const int ch = i / C, cc = i % C, l = cc % 32, j = cc / 32;
     const int c = ch * C + cc;
-    xn_s[ch * C + l * 4 + j] = c < d ? __fmul_rn(__fmul_rn(load_f32(xr_s, c), r), __ldg(gamma + c)) : 0.0f;
+    xn_s[ch * C + l * 4 + j] = c < d ? __fmul_rn(__fmul_rn(load_f32(xr_s, c), r), g_s[c]) : 0.0f;
   }
   __syncthreads();
   const int e = warp;
@@ -479,6 +511,122 @@ __global__ void __launch_bounds__(1024)
     const float v[1] = {lane < E ? lg_s[lane] : 0.0f};
     warp_topk_softmax<1>(v, E, k, lane, topk_idx + static_cast<uint64_t>(t) * k, topk_w + static_cast<uint64_t>(t) * k);
   }
+}
+
+// Tiny batches (decode, at most kRouterTinyMaxN tokens, d <= 4096): the
+// gate GEMV is spread over blocks of kRouterTinyExperts experts per token
+// instead of one block per token, so the gate rows stream through many SMs.
+// Each warp holds its expert's packed gate row in registers, loaded before
+// griddepcontrol.wait (the weights depend on no earlier kernel), and runs
+// the lane chains of router_small_kernel in the same order (bit-identical
+// logits).  The last block of a token to finish (a per-token counter, reset
+// by that block) does the top-k + softmax.  Block (t, 0) also writes 1/rms
+// and the normalized f16 row, and block (0, 0) zeroes the layer's status
+// words for the kernels after it (after its wait).
+constexpr int kRouterTinyMaxN = 8;
+constexpr int kRouterTinyExperts = 8;
+template <typename XT, int NCH>
+__global__ void __launch_bounds__(32 * kRouterTinyExperts)
+    router_tiny_kernel(const XT* __restrict__ x, int n, int d, int E, int k, const float* __restrict__ gamma,
+                       const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
+                       float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
+                       float* __restrict__ rscale, int x_aligned, __half* __restrict__ xh, float xh_scale,
+                       int* __restrict__ tok_ctr, int* __restrict__ status, int status_words) {
+  const int C = kRouterChunk;
+  const int nch = (d + C - 1) / C, full = d / C;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int t = blockIdx.x, e = blockIdx.y * kRouterTinyExperts + warp;
+  extern __shared__ __align__(16) float router_tiny_smem[];
+  float* g_s = router_tiny_smem;                           // [d] gamma
+  XT* x_s = reinterpret_cast<XT*>(router_tiny_smem + d);   // [d] raw token row
+  __shared__ int last;
+  // the gate row and gamma are constants: fetched while the previous kernel finishes
+  float4 wv[NCH];
+  if (e < E) {
+    const float* wrow = gate_packed + (static_cast<uint64_t>(e / kRouterGroup) * nch) * kRouterGroup * C +
+                        (e % kRouterGroup) * C + lane * 4;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch)
+      if (ch < nch) wv[ch] = __ldg(reinterpret_cast<const float4*>(wrow + static_cast<uint64_t>(ch) * kRouterGroup * C));
+  }
+  for (int i = threadIdx.x; i < d / 4; i += blockDim.x) cp_async16(g_s + 4 * i, gamma + 4 * i, 16);  // d % 32 == 0
+  cp_async_commit();
+  // from here on the previous kernel in the stream has completed (it may be
+  // the last forward's expert kernel, which still uses the status words)
+  griddep_wait();
+  if (status != nullptr && t == 0 && blockIdx.y == 0)
+    for (int i = threadIdx.x; i < status_words; i += blockDim.x) status[i] = 0;
+  const XT* xr = x + static_cast<uint64_t>(t) * d;
+  constexpr int kEpv = 16 / static_cast<int>(sizeof(XT));
+  if (x_aligned) {
+    for (int i = threadIdx.x; i < d / kEpv; i += blockDim.x) cp_async16(x_s + kEpv * i, xr + kEpv * i, 16);
+    cp_async_commit();
+  } else {
+    for (int i = threadIdx.x; i < d; i += blockDim.x) x_s[i] = xr[i];
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  float ss = 0.0f;
+#pragma unroll 8
+  for (int c = lane; c < d; c += 32) {
+    const float f = load_f32(x_s, c);
+    ss = __fmaf_rn(f, f, ss);
+  }
+  ss = warp_sum_butterfly(ss);
+  const float r = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, static_cast<float>(d)), eps)));
+  if (e < E) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int ch = 0; ch < NCH; ++ch) {
+      if (ch < full) {
+        const float* wf = reinterpret_cast<const float*>(&wv[ch]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int c = ch * C + lane + 32 * q;
+          acc = __fmaf_rn(__fmul_rn(__fmul_rn(load_f32(x_s, c), r), g_s[c]), wf[q], acc);
+        }
+      } else if (ch < nch) {
+        // ragged last chunk: only the lane's columns below d join its chain
+        const float* wf = reinterpret_cast<const float*>(&wv[ch]);
+        for (int q = 0; q < 4; ++q) {
+          const int c = ch * C + lane + 32 * q;
+          if (c >= d) break;
+          acc = __fmaf_rn(__fmul_rn(__fmul_rn(load_f32(x_s, c), r), g_s[c]), wf[q], acc);
+        }
+      }
+    }
+    const float sum = warp_sum_butterfly(acc);
+    if (lane == 0) logits_out[static_cast<uint64_t>(t) * E + e] = __fadd_rn(sum, __ldg(gate_b + e));
+  }
+  if (blockIdx.y == 0) {
+    if (threadIdx.x == 0) rscale[t] = r;
+    if (xh) write_xh_row(x_s, d, r, g_s, xh_scale, xh + static_cast<uint64_t>(t) * d, threadIdx.x, blockDim.x);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(tok_ctr + t, 1) == static_cast<int>(gridDim.y) - 1;
+  }
+  __syncthreads();
+  if (!last || warp != 0) return;
+  __threadfence();
+  const float* lg = logits_out + static_cast<uint64_t>(t) * E;
+  int32_t* io = topk_idx + static_cast<uint64_t>(t) * k;
+  float* wo = topk_w + static_cast<uint64_t>(t) * k;
+  auto run = [&](auto pl) {
+    constexpr int PL = decltype(pl)::value;
+    float v[PL];
+#pragma unroll
+    for (int i = 0; i < PL; ++i) v[i] = lane + 32 * i < E ? __ldcg(lg + lane + 32 * i) : 0.0f;
+    warp_topk_softmax<PL>(v, E, k, lane, io, wo);
+  };
+  if (E <= 32) run(std::integral_constant<int, 1>());
+  else if (E <= 64) run(std::integral_constant<int, 2>());
+  else if (E <= 128) run(std::integral_constant<int, 4>());
+  else if (E <= 256) run(std::integral_constant<int, 8>());
+  else if (E <= 512) run(std::integral_constant<int, 16>());
+  else run(std::integral_constant<int, 32>());
+  if (lane == 0) tok_ctr[t] = 0;  // ready for the next forward
 }
 
 // ------------------------------------------------------------------ permute
@@ -1470,314 +1618,6 @@ __global__ void simt_w2_kernel(const float* __restrict__ act, int fp, int d, int
 
 }  // namespace
 
-// ------------------------------------------------------------------ fused dequant-GEMV (few pairs)
-// For small batches (a handful of pairs per expert) the tensor-core tiles
-// leave most SMs idle; these kernels spread the weights over the whole GPU
-// instead.  A block stages the normalized activations of kGemvPairs (1, 2, 4 or 8)
-// pairs of its expert in shared memory; each warp streams kGemvRows weight
-// rows in 8-byte coalesced loads (16 E2M1 codes per lane, one 32-column
-// scale block per lane pair), decodes them two at a time in hardware, forms
-// 16-element partial dot products, applies the block scale once per partial,
-// and reduces over the warp with shuffles.  f32 throughout.
-constexpr int kGemvRows = 2;
-constexpr int kGemvChunks = 8;  // 512-column chunks of a weight row held in registers (K <= 4096)
-
-__device__ __forceinline__ void e2m1x8_to_f32(uint32_t w, float (&o)[8]) {
-  uint32_t h[4];
-  asm("{\n\t.reg .b8 b0, b1, b2, b3;\n\t"
-      "mov.b32 {b0, b1, b2, b3}, %4;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %0, b0;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %1, b1;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %2, b2;\n\t"
-      "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
-      : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
-      : "r"(w));
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&h[i]));
-    o[2 * i] = f.x;      // low nibble: even column
-    o[2 * i + 1] = f.y;  // high nibble: odd column
-  }
-}
-
-// 2^(s - 127) for an E8M0 byte (s = 0 gives the subnormal 2^-127, 255 gives inf).
-__device__ __forceinline__ float e8m0_value(uint32_t s) {
-  return s == 0 ? __int_as_float(0x00400000) : __int_as_float(static_cast<int>(s) << 23);
-}
-
-// Shared-memory position of activation column c: a lane's 16 consecutive
-// columns of a 512-column group are 4 float4 spaced 128 floats apart, so the
-// 8 lanes of a quarter warp read 128 contiguous bytes (no bank conflicts).
-__device__ __forceinline__ int gemv_slot(int c) {
-  return (c & ~511) + ((c & 15) >> 2) * 128 + ((c & 511) >> 4) * 4 + (c & 3);
-}
-
-// Weights of one 16-column lane chunk for kGemvRows rows (raw codes + scales).
-struct GemvW {
-  uint2 b[kGemvRows];
-  uint32_t s[kGemvRows];
-};
-__device__ __forceinline__ void gemv_load(const uint8_t* const (&row_ptr)[kGemvRows], const uint8_t* sfa,
-                                          const uint32_t (&rid)[kGemvRows], uint32_t kchunks, int kc, GemvW& w) {
-#pragma unroll
-  for (int r = 0; r < kGemvRows; ++r) {
-    w.b[r] = __ldg(reinterpret_cast<const uint2*>(row_ptr[r] + kc / 2));
-    w.s[r] = __ldg(sfa + w_sf_offset(rid[r], static_cast<uint32_t>(kc / 32), kchunks));
-  }
-}
-
-// Partial dot products of the chunk's kGemvRows rows with the kGemvPairs
-// staged activation rows (u in gemv_slot order, ld floats per row).
-template <int kGemvPairs>
-__device__ __forceinline__ void gemv_chunk(const GemvW& wr, const float* u, int ld, int kc,
-                                           float (&acc)[kGemvRows][kGemvPairs]) {
-  float w[kGemvRows][16];
-  float sc[kGemvRows];
-#pragma unroll
-  for (int r = 0; r < kGemvRows; ++r) {
-    // opaque copies: the decode stays at the point of use instead of being
-    // hoisted out of the pass loop (which would hold every chunk decoded)
-    uint32_t bx, by;
-    asm volatile("mov.b32 %0, %1;" : "=r"(bx) : "r"(wr.b[r].x));
-    asm volatile("mov.b32 %0, %1;" : "=r"(by) : "r"(wr.b[r].y));
-    float lo[8], hi[8];
-    e2m1x8_to_f32(bx, lo);
-    e2m1x8_to_f32(by, hi);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      w[r][q] = lo[q];
-      w[r][8 + q] = hi[q];
-    }
-    sc[r] = e8m0_value(wr.s[r]);
-  }
-  const int base = gemv_slot(kc);
-#pragma unroll
-  for (int i = 0; i < kGemvPairs; ++i) {
-    float xv[16];
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const float4 v = *reinterpret_cast<const float4*>(u + i * ld + base + q * 128);
-      xv[4 * q] = v.x; xv[4 * q + 1] = v.y; xv[4 * q + 2] = v.z; xv[4 * q + 3] = v.w;
-    }
-#pragma unroll
-    for (int r = 0; r < kGemvRows; ++r) {
-      float s = 0.0f;
-#pragma unroll
-      for (int q = 0; q < 16; ++q) s = fmaf(w[r][q], xv[q], s);
-      acc[r][i] = fmaf(s, sc[r], acc[r][i]);
-    }
-  }
-}
-
-// Activation staging: rows i < np of `src` (row r at src_row[i], n columns,
-// n a multiple of 8) into u[i * ld + gemv_slot(c)], scaled per row by
-// row_scale[i] and per column by col_scale (both optional).  Each thread
-// issues four 16-byte loads before it converts and stores anything.
-template <typename T>
-__device__ __forceinline__ void gemv_load8(const T* p, float (&v)[8]);
-template <>
-__device__ __forceinline__ void gemv_load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-  for (int h = 0; h < 4; ++h) {
-    v[2 * h] = __uint_as_float(w[h] << 16);
-    v[2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
-  }
-}
-template <>
-__device__ __forceinline__ void gemv_load8<float>(const float* p, float (&v)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
-template <typename T>
-__device__ __forceinline__ void gemv_stage(float* u, int ld, const T* const* src_row, const float* row_scale,
-                                           const float* __restrict__ col_scale, int np, int n) {
-  const int g8 = n / 8;  // 8-column groups per row
-  const int total = np * g8;
-  for (int g0 = threadIdx.x; g0 < total; g0 += 4 * blockDim.x) {
-    float v[4][8];
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int g = g0 + b * blockDim.x;
-      if (g < total) {
-        const int i = g / g8, c = (g - i * g8) * 8;
-        gemv_load8(src_row[i] + c, v[b]);
-      }
-    }
-#pragma unroll
-    for (int b = 0; b < 4; ++b) {
-      const int g = g0 + b * blockDim.x;
-      if (g < total) {
-        const int i = g / g8, c = (g - i * g8) * 8;
-        float cs[8];
-        if (col_scale) {
-          const float4 a = __ldg(reinterpret_cast<const float4*>(col_scale + c));
-          const float4 bb = __ldg(reinterpret_cast<const float4*>(col_scale + c) + 1);
-          cs[0] = a.x; cs[1] = a.y; cs[2] = a.z; cs[3] = a.w; cs[4] = bb.x; cs[5] = bb.y; cs[6] = bb.z; cs[7] = bb.w;
-        }
-        float* dst = u + i * ld;
-        const float rs = row_scale ? row_scale[i] : 1.0f;
-        // columns c..c+7 lie in one 4-column quad pair of the same 16-column lane chunk
-        float o[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) o[q] = col_scale ? __fmul_rn(__fmul_rn(v[b][q], rs), cs[q]) : v[b][q];
-        *reinterpret_cast<float4*>(dst + gemv_slot(c)) = make_float4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<float4*>(dst + gemv_slot(c + 4)) = make_float4(o[4], o[5], o[6], o[7]);
-      }
-    }
-  }
-}
-
-// W1 + SwiGLU-clamp: block (8 GLU units, expert blockIdx.y), warp = 1 unit
-// (its GLU row and its linear row).  act [rows][fp] f32.
-template <typename XT, int kGemvPairs>
-__global__ void __launch_bounds__(256)
-    gemv_w1_kernel(const XT* __restrict__ x, int d, int k, const float* __restrict__ gamma,
-                   const float* __restrict__ rscale, const uint8_t* __restrict__ w1q, const uint8_t* __restrict__ w1sf,
-                   const float* __restrict__ b1, int fp, int kp1, const int32_t* __restrict__ poff,
-                   const int32_t* __restrict__ counts, const int32_t* __restrict__ perm_p, int pair_k, float alpha,
-                   float limit, float* __restrict__ act) {
-  extern __shared__ __align__(16) float gemv_u[];  // [kGemvPairs][d rounded up to 512], gemv_slot order
-  const int e = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int j = blockIdx.x * 8 + warp;
-  const uint32_t rows = 2u * static_cast<uint32_t>(fp);
-  const uint32_t rb = static_cast<uint32_t>(kp1) / 2, kchunks = static_cast<uint32_t>(kp1) / kTileK;
-  const uint8_t* codes = w1q + static_cast<uint64_t>(e) * rows * rb;
-  const uint8_t* sfa = w1sf + static_cast<uint64_t>(e) * w_sf_row_pairs(rows) * kchunks * kWSfPairBytes;
-  const bool ok = j < fp;
-  const uint32_t rid[kGemvRows] = {w1_packed_row(ok ? j : 0, 0), w1_packed_row(ok ? j : 0, 1)};
-  const uint8_t* rp[kGemvRows];
-#pragma unroll
-  for (int r = 0; r < kGemvRows; ++r) rp[r] = codes + static_cast<uint64_t>(rid[r]) * rb;
-  const int ld = (d + 511) & ~511;  // staged row length (gemv_slot groups of 512)
-  // the warp's rows (at most kGemvChunks * 512 columns, checked by the
-  // launcher) are loaded once, before the activations are staged, and serve
-  // every pass
-  GemvW w0[kGemvChunks];
-  if (ok) {
-#pragma unroll
-    for (int c = 0; c < kGemvChunks; ++c)
-      if (c * 512 + lane * 16 < d) gemv_load(rp, sfa, rid, kchunks, c * 512 + lane * 16, w0[c]);
-  }
-  const int cnt = __ldg(counts + e), p0 = __ldg(poff + e);
-  for (int base = 0; base < cnt; base += kGemvPairs) {
-    const int np = min(kGemvPairs, cnt - base);
-    __syncthreads();  // the previous pass's activations are consumed
-    // rows past np stay stale: they only feed sums that are never stored
-    {
-      const XT* src[kGemvPairs];
-      float rsv[kGemvPairs];
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) {
-        const int t = i < np ? __ldg(perm_p + p0 + base + i) / pair_k : 0;
-        src[i] = x + static_cast<uint64_t>(t) * d;
-        rsv[i] = __ldg(rscale + t);
-      }
-      gemv_stage(gemv_u, ld, src, rsv, gamma, np, d);
-    }
-    __syncthreads();
-    if (!ok) continue;
-    float acc[kGemvRows][kGemvPairs];
-#pragma unroll
-    for (int r = 0; r < kGemvRows; ++r)
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) acc[r][i] = 0.0f;
-#pragma unroll
-    for (int c = 0; c < kGemvChunks; ++c) {
-      const int kc = c * 512 + lane * 16;
-      if (kc < d) gemv_chunk<kGemvPairs>(w0[c], gemv_u, ld, kc, acc);
-    }
-#pragma unroll
-    for (int r = 0; r < kGemvRows; ++r)
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) acc[r][i] = warp_sum_butterfly(acc[r][i]);
-    const float bg = __ldg(b1 + static_cast<uint64_t>(e) * rows + rid[0]);
-    const float bl = __ldg(b1 + static_cast<uint64_t>(e) * rows + rid[1]);
-#pragma unroll
-    for (int i = 0; i < kGemvPairs; ++i) {
-      if (lane == i && i < np) {
-        const float xg = fminf(acc[0][i] + bg, limit);
-        const float xl = fmaxf(-limit, fminf(acc[1][i] + bl, limit));
-        act[static_cast<uint64_t>(p0 + base + i) * fp + j] = (xg / (1.0f + expf(-alpha * xg))) * (xl + 1.0f);
-      }
-    }
-  }
-}
-
-// W2 + bias + route weight: block (16 output columns, expert blockIdx.y),
-// warp = kGemvRows outputs.  y_pair [rows][d] f32.
-template <int kGemvPairs>
-__global__ void __launch_bounds__(256)
-    gemv_w2_kernel(const float* __restrict__ act, int fp, int d, const uint8_t* __restrict__ w2q,
-                   const uint8_t* __restrict__ w2sf, const float* __restrict__ b2, float bias_mult, int kp2,
-                   const int32_t* __restrict__ poff, const int32_t* __restrict__ counts,
-                   const int32_t* __restrict__ perm_p, const float* __restrict__ topk_w, float* __restrict__ y_pair) {
-  extern __shared__ __align__(16) float gemv_a[];  // [kGemvPairs][fp rounded up to 512], gemv_slot order
-  const int e = blockIdx.y;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int c0 = blockIdx.x * 16 + warp * kGemvRows;
-  const uint32_t rb = static_cast<uint32_t>(kp2) / 2, kchunks = static_cast<uint32_t>(kp2) / kTileK;
-  const uint8_t* codes = w2q + static_cast<uint64_t>(e) * d * rb;
-  const uint8_t* sfa = w2sf + static_cast<uint64_t>(e) * w_sf_row_pairs(static_cast<uint32_t>(d)) * kchunks * kWSfPairBytes;
-  const bool ok = c0 < d;
-  uint32_t rid[kGemvRows];
-  const uint8_t* rp[kGemvRows];
-#pragma unroll
-  for (int r = 0; r < kGemvRows; ++r) {
-    rid[r] = static_cast<uint32_t>(min(c0 + r, d - 1));
-    rp[r] = codes + static_cast<uint64_t>(rid[r]) * rb;
-  }
-  const int ld = (fp + 511) & ~511;
-  GemvW w0[kGemvChunks];
-  if (ok) {
-#pragma unroll
-    for (int c = 0; c < kGemvChunks; ++c)
-      if (c * 512 + lane * 16 < fp) gemv_load(rp, sfa, rid, kchunks, c * 512 + lane * 16, w0[c]);
-  }
-  const int cnt = __ldg(counts + e), p0 = __ldg(poff + e);
-  for (int base = 0; base < cnt; base += kGemvPairs) {
-    const int np = min(kGemvPairs, cnt - base);
-    __syncthreads();
-    {
-      const float* src[kGemvPairs];
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) src[i] = act + static_cast<uint64_t>(p0 + base + (i < np ? i : 0)) * fp;
-      gemv_stage<float>(gemv_a, ld, src, nullptr, nullptr, np, fp);
-    }
-    __syncthreads();
-    if (!ok) continue;
-    float acc[kGemvRows][kGemvPairs];
-#pragma unroll
-    for (int r = 0; r < kGemvRows; ++r)
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) acc[r][i] = 0.0f;
-#pragma unroll
-    for (int c = 0; c < kGemvChunks; ++c) {
-      const int kc = c * 512 + lane * 16;
-      if (kc < fp) gemv_chunk<kGemvPairs>(w0[c], gemv_a, ld, kc, acc);
-    }
-#pragma unroll
-    for (int r = 0; r < kGemvRows; ++r)
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) acc[r][i] = warp_sum_butterfly(acc[r][i]);
-#pragma unroll
-    for (int r = 0; r < kGemvRows; ++r) {
-      const int c = c0 + r;
-#pragma unroll
-      for (int i = 0; i < kGemvPairs; ++i) {
-        if (lane == r * kGemvPairs + i && i < np && c < d) {
-          const int pos = p0 + base + i;
-          const float bb = __ldg(b2 + static_cast<uint64_t>(e) * d + c) * bias_mult;
-          y_pair[static_cast<uint64_t>(pos) * d + c] = (acc[r][i] + bb) * __ldg(topk_w + __ldg(perm_p + pos));
-        }
-      }
-    }
-  }
-}
-
 // ------------------------------------------------------------------ launchers
 cudaError_t launch_dequant_bytes(const uint8_t* blocks, uint64_t rows, uint64_t b, const uint8_t* scales, float* out,
                                  cudaStream_t st) {
@@ -1829,12 +1669,29 @@ static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, int k, c
 template <typename XT>
 static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, const float* gamma,
                                    const float* gate_packed, const float* gate_b, float eps, float* logits,
-                                   int32_t* topk_idx, float* topk_w, float* rscale, cudaStream_t st) {
+                                   int32_t* topk_idx, float* topk_w, float* rscale, __half* xh, float xh_scale,
+                                   int* tok_ctr, int* status, int status_words, cudaStream_t st) {
   const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
+  if (tok_ctr != nullptr && n <= kRouterTinyMaxN && d <= 32 * kRouterChunk) {
+    const size_t smem = static_cast<size_t>(d) * sizeof(float) + (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16;
+    const dim3 grid(n, (E + kRouterTinyExperts - 1) / kRouterTinyExperts), block(32 * kRouterTinyExperts);
+    const int nch = (d + kRouterChunk - 1) / kRouterChunk;
+    auto go = [&](auto fn) -> cudaError_t {
+      const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+      if (ce != cudaSuccess) return ce;
+      return launch_kernel(fn, grid, block, smem, st, x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx,
+                           topk_w, rscale, aligned, xh, xh_scale, tok_ctr, status, status_words);
+    };
+    if (nch <= 8) return go(router_tiny_kernel<XT, 8>);
+    if (nch <= 16) return go(router_tiny_kernel<XT, 16>);
+    if (nch <= 24) return go(router_tiny_kernel<XT, 24>);
+    return go(router_tiny_kernel<XT, 32>);
+  }
   if (n <= kRouterSmallMaxN && E <= kRouterGroup && d <= kRouterSmallMaxD) {
     const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float) +
-                        (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16;
-    ensure_dynamic_smem(reinterpret_cast<const void*>(router_small_kernel<XT>), smem);
+                        (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16 + static_cast<size_t>(d) * sizeof(float);
+    const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(router_small_kernel<XT>), smem);
+    if (ce != cudaSuccess) return ce;
     // one warp per expert, and at least 8 warps to stage and normalize the row
     return launch_kernel(router_small_kernel<XT>, dim3(n), dim3(32 * (E < 8 ? 8 : E)), smem, st,
                          x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx, topk_w, rscale, aligned);
@@ -1860,12 +1717,15 @@ static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, cons
 
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
-                          float* topk_w, float* rscale, cudaStream_t st) {
+                          float* topk_w, float* rscale, cudaStream_t st, __half* xh, float xh_scale, int* tok_ctr,
+                          int* status, int status_words) {
   if (n == 0) return cudaSuccess;
   return x_dtype == 0 ? launch_router_x(static_cast<const float*>(x), n, d, E, k, gamma, gate_packed, gate_b, eps,
-                                        logits, topk_idx, topk_w, rscale, st)
+                                        logits, topk_idx, topk_w, rscale, xh, xh_scale, tok_ctr, status, status_words,
+                                        st)
                       : launch_router_x(static_cast<const __nv_bfloat16*>(x), n, d, E, k, gamma, gate_packed, gate_b,
-                                        eps, logits, topk_idx, topk_w, rscale, st);
+                                        eps, logits, topk_idx, topk_w, rscale, xh, xh_scale, tok_ctr, status,
+                                        status_words, st);
 }
 
 size_t permute_scratch_ints(int P, int E) {
@@ -2031,66 +1891,6 @@ cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_
   return cudaGetLastError();
 }
 
-template <int PB>
-static void gemv_w1_pb(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
-                       const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
-                       const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
-                       float* act, cudaStream_t st) {
-  const dim3 grid((fp + 7) / 8, E);
-  const size_t smem = static_cast<size_t>(PB) * ((d + 511) & ~511) * sizeof(float);
-  if (x_dtype == 0) {
-    ensure_dynamic_smem(reinterpret_cast<const void*>(gemv_w1_kernel<float, PB>), smem);
-    gemv_w1_kernel<float, PB><<<grid, 256, smem, st>>>(static_cast<const float*>(x), d, k, gamma, rscale, w1q, w1sf,
-                                                       b1, fp, kp1, poff, counts, perm_p, k, alpha, limit, act);
-  } else {
-    ensure_dynamic_smem(reinterpret_cast<const void*>(gemv_w1_kernel<__nv_bfloat16, PB>), smem);
-    gemv_w1_kernel<__nv_bfloat16, PB><<<grid, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(x), d, k, gamma,
-                                                               rscale, w1q, w1sf, b1, fp, kp1, poff, counts, perm_p,
-                                                               k, alpha, limit, act);
-  }
-}
-
-template <int PB>
-static void gemv_w2_pb(const float* act, int fp, int d, const uint8_t* w2q, const uint8_t* w2sf, const float* b2,
-                       float bias_mult, int kp2, int E, const int32_t* poff, const int32_t* counts,
-                       const int32_t* perm_p, const float* topk_w, float* y_pair, cudaStream_t st) {
-  const dim3 grid((d + 15) / 16, E);
-  const size_t smem = static_cast<size_t>(PB) * ((fp + 511) & ~511) * sizeof(float);
-  ensure_dynamic_smem(reinterpret_cast<const void*>(gemv_w2_kernel<PB>), smem);
-  gemv_w2_kernel<PB><<<grid, 256, smem, st>>>(act, fp, d, w2q, w2sf, b2, bias_mult, kp2, poff, counts, perm_p,
-                                              topk_w, y_pair);
-}
-
-// pairs per pass: the smallest of 1, 2, 4, 8 covering max_pairs (an upper
-// bound of any expert's count), so small batches do no padded work
-cudaError_t launch_gemv_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
-                           const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
-                           const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
-                           float* act, int max_pairs, cudaStream_t st) {
-  if (max_pairs <= 1)
-    gemv_w1_pb<1>(x, x_dtype, d, k, gamma, rscale, w1q, w1sf, b1, fp, kp1, E, poff, counts, perm_p, alpha, limit, act, st);
-  else if (max_pairs <= 2)
-    gemv_w1_pb<2>(x, x_dtype, d, k, gamma, rscale, w1q, w1sf, b1, fp, kp1, E, poff, counts, perm_p, alpha, limit, act, st);
-  else if (max_pairs <= 4)
-    gemv_w1_pb<4>(x, x_dtype, d, k, gamma, rscale, w1q, w1sf, b1, fp, kp1, E, poff, counts, perm_p, alpha, limit, act, st);
-  else
-    gemv_w1_pb<8>(x, x_dtype, d, k, gamma, rscale, w1q, w1sf, b1, fp, kp1, E, poff, counts, perm_p, alpha, limit, act, st);
-  return cudaGetLastError();
-}
-
-cudaError_t launch_gemv_w2(const float* act, int fp, int d, const uint8_t* w2q, const uint8_t* w2sf, const float* b2,
-                           float bias_mult, int kp2, int E, const int32_t* poff, const int32_t* counts,
-                           const int32_t* perm_p, const float* topk_w, float* y_pair, int max_pairs, cudaStream_t st) {
-  if (max_pairs <= 1)
-    gemv_w2_pb<1>(act, fp, d, w2q, w2sf, b2, bias_mult, kp2, E, poff, counts, perm_p, topk_w, y_pair, st);
-  else if (max_pairs <= 2)
-    gemv_w2_pb<2>(act, fp, d, w2q, w2sf, b2, bias_mult, kp2, E, poff, counts, perm_p, topk_w, y_pair, st);
-  else if (max_pairs <= 4)
-    gemv_w2_pb<4>(act, fp, d, w2q, w2sf, b2, bias_mult, kp2, E, poff, counts, perm_p, topk_w, y_pair, st);
-  else
-    gemv_w2_pb<8>(act, fp, d, w2q, w2sf, b2, bias_mult, kp2, E, poff, counts, perm_p, topk_w, y_pair, st);
-  return cudaGetLastError();
-}
 
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
                            const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,

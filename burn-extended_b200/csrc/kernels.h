@@ -1,5 +1,6 @@
 // kernels.h -- launchers of the CUDA-core kernels (kernels.cu).
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <cstdint>
 
@@ -36,9 +37,13 @@ inline void pack_router_gate(const float* w, int E, int d, float* out) {
 
 // gate_packed: pack_router_gate layout.  Small batches (n <= 512, E <= 32)
 // run as one launch (RmsNorm + logits + top-k), larger ones as two or three.
+// With tok_ctr ([n] ints, zero; the kernel leaves them zero) batches of at
+// most 8 tokens run on many blocks per token (router_tiny_kernel), which
+// also zeroes status[0 .. status_words) when status is given.
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
-                          float* topk_w, float* rscale, cudaStream_t st);
+                          float* topk_w, float* rscale, cudaStream_t st, __half* xh = nullptr, float xh_scale = 1.0f,
+                          int* tok_ctr = nullptr, int* status = nullptr, int status_words = 0);
 // Canonical permutation.  With scratch (permute_scratch_ints(P, E) int32,
 // zeroed once before first use) and P >= kPermMultiBlockMin it runs on many
 // blocks; otherwise on one block with no scratch.
@@ -92,16 +97,56 @@ cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t*
 cudaError_t launch_iota(int32_t* a, int n, cudaStream_t st);
 cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
                               uint32_t* slot, cudaStream_t st);
-// Fused dequant-GEMV expert FFN for a few pairs per expert (f32 act / y_pair);
-// d and the padded ffn width must be at most kGemvMaxK.
-constexpr int kGemvMaxK = 4096;
-cudaError_t launch_gemv_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
-                           const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
-                           const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,
-                           float* act, int max_pairs, cudaStream_t st);
-cudaError_t launch_gemv_w2(const float* act, int fp, int d, const uint8_t* w2q, const uint8_t* w2sf, const float* b2,
-                           float bias_mult, int kp2, int E, const int32_t* poff, const int32_t* counts,
-                           const int32_t* perm_p, const float* topk_w, float* y_pair, int max_pairs, cudaStream_t st);
+// Fused dequant-GEMV expert FFN for a few pairs per expert (dqgemv.cu):
+// W1 + SwiGLU-clamp + W2 + bias + route weight in one launch.  d is a
+// multiple of 32, fp of 64, both at most kDqMaxK.
+constexpr int kDqMaxK = 4096;
+constexpr int kDqSrcF32 = 0, kDqSrcBf16 = 1, kDqSrcF16 = 2;
+struct DqParams {
+  int d, fp, kp1, kp2;     // kp: padded row length (codes kp / 2 bytes per row)
+  const uint8_t* w1q;      // [E][2 fp][kp1 / 2], GLU / linear rows in 64-row blocks
+  const uint8_t* w1sr;     // [E][2 fp][sr1] E8M0 scales, row-major copy
+  uint32_t sr1;            // scale row stride (kp1 / 32 rounded up to 16)
+  const float* b1;         // [E][2 fp] packed row order
+  const uint8_t* w2q;      // [E][d][kp2 / 2]
+  const uint8_t* w2sr;     // [E][d][sr2]
+  uint32_t sr2;
+  const float* b2;         // [E][d]
+  float bias_mult;
+  int E;
+  const int32_t* poff;     // [E] first pair position of each expert
+  const int32_t* counts;   // [E]
+  const int32_t* perm;     // [pairs] position -> canonical pair t * k + s
+  const int32_t* topk_idx; // [P] canonical expert ids (fused mode, P <= 64)
+  int P;
+  int pair_k;
+  const __half* xh;        // [n][d] normalized token rows * x_scale as f16 (router output), or null
+  const void* x;           // [n][d] token rows (staged from here when xh is null)
+  int x_dtype;             // kDqSrcF32 / kDqSrcBf16
+  const float* gamma;      // [d] RmsNorm gain
+  const float* rscale;     // [n] 1 / rms
+  float x_scale, inv_x_scale;      // power of two on the staged f16 token rows
+  float alpha, limit;
+  float act_scale, inv_act_scale;  // power of two on the f16 SwiGLU rows
+  __half* act;             // [pairs][fp] SwiGLU rows (W1 -> W2)
+  float* y_pair;           // [pairs][d] f32
+  const float* topk_w;     // [pairs] canonical route weights
+  int fused;               // pairs from topk_idx, act / y_pair rows by canonical pair, combine here
+  int n_tok;               // fused: tokens
+  int residual;            // fused: y = x + moe(x)
+  void* y;                 // fused: [n][d] layer output
+  int y_dtype;             // fused: kDqSrcF32 / kDqSrcBf16
+  int32_t* offsets;        // fused: canonical maps written for the caller ([E + 1], [P], [P])
+  int32_t* perm_c;
+  int32_t* inv_c;
+  int* done;               // fused: finished-block counter, zero at launch
+  int* err;                // status word
+  int* sync;               // [E] per-expert arrival counters, zero at launch
+  int ps;                  // pairs staged per pass (shared memory: ps * 2 KB per 1024 columns)
+  uint32_t stage_bytes;    // set by the launcher
+};
+cudaError_t launch_dqgemv_ffn(DqParams a, int max_pairs_per_expert, int max_experts, int num_sms, size_t smem_limit,
+                              cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
                            const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
                            const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,

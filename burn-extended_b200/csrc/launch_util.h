@@ -61,6 +61,16 @@ inline cudaError_t launch_kernel(void (*kernel)(KArgs...), dim3 grid, dim3 block
 // Waits until the kernels this one depends on have completed and their
 // writes are visible (returns at once for a plain launch).
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Lets the next kernel of the chain launch before this one completes.
+// Invariant of every chain here: a kernel calls this only after its own
+// griddep_wait().  So when a dependent starts, every kernel two or more
+// launches back has completed and its writes are visible, and the dependent
+// may read those before its own wait (the tensor-core GEMM reads the tile
+// prefix sums of the permutation there, the W2 dequant-GEMV the pair counts).
+// Only what the immediately preceding kernel writes needs the wait.
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 #endif
 
 }  // namespace mxmoe

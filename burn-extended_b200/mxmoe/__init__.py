@@ -18,7 +18,7 @@ from typing import Optional
 
 import numpy as np
 
-from ._lib import (BF16, F32, FLAG_BIAS_PER_FTILE, FLAG_DISABLED, FLAG_INTERLEAVED_GLU, FLAG_NO_FP4,
+from ._lib import (BF16, F32, FLAG_BIAS_PER_FTILE, FLAG_DISABLED, FLAG_INTERLEAVED_GLU, FLAG_NO_FP4, FLAG_NO_GEMV,
                    FLAG_NO_RESIDUAL, FLAG_SIMT, Config, MxMoeError, QuantDesc, check, exported_symbols, last_error, lib)
 
 __all__ = [
@@ -95,6 +95,7 @@ class MoeConfig:
     residual: bool = True
     simt: bool = False
     fp4_decode: bool = True  # kind::mxf4 tiles for decode batches (FLAG_NO_FP4 when False)
+    gemv_decode: bool = True  # CUDA-core dequant-GEMV for tiny batches (FLAG_NO_GEMV when False)
 
     def flags(self) -> int:
         f = 0
@@ -110,6 +111,8 @@ class MoeConfig:
             f |= FLAG_SIMT
         if not self.fp4_decode:
             f |= FLAG_NO_FP4
+        if not self.gemv_decode:
+            f |= FLAG_NO_GEMV
         return f
 
     def init(self, device: int = 0) -> "MoeGatedSwiGLU":

@@ -22,6 +22,7 @@ FLAG_DISABLED = 0x8
 FLAG_SIMT = 0x10
 FLAG_NO_GRAPHS = 0x20
 FLAG_NO_FP4 = 0x40
+FLAG_NO_GEMV = 0x80
 
 
 class MxMoeError(RuntimeError):

@@ -71,6 +71,10 @@ typedef enum mxmoe_dtype {
                                             tensor-core tiles instead of the
                                             kind::mxf4 tiles with a four-term
                                             E2M1 activation */
+#define MXMOE_FLAG_NO_GEMV         0x80u /* never run tiny batches (at most 64
+                                            routed pairs) on the CUDA-core
+                                            dequant-GEMV; they take the
+                                            tensor-core tiles like any other */
 
 /* Mirrors moe::MoeConfig (src/moe/mod.rs:22-33).  `initializer` and `verbose`
  * have no device meaning; swiglu_alpha / swiglu_limit are honoured (the

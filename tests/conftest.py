@@ -28,3 +28,16 @@ def pytest_collection_modifyitems(config, items):
     for item in items:
         if "gpu" in item.keywords:
             item.add_marker(skip)
+
+
+def pytest_terminal_summary(terminalreporter, exitstatus, config):
+    try:
+        from moe_testutil import MAX_ABS_TOL, MARGINS, REL_L2_TOL
+    except Exception:
+        return
+    if not MARGINS:
+        return
+    tr = terminalreporter
+    tr.write_sep("-", f"layer output margins (bounds: max_abs {MAX_ABS_TOL:g}, rel_l2 {REL_L2_TOL:g})")
+    for tag, max_abs, rel in MARGINS:
+        tr.write_line(f"{tag:<60s} max_abs {max_abs:.3e}  rel_l2 {rel:.3e}")

@@ -22,8 +22,14 @@ def errors(y, ref):
     return float(max_abs), float(rel)
 
 
+# (tag, max_abs, rel_l2) of every layer comparison in this session; conftest
+# prints them at the end so the margin to the bounds is visible.
+MARGINS = []
+
+
 def assert_close(y, ref, tag=""):
     max_abs, rel = errors(y, ref)
+    MARGINS.append((tag, max_abs, rel))
     assert max_abs <= MAX_ABS_TOL and rel <= REL_L2_TOL, f"{tag}: max_abs={max_abs:.3e} rel_l2={rel:.3e}"
     return max_abs, rel
 

@@ -11,10 +11,13 @@ from mxmoe.ep import CudaExpertBackend, shard_bounds
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_sharded_layers_match_full_layer(world):
+@pytest.mark.parametrize("world,n", [(2, 200), (4, 200), (2, 1), (4, 1)])
+def test_sharded_layers_match_full_layer(world, n):
+    """n = 1: every shard runs at most four routed pairs through the
+    dequant-GEMV's non-fused mode (permutation maps in, y_pair rows out),
+    the full layer through its fused mode."""
     import torch
-    inp = synth.make_inputs(1024, 512, 8, 4, 200, True, seed=21)
+    inp = synth.make_inputs(1024, 512, 8, 4, n, True, seed=21)
     full = make_layer(inp)
     x = to_device_x(inp)
     y_full = full.forward(x, out_dtype=torch.float32)
