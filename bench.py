@@ -132,7 +132,7 @@ def run_reference(args, world, rank):
     from mxmoe import synth
     inp = synth.make_config("prefill", seed=args.seed)
     sample = args.ref_sample
-    for _ in range(args.warmup if args.warmup < 1 else 1):
+    for _ in range(args.warmup):
         cpu_reference(inp, sample)
     times = [cpu_reference(inp, sample) for _ in range(args.steps)]
     total = sum(times)
@@ -204,6 +204,57 @@ def measure_decode(args, local, dev, hbm_peak):
                             "traffic": W1_DECODE_TRAFFIC},
             "clocks": dec_clocks,
             "l2": "weights of the 32 experts (423 MB) exceed the 126 MB L2; no flush"}
+
+
+def measure_decode_batches(args, local, dev, hbm_peak):
+    """Small-batch decode of the GPT-OSS-20B-shaped layer (32 experts, top-4)
+    at 1, 2, 4, 8 and 16 tokens through the default dispatch (the fused
+    dequant-GEMV kernel up to 4 routed pairs, the kind::mxf4 tensor-core tiles
+    above).  GB/s = bytes of the experts the batch touches (codes, scales,
+    biases) plus router weights and x / y, per layer forward.  The weights
+    (423 MB) exceed the 126 MB L2, and consecutive forwards use different
+    tokens and so different experts."""
+    import torch
+    import mxmoe
+    from mxmoe import synth
+    d = f = 2880
+    per_expert = 2 * f * d // 2 + 2 * f * d // 32 + d * f // 2 + d * f // 32 + 2 * (2 * f + d)
+    base = synth.make_config("decode", seed=args.seed + 3)
+    L = mxmoe.MoeConfig(base.d, base.f, base.E, base.k).init(local)
+    L.set_router(base.gamma, base.gate_w, base.gate_b)
+    L.set_resident(base.host, base.b1, base.b2)
+    L.reserve(16)
+    out = {}
+    for n in (1, 2, 4, 8, 16):
+        # 32 different token batches in rotation: the touched experts change
+        xs = [torch.from_numpy(synth.rank_tokens(base, r, args.seed).x[:n]).to(torch.bfloat16).to(dev)
+              for r in range(32)]
+        touched = []
+        for xi in xs:
+            L.forward(xi)
+            rr = L.routing_results(n)
+            touched.append(int((np.diff(rr["offsets"].cpu().numpy()) > 0).sum()))
+        for _ in range(3):
+            for xi in xs:
+                L.forward(xi)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        calls = max(args.steps, 1) * len(xs)
+        s.record()
+        for i in range(calls):
+            L.forward(xs[i % len(xs)])
+        e.record()
+        torch.cuda.synchronize()
+        us = s.elapsed_time(e) / calls * 1e3
+        nbytes = float(np.mean(touched)) * per_expert + 2 * base.E * d + base.E * 2 + 2 * n * d * 2
+        out[f"n{n}"] = {"us_per_layer": us, "tokens_per_s": n / (us / 1e6), "experts_touched": float(np.mean(touched)),
+                        "bytes": nbytes, "gbs": nbytes / (us / 1e6) / 1e9,
+                        "hbm_frac": nbytes / (us / 1e6) / 1e9 / hbm_peak,
+                        "x_touched_bytes_at_peak": us / (nbytes / (hbm_peak * 1e9) * 1e6),
+                        "path": "dequant-GEMV (fused)" if n * base.k <= 4 else "kind::mxf4 tensor-core tiles"}
+    L.close()
+    return {"config": "gptoss20b_moe_decode at batch 1..16 (32 experts, top-4), bf16 x, default dispatch",
+            "rotation": "32 token batches per n (different experts each)", **out}
 
 
 def measure_microbench(args, local, dev, hbm_peak):
@@ -310,6 +361,9 @@ def run_ours(args, world, rank, local):
     if args.only == "microbench":
         print(json.dumps({"microbench": measure_microbench(args, local, dev, hbm_peak)}), flush=True)
         return
+    if args.only == "decode_batches":
+        print(json.dumps({"decode_batches": measure_decode_batches(args, local, dev, hbm_peak)}), flush=True)
+        return
     if args.only == "gptoss120b":
         print(json.dumps({"gptoss120b": measure_120b(args, local, dev)}), flush=True)
         return
@@ -414,9 +468,16 @@ def run_ours(args, world, rank, local):
     w2_flops = 2.0 * P * d * f
     t_w1 = stages["w1_gemm"] / 1e3
     achieved = w1_flops / t_w1 / 1e12
+    # W1 is timed alone (CUDA events around its launch inside a 1.5 ms step),
+    # so the denominator is the burst bf16 peak; the two-term E4M3 x E2M1 MMA
+    # pair issues at the bf16-equivalent rate.  North star's MXF4 target is
+    # also reported: MXF4 dense is 4x bf16 dense (9 vs 2.25 PFLOP/s nominal),
+    # applied to the measured bf16 burst.
     roofline = {"bound": "tensor", "kernel": "tc_moe_gemm_kernel (W1 + SwiGLU)", "achieved": achieved,
-                "peak": tc_sust, "unit": "TFLOP/s", "frac": achieved / tc_sust,
-                "peak_source": f"{peak_src} bf16 sustained (the 2-term E4M3 x E2M1 MMA pair issues at the bf16-equivalent rate)",
+                "peak": tc_burst, "unit": "TFLOP/s", "frac": achieved / tc_burst,
+                "peak_source": f"{peak_src} bf16 burst (kernel timed alone)",
+                "frac_of_mxf4_peak": achieved / (4.0 * tc_burst),
+                "mxf4_peak_source": f"4 x {peak_src} bf16 burst (nominal MXF4 : bf16 dense = 9 : 2.25)",
                 "traffic": W1_PREFILL_TRAFFIC, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
                 "of one W1 launch (profiles/tc_moe_gemm_prefill_gptoss20b.txt)",
                 "flops_per_launch": w1_flops}
@@ -442,6 +503,7 @@ def run_ours(args, world, rank, local):
 
     extra["decode"] = measure_decode(args, local, dev, hbm_peak)
     if args.only == "all":
+        extra["decode_batches"] = measure_decode_batches(args, local, dev, hbm_peak)
         extra["microbench"] = measure_microbench(args, local, dev, hbm_peak)
         extra["gptoss120b"] = measure_120b(args, local, dev)
 
@@ -479,7 +541,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=24)
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["all", "prefill", "decode", "microbench", "gptoss120b"], default="all",
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "decode_batches", "microbench", "gptoss120b"],
+                    default="all",
                     help="run only that leg (profiling runs); 'all' adds decode, microbench and gptoss120b as extras")
     args = ap.parse_args()
     world, rank, local = dist_setup(args.gpus)

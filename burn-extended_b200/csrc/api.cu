@@ -127,6 +127,11 @@ uint32_t dq_scale_row_bytes(uint32_t kp) { return round_up(kp / 32u, 16u); }
 constexpr int kStatusSyncOffset = 16;
 constexpr int kStatusDoneWord = 1;  // dequant-GEMV fused mode: finished-block counter
 
+// mxmoe_forward_host splits large batches into up to this many chunks so
+// that the copies of one chunk overlap the forward of another.
+constexpr int kHostChunksMax = 4;
+constexpr uint32_t kHostChunkMinTokens = 1024;
+
 // The dequant-GEMV takes forwards of at most this many routed pairs (so at
 // most this many tokens); the router then also writes their normalized f16
 // rows for it.
@@ -269,6 +274,16 @@ struct mxmoe_layer {
     bool failed = false;  // capture failed for this key: run directly
   } graph;
   cudaStream_t cap_stream = nullptr;  // capture happens here; replays go to the caller's stream
+  // mxmoe_forward_host: device copies of the host rows, copy streams and
+  // per-chunk events and status words (this layer's device only)
+  struct HostStaging {
+    void* dx = nullptr;
+    void* dy = nullptr;
+    size_t cx = 0, cy = 0;
+    cudaStream_t s_in = nullptr, s_out = nullptr;
+    cudaEvent_t ev_in[kHostChunksMax] = {}, ev_done[kHostChunksMax] = {};
+    int* status = nullptr;  // pinned host, one word per chunk
+  } hs;
   // expert parallelism over peer memory: the workspace is shared with peers and must not move
   bool ep_reserved = false;
   uint32_t ep_world = 0, ep_max_tokens = 0;
@@ -859,6 +874,18 @@ int mxmoe_destroy(mxmoe_layer* L) {
     if (e) cudaEventDestroy(e);
   if (L->graph.exec) cudaGraphExecDestroy(L->graph.exec);
   if (L->cap_stream) cudaStreamDestroy(L->cap_stream);
+  {
+    auto& h = L->hs;
+    if (h.dx) cudaFree(h.dx);
+    if (h.dy) cudaFree(h.dy);
+    if (h.s_in) cudaStreamDestroy(h.s_in);
+    if (h.s_out) cudaStreamDestroy(h.s_out);
+    for (int i = 0; i < kHostChunksMax; ++i) {
+      if (h.ev_in[i]) cudaEventDestroy(h.ev_in[i]);
+      if (h.ev_done[i]) cudaEventDestroy(h.ev_done[i]);
+    }
+    if (h.status) cudaFreeHost(h.status);
+  }
   delete L;
   return MXMOE_OK;
 }
@@ -1140,35 +1167,81 @@ int mxmoe_forward_host(mxmoe_layer* L, const void* x_host, mxmoe_dtype x_dtype, 
   TRY(check_layer(L));
   if (n_tokens == 0) return MXMOE_OK;
   if (!x_host || !y_host) return fail(MXMOE_ERR_INVALID_ARG, "null host buffer");
+  if ((x_dtype != MXMOE_F32 && x_dtype != MXMOE_BF16) || (y_dtype != MXMOE_F32 && y_dtype != MXMOE_BF16))
+    return fail(MXMOE_ERR_INVALID_ARG, "bad dtype");
   DeviceGuard g(L->cfg.device);
   cudaStream_t st = as_stream(stream);
-  const size_t xb = static_cast<size_t>(n_tokens) * L->d * (x_dtype == MXMOE_F32 ? 4 : 2);
-  const size_t yb = static_cast<size_t>(n_tokens) * L->d * (y_dtype == MXMOE_F32 ? 4 : 2);
+  const size_t xrow = static_cast<size_t>(L->d) * (x_dtype == MXMOE_F32 ? 4 : 2);
+  const size_t yrow = static_cast<size_t>(L->d) * (y_dtype == MXMOE_F32 ? 4 : 2);
+  const size_t xb = n_tokens * xrow, yb = n_tokens * yrow;
   TRY(ensure_workspace(L, n_tokens, L->k));
-  // Staging buffers for the host call live in the workspace's activation-code
-  // area only if it is large enough; otherwise dedicated buffers are kept.
-  static thread_local void* dx = nullptr;
-  static thread_local void* dy = nullptr;
-  static thread_local size_t cx = 0, cy = 0;
-  if (cx < xb) {
-    if (dx) cudaFree(dx);
-    dx = nullptr;
-    CUDA_TRY(cudaMalloc(&dx, xb));
-    cx = xb;
+  auto& h = L->hs;
+  if (!h.s_in) {
+    CUDA_TRY(cudaStreamCreateWithFlags(&h.s_in, cudaStreamNonBlocking));
+    CUDA_TRY(cudaStreamCreateWithFlags(&h.s_out, cudaStreamNonBlocking));
+    for (int i = 0; i < kHostChunksMax; ++i) {
+      CUDA_TRY(cudaEventCreateWithFlags(&h.ev_in[i], cudaEventDisableTiming));
+      CUDA_TRY(cudaEventCreateWithFlags(&h.ev_done[i], cudaEventDisableTiming));
+    }
+    CUDA_TRY(cudaMallocHost(&h.status, kHostChunksMax * sizeof(int)));
   }
-  if (cy < yb) {
-    if (dy) cudaFree(dy);
-    dy = nullptr;
-    CUDA_TRY(cudaMalloc(&dy, yb));
-    cy = yb;
+  if (h.cx < xb) {
+    if (h.dx) cudaFree(h.dx);
+    h.dx = nullptr;
+    h.cx = 0;
+    CUDA_TRY(cudaMalloc(&h.dx, xb));
+    h.cx = xb;
   }
-  CUDA_TRY(cudaMemcpyAsync(dx, x_host, xb, cudaMemcpyHostToDevice, st));
-  TRY(mxmoe_forward(L, dx, x_dtype, dy, y_dtype, n_tokens, stream));
-  CUDA_TRY(cudaMemcpyAsync(y_host, dy, yb, cudaMemcpyDeviceToHost, st));
+  if (h.cy < yb) {
+    if (h.dy) cudaFree(h.dy);
+    h.dy = nullptr;
+    h.cy = 0;
+    CUDA_TRY(cudaMalloc(&h.dy, yb));
+    h.cy = yb;
+  }
+  // Chunks of whole 128-token blocks: chunk i's host->device copy runs on
+  // s_in, its forward on the caller's stream, its device->host copy on s_out,
+  // so the copies of neighbouring chunks overlap each forward.  The first
+  // and last chunks are small (an eighth of the batch each), since nothing
+  // overlaps the first copy in or the last copy out; the middle two carry
+  // the rest.
+  uint32_t bounds[kHostChunksMax + 1] = {0};
+  uint32_t chunks = 1;
+  bounds[1] = n_tokens;
+  if (n_tokens >= 4 * kHostChunkMinTokens) {
+    const uint32_t edge = round_up(n_tokens / 8, 128), mid = round_up((n_tokens - 2 * edge) / 2, 128);
+    chunks = 4;
+    bounds[1] = edge;
+    bounds[2] = edge + mid;
+    bounds[3] = n_tokens - edge;
+    bounds[4] = n_tokens;
+  } else if (n_tokens >= 2 * kHostChunkMinTokens) {
+    chunks = 2;
+    bounds[1] = round_up(n_tokens / 2, 128);
+    bounds[2] = n_tokens;
+  }
+  for (uint32_t i = 0; i < chunks; ++i) h.status[i] = 0;
+  uint32_t used = 0;
+  for (uint32_t i = 0; i < chunks && bounds[i] < bounds[i + 1]; ++i, ++used) {
+    const uint32_t t0 = bounds[i], nt = bounds[i + 1] - bounds[i];
+    char* dxi = static_cast<char*>(h.dx) + t0 * xrow;
+    char* dyi = static_cast<char*>(h.dy) + t0 * yrow;
+    CUDA_TRY(cudaMemcpyAsync(dxi, static_cast<const char*>(x_host) + t0 * xrow, nt * xrow, cudaMemcpyHostToDevice,
+                             h.s_in));
+    CUDA_TRY(cudaEventRecord(h.ev_in[i], h.s_in));
+    CUDA_TRY(cudaStreamWaitEvent(st, h.ev_in[i], 0));
+    TRY(mxmoe_forward(L, dxi, x_dtype, dyi, y_dtype, nt, st));
+    // each forward resets the status word: keep this chunk's
+    CUDA_TRY(cudaMemcpyAsync(&h.status[i], L->err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CUDA_TRY(cudaEventRecord(h.ev_done[i], st));
+    CUDA_TRY(cudaStreamWaitEvent(h.s_out, h.ev_done[i], 0));
+    CUDA_TRY(cudaMemcpyAsync(static_cast<char*>(y_host) + t0 * yrow, dyi, nt * yrow, cudaMemcpyDeviceToHost, h.s_out));
+  }
+  CUDA_TRY(cudaStreamSynchronize(h.s_out));
   CUDA_TRY(cudaStreamSynchronize(st));
-  int herr = 0;
-  CUDA_TRY(cudaMemcpy(&herr, L->err, sizeof(int), cudaMemcpyDeviceToHost));
-  return device_status(herr);
+  for (uint32_t i = 0; i < used; ++i)
+    if (h.status[i] != 0) return device_status(h.status[i]);
+  return MXMOE_OK;
 }
 
 int mxmoe_sync_status(mxmoe_layer* L, void* stream) {

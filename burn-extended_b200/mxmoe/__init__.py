@@ -32,9 +32,9 @@ def _torch():
     return torch
 
 
-def _stream_ptr(stream=None) -> int:
+def _stream_ptr(stream=None, device=None) -> int:
     torch = _torch()
-    s = stream if stream is not None else torch.cuda.current_stream()
+    s = stream if stream is not None else torch.cuda.current_stream(device)
     return s.cuda_stream
 
 
@@ -188,7 +188,7 @@ class MoeGatedSwiGLU:
         else:
             y = torch.empty(xc.shape, dtype=out_dtype or xc.dtype, device=xc.device)
         check(lib().mxmoe_forward(self._h, xc.data_ptr(), _dtype_code(xc), y.data_ptr(), _dtype_code(y), n,
-                                  _stream_ptr(stream)))
+                                  _stream_ptr(stream, self.device)))
         return y
 
     def forward_host(self, x_host, y_host, stream=None):
@@ -200,7 +200,7 @@ class MoeGatedSwiGLU:
         yd = _dtype_code(y_host) if hasattr(y_host, "data_ptr") else (F32 if y_host.dtype == np.float32 else BF16)
         xp = x_host.data_ptr() if hasattr(x_host, "data_ptr") else x_host.ctypes.data
         yp = y_host.data_ptr() if hasattr(y_host, "data_ptr") else y_host.ctypes.data
-        check(lib().mxmoe_forward_host(self._h, xp, xd, yp, yd, n, _stream_ptr(stream)))
+        check(lib().mxmoe_forward_host(self._h, xp, xd, yp, yd, n, _stream_ptr(stream, self.device)))
 
     STAGES = ("router", "permute", "quantize", "w1_gemm", "w2_gemm", "combine")
 
@@ -215,7 +215,7 @@ class MoeGatedSwiGLU:
         return {name: float(arr[i]) for i, name in enumerate(self.STAGES[:cnt.value])}
 
     def sync_status(self, stream=None):
-        check(lib().mxmoe_sync_status(self._h, _stream_ptr(stream)))
+        check(lib().mxmoe_sync_status(self._h, _stream_ptr(stream, self.device)))
 
     def routing_results(self, n_tokens: int) -> dict:
         """Copies of the last forward's routing tensors (for parity checks)."""
@@ -240,7 +240,7 @@ class MoeGatedSwiGLU:
         n = x.numel() // self.cfg.d_model
         ptr = lambda t: t.data_ptr() if t is not None else None
         check(lib().mxmoe_route(self._h, x.data_ptr(), _dtype_code(x), n, rscale.data_ptr(), topk_idx.data_ptr(),
-                                topk_w.data_ptr(), ptr(offsets), ptr(perm), ptr(inv), _stream_ptr(stream)))
+                                topk_w.data_ptr(), ptr(offsets), ptr(perm), ptr(inv), _stream_ptr(stream, self.device)))
 
     def forward_local(self, xr, rscale, expert, weight, out, stream=None):
         """Expert FFN of this layer's shard for dispatched pairs (out: f32 or bf16)."""
@@ -249,7 +249,7 @@ class MoeGatedSwiGLU:
             return
         check(lib().mxmoe_forward_local(self._h, xr.data_ptr(), _dtype_code(xr), rscale.data_ptr(),
                                         expert.data_ptr(), weight.data_ptr(), n, out.data_ptr(), _dtype_code(out),
-                                        _stream_ptr(stream)))
+                                        _stream_ptr(stream, self.device)))
 
     def close(self):
         if getattr(self, "_h", None) is not None and self._h.value:

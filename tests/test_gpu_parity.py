@@ -315,6 +315,44 @@ def test_forward_host_matches_device(torch):
     layer.close()
 
 
+def test_forward_host_chunked_matches_device(torch):
+    # 4096 tokens: four chunks whose copies overlap the neighbouring forwards
+    inp = synth.make_inputs(1024, 512, 8, 4, 4096, True, seed=8)
+    layer = make_layer(inp)
+    x = to_device_x(inp)
+    yd = layer.forward(x, out_dtype=torch.float32)
+    xh = x.cpu().pin_memory()
+    yh = torch.empty(xh.shape, dtype=torch.float32).pin_memory()
+    layer.forward_host(xh, yh)
+    assert torch.equal(yh, yd.cpu())
+    layer.close()
+
+
+def _gpu_count():
+    try:
+        import torch as t
+        return t.cuda.device_count()
+    except Exception:
+        return 0
+
+
+@pytest.mark.skipif(_gpu_count() < 2, reason="needs two GPUs")
+def test_forward_host_two_devices_one_thread(torch):
+    # one host thread drives layers on two GPUs: each layer keeps its own
+    # device staging buffers and streams
+    inp = synth.make_config("decode", seed=5)
+    want, _, _ = oracle_forward(inp)
+    layers = [make_layer(inp, device=dev) for dev in (0, 1)]
+    xh = torch.from_numpy(inp.x).to(torch.bfloat16).pin_memory()
+    for _ in range(2):
+        for L in layers:
+            yh = torch.empty(xh.shape, dtype=torch.float32).pin_memory()
+            L.forward_host(xh, yh)
+            assert_close(yh.numpy(), want, f"forward_host on device {L.device}")
+    for L in layers:
+        L.close()
+
+
 def test_errors_are_reported(torch):
     inp = synth.make_inputs(256, 256, 2, 2, 4, True, seed=1)
     cfg = mxmoe.MoeConfig(256, 256, 2, 2)
