@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <climits>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -126,6 +127,8 @@ uint32_t dq_scale_row_bytes(uint32_t kp) { return round_up(kp / 32u, 16u); }
 // before every forward.
 constexpr int kStatusSyncOffset = 16;
 constexpr int kStatusDoneWord = 1;  // dequant-GEMV fused mode: finished-block counter
+// Wait limit of a forward run under mxmoe_set_fault_injection.
+constexpr unsigned long long kFaultWaitNs = 1000ull * 1000ull;  // 1 ms
 
 // mxmoe_forward_host splits large batches into up to this many chunks so
 // that the copies of one chunk overlap the forward of another.
@@ -261,6 +264,7 @@ struct mxmoe_layer {
   uint32_t last_n = 0;
   bool profiling = false;
   bool profile_valid = false;
+  uint32_t fault = 0;  // mxmoe_set_fault_injection: applies to the next forward, then clears
   // CUDA-graph replay of mxmoe_forward: bumped by anything that moves a buffer
   // or changes a launch (uploads, workspace growth, shard changes)
   uint64_t generation = 0;
@@ -534,6 +538,10 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
   p.k = static_cast<int>(k);
   p.topk_w = route_w;
   p.err = L->err;
+  if (L->fault == MXMOE_FAULT_SKIP_SIGNAL) {
+    p.skip_stage = 1;
+    p.wait_ns = kFaultWaitNs;
+  }
   p.d = L->d;
   p.units = static_cast<int>(L->fp);
   p.stages = tc_gemm_max_stages(true, 256, 1, L->smem_limit, PT, true, true);
@@ -637,6 +645,10 @@ int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint3
   a.topk_w = route_w;
   a.err = L->err;
   a.sync = L->err + kStatusSyncOffset;
+  if (L->fault == MXMOE_FAULT_SKIP_SIGNAL) {
+    a.skip_arrival = 1;
+    a.wait_ns = kFaultWaitNs;
+  }
   if (y) {
     a.fused = 1;
     a.topk_idx = w.topk_idx;
@@ -710,6 +722,10 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.k = static_cast<int>(k);
   p.topk_w = route_w;
   p.err = L->err;
+  if (L->fault == MXMOE_FAULT_SKIP_SIGNAL) {
+    p.skip_stage = 1;
+    p.wait_ns = kFaultWaitNs;
+  }
   p.d = L->d;
   p.units = static_cast<int>(L->fp);
   // W1 + SwiGLU: weights W1, activations x terms; writes act terms.
@@ -1133,6 +1149,12 @@ int mxmoe_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, void* y, m
   TRY(ensure_workspace(L, n_tokens, L->k));
   if (forward_plan(L, static_cast<uint64_t>(n_tokens) * L->k, x_terms_for(L, x_dtype)).fp4) TRY(ensure_f4(L));
   L->profile_valid = false;
+  if (L->fault) {
+    // a fault-injected forward runs once, directly, and is not cached as a graph
+    const int rc = forward_chain(L, x, x_dtype, y, y_dtype, n_tokens, st);
+    L->fault = 0;
+    return rc;
+  }
   if (!L->profiling && !(L->cfg.flags & MXMOE_FLAG_NO_GRAPHS)) {
     auto& gr = L->graph;
     const bool same = gr.x == x && gr.y == y && gr.n == n_tokens && gr.xd == x_dtype && gr.yd == y_dtype &&
@@ -1298,18 +1320,26 @@ int mxmoe_topk_softmax(const float* logits, uint32_t n_tokens, uint32_t num_expe
 int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k, uint32_t num_experts, int32_t* offsets,
                   int32_t* perm, int32_t* inv, void* stream) {
   if (num_experts == 0 || num_experts > 1024) return fail(MXMOE_ERR_UNSUPPORTED, "num_experts %u", num_experts);
-  if (!offsets || (n_tokens * k > 0 && (!topk_idx || !perm || !inv)))
-    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
+  if (P > static_cast<uint64_t>(INT32_MAX)) return fail(MXMOE_ERR_TOO_LARGE, "n_tokens * k = %llu pairs", (unsigned long long)P);
+  if (!offsets || (P > 0 && (!topk_idx || !perm || !inv))) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   // pad = 1 makes the padded maps equal to the canonical ones; the scratch
   // outputs (poff, counts) are written to the tail of `offsets`' companion
   // buffers allocated here.
   int32_t* tmp = nullptr;
   TRY(dalloc(&tmp, 2 * (num_experts + 1)));
   cudaStream_t st = as_stream(stream);
-  CUDA_TRY(launch_permute(topk_idx, static_cast<int>(n_tokens * k), num_experts, 1, 1, offsets, nullptr, nullptr, tmp,
-                          tmp + num_experts + 1, nullptr, perm, inv, st));
-  CUDA_TRY(cudaStreamSynchronize(st));
+  const cudaError_t le = launch_permute(topk_idx, static_cast<int>(P), num_experts, 1, 1, offsets, nullptr, nullptr,
+                                        tmp, tmp + num_experts + 1, nullptr, perm, inv, st);
+  const cudaError_t se = le == cudaSuccess ? cudaStreamSynchronize(st) : le;
   dfree(tmp);
+  CUDA_TRY(se);
+  // ids outside [0, num_experts) are left out of the maps: the total falls short
+  int32_t total = 0;
+  CUDA_TRY(cudaMemcpy(&total, offsets + num_experts, sizeof(int32_t), cudaMemcpyDeviceToHost));
+  if (static_cast<uint64_t>(total) != P)
+    return fail(MXMOE_ERR_INVALID_ARG, "%llu of %llu expert ids lie outside [0, %u)",
+                (unsigned long long)(P - static_cast<uint64_t>(total)), (unsigned long long)P, num_experts);
   return MXMOE_OK;
 }
 
@@ -1353,13 +1383,21 @@ int mxmoe_permute_noalloc(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k
   if (num_experts > kNoAllocMaxExperts)
     return fail(MXMOE_ERR_TOO_LARGE, "mxmoe_permute_noalloc handles at most %u experts (got %u)",
                 kNoAllocMaxExperts, num_experts);
-  if (!offsets || (n_tokens * k > 0 && (!topk_idx || !perm || !inv)))
-    return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  const uint64_t P = static_cast<uint64_t>(n_tokens) * k;
+  if (P > static_cast<uint64_t>(INT32_MAX)) return fail(MXMOE_ERR_TOO_LARGE, "n_tokens * k = %llu pairs", (unsigned long long)P);
+  if (!offsets || (P > 0 && (!topk_idx || !perm || !inv))) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   int32_t* scratch = nullptr;
   TRY(scratch_for_current_device(&scratch));
   // The kernel writes every scratch entry it reads, so nothing needs clearing.
-  CUDA_TRY(launch_permute(topk_idx, static_cast<int>(n_tokens * k), num_experts, 1, 1, offsets, nullptr, nullptr,
-                          scratch, scratch + num_experts + 1, nullptr, perm, inv, as_stream(stream)));
+  CUDA_TRY(launch_permute(topk_idx, static_cast<int>(P), num_experts, 1, 1, offsets, nullptr, nullptr, scratch,
+                          scratch + num_experts + 1, nullptr, perm, inv, as_stream(stream)));
+  return MXMOE_OK;
+}
+
+int mxmoe_set_fault_injection(mxmoe_layer* L, uint32_t mode) {
+  TRY(check_layer(L));
+  if (mode > MXMOE_FAULT_SKIP_SIGNAL) return fail(MXMOE_ERR_INVALID_ARG, "unknown fault mode %u", mode);
+  L->fault = mode;
   return MXMOE_OK;
 }
 

@@ -647,13 +647,15 @@ __global__ void __launch_bounds__(kDqThreads, 1) mxmoe_dqgemv_ffn_kernel(const D
         if (threadIdx.x == 0) {
           // this block's SwiGLU columns are written: meet the expert's other blocks
           __threadfence();
-          atomicAdd(arrive, 1);
+          // (test hook: block 0 stays silent, so its expert's wait runs out)
+          if (!(a.skip_arrival && blockIdx.x == 0)) atomicAdd(arrive, 1);
           const unsigned long long t0 = global_timer_ns();
+          const unsigned long long limit = a.wait_ns ? a.wait_ns : kWaitTimeoutNs;
           while (true) {
             int v;
             asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(arrive) : "memory");
             if (v >= s.G) break;
-            if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+            if (global_timer_ns() - t0 > limit) {
               atomicCAS(a.err, 0, kDqErrExpert);
               break;
             }

@@ -202,6 +202,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   int* err = p.err;
+  const unsigned long long wait_ns = p.wait_ns ? p.wait_ns : kWaitTimeoutNs;
   const int N = p.N;                             // weights-as-A: pairs per tile; tokens-as-A: 256
   const int PT = kTok ? p.sf_rows : N;           // pairs per tile
   const int nacc = (!kTok && N <= 128) ? 2 : 1;  // accumulator buffers
@@ -269,9 +270,17 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
       const int row0 = __ldg(p.poff + e) + pt * PT;  // first activation row of the tile
       const uint64_t rbx = static_cast<uint64_t>(row0) / p.sf_rows;
       for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kDevTimeoutEmpty)) {
+        if (!mbar_wait(&empty_bar[stage], phase ^ 1u, err, kDevTimeoutEmpty, wait_ns)) {
           ok = false;
           break;
+        }
+        if (p.skip_stage && blockIdx.x == 0 && t == static_cast<int>(blockIdx.x) && kt == 0) {
+          // test hook: this stage is never armed; the MMA issuer's wait for it runs out
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+          continue;
         }
         uint8_t* sb = smem + stage * plan.stage_bytes;
         uint8_t* w_s = kTok ? sb + plan.a_terms * plan.a_bytes : sb;
@@ -356,7 +365,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     const uint32_t mma_n = kTok ? 256u : static_cast<uint32_t>(N);
     bool ok = true;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      if (!mbar_wait(&tmem_empty[acc], acc_phase[acc] ^ 1u, err, kDevTimeoutTmemEmpty)) break;
+      if (!mbar_wait(&tmem_empty[acc], acc_phase[acc] ^ 1u, err, kDevTimeoutTmemEmpty, wait_ns)) break;
       acc_phase[acc] ^= 1u;
       tc_fence_after();
       const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 128);
@@ -366,7 +375,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
         // FP4 tiles copy their scales from this thread instead (below): a copy
         // issued by another thread queues behind this thread's MMAs, and
         // waiting for its commit would drain the tensor pipe every stage.
-        if (!mbar_wait(kF4 ? &full_bar[stage] : &sf_full[stage], phase, err, kDevTimeoutFull)) {
+        if (!mbar_wait(kF4 ? &full_bar[stage] : &sf_full[stage], phase, err, kDevTimeoutFull, wait_ns)) {
           ok = false;
           break;
         }
@@ -446,7 +455,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     const int mma_terms = (kTok && p.stacked) ? 1 : terms;
     for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
       for (int kt = 0; kt < p.k_tiles; ++kt) {
-        if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull)) {
+        if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull, wait_ns)) {
           ok = false;
           break;
         }
@@ -491,7 +500,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
       int e = 0, wt = 0, pt = 0;
       if (!dry) {
         decode_tile(p, t, e, wt, pt);
-        if (!mbar_wait(&tmem_full[acc], acc_phase[acc], err, kDevTimeoutTmemFull)) break;
+        if (!mbar_wait(&tmem_full[acc], acc_phase[acc], err, kDevTimeoutTmemFull, wait_ns)) break;
         acc_phase[acc] ^= 1u;
         tc_fence_after();
       }

@@ -654,13 +654,15 @@ __device__ __forceinline__ unsigned same_expert_lanes(int ex, int nbits) {
 
 // Expert ids of pairs [base0, base0 + 32*kPermBatch) (-1 past p_end) into a
 // warp's staging buffer; all loads in flight together.
-__device__ __forceinline__ void stage_expert_ids(const int32_t* __restrict__ topk_idx, int base0, int p_end, int lane,
+__device__ __forceinline__ void stage_expert_ids(const int32_t* __restrict__ topk_idx, int E, int base0, int p_end,
+                                                 int lane,
                                                  int32_t* stg) {
   int v[kPermBatch];
 #pragma unroll
   for (int b = 0; b < kPermBatch; ++b) {
     const int p = base0 + 32 * b + lane;
-    v[b] = p < p_end ? __ldg(topk_idx + p) : -1;
+    const int id = p < p_end ? __ldg(topk_idx + p) : -1;
+    v[b] = id >= 0 && id < E ? id : -1;  // ids outside [0, E) are absent from the maps
   }
   __syncwarp();  // the previous batch is consumed
 #pragma unroll
@@ -688,7 +690,7 @@ __global__ void __launch_bounds__(kPermThreads)
   // warp's staging buffer, then consumed by a rolled loop (a one-block kernel
   // runs each instruction once, so the loop body is kept small).
   for (int base0 = p_begin; base0 < p_end; base0 += 32 * kPermBatch) {
-    stage_expert_ids(topk_idx, base0, p_end, lane, stg);
+    stage_expert_ids(topk_idx, E, base0, p_end, lane, stg);
     for (int b = 0; b < kPermBatch && base0 + 32 * b < p_end; ++b) {
       const int ex = stg[32 * b + lane];
       const unsigned grp = same_expert_lanes(ex, nbits);
@@ -775,11 +777,15 @@ __global__ void __launch_bounds__(kPermThreads)
   __syncthreads();
   // pass 2: stable ranks within each expert, (token, slot) order
   for (int base0 = p_begin; base0 < p_end; base0 += 32 * kPermBatch) {
-    stage_expert_ids(topk_idx, base0, p_end, lane, stg);
+    stage_expert_ids(topk_idx, E, base0, p_end, lane, stg);
     for (int b = 0; b < kPermBatch && base0 + 32 * b < p_end; ++b) {
       const int p = base0 + 32 * b + lane;
       const int ex = stg[32 * b + lane];
       const unsigned grp = same_expert_lanes(ex, nbits);
+      if (ex < 0 && p < p_end) {  // an id outside [0, E): no position
+        inv_p[p] = -1;
+        if (inv_c) inv_c[p] = -1;
+      }
       if (ex >= 0) {
         const int rank = cnt[warp * E + ex] + __popc(grp & ((1u << lane) - 1u));
         const int pos_p = pstart[ex] + rank;
@@ -861,7 +867,10 @@ __global__ void __launch_bounds__(kPermChunkThreads)
   for (int e = threadIdx.x; e < E; e += blockDim.x) sh[e] = 0;
   __syncthreads();
   const int p0 = blockIdx.x * kPermChunk;
-  for (int p = p0 + threadIdx.x; p < min(P, p0 + kPermChunk); p += blockDim.x) atomicAdd(&sh[__ldg(topk_idx + p)], 1);
+  for (int p = p0 + threadIdx.x; p < min(P, p0 + kPermChunk); p += blockDim.x) {
+    const int id = __ldg(topk_idx + p);
+    if (id >= 0 && id < E) atomicAdd(&sh[id], 1);  // ids outside [0, E) are absent from the maps
+  }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) hist[static_cast<uint64_t>(blockIdx.x) * E + e] = sh[e];
   __threadfence();
@@ -927,7 +936,8 @@ __global__ void __launch_bounds__(kPermChunkThreads)
 #pragma unroll
   for (int r = 0; r < kRows; ++r) {
     const int p = pw + 32 * r + lane;
-    exv[r] = p < P ? __ldg(topk_idx + p) : -1;
+    const int id = p < P ? __ldg(topk_idx + p) : -1;
+    exv[r] = id >= 0 && id < E ? id : -1;
   }
   __syncthreads();
 #pragma unroll
@@ -949,6 +959,10 @@ __global__ void __launch_bounds__(kPermChunkThreads)
 #pragma unroll
   for (int r = 0; r < kRows; ++r) {
     const int ex = exv[r];
+    if (ex < 0 && pw + 32 * r + lane < P) {  // an id outside [0, E): no position
+      inv_p[pw + 32 * r + lane] = -1;
+      if (inv_c) inv_c[pw + 32 * r + lane] = -1;
+    }
     if (ex >= 0) {
       const int p = pw + 32 * r + lane;
       const int rank = wcnt[warp * E + ex] + __popc(grp[r] & ((1u << lane) - 1u));
@@ -1658,7 +1672,10 @@ static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, int k, c
   const size_t smem = static_cast<size_t>(router_stages<BT>()) * router_stage_bytes<XT, BT>() +
                       2 * static_cast<size_t>(BT) * kRouterChunk * sizeof(float);
   const auto fn = router_logits_kernel<XT, TT, TE>;
-  ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+  {
+    const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
+    if (ce != cudaSuccess) return ce;
+  }
   return launch_kernel(fn, grid, dim3(kRouterThreads), smem, st, x, n, d, E, gamma, gate_packed, gate_b, rscale, logits,
                        aligned, k, topk_idx, topk_w);
 }
@@ -1738,17 +1755,26 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
   if (scratch && P >= kPermMultiBlockMin) {
     const int nch = (P + kPermChunk - 1) / kPermChunk;
     const size_t hsmem = 4 * static_cast<size_t>(E) * sizeof(int32_t);
-    ensure_dynamic_smem(reinterpret_cast<const void*>(perm_hist_kernel), hsmem);
+    {
+      const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(perm_hist_kernel), hsmem);
+      if (ce != cudaSuccess) return ce;
+    }
     cudaError_t pe = launch_kernel(perm_hist_kernel, dim3(nch), dim3(kPermChunkThreads), hsmem, st, topk_idx, P, E, pad,
                                    N, scratch, offsets, poff, counts, ntile_prefix);
     if (pe != cudaSuccess) return pe;
     const size_t ssmem = (kPermChunkThreads / 32) * static_cast<size_t>(E) * sizeof(int32_t);
-    ensure_dynamic_smem(reinterpret_cast<const void*>(perm_scatter_kernel), ssmem);
+    {
+      const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(perm_scatter_kernel), ssmem);
+      if (ce != cudaSuccess) return ce;
+    }
     return launch_kernel(perm_scatter_kernel, dim3(nch), dim3(kPermChunkThreads), ssmem, st, topk_idx, P, E, scratch,
                          perm_c, inv_c, perm_p, inv_p);
   }
   const size_t smem = (static_cast<size_t>(34) * E + 32 * 32 * kPermBatch) * sizeof(int32_t);
-  ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
+  {
+    const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
+    if (ce != cudaSuccess) return ce;
+  }
   return launch_kernel(permute_kernel, dim3(1), dim3(kPermThreads), smem, st, topk_idx, P, E, pad, N, offsets, perm_c,
                        inv_c, poff, counts, ntile_prefix, perm_p, inv_p);
 }
@@ -1828,7 +1854,10 @@ cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, 
                              int32_t* src_base, int32_t* poff, int32_t* seg_counts, int32_t* ntile_prefix,
                              cudaStream_t st) {
   const size_t smem = 3ull * E * sizeof(int32_t);
-  ensure_dynamic_smem(reinterpret_cast<const void*>(ep_layout_kernel), smem);
+  {
+    const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(ep_layout_kernel), smem);
+    if (ce != cudaSuccess) return ce;
+  }
   ep_layout_kernel<<<1, 256, smem, st>>>(counts, world, rank, E, epr, pad, n_tile, src_base, poff, seg_counts,
                                          ntile_prefix);
   return cudaGetLastError();
@@ -1857,7 +1886,10 @@ cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t*
                              int* err, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   const size_t smem = (2ull * epr + 1) * sizeof(int32_t);
-  ensure_dynamic_smem(reinterpret_cast<const void*>(ep_return_kernel), smem);
+  {
+    const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(ep_return_kernel), smem);
+    if (ce != cudaSuccess) return ce;
+  }
   ep_return_kernel<<<(rows + 7) / 8, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
                                                        static_cast<uint32_t>(d) * 2u, rows, poff, seg_counts, epr,
                                                        slot, world, peer_ret, ret_rows, err);
@@ -1870,7 +1902,10 @@ cudaError_t launch_ep_unpack(const void* meta, const uint8_t* sf_rows, uint32_t 
                              cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
   const size_t smem = (2ull * epr + 1) * sizeof(int32_t);
-  ensure_dynamic_smem(reinterpret_cast<const void*>(ep_unpack_kernel), smem);
+  {
+    const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(ep_unpack_kernel), smem);
+    if (ce != cudaSuccess) return ce;
+  }
   ep_unpack_kernel<<<(rows + 7) / 8, 256, smem, st>>>(static_cast<const uint4*>(meta), sf_rows, sf_row_bytes, terms, nb,
                                                        rows, poff, seg_counts, epr, rs, wt, slot, xsf, sf_term_stride,
                                                        kchunks, pt, stacked);

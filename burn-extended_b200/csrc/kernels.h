@@ -142,6 +142,8 @@ struct DqParams {
   int* done;               // fused: finished-block counter, zero at launch
   int* err;                // status word
   int* sync;               // [E] per-expert arrival counters, zero at launch
+  int skip_arrival;        // test hook: block 0 never signals its W1 completion
+  unsigned long long wait_ns;  // limit of the W1 -> W2 wait (0: the default 2 s)
   int ps;                  // pairs staged per pass (shared memory: ps * 2 KB per 1024 columns)
   uint32_t stage_bytes;    // set by the launcher
 };

@@ -65,7 +65,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
 // The poll loop touches no global memory while the wait is young: a global
 // load there would delay noticing the flip by a memory round trip.  Only
 // waits older than kErrPollAfterNs also look at *err.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code) {
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* err, int code,
+                                          unsigned long long timeout_ns = kWaitTimeoutNs) {
   const uint32_t addr = smem_u32(bar);
   if (mbar_try_wait(addr, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
@@ -74,7 +75,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(addr, parity)) return true;
     const unsigned long long dt = global_timer_ns() - t0;
-    if (dt > kWaitTimeoutNs) {
+    if (dt > timeout_ns) {
       if (err != nullptr) atomicCAS(err, 0, code);
       return false;
     }

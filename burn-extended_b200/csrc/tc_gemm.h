@@ -55,6 +55,11 @@ struct TcParams {
   int y_by_pair;  // W2 output row = the pair's own index (received row) instead of its sorted position
   int d;
   int* err;                 // device status word (0 = ok)
+  // Test hook (mxmoe_set_fault_injection): with skip_stage set, CTA 0's
+  // producer never arms its first pipeline stage, so the MMA issuer's wait
+  // for it runs out; wait_ns limits the waits that record a status.
+  int skip_stage;
+  unsigned long long wait_ns;
 };
 
 size_t tc_gemm_smem_bytes(bool tokens_as_a, int N, int terms, int stages, int pair_tile, bool stacked,

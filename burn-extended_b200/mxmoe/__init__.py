@@ -204,6 +204,12 @@ class MoeGatedSwiGLU:
 
     STAGES = ("router", "permute", "quantize", "w1_gemm", "w2_gemm", "combine")
 
+    def inject_fault(self, mode: int = 1):
+        """Test hook (mxmoe_set_fault_injection): the next forward withholds
+        one device-side signal so that a bounded wait runs out (1 ms) and
+        sync_status raises MxMoeError(MXMOE_ERR_TIMEOUT).  No GPU fault."""
+        check(lib().mxmoe_set_fault_injection(self._h, mode))
+
     def set_profiling(self, enable: bool = True):
         check(lib().mxmoe_set_profiling(self._h, 1 if enable else 0))
 

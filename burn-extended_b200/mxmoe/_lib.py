@@ -89,6 +89,7 @@ _SIGS = {
     "mxmoe_sync_status": ([_vp, _vp], _i32),
     "mxmoe_set_expert_shard": ([_vp, _u32, _u32], _i32),
     "mxmoe_set_profiling": ([_vp, _i32], _i32),
+    "mxmoe_set_fault_injection": ([_vp, _u32], _i32),
     "mxmoe_last_profile": ([_vp, ctypes.POINTER(ctypes.c_float), _i32, ctypes.POINTER(_i32)], _i32),
     "mxmoe_route": ([_vp, _vp, _i32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "mxmoe_gather_pairs": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i32),

@@ -208,7 +208,10 @@ MXMOE_API int mxmoe_topk_softmax(const float* logits, uint32_t n_tokens,
 
 /* Canonical permutation of given top-k indices (replaces the dense masks of
  * src/moe/mod.rs:279-288): stable counting sort of pairs p = t*k+s by expert.
- * offsets [E+1], perm [n*k], inv [n*k].  Device pointers. */
+ * offsets [E+1], perm [n*k], inv [n*k].  Device pointers.  Synchronizes
+ * `stream`.  Ids outside [0, num_experts) are left out of the maps (their inv
+ * entry is -1) and the call returns MXMOE_ERR_INVALID_ARG; n*k above INT32_MAX
+ * returns MXMOE_ERR_TOO_LARGE. */
 MXMOE_API int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t k,
                   uint32_t num_experts, int32_t* offsets, int32_t* perm,
                   int32_t* inv, void* stream);
@@ -223,8 +226,12 @@ MXMOE_API int mxmoe_permute(const int32_t* topk_idx, uint32_t n_tokens, uint32_t
  * looks the array's device address up (cudaGetSymbolAddress) -- make that
  * first call before any stream capture.  All calls share the one array, so
  * calls that overlap on the GPU (different streams, different threads) race;
- * serialize them.  Unlike mxmoe_permute it does not synchronize `stream`.
- * Device pointers, same meaning as mxmoe_permute. */
+ * serialize them.  Unlike mxmoe_permute it does not synchronize `stream`, so
+ * ids outside [0, num_experts) cannot be reported: they are left out of the
+ * maps (inv entry -1, offsets[E] short of n*k).  It always runs the one-block
+ * permutation (1024 threads), fine for decode and small prefill batches but
+ * slow past tens of thousands of pairs, where mxmoe_permute's multi-block form
+ * takes over.  Device pointers, same meaning as mxmoe_permute. */
 MXMOE_API int mxmoe_permute_noalloc(const int32_t* topk_idx, uint32_t n_tokens,
                                     uint32_t k, uint32_t num_experts,
                                     int32_t* offsets, int32_t* perm,
@@ -242,6 +249,21 @@ MXMOE_API int mxmoe_sync_status(mxmoe_layer* layer, void* stream);
  * waits for the last forward and writes up to `cap` stage times in
  * milliseconds (returns the stage count through *count). */
 MXMOE_API int mxmoe_set_profiling(mxmoe_layer* layer, int enable);
+
+/* Test hook for the failure path; no counterpart in the reference, whose
+ * errors are panics (src/moe/mod.rs:112).  MXMOE_FAULT_SKIP_SIGNAL makes the
+ * next mxmoe_forward of this layer withhold one device-side signal: the
+ * tensor-core GEMM leaves one pipeline stage unarmed (its consumer's wait
+ * runs out), the dequant-GEMV's block 0 never reports its W1 columns (its
+ * expert's other blocks stop waiting).  The waits of that forward give up
+ * after 1 ms instead of 2 s, record MXMOE_ERR_TIMEOUT in the layer's status
+ * (mxmoe_sync_status reports it), drain their copies and MMAs, free TMEM and
+ * return; the output of that forward is undefined.  Nothing faults, traps or
+ * hangs, and the next forward runs normally.  The injected forward is never
+ * captured as a CUDA graph.  MXMOE_FAULT_NONE clears a pending injection. */
+#define MXMOE_FAULT_NONE 0u
+#define MXMOE_FAULT_SKIP_SIGNAL 1u
+MXMOE_API int mxmoe_set_fault_injection(mxmoe_layer* layer, uint32_t mode);
 MXMOE_API int mxmoe_last_profile(mxmoe_layer* layer, float* ms, int cap,
                                  int* count);
 

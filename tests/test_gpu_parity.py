@@ -72,6 +72,18 @@ def test_permute_bit_exact(torch, n, k, E):
         assert np.array_equal(g.cpu().numpy(), w)
 
 
+@pytest.mark.parametrize("n", [37, 5000])  # one-block and multi-block forms
+def test_permute_rejects_ids_out_of_range(torch, n):
+    rng = np.random.default_rng(n)
+    E = 16
+    topk = rng.integers(0, E, size=(n, 2)).astype(np.int32)
+    topk[3, 1] = E        # past the last expert
+    topk[n - 1, 0] = -4   # negative
+    with pytest.raises(mxmoe.MxMoeError) as ei:
+        mxmoe.permute(torch.from_numpy(topk).cuda(), E)
+    assert ei.value.code == 1  # MXMOE_ERR_INVALID_ARG
+
+
 def test_permute_all_to_one_expert_and_empty_experts(torch):
     topk = np.zeros((1000, 1), dtype=np.int32) + 5
     want = oracle.permute(topk, 16)
