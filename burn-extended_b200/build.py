@@ -13,7 +13,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 OUT = os.path.join(HERE, "mxmoe", "libmxmoe.so")
-SOURCES = ["api.cu", "kernels.cu", "dqgemv.cu", "gemm_tc.cu", "modelbin.cpp", "safetensors.cpp"]
+SOURCES = ["api.cu", "kernels.cu", "dqgemv.cu", "attention.cu", "gemm_tc.cu", "modelbin.cpp", "safetensors.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -62,6 +62,16 @@ class QuantDesc(ctypes.Structure):
     ]
 
 
+class MqaConfig(ctypes.Structure):
+    _fields_ = [("d_model", ctypes.c_uint32), ("n_heads", ctypes.c_uint32), ("kv_heads", ctypes.c_uint32),
+                ("head_dim", ctypes.c_uint32), ("flags", ctypes.c_uint32), ("device", ctypes.c_int32)]
+
+
+class MqaRope(ctypes.Structure):
+    _fields_ = [("max_seq_len", ctypes.c_uint32), ("theta", ctypes.c_float), ("scaling_factor", ctypes.c_float),
+                ("initial_context", ctypes.c_float), ("ntk_alpha", ctypes.c_float), ("ntk_beta", ctypes.c_float)]
+
+
 _vp = ctypes.c_void_p
 _u32 = ctypes.c_uint32
 _u64 = ctypes.c_uint64
@@ -90,6 +100,16 @@ _SIGS = {
     "mxmoe_set_expert_shard": ([_vp, _u32, _u32], _i32),
     "mxmoe_set_profiling": ([_vp, _i32], _i32),
     "mxmoe_set_fault_injection": ([_vp, _u32], _i32),
+    "mxmqa_create": ([ctypes.POINTER(MqaConfig), ctypes.POINTER(_vp)], _i32),
+    "mxmqa_destroy": ([_vp], _i32),
+    "mxmqa_set_weights": ([_vp] + [_vp] * 8 + [_i32, _vp], _i32),
+    "mxmqa_set_sinks": ([_vp, _vp], _i32),
+    "mxmqa_set_rope": ([_vp, ctypes.POINTER(MqaRope)], _i32),
+    "mxmqa_cache_create": ([_vp, _u32, _u32, _u32, ctypes.POINTER(_vp)], _i32),
+    "mxmqa_cache_reset": ([_vp], _i32),
+    "mxmqa_cache_state": ([_vp, ctypes.POINTER(_u64), ctypes.POINTER(_u64)], _i32),
+    "mxmqa_cache_destroy": ([_vp], _i32),
+    "mxmqa_forward_streaming": ([_vp, _vp, _vp, _i32, _u32, _u32, _u64, _u32, _vp, _vp, _vp, _i32, _vp], _i32),
     "mxmoe_last_profile": ([_vp, ctypes.POINTER(ctypes.c_float), _i32, ctypes.POINTER(_i32)], _i32),
     "mxmoe_route": ([_vp, _vp, _i32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i32),
     "mxmoe_gather_pairs": ([_vp, _i32, _u32, _u32, _u32, _vp, _vp, _vp, _vp, _vp, _vp, _vp], _i32),

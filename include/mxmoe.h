@@ -471,6 +471,94 @@ MXMOE_API int mxmoe_safetensors_load_layer(const char* const* paths, uint32_t n_
                                  const mxmoe_config* cfg, uint32_t expert_begin, uint32_t expert_count,
                                  void* stream, mxmoe_layer** out);
 
+/* ===================== streaming multi-query attention =====================
+ * The attention half of a GPT-OSS decoder block:
+ * StreamingMultiQueryAttention::forward_streaming
+ * (src/attention/streaming_mqa.rs:239-435) with its rolling KV cache
+ * StreamingMqaCache (:132-203), window policy AttnWindow
+ * (src/attention/streaming.rs:14-19), sinks and quiet softmax
+ * (src/attention/core.rs:7-55), cache eviction evict_and_roll_mqa
+ * (src/attention/cache_ops.rs:74-117) and RoPE with NTK/YaRN scaling
+ * (burn RotaryEncoding, src/rope/mod.rs:11-50).  Dropout is inference-off. */
+
+#define MXMQA_FLAG_QUIET_SOFTMAX 0x1u /* quiet_softmax: 1 joins the normalizer */
+#define MXMQA_FLAG_PRE_SCALED_QK 0x2u /* skip the 1/sqrt(d_k) score scale */
+#define MXMQA_FLAG_ROPE_BY_HEAD  0x4u /* reproduce the reference's RoPE call
+                                         exactly: it applies burn's rotation
+                                         (which rotates along dim -2) to a
+                                         [B, T, heads, d_k] tensor, so the
+                                         angle index is start_pos + head, not
+                                         start_pos + token.  Default off: the
+                                         angle index is the token position */
+
+/* Mirrors StreamingMultiQueryAttentionConfig (src/attention/streaming_mqa.rs:12-42)
+ * without the initializer (weights are always loaded). */
+typedef struct mxmqa_config {
+  uint32_t d_model;
+  uint32_t n_heads;
+  uint32_t kv_heads;   /* num_key_value_heads; n_heads % kv_heads == 0 */
+  uint32_t head_dim;   /* multiple of 4, at most 256 */
+  uint32_t flags;      /* MXMQA_FLAG_* */
+  int32_t device;
+} mxmqa_config;
+
+/* burn RotaryEncodingConfig + the NTK/YaRN scaling of init_ntk_yarn. */
+typedef struct mxmqa_rope {
+  uint32_t max_seq_len;    /* informational (positions are not table-limited) */
+  float theta;             /* base, 10000 by default */
+  float scaling_factor;    /* <= 1: plain RoPE */
+  float initial_context;   /* YaRN: original context length */
+  float ntk_alpha;
+  float ntk_beta;
+} mxmqa_rope;
+
+typedef struct mxmqa_layer mxmqa_layer;
+typedef struct mxmqa_cache mxmqa_cache;
+
+/* Replaces StreamingMultiQueryAttentionConfig::init (:94-131). */
+MXMOE_API int mxmqa_create(const mxmqa_config* cfg, mxmqa_layer** out);
+MXMOE_API int mxmqa_destroy(mxmqa_layer* layer);
+
+/* The query / key / value / output Linear layers as Burn stores them:
+ * weight [d_in][d_out], bias [d_out] (NULL = zero).  q: d_model -> n_heads *
+ * head_dim, k and v: d_model -> kv_heads * head_dim, o: n_heads * head_dim ->
+ * d_model.  Host pointers; copies are made. */
+MXMOE_API int mxmqa_set_weights(mxmqa_layer* layer, const void* wq, const void* bq, const void* wk,
+                                const void* bk, const void* wv, const void* bv, const void* wo,
+                                const void* bo, mxmoe_dtype dtype, void* stream);
+
+/* The module's learned sinks (learned_sinks, :117-124): [kv_heads][groups]
+ * logits, host f32; NULL removes them. */
+MXMOE_API int mxmqa_set_sinks(mxmqa_layer* layer, const float* sinks);
+
+/* RoPE for every forward of this layer (StreamingMqaParams::rope); NULL = none. */
+MXMOE_API int mxmqa_set_rope(mxmqa_layer* layer, const mxmqa_rope* rope);
+
+/* StreamingMqaCache::new (:146-167): batch x cache_len tokens of kv_heads x
+ * head_dim keys and values (f32) on the layer's device, of which the first
+ * sink_tokens written are never evicted. */
+MXMOE_API int mxmqa_cache_create(const mxmqa_layer* layer, uint32_t batch, uint32_t cache_len,
+                                 uint32_t sink_tokens, mxmqa_cache** out);
+/* StreamingMqaCache::reset (:169-173). */
+MXMOE_API int mxmqa_cache_reset(mxmqa_cache* cache);
+/* global_end_index and local_end_index (len()) of the cache. */
+MXMOE_API int mxmqa_cache_state(const mxmqa_cache* cache, uint64_t* global_end, uint64_t* local_end);
+MXMOE_API int mxmqa_cache_destroy(mxmqa_cache* cache);
+
+/* forward_streaming (:239-435): x [batch][seq_len][d_model] device (f32 or
+ * bf16), written to the cache at absolute positions start_pos ..; window 0 =
+ * AttnWindow::Full, w > 0 = AttnWindow::Window(w) (sink tokens + the w most
+ * recent); sinks: device [n_heads] logits for this call (NULL: the module's);
+ * attn_bias: device [batch][n_heads][seq_len][active window] f32 or NULL.
+ * Like the reference, no causal mask is applied inside a chunk.  y
+ * [batch][seq_len][d_model] device.  Stream-ordered; the cache bookkeeping
+ * is host state, so calls on one cache must be issued in order. */
+MXMOE_API int mxmqa_forward_streaming(mxmqa_layer* layer, mxmqa_cache* cache, const void* x,
+                                      mxmoe_dtype x_dtype, uint32_t batch, uint32_t seq_len,
+                                      uint64_t start_pos, uint32_t window, const float* sinks,
+                                      const float* attn_bias, void* y, mxmoe_dtype y_dtype,
+                                      void* stream);
+
 #ifdef __cplusplus
 }
 #endif

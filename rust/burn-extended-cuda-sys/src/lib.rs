@@ -98,6 +98,46 @@ pub struct mxmoe_layer {
     _private: [u8; 0],
 }
 
+/// Streaming multi-query attention configuration (`mxmqa_config`).
+#[repr(C)]
+#[derive(Clone, Copy, Debug, Default)]
+pub struct mxmqa_config {
+    pub d_model: u32,
+    pub n_heads: u32,
+    pub kv_heads: u32,
+    pub head_dim: u32,
+    pub flags: u32,
+    pub device: i32,
+}
+
+/// RoPE with NTK/YaRN scaling (`mxmqa_rope`).
+#[repr(C)]
+#[derive(Clone, Copy, Debug, Default)]
+pub struct mxmqa_rope {
+    pub max_seq_len: u32,
+    pub theta: f32,
+    pub scaling_factor: f32,
+    pub initial_context: f32,
+    pub ntk_alpha: f32,
+    pub ntk_beta: f32,
+}
+
+pub const MXMQA_FLAG_QUIET_SOFTMAX: u32 = 0x1;
+pub const MXMQA_FLAG_PRE_SCALED_QK: u32 = 0x2;
+pub const MXMQA_FLAG_ROPE_BY_HEAD: u32 = 0x4;
+
+/// Opaque attention layer handle.
+#[repr(C)]
+pub struct mxmqa_layer {
+    _private: [u8; 0],
+}
+
+/// Opaque streaming KV cache handle.
+#[repr(C)]
+pub struct mxmqa_cache {
+    _private: [u8; 0],
+}
+
 extern "C" {
     pub fn mxmoe_abi_version() -> c_int;
     pub fn mxmoe_build_info() -> *const c_char;
@@ -342,6 +382,49 @@ extern "C" {
         expert_count: u32,
         stream: *mut c_void,
         out: *mut *mut mxmoe_layer,
+    ) -> c_int;
+
+    pub fn mxmqa_create(cfg: *const mxmqa_config, out: *mut *mut mxmqa_layer) -> c_int;
+    pub fn mxmqa_destroy(layer: *mut mxmqa_layer) -> c_int;
+    pub fn mxmqa_set_weights(
+        layer: *mut mxmqa_layer,
+        wq: *const c_void,
+        bq: *const c_void,
+        wk: *const c_void,
+        bk: *const c_void,
+        wv: *const c_void,
+        bv: *const c_void,
+        wo: *const c_void,
+        bo: *const c_void,
+        dtype: mxmoe_dtype,
+        stream: *mut c_void,
+    ) -> c_int;
+    pub fn mxmqa_set_sinks(layer: *mut mxmqa_layer, sinks: *const f32) -> c_int;
+    pub fn mxmqa_set_rope(layer: *mut mxmqa_layer, rope: *const mxmqa_rope) -> c_int;
+    pub fn mxmqa_cache_create(
+        layer: *const mxmqa_layer,
+        batch: u32,
+        cache_len: u32,
+        sink_tokens: u32,
+        out: *mut *mut mxmqa_cache,
+    ) -> c_int;
+    pub fn mxmqa_cache_reset(cache: *mut mxmqa_cache) -> c_int;
+    pub fn mxmqa_cache_state(cache: *const mxmqa_cache, global_end: *mut u64, local_end: *mut u64) -> c_int;
+    pub fn mxmqa_cache_destroy(cache: *mut mxmqa_cache) -> c_int;
+    pub fn mxmqa_forward_streaming(
+        layer: *mut mxmqa_layer,
+        cache: *mut mxmqa_cache,
+        x: *const c_void,
+        x_dtype: mxmoe_dtype,
+        batch: u32,
+        seq_len: u32,
+        start_pos: u64,
+        window: u32,
+        sinks: *const f32,
+        attn_bias: *const f32,
+        y: *mut c_void,
+        y_dtype: mxmoe_dtype,
+        stream: *mut c_void,
     ) -> c_int;
 }
 

@@ -16,7 +16,7 @@ HEADER = os.path.join(ROOT, "include", "mxmoe.h")
 
 def header_symbols():
     txt = open(HEADER).read()
-    return sorted(set(re.findall(r"MXMOE_API\s+(?:const\s+)?\w+\**\s+\**(mxmoe_\w+)\s*\(", txt)))
+    return sorted(set(re.findall(r"MXMOE_API\s+(?:const\s+)?\w+\**\s+\**(mx(?:moe|mqa)_\w+)\s*\(", txt)))
 
 
 def test_header_declares_expected_entry_points():

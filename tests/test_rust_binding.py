@@ -15,7 +15,7 @@ C_TO_RUST = {"uint32_t": "u32", "int32_t": "i32", "uint64_t": "u64", "float": "f
 def header_functions():
     s = open(HEADER).read()
     out = {}
-    for m in re.finditer(r"MXMOE_API\s+[\w\s\*]+?\b(mxmoe_\w+)\s*\(([^;]*?)\);", s, re.S):
+    for m in re.finditer(r"MXMOE_API\s+[\w\s\*]+?\b(mx(?:moe|mqa)_\w+)\s*\(([^;]*?)\);", s, re.S):
         args = " ".join(m.group(2).split())
         out[m.group(1)] = 0 if args in ("", "void") else args.count(",") + 1
     return out
@@ -25,7 +25,7 @@ def rust_functions():
     s = open(SYS).read()
     block = s[s.index('extern "C" {'):s.index("pub mod cudart")]
     out = {}
-    for m in re.finditer(r"pub fn (mxmoe_\w+)\s*\(([^)]*)\)", block, re.S):
+    for m in re.finditer(r"pub fn (mx(?:moe|mqa)_\w+)\s*\(([^)]*)\)", block, re.S):
         args = [a for a in " ".join(m.group(2).split()).split(",") if a.strip()]
         out[m.group(1)] = len(args)
     return out
@@ -52,7 +52,7 @@ def test_same_entry_points():
 
 
 def test_structs_match_header():
-    for name in ("mxmoe_config", "mxmoe_quant_desc", "mxmoe_modelbin_header"):
+    for name in ("mxmoe_config", "mxmoe_quant_desc", "mxmoe_modelbin_header", "mxmqa_config", "mxmqa_rope"):
         hs, rs = header_struct(name), rust_struct(name)
         assert [n for _, n in hs] == [n for n, _ in rs], name
         for (ct, n), (_, rt) in zip(hs, rs):
