@@ -122,11 +122,11 @@ void dfree(T*& p) {
 // to 16, so that a row range is one bulk copy.
 uint32_t dq_scale_row_bytes(uint32_t kp) { return round_up(kp / 32u, 16u); }
 
-// Status block: word 0 is the status code; from kStatusSyncOffset on, one
-// arrival counter per local expert (dequant-GEMV W1 -> W2 handoff).  Zeroed
-// before every forward.
+// Status block: word 0 is the status code, words 2-4 where the dequant-GEMV's
+// W1 -> W2 grid wait gave up (-1, arrivals seen, arrivals expected), word
+// kStatusSyncOffset that wait's arrival counter; the words after it are
+// spare (one per local expert).  Zeroed before every forward.
 constexpr int kStatusSyncOffset = 16;
-constexpr int kStatusDoneWord = 1;  // dequant-GEMV fused mode: finished-block counter
 // Wait limit of a forward run under mxmoe_set_fault_injection.
 constexpr unsigned long long kFaultWaitNs = 1000ull * 1000ull;  // 1 ms
 
@@ -441,9 +441,12 @@ int ensure_f4(mxmoe_layer* L) {
 
 // Power of two p with bound * p <= 2^14 (f16 keeps 11 significant bits up to
 // 65504, so the scaled operand stays normal and well inside the range).
+// Power of two that maps |v| <= bound to at most 512: the dequant-GEMV sums
+// 16 products of an E2M1 value (|code| <= 6) and a scaled activation in f16,
+// 16 * 6 * 512 = 49152 < 65504.
 float f16_range_scale(float bound) {
   if (!(bound > 0.0f) || !std::isfinite(bound)) return 1.0f;
-  const int ex = static_cast<int>(std::floor(std::log2(16384.0f / bound)));
+  const int ex = static_cast<int>(std::floor(std::log2(512.0f / bound)));
   return std::ldexp(1.0f, std::max(-60, std::min(60, ex)));
 }
 
@@ -596,20 +599,17 @@ int run_experts_f4(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, u
 // pairs.  With y (fused mode, mxmoe_forward) it also combines into y and
 // writes the canonical routing maps, and needs no permutation kernel before
 // it: its pairs come from the top-k ids and the router's f16 rows xh.
-// Without y it reads the permutation's counts / offsets / perm and writes
-// y_pair rows for mxmoe_combine.
+// Without y it takes each pair's local expert (pair_expert) and writes pair
+// row inv[pair] of y_pair for mxmoe_combine.
 int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
-               const float* route_w, const int32_t* perm, cudaStream_t st, const __half* xh = nullptr,
-               void* y = nullptr, int y_dtype = MXMOE_F32) {
+               const float* route_w, const int32_t* pair_expert, const int32_t* inv, cudaStream_t st,
+               const __half* xh = nullptr, void* y = nullptr, int y_dtype = MXMOE_F32) {
   Workspace& w = L->ws;
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
   // SwiGLU rows as f16 in the f32 activation buffer (half its bytes)
   if (!w.act_f32) TRY(dalloc(&w.act_f32, static_cast<size_t>(w.rows) * L->fp));
   w.pair_dtype = MXMOE_F32;
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[3], st));
-  // a token's k experts are distinct, so no expert gets more than n_tok pairs
-  const int max_pe = static_cast<int>(std::min<uint64_t>(n_tok, P));
-  const int max_ex = static_cast<int>(std::min<uint64_t>(P, L->e_count));
   DqParams a{};
   a.d = static_cast<int>(L->d);
   a.fp = static_cast<int>(L->fp);
@@ -625,9 +625,8 @@ int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint3
   a.b2 = L->b2;
   a.bias_mult = (L->cfg.flags & MXMOE_FLAG_BIAS_PER_FTILE) ? static_cast<float>((L->f + 255) / 256) : 1.0f;
   a.E = static_cast<int>(L->e_count);
-  a.poff = w.poff;
-  a.counts = w.counts;
-  a.perm = perm ? perm : w.perm_p;
+  a.topk_idx = pair_expert;
+  a.P = static_cast<int>(P);
   a.pair_k = static_cast<int>(k);
   a.xh = xh;
   a.x = x;
@@ -642,6 +641,7 @@ int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint3
   a.inv_act_scale = 1.0f / L->dq_act_scale;
   a.act = reinterpret_cast<__half*>(w.act_f32);
   a.y_pair = w.y_pair;
+  a.inv = inv;
   a.topk_w = route_w;
   a.err = L->err;
   a.sync = L->err + kStatusSyncOffset;
@@ -651,8 +651,6 @@ int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint3
   }
   if (y) {
     a.fused = 1;
-    a.topk_idx = w.topk_idx;
-    a.P = static_cast<int>(P);
     a.n_tok = static_cast<int>(n_tok);
     a.residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;
     a.y = y;
@@ -660,11 +658,8 @@ int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint3
     a.offsets = w.offsets;
     a.perm_c = w.perm_c;
     a.inv_c = w.inv_c;
-    a.done = L->err + kStatusDoneWord;
   }
-  // pairs staged per pass: up to 16 (several passes only for skewed batches)
-  a.ps = max_pe <= 1 ? 1 : max_pe <= 2 ? 2 : max_pe <= 4 ? 4 : max_pe <= 8 ? 8 : 16;
-  CUDA_TRY(launch_dqgemv_ffn(a, max_pe, max_ex, L->num_sms, L->smem_limit, st));
+  CUDA_TRY(launch_dqgemv_ffn(a, L->num_sms, L->smem_limit, st));
   if (L->profiling) {
     CUDA_TRY(cudaEventRecord(L->ev[4], st));  // W1, W2 (and in fused mode the combine) are one launch
     CUDA_TRY(cudaEventRecord(L->ev[5], st));
@@ -694,7 +689,9 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
     if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
     return MXMOE_OK;
   }
-  if (tp.gemv) return run_dqgemv(L, x, x_dtype, n_tok, k, rscale, route_w, perm, st);
+  // (the dequant-GEMV plan comes only from mxmoe_forward_local, whose pairs'
+  // local experts are ws.local_idx)
+  if (tp.gemv) return run_dqgemv(L, x, x_dtype, n_tok, k, rscale, route_w, w.local_idx, w.inv_p, st);
   const uint64_t kc1 = L->kp1 / kTileK, kc2 = L->kp2 / kTileK;
   if (tp.fp4)
     return run_experts_f4(L, x, x_dtype, n_tok, k, rscale, route_w, tp, st, ret_ptrs, ret_slot, y_by_pair, perm);
@@ -1087,7 +1084,7 @@ static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, voi
   if (tp.gemv) {
     // router -> one fused kernel (expert FFN, combine, routing maps)
     if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
-    TRY(run_dqgemv(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, nullptr, st, xh, y, y_dtype));
+    TRY(run_dqgemv(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, w.topk_idx, nullptr, st, xh, y, y_dtype));
     return MXMOE_OK;
   }
   CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, tp.fp4 ? tp.pair_tile : kRowBlock, tp.pair_tile,
@@ -1271,9 +1268,12 @@ int mxmoe_sync_status(mxmoe_layer* L, void* stream) {
   DeviceGuard g(L->cfg.device);
   CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
   CUDA_TRY(cudaGetLastError());
-  int herr = 0;
-  CUDA_TRY(cudaMemcpy(&herr, L->err, sizeof(int), cudaMemcpyDeviceToHost));
-  return device_status(herr);
+  int herr[5] = {0, 0, 0, 0, 0};
+  CUDA_TRY(cudaMemcpy(herr, L->err, sizeof(herr), cudaMemcpyDeviceToHost));
+  if (herr[0] == 8)
+    return fail(MXMOE_ERR_TIMEOUT, "dequant-GEMV W1->W2 grid wait gave up: saw %d of %d block arrivals", herr[3],
+                herr[4]);
+  return device_status(herr[0]);
 }
 
 int mxmoe_routing_results(mxmoe_layer* L, const int32_t** topk_idx, const float** topk_w, const int32_t** offsets,

@@ -1,62 +1,63 @@
 // dqgemv.cu -- fused MXFP4 dequant-GEMV expert FFN for decode batches (at
-// most a few routed pairs), on CUDA cores: W1 + SwiGLU-clamp and W2 + bias +
-// route weight in one launch.
+// most a few routed pairs), on CUDA cores: W1 + SwiGLU-clamp, W2 + bias +
+// route weight and (in the fused forward) the expert-order combine with the
+// residual, in one launch.
 //
 // Replaces, for few-token batches, the per-element byte-wise dequant loops of
-// w1_swiglu_dense_kernel / w2_scatter_dense_kernel (src/quant/gpu.rs:89-192):
-// there every token-row thread re-reads each weight byte and recomputes
-// exp(s * ln 2) per element; here each weight byte crosses HBM once per
-// forward, is decoded two codes per instruction, and serves every routed pair
-// of its expert.
+// w1_swiglu_dense_kernel / w2_scatter_dense_kernel (src/quant/gpu.rs:89-192)
+// and the per-expert accumulation of src/moe/mod.rs:279-411: there every
+// token-row thread re-reads each weight byte and recomputes exp(s * ln 2) per
+// element; here each weight byte crosses HBM once per forward, is decoded two
+// codes per instruction, and serves every routed pair of its expert.
 //
-// Work split (no host sync): one block per SM.  Each block finds the experts
-// with routed pairs, serves expert b % nt of the nt touched ones, and walks
-// that expert's W1 and then W2 row items with the other blocks of the same
-// expert (block-strided).  Untouched experts cost nothing.
+// Work split (no host sync, one block per SM, cooperative launch):
+//   W1: the GLU units of the touched experts, laid end to end in increasing
+//       expert order, are cut into gridDim.x equal contiguous ranges; block b
+//       computes range b for all of its expert's pairs.
+//   W2: the d output columns are cut into gridDim.x equal ranges; block b
+//       computes its columns for every touched expert, so it holds all k
+//       contributions of its columns and (fused forward) adds them in
+//       increasing expert order plus the residual and writes y itself.
+//   Between the two phases the blocks meet once on a grid-wide arrival
+//   counter (bounded wait; on timeout a status code and the arrival count
+//   are recorded and the kernel runs to its end).
 //
-// Block = 16 warps, each streaming its own items through a private ring of
-// shared-memory stages with 16-byte cp.async copies (L2 evict-first): D - 1
-// items in flight while one is computed.  An item is two weight rows (W1: a
-// GLU unit's GLU and linear row; W2: output columns 2m, 2m + 1) with their
-// E8M0 scale rows (a row-major copy of the scales kept for this kernel).
-// Items are taken in order from a per-block counter; W2's weights are
-// already arriving while the last W1 items are computed.
+// Data movement: a copy warp streams the block's weight ranges (contiguous
+// rows: a W1 chunk is up to 8 GLU rows plus their 8 linear partner rows, a
+// W2 chunk up to a slot's worth of output rows, each with its E8M0 scale
+// rows) into a ring of shared-memory slots with cp.async.bulk (L2
+// evict-first), one mbarrier pair per slot, keeping about 48 KB in flight per
+// SM (its share of HBM bandwidth times latency; more only lengthens the
+// memory queues the compute warps' own reads wait in).  It runs ahead into W2
+// while W1 is computed, so the W2 weights are on chip when the grid barrier
+// opens.  The block's small reads (token rows, biases) are issued before the
+// weight stream.  Items (a W1 GLU unit = two rows, or a W2 column pair) go to
+// the 16 compute warps round robin over the block's whole sequence.
 //
 // Math: lane l covers the 32-column blocks kb = l + 32 i of both rows (one
 // 16-byte code load each, conflict-free), decodes them with
-// cvt.rn.f16x2.e2m1x2 and multiplies with `fma.rn.f32.f16` against the
-// activation rows staged in shared memory as f16: the E2M1 value times the
-// f16 activation is exact, the sum is f32.  Per block the sum is scaled once
-// by 2^(s - 127); the warp then reduces all (row, pair) sums at once by
-// halving exchanges.  The K loop is unrolled at compile time (KI blocks per
-// lane) and the pair count is dispatched to unrolled variants, so the
-// instruction stream has no runtime predicates or divergent branches.
+// cvt.rn.f16x2.e2m1x2 and multiplies pairs of columns with packed f16 FMAs
+// against the activation rows staged in shared memory as f16: each E2M1 value
+// times the f16 activation rounds once, the 16 products of a block half sum
+// in f16 (the activation scales keep |sum| <= 16 * 6 * 512), the two halves
+// and every block after that in f32.  Per block the sum is scaled once by
+// 2^(s - 127); the warp then reduces all (row, pair) sums at once by halving
+// exchanges.  The K loop is unrolled at compile time (KI blocks per lane) and
+// the pair count is dispatched to unrolled variants.
 //
-// Activations: W1 stages the router's normalized token rows (x * (1/rms) *
-// gamma as f16, written by the router), W2 the f16 SwiGLU rows W1 wrote;
-// both carry a power of two that keeps them in f16's normal range (|x_hat| <=
+// Activations: W1 stages one router-normalized token row per token (x *
+// (1/rms) * gamma as f16, written by the router), W2 the f16 SwiGLU row of
+// each pair; both carry a power of two that bounds them by 512 (|x_hat| <=
 // sqrt(d) * max|gamma| after RmsNorm; |act| <= max(limit, 0.28 / alpha) *
-// (limit + 1) after the clamp).  The swizzle puts lane l's four 16-byte pieces
-// of a 32-column block 512 bytes apart, so a quarter warp reads 128
-// contiguous bytes.  The staged rows are copied before the weight stream
-// starts: behind it they would wait for every SM's weight requests.
-//
-// W1 -> W2: W2 needs every SwiGLU column of its expert, written by all blocks
-// of that expert.  The blocks meet on a per-expert arrival counter in global
-// memory, zeroed before every forward.  The launch is cooperative (all blocks
-// resident at once), and the wait is bounded: on timeout it records a status
-// code and the kernel carries on to its end.
-//
-// Fused mode (mxmoe_forward): no permutation kernel runs before this one; the
-// blocks take their pairs from the canonical top-k ids, and the last block to
-// finish adds each token's pair rows in increasing expert order plus the
-// residual and writes the canonical routing maps.  The forward is then the
-// router and this kernel.
+// (limit + 1) after the clamp), which keeps the f16 block sums finite.  The
+// swizzle puts lane l's four 16-byte pieces of a 32-column block 512 bytes
+// apart, so a quarter warp reads 128 contiguous bytes.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 
 #include "kernels.h"
 #include "launch_util.h"
@@ -66,6 +67,20 @@
 namespace mxmoe {
 
 namespace {
+
+constexpr int kDqWarps = 16;                     // compute warps per block
+constexpr int kDqConsumers = 32 * kDqWarps;
+constexpr int kDqThreads = kDqConsumers + 32;    // + the copy warp
+constexpr int kDqMaxPairs = 8;                   // routed pairs per launch
+constexpr int kDqMaxSlots = 8;
+constexpr int kDqMaxCols = 64;                   // W2 output columns per block
+constexpr int kDqMaxUnits = 256;                 // W1 GLU units per block
+constexpr int kDqRows = 2;                       // weight rows per item
+// per-block float scratch after the staged rows: W2 partial sums, W1 / W2 biases
+constexpr int kDqScratchFloats = kDqMaxPairs * kDqMaxCols + 2 * kDqMaxUnits + kDqMaxPairs * kDqMaxCols;
+// status codes of this kernel (the layer's status word)
+constexpr int kDqErrGrid = 8;  // the blocks did not all finish W1 in time
+constexpr int kDqErrCopy = 9;  // a weight chunk did not land, or a slot was not released, in time
 
 // Build-time timeline probe (-DMXMOE_DQ_TRACE, never in the shipped build):
 // lane 0 of every warp stamps %globaltimer at fixed event slots.
@@ -83,11 +98,11 @@ __device__ unsigned long long g_dq_trace[160 * 17 * kDqTraceSlots];
   } while (0)
 #endif
 
-constexpr int kDqWarps = 16;  // warps per block
-constexpr int kDqThreads = 32 * kDqWarps;
-constexpr int kDqRows = 2;  // weight rows per item
-// status codes of this kernel (the layer's status word)
-constexpr int kDqErrExpert = 8;  // the blocks of an expert did not all finish W1 in time
+__device__ __forceinline__ __half2 u32_h2(uint32_t u) {
+  __half2 h;
+  memcpy(&h, &u, 4);
+  return h;
+}
 
 // E2M1 code word (8 codes, low nibble first) -> four f16x2 (low half = even column).
 __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
@@ -99,30 +114,6 @@ __device__ __forceinline__ void e2m1x8_to_f16x2(uint32_t w, uint32_t (&h)[4]) {
       "cvt.rn.f16x2.e2m1x2 %3, b3;\n\t}"
       : "=r"(h[0]), "=r"(h[1]), "=r"(h[2]), "=r"(h[3])
       : "r"(w));
-}
-
-// a0 += the even-column products, a1 += the odd ones, over 8 columns: w (four
-// f16x2 weights) times x (four f16x2 activations), exact products, f32 sums.
-__device__ __forceinline__ void fma8_f16_f32(float& a0, float& a1, const uint32_t (&w)[4], uint4 x) {
-  asm("{\n\t.reg .f16 wl0, wh0, wl1, wh1, wl2, wh2, wl3, wh3, xl0, xh0, xl1, xh1, xl2, xh2, xl3, xh3;\n\t"
-      "mov.b32 {wl0, wh0}, %2;\n\t"
-      "mov.b32 {wl1, wh1}, %3;\n\t"
-      "mov.b32 {wl2, wh2}, %4;\n\t"
-      "mov.b32 {wl3, wh3}, %5;\n\t"
-      "mov.b32 {xl0, xh0}, %6;\n\t"
-      "mov.b32 {xl1, xh1}, %7;\n\t"
-      "mov.b32 {xl2, xh2}, %8;\n\t"
-      "mov.b32 {xl3, xh3}, %9;\n\t"
-      "fma.rn.f32.f16 %0, wl0, xl0, %0;\n\t"
-      "fma.rn.f32.f16 %1, wh0, xh0, %1;\n\t"
-      "fma.rn.f32.f16 %0, wl1, xl1, %0;\n\t"
-      "fma.rn.f32.f16 %1, wh1, xh1, %1;\n\t"
-      "fma.rn.f32.f16 %0, wl2, xl2, %0;\n\t"
-      "fma.rn.f32.f16 %1, wh2, xh2, %1;\n\t"
-      "fma.rn.f32.f16 %0, wl3, xl3, %0;\n\t"
-      "fma.rn.f32.f16 %1, wh3, xh3, %1;\n\t}"
-      : "+f"(a0), "+f"(a1)
-      : "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(x.x), "r"(x.y), "r"(x.z), "r"(x.w));
 }
 
 // 2^(s - 127) for an E8M0 byte (0 -> 2^-127, 255 -> inf, as the format's
@@ -137,61 +128,6 @@ __device__ __forceinline__ int dq_piece(int p, int ki, int kb, int q) {
   return p * ki * 128 + ((kb >> 5) * 4 + q) * 32 + (kb & 31);
 }
 
-
-struct DqSlot {
-  int e;     // local expert
-  int g, G;  // this block's index among the G blocks of its expert
-};
-
-// The touched experts (count > 0) in increasing index are numbered 0..nt-1;
-// block b serves number b % nt as block b / nt of its group.  Every warp
-// computes the same answer.  Counts are read through L2.
-__device__ __forceinline__ bool dq_find_slot(const int32_t* counts, int E, const int (&cnt_r)[4], DqSlot& s) {
-  const int lane = threadIdx.x & 31;
-  // experts below 128 come from the preloaded counts, the rest are loaded
-  uint32_t mask[4];
-  int nt = 0;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    mask[i] = __ballot_sync(0xFFFFFFFFu, cnt_r[i] > 0);
-    nt += __popc(mask[i]);
-  }
-  for (int base = 128; base < E; base += 32) {
-    const int e = base + lane;
-    nt += __popc(__ballot_sync(0xFFFFFFFFu, e < E && __ldcg(counts + e) > 0));
-  }
-  if (nt == 0) return false;
-  const int B = gridDim.x, b = blockIdx.x;
-  const int slot = b % nt;
-  s.g = b / nt;
-  s.G = (B - slot + nt - 1) / nt;
-  int seen = 0;
-  for (int base = 0; base < E; base += 32) {
-    const int e = base + lane;
-    uint32_t m = 0;
-    if (base < 128) {
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        if (base == 32 * i) m = mask[i];
-    } else {
-      m = __ballot_sync(0xFFFFFFFFu, e < E && __ldcg(counts + e) > 0);
-    }
-    const int n = __popc(m);
-    if (slot < seen + n) {
-      for (int r = slot - seen; r > 0; --r) m &= m - 1;
-      s.e = base + __ffs(m) - 1;
-      return true;
-    }
-    seen += n;
-  }
-  return false;
-}
-
-// Position of the r-th set bit (r < popc(m)).
-__device__ __forceinline__ int dq_nth_bit(uint32_t m, int r) {
-  for (; r > 0; --r) m &= m - 1;
-  return __ffs(m) - 1;
-}
 
 // 8 consecutive source values -> f32 (f16 sources were written earlier in
 // this forward by other blocks: read through L2).
@@ -219,100 +155,6 @@ __device__ __forceinline__ void dq_src8(const void* p, int dtype, float (&v)[8])
   }
 }
 
-// Synchronous W1 staging from the token rows x (when no f16 rows were
-// prepared): np rows of x * (1/rms) * gamma * x_scale as f16, in dq_piece
-// order.  Piece p of a row is (kb = p / 4, q = p % 4): consecutive threads
-// read consecutive 16-byte pieces of the source row.
-__device__ void dq_stage_x(uint4* xs, const DqParams& a, int ki, int p0, int base, int np) {
-  const int kbr = a.d / 32;
-  for (int j = 0; j < np; ++j) {
-    const int t = __ldcg(a.perm + p0 + base + j) / a.pair_k;
-    const float rs = __ldcg(a.rscale + t) * a.x_scale;
-    for (int p = threadIdx.x; p < 4 * kbr; p += kDqThreads) {
-      const int kb = p >> 2, q = p & 3, c = kb * 32 + q * 8;
-      float v[8];
-      dq_src8(static_cast<const char*>(a.x) + (static_cast<uint64_t>(t) * a.d + c) * (a.x_dtype == kDqSrcF32 ? 4 : 2),
-              a.x_dtype, v);
-      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gamma + c));
-      const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gamma + c) + 1);
-      v[0] *= g0.x; v[1] *= g0.y; v[2] *= g0.z; v[3] *= g0.w; v[4] *= g1.x; v[5] *= g1.y; v[6] *= g1.z; v[7] *= g1.w;
-      uint4 o;
-      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const __half2 hv = __floats2half2_rn(v[2 * h] * rs, v[2 * h + 1] * rs);
-        ow[h] = *reinterpret_cast<const uint32_t*>(&hv);
-      }
-      xs[dq_piece(j, ki, kb, q)] = o;
-    }
-  }
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
-}
-// Asynchronous staging of np f16 rows of K columns into xs (dq_piece order),
-// row j at rows[j] (shared memory, filled by the caller): one 16-byte copy per
-// piece, issued by all threads; the caller commits and waits.
-__device__ __forceinline__ void dq_stage_async(uint4* xs, const __half* const* rows, int K, int ki, int np) {
-  const int kbr = K / 32;
-  for (int j = 0; j < np; ++j) {
-    const __half* src = rows[j];
-    for (int p = threadIdx.x; p < 4 * kbr; p += kDqThreads) {
-      const int kb = p >> 2, q = p & 3;
-      cp_async16(smem_u32(xs + dq_piece(j, ki, kb, q)), src + kb * 32 + q * 8);
-    }
-  }
-}
-
-// Item t of a block's sequence: W1 items (passes x c1), then W2 items (passes x c2).
-struct DqItem {
-  bool w2;
-  int pass, m;
-};
-__device__ __forceinline__ DqItem dq_item(int t, int n1, int c1, int c2, int g, int G, int passes) {
-  DqItem it;
-  it.w2 = t >= n1;
-  const int u = it.w2 ? t - n1 : t;
-  const int c = it.w2 ? c2 : c1;
-  it.pass = passes == 1 ? 0 : u / c;  // one pass is the common case: no division
-  it.m = g + (u - it.pass * c) * G;
-  return it;
-}
-
-// Weight rows of an item: W1 item m = GLU unit m (its GLU row, then its
-// linear row, in the packed order); W2 item m = output columns 2m, 2m + 1.
-__device__ __forceinline__ uint32_t dq_row(const DqItem& it, int r) {
-  return it.w2 ? 2u * it.m + r : w1_packed_row(static_cast<uint32_t>(it.m), static_cast<uint32_t>(r));
-}
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, uint64_t pol) {
-  asm volatile("cp.async.cg.shared.global.L2::cache_hint [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "l"(pol)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-
-// The warp's copies of item t into its stage buffer: the codes of the two
-// rows, then their scale rows, 16 bytes per lane and instruction.
-__device__ __forceinline__ void dq_issue(const DqParams& a, int e, const DqItem& it, uint8_t* buf, int lane,
-                                         uint64_t pol) {
-  const uint32_t rb = static_cast<uint32_t>(it.w2 ? a.kp2 : a.kp1) / 2, sr = it.w2 ? a.sr2 : a.sr1;
-  const uint32_t rows = it.w2 ? static_cast<uint32_t>(a.d) : 2u * a.fp;
-  const uint8_t* q = (it.w2 ? a.w2q : a.w1q) + static_cast<uint64_t>(e) * rows * rb;
-  const uint8_t* sc = (it.w2 ? a.w2sr : a.w1sr) + static_cast<uint64_t>(e) * rows * sr;
-  const uint32_t dst = smem_u32(buf);
-#pragma unroll
-  for (int r = 0; r < kDqRows; ++r) {
-    const uint64_t row = dq_row(it, r);
-    for (uint32_t k = lane * 16u; k < rb; k += 512u) cp_async16(dst + r * rb + k, q + row * rb + k, pol);
-    for (uint32_t k = lane * 16u; k < sr; k += 512u) cp_async16(dst + kDqRows * rb + r * sr + k, sc + row * sr + k, pol);
-  }
-}
-
 // Sum over the warp of V values per lane (V a power of two <= 32) in
 // V - 1 + (5 - log2 V) shuffles: halving exchanges leave lane L with value
 // L % V of its group, then butterflies finish it.  Returns lane L's total of
@@ -335,19 +177,126 @@ __device__ __forceinline__ float dq_warp_reduce(float (&v)[V], int lane) {
   return r;
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async4(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;" ::: "memory"); }
+// The compute warps' own barrier (the copy warp never joins it).
+__device__ __forceinline__ void dq_bar() { asm volatile("bar.sync 1, %0;" ::"n"(kDqConsumers) : "memory"); }
+
+// The routed pairs of this launch, sorted by (expert, pair): rank r is pair
+// pair[r] of token tok[r] on local expert exp[r] with route weight w[r].
+// Touched expert i (increasing) is te_exp[i], owning ranks te_lo[i] ..
+// te_lo[i + 1] - 1.  W1 stages one row per token (row t = token t), W2 one
+// per rank (ident).
+struct DqTable {
+  int pair[kDqMaxPairs], tok[kDqMaxPairs], exp[kDqMaxPairs];
+  float w[kDqMaxPairs];
+  int te_exp[kDqMaxPairs], te_lo[kDqMaxPairs + 1];
+  int ident[kDqMaxPairs];
+  int n, nt;
+};
+
+// One piece of a block's weight stream.
+struct DqChunk {
+  int w2;   // 0: W1 GLU units r0 .. r0 + len - 1; 1: W2 rows (output columns) r0 ..
+  int ei;   // touched-expert number
+  int r0, len;
+};
+
+// A block's chunk sequence: its W1 units [u, u1) of the touched experts' GLU
+// units laid end to end (expert-major), in pieces of at most cu units that
+// stay inside one 64-unit GLU block; then, for each touched expert in
+// increasing order, its output rows [c0, c1) of W2 in pieces of at most cr.
+// The copy warp and the compute warps walk the same sequence.
+struct DqWalk {
+  int u, u1, fp, cu;
+  int ei, nt, c, c0, c1, cr;
+  __device__ bool next(DqChunk& ch) {
+    if (u < u1) {
+      const int e = u / fp, m = u - e * fp;
+      const int len = min(min(u1 - u, cu), kGluBlock - m % kGluBlock);
+      ch = DqChunk{0, e, m, len};
+      u += len;
+      return true;
+    }
+    while (ei < nt) {
+      if (c < c1) {
+        const int len = min(c1 - c, cr);
+        ch = DqChunk{1, ei, c, len};
+        c += len;
+        return true;
+      }
+      ++ei;
+      c = c0;
+    }
+    return false;
+  }
+};
+
+// Synchronous W1 staging from the token rows x (when no f16 rows were
+// prepared): rows t < ntok of x * (1/rms) * gamma * x_scale as f16, in
+// dq_piece order.  Consecutive threads read consecutive 16-byte pieces.
+__device__ void dq_stage_x(uint4* xs, const DqParams& a, int ntok, int ki) {
+  const int kbr = a.d / 32;
+  for (int t = 0; t < ntok; ++t) {
+    const float rs = __ldcg(a.rscale + t) * a.x_scale;
+    for (int p = threadIdx.x; p < 4 * kbr; p += kDqConsumers) {
+      const int kb = p >> 2, q = p & 3, c = kb * 32 + q * 8;
+      float v[8];
+      dq_src8(static_cast<const char*>(a.x) + (static_cast<uint64_t>(t) * a.d + c) * (a.x_dtype == kDqSrcF32 ? 4 : 2),
+              a.x_dtype, v);
+      const float4 g0 = __ldg(reinterpret_cast<const float4*>(a.gamma + c));
+      const float4 g1 = __ldg(reinterpret_cast<const float4*>(a.gamma + c) + 1);
+      v[0] *= g0.x; v[1] *= g0.y; v[2] *= g0.z; v[3] *= g0.w; v[4] *= g1.x; v[5] *= g1.y; v[6] *= g1.z; v[7] *= g1.w;
+      uint4 o;
+      uint32_t* ow = reinterpret_cast<uint32_t*>(&o);
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const __half2 hv = __floats2half2_rn(v[2 * h] * rs, v[2 * h + 1] * rs);
+        ow[h] = *reinterpret_cast<const uint32_t*>(&hv);
+      }
+      xs[dq_piece(t, ki, kb, q)] = o;
+    }
+  }
+}
+
+// Asynchronous staging of n f16 rows of K columns into xs (dq_piece order),
+// staged row j from base + key[j] * stride: one 16-byte copy per piece,
+// issued by the compute threads; the caller commits and waits.
+__device__ __forceinline__ void dq_stage_async(uint4* xs, const __half* base, const int* key, uint64_t stride, int n,
+                                               int K, int ki) {
+  const int kbr = K / 32;
+  for (int j = 0; j < n; ++j) {
+    const __half* src = base + static_cast<uint64_t>(key[j]) * stride;
+    for (int p = threadIdx.x; p < 4 * kbr; p += kDqConsumers) {
+      const int kb = p >> 2, q = p & 3;
+      cp_async16(smem_u32(xs + dq_piece(j, ki, kb, q)), src + kb * 32 + q * 8);
+    }
+  }
+}
+
 __host__ __device__ constexpr int dq_pow2(int n) { return n <= 1 ? 1 : n <= 2 ? 2 : n <= 4 ? 4 : 8; }
 
-// Dot products of the item's two weight rows (stage buffer sb) with staged
-// rows j0 .. j0 + NP - 1, reduced over the warp: lane L returns the sum of
-// (row (L % V) / NPP, pair L % NPP), V = 2 * NPP.  Fully unrolled over the
-// KI 32-column blocks of a lane; lanes past the last block read zero codes.
+// Dot products of two weight rows (codes c0 / c1, scale rows s0 / s1) with
+// the staged rows of ranks j0 .. j0 + NP - 1 (staged row rix[rank]), reduced
+// over the warp: lane L returns the sum of (row (L % V) / NPP, rank j0 +
+// L % NPP), V = 2 * NPP.  Fully unrolled over the KI 32-column blocks of a
+// lane; lanes past the last block read zero codes.
 template <int KI, int NP>
-__device__ __forceinline__ float dq_dot(const uint8_t* sb, uint32_t rb, uint32_t sr, const uint4* xs, int kbr,
-                                        int lane, int j0) {
+__device__ __forceinline__ float dq_dot(const uint8_t* c0, const uint8_t* c1, const uint8_t* s0, const uint8_t* s1,
+                                        const uint4* xs, const int* rix, int kbr, int lane, int j0) {
   constexpr int NPP = dq_pow2(NP);
   float acc[kDqRows * NPP];
 #pragma unroll
   for (int i = 0; i < kDqRows * NPP; ++i) acc[i] = 0.0f;
+  int row[NP];
+#pragma unroll
+  for (int j = 0; j < NP; ++j) row[j] = rix[j0 + j];
 #pragma unroll
   for (int i = 0; i < KI; ++i) {
     const int kb = lane + 32 * i;
@@ -357,359 +306,358 @@ __device__ __forceinline__ float dq_dot(const uint8_t* sb, uint32_t rb, uint32_t
 #pragma unroll
     for (int r = 0; r < kDqRows; ++r) {
       uint4 cw = make_uint4(0u, 0u, 0u, 0u);
-      if (ok) cw = *reinterpret_cast<const uint4*>(sb + r * rb + kb * 16);
+      if (ok) cw = *reinterpret_cast<const uint4*>((r ? c1 : c0) + kb * 16);
       e2m1x8_to_f16x2(cw.x, h[r][0]);
       e2m1x8_to_f16x2(cw.y, h[r][1]);
       e2m1x8_to_f16x2(cw.z, h[r][2]);
       e2m1x8_to_f16x2(cw.w, h[r][3]);
-      sc[r] = ok ? e8m0_to_f32(sb[kDqRows * rb + r * sr + kb]) : 0.0f;
+      sc[r] = ok ? e8m0_to_f32((r ? s1 : s0)[kb]) : 0.0f;
     }
 #pragma unroll
     for (int j = 0; j < NP; ++j) {
       uint4 xv[4];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) xv[q] = xs[dq_piece(j0 + j, KI, kb, q)];
+      for (int q = 0; q < 4; ++q) xv[q] = xs[dq_piece(row[j], KI, kb, q)];
 #pragma unroll
       for (int r = 0; r < kDqRows; ++r) {
-        float a0 = 0.0f, a1 = 0.0f, a2 = 0.0f, a3 = 0.0f;  // four short chains
-        fma8_f16_f32(a0, a1, h[r][0], xv[0]);
-        fma8_f16_f32(a2, a3, h[r][1], xv[1]);
-        fma8_f16_f32(a0, a1, h[r][2], xv[2]);
-        fma8_f16_f32(a2, a3, h[r][3], xv[3]);
-        acc[r * NPP + j] = fmaf((a0 + a1) + (a2 + a3), sc[r], acc[r * NPP + j]);
+        // packed f16 products summed in f16 over the block's 32 columns (two
+        // chains of 8), then one f32 scale step
+        __half2 p0 = __float2half2_rn(0.0f), p1 = p0;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          p0 = __hfma2(u32_h2(h[r][q][0]), u32_h2(xv[q].x), p0);
+          p1 = __hfma2(u32_h2(h[r][q][1]), u32_h2(xv[q].y), p1);
+          p0 = __hfma2(u32_h2(h[r][q][2]), u32_h2(xv[q].z), p0);
+          p1 = __hfma2(u32_h2(h[r][q][3]), u32_h2(xv[q].w), p1);
+        }
+        const float2 f = __half22float2(__hadd2(p0, p1));
+        acc[r * NPP + j] = fmaf(f.x + f.y, sc[r], acc[r * NPP + j]);
       }
     }
   }
   return dq_warp_reduce<kDqRows * NPP>(acc, lane);
 }
 
-// One item's outputs for staged rows j0 .. j0 + NP - 1 of its pass.
+// W1 item: GLU unit m of one expert (its GLU row c0/s0 and linear row c1/s1)
+// against ranks j0 .. j0 + NP - 1 -> the SwiGLU values of those pairs.
 template <int KI, int NP>
-__device__ __forceinline__ void dq_finish(const DqParams& a, const DqItem& it, const uint8_t* sb, const uint4* xs,
-                                          const float* rw, const int* pos_s, int lane, int j0, float bias) {
+__device__ __forceinline__ void dq_w1_item(const DqParams& a, const DqTable& tb, const uint8_t* c0, const uint8_t* c1,
+                                           const uint8_t* s0, const uint8_t* s1, const uint4* xs, int lane, int j0,
+                                           int m, float bias) {
   constexpr int NPP = dq_pow2(NP);
-  const uint32_t rb = static_cast<uint32_t>(it.w2 ? a.kp2 : a.kp1) / 2, sr = it.w2 ? a.sr2 : a.sr1;
-  const int kbr = (it.w2 ? a.fp : a.d) / 32;
-  const float v = dq_dot<KI, NP>(sb, rb, sr, xs, kbr, lane, j0);
+  const float v = dq_dot<KI, NP>(c0, c1, s0, s1, xs, tb.tok, a.d / 32, lane, j0);
+  // lane j (< NPP) holds the GLU row's sum of rank j0 + j, lane NPP + j the linear row's
+  const float vl = __shfl_sync(0xFFFFFFFFu, v, (lane + NPP) & 31);
+  const float bg = __shfl_sync(0xFFFFFFFFu, bias, 0), bl = __shfl_sync(0xFFFFFFFFu, bias, 1);
+  if (lane < NP) {
+    const float xg = fminf(v * a.inv_x_scale + bg, a.limit);
+    const float xl = fmaxf(-a.limit, fminf(vl * a.inv_x_scale + bl, a.limit));
+    const float act = (xg / (1.0f + expf(-a.alpha * xg))) * (xl + 1.0f);
+    a.act[static_cast<uint64_t>(tb.pair[j0 + lane]) * a.fp + m] = __float2half_rn(act * a.act_scale);
+  }
+}
+
+// W2 item: output columns col, col + 1 (nrow of them valid) of one expert
+// against ranks j0 .. j0 + NP - 1: (sum / act_scale + b2) * route weight,
+// into the block's partial sums (fused) or the pair rows of y_pair.
+template <int KI, int NP>
+__device__ __forceinline__ void dq_w2_item(const DqParams& a, const DqTable& tb, const uint8_t* c0, const uint8_t* c1,
+                                           const uint8_t* s0, const uint8_t* s1, const uint4* xs, int lane, int j0,
+                                           int col, int nrow, int col0, float bias, float* partial) {
+  constexpr int NPP = dq_pow2(NP);
+  const float v = dq_dot<KI, NP>(c0, c1, s0, s1, xs, tb.ident, a.fp / 32, lane, j0);
   const int vi = lane % (kDqRows * NPP), r = vi / NPP, j = vi % NPP;
   const float br = __shfl_sync(0xFFFFFFFFu, bias, r);
-  if (!it.w2) {
-    // lane j (< NPP) holds the GLU row's sum of pair j, lane NPP + j the linear row's
-    const float vl = __shfl_sync(0xFFFFFFFFu, v, (lane + NPP) & 31);
-    const float bl = __shfl_sync(0xFFFFFFFFu, bias, 1);
-    if (lane < NP) {
-      const float xg = fminf(v * a.inv_x_scale + br, a.limit);
-      const float xl = fmaxf(-a.limit, fminf(vl * a.inv_x_scale + bl, a.limit));
-      const float act = (xg / (1.0f + expf(-a.alpha * xg))) * (xl + 1.0f);
-      a.act[static_cast<uint64_t>(pos_s[j0 + lane]) * a.fp + it.m] = __float2half_rn(act * a.act_scale);
-    }
-  } else if (lane < kDqRows * NPP && j < NP) {
-    a.y_pair[static_cast<uint64_t>(pos_s[j0 + j]) * a.d + 2 * it.m + r] = (v * a.inv_act_scale + br) * rw[j0 + j];
+  if (lane < kDqRows * NPP && j < NP && r < nrow) {
+    const int rank = j0 + j;
+    const float val = (v * a.inv_act_scale + br) * tb.w[rank];
+    if (a.fused)
+      partial[rank * kDqMaxCols + col + r - col0] = val;
+    else
+      a.y_pair[static_cast<uint64_t>(__ldg(a.inv + tb.pair[rank])) * a.d + col + r] = val;
   }
 }
 
-// D: stage buffers per warp (D - 1 items in flight while one is computed).
-// Fused mode (a.fused, at most 64 routed pairs): no permutation kernel runs
-// before this one.  Each block derives the touched experts and its expert's
-// pairs from the canonical top-k ids; act and y_pair rows are indexed by the
-// canonical pair t * k + s; the last block to finish adds the k pair rows of
-// every token in increasing expert order (plus the residual), as the combine
-// kernel does, and writes the canonical routing maps (offsets, perm, inv).
-__device__ void dq_combine_and_maps(const DqParams& a, const int32_t* tk_s) {
-  const int P = a.P, k = a.pair_k, n = a.n_tok, d = a.d;
-  // canonical maps: stable sort of the pairs by expert id
-  for (int e = threadIdx.x; e <= a.E; e += kDqThreads) {
-    int c = 0;
-    for (int p = 0; p < P; ++p) c += tk_s[p] < e;
-    a.offsets[e] = c;
-  }
-  for (int p = threadIdx.x; p < P; p += kDqThreads) {
-    const int id = tk_s[p];
-    int pos = 0;
-    for (int q = 0; q < P; ++q) pos += tk_s[q] < id || (tk_s[q] == id && q < p);
-    a.perm_c[pos] = p;
-    a.inv_c[p] = pos;
-  }
-  // y[t] = x[t] + sum over the token's pairs in increasing expert order
-  const int c4 = d / 4;
-  for (int i = threadIdx.x; i < n * c4; i += kDqThreads) {
-    const int t = i / c4, c = (i - t * c4) * 4;
-    int ord[kMaxTopK], ex[kMaxTopK];
-    for (int q = 0; q < k; ++q) {
-      ord[q] = t * k + q;
-      ex[q] = tk_s[t * k + q];
-    }
-    for (int q = 1; q < k; ++q)
-      for (int b = q; b > 0 && ex[b - 1] > ex[b]; --b) {
-        int tmp = ex[b]; ex[b] = ex[b - 1]; ex[b - 1] = tmp;
-        tmp = ord[b]; ord[b] = ord[b - 1]; ord[b - 1] = tmp;
-      }
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int q = 0; q < k; ++q) {
-      const float4 v = __ldcg(reinterpret_cast<const float4*>(a.y_pair + static_cast<uint64_t>(ord[q]) * d + c));
-      acc.x = __fadd_rn(acc.x, v.x); acc.y = __fadd_rn(acc.y, v.y);
-      acc.z = __fadd_rn(acc.z, v.z); acc.w = __fadd_rn(acc.w, v.w);
-    }
-    if (a.residual) {
-      float xv[4];
-      if (a.x_dtype == kDqSrcF32) {
-        const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(a.x) + static_cast<uint64_t>(t) * d + c));
-        xv[0] = f.x; xv[1] = f.y; xv[2] = f.z; xv[3] = f.w;
-      } else {
-        const uint2 u = __ldg(reinterpret_cast<const uint2*>(static_cast<const __nv_bfloat16*>(a.x) + static_cast<uint64_t>(t) * d + c));
-        xv[0] = __uint_as_float(u.x << 16); xv[1] = __uint_as_float(u.x & 0xFFFF0000u);
-        xv[2] = __uint_as_float(u.y << 16); xv[3] = __uint_as_float(u.y & 0xFFFF0000u);
-      }
-      acc.x = __fadd_rn(xv[0], acc.x); acc.y = __fadd_rn(xv[1], acc.y);
-      acc.z = __fadd_rn(xv[2], acc.z); acc.w = __fadd_rn(xv[3], acc.w);
-    }
-    if (a.y_dtype == kDqSrcF32) {
-      *reinterpret_cast<float4*>(static_cast<float*>(a.y) + static_cast<uint64_t>(t) * d + c) = acc;
-    } else {
-      const __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.y) + static_cast<uint64_t>(t) * d + c) =
-          make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
+template <int KI, bool W2>
+__device__ __forceinline__ void dq_item(const DqParams& a, const DqTable& tb, const uint8_t* c0, const uint8_t* c1,
+                                        const uint8_t* s0, const uint8_t* s1, const uint4* xs, int lane, int j0,
+                                        int np, int r0, int nrow, int col0, float bias, float* partial) {
+  // groups of up to four ranks, each with its own unrolled kernel
+  for (int g = 0; g < np; g += 4) {
+    switch (min(4, np - g)) {
+#define DQ_CASE(N)                                                                                \
+  case N:                                                                                         \
+    if (W2)                                                                                       \
+      dq_w2_item<KI, N>(a, tb, c0, c1, s0, s1, xs, lane, j0 + g, r0, nrow, col0, bias, partial); \
+    else                                                                                          \
+      dq_w1_item<KI, N>(a, tb, c0, c1, s0, s1, xs, lane, j0 + g, r0, bias);                      \
+    break;
+      DQ_CASE(1)
+      DQ_CASE(2)
+      DQ_CASE(3)
+      DQ_CASE(4)
+#undef DQ_CASE
     }
   }
 }
 
-// D: stage buffers per warp (D - 1 items in flight while one is computed).
-template <int D, int KI>
+template <int KI>
 __global__ void __launch_bounds__(kDqThreads, 1) mxmoe_dqgemv_ffn_kernel(const DqParams a) {
   extern __shared__ __align__(128) uint8_t dq_smem[];
-  __shared__ uint32_t present[32];  // fused mode: touched experts (E <= 1024) as a bit set
-  __shared__ int32_t tk_s[64];      // fused mode: the canonical top-k ids
-  __shared__ int last_block;
+  __shared__ DqTable tb;
+  __shared__ __align__(8) uint64_t full_bar[kDqMaxSlots], empty_bar[kDqMaxSlots];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr int ki = KI;  // 32-column blocks per lane (staged row stride: KI * 1024 columns)
-  uint4* xs = reinterpret_cast<uint4*>(dq_smem + static_cast<size_t>(kDqWarps) * D * a.stage_bytes);
-  float* rw = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + static_cast<size_t>(a.ps) * ki * 2048);
-  int* pos_s = reinterpret_cast<int*>(rw + 16);
-  const __half** rows_s = reinterpret_cast<const __half**>(pos_s + 16);
-  int* next = reinterpret_cast<int*>(rows_s + 16);
+  const int S = a.slots;
+  const uint32_t SB = a.slot_bytes;
+  uint8_t* slots = dq_smem;
+  uint4* xs = reinterpret_cast<uint4*>(dq_smem + static_cast<size_t>(S) * SB);
+  float* partial = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(xs) + static_cast<size_t>(a.xs_rows) * KI * 2048);
+  float* bias1 = partial + kDqMaxPairs * kDqMaxCols;  // [unit][GLU, linear] of the block's W1 units
+  float* bias2 = bias1 + 2 * kDqMaxUnits;             // [touched expert][column] of the block's W2 columns
+  const uint32_t rb1 = static_cast<uint32_t>(a.kp1) / 2, rb2 = static_cast<uint32_t>(a.kp2) / 2;
   // set-up that reads nothing from earlier kernels runs before the wait:
   // staged columns past K stay finite (zero) for the lanes that read them
-  if (threadIdx.x == 0) *next = 0;
-  if (threadIdx.x < 32) present[threadIdx.x] = 0u;
-  for (int i = threadIdx.x; i < a.ps * KI * 128; i += kDqThreads) xs[i] = make_uint4(0u, 0u, 0u, 0u);
+  if (threadIdx.x == kDqConsumers) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], kDqWarps);
+    }
+    fence_barrier_init();
+  }
+  for (int i = threadIdx.x; i < a.xs_rows * KI * 128; i += kDqThreads) xs[i] = make_uint4(0u, 0u, 0u, 0u);
   // what the kernel reads next comes from the kernels just before
   griddep_wait();
   griddep_launch_dependents();
   DQ_T(0);
-  DqSlot s;
-  int e, cnt, p0;
-  uint32_t pm[2] = {0u, 0u};  // the expert's pairs among the (at most 64) routed pairs
-  if (a.fused) {
-    if (threadIdx.x < a.P) {
-      const int id = __ldcg(a.topk_idx + threadIdx.x);
-      tk_s[threadIdx.x] = id;
-      atomicOr(&present[id >> 5], 1u << (id & 31));
+  if (warp == 0) {
+    // the pairs, sorted by (expert, pair) with a rank count over the lanes
+    int id = -1;
+    float w = 0.0f;
+    if (lane < a.P) {
+      id = __ldcg(a.topk_idx + lane);
+      w = __ldcg(a.topk_w + lane);
     }
-    __syncthreads();
-    // touched experts in increasing index: number b % nt serves this block
-    const uint32_t w = present[lane];
-    int pre = __popc(w);
+    const bool ok = lane < a.P && id >= 0 && id < a.E;
+    const uint32_t key = ok ? (static_cast<uint32_t>(id) << 3) | static_cast<uint32_t>(lane) : 0xFFFFFFFFu;
+    int rank = 0;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xFFFFFFFFu, pre, o);
-      if (lane >= o) pre += v;
+    for (int j = 0; j < kDqMaxPairs; ++j) rank += __shfl_sync(0xFFFFFFFFu, key, j) < key ? 1 : 0;
+    const int nv = __popc(__ballot_sync(0xFFFFFFFFu, ok));
+    if (ok) {
+      tb.pair[rank] = lane;
+      tb.tok[rank] = lane / a.pair_k;
+      tb.exp[rank] = id;
+      tb.w[rank] = w;
     }
-    const int nt = __shfl_sync(0xFFFFFFFFu, pre, 31);
-    const int slot = blockIdx.x % nt;
-    s.g = blockIdx.x / nt;
-    s.G = (gridDim.x - slot + nt - 1) / nt;
-    const uint32_t hit = __ballot_sync(0xFFFFFFFFu, pre > slot);
-    const int wl = __ffs(hit) - 1;  // word holding the slot-th touched expert
-    const int before = __shfl_sync(0xFFFFFFFFu, pre - __popc(w), wl);
-    e = 32 * wl + dq_nth_bit(__shfl_sync(0xFFFFFFFFu, w, wl), slot - before);
-#pragma unroll
-    for (int i = 0; i < 2; ++i) pm[i] = __ballot_sync(0xFFFFFFFFu, 32 * i + lane < a.P && tk_s[32 * i + lane] == e);
-    cnt = __popc(pm[0]) + __popc(pm[1]);
-    p0 = 0;
-  } else {
-    // one round of independent loads: the pair counts and offsets of up to
-    // 128 experts
-    constexpr int kCR = 4;
-    int cnt_r[kCR], off_r[kCR];
-#pragma unroll
-    for (int i = 0; i < kCR; ++i) {
-      const int ex = 32 * i + lane;
-      cnt_r[i] = ex < a.E ? __ldcg(a.counts + ex) : 0;
-      off_r[i] = ex < a.E ? __ldcg(a.poff + ex) : 0;
-    }
-    if (!dq_find_slot(a.counts, a.E, cnt_r, s)) return;
-    e = s.e;
-    if (e < 32 * kCR) {
-      int c = 0, o = 0;
-#pragma unroll
-      for (int i = 0; i < kCR; ++i)
-        if (e / 32 == i) {
-          c = cnt_r[i];
-          o = off_r[i];
-        }
-      cnt = __shfl_sync(0xFFFFFFFFu, c, e & 31);
-      p0 = __shfl_sync(0xFFFFFFFFu, o, e & 31);
-    } else {
-      cnt = __ldcg(a.counts + e);
-      p0 = __ldcg(a.poff + e);
-    }
-  }
-  DQ_T(1);
-  const int passes = (cnt + a.ps - 1) / a.ps;
-  const int items1 = a.fp, items2 = a.d / 2;
-  const int c1 = s.g < items1 ? (items1 - s.g + s.G - 1) / s.G : 0;
-  const int c2 = s.g < items2 ? (items2 - s.g + s.G - 1) / s.G : 0;
-  const int n1 = passes * c1, total = n1 + passes * c2;
-  uint8_t* ring = dq_smem + static_cast<size_t>(warp) * D * a.stage_bytes;
-  DQ_T(60);
-  // Stages one pass's activation rows: W1 the router's f16 token rows (or,
-  // without them, x normalized here), W2 the SwiGLU rows; the rows' pair
-  // positions go to pos_s and their route weights to rw.  Copies are
-  // committed as one group.
-  auto stage = [&](bool w2, int pass) {
-    const int base = pass * a.ps, np = min(a.ps, cnt - base);
-    __syncthreads();  // the previous pass's rows (and the zero fill) are done with
-    if (threadIdx.x < np) {
-      const int r = base + threadIdx.x;
-      int pair, pos;
-      if (a.fused) {
-        const int c0 = __popc(pm[0]);
-        pair = r < c0 ? dq_nth_bit(pm[0], r) : 32 + dq_nth_bit(pm[1], r - c0);
-        pos = pair;
-      } else {
-        pos = p0 + r;
-        pair = __ldcg(a.perm + pos);
-      }
-      pos_s[threadIdx.x] = pos;
-      rows_s[threadIdx.x] = w2 ? a.act + static_cast<uint64_t>(pos) * a.fp
-                               : (a.xh ? a.xh + static_cast<uint64_t>(pair / a.pair_k) * a.d : nullptr);
-      if (w2) rw[threadIdx.x] = __ldg(a.topk_w + pair);
-    }
-    __syncthreads();
-    if (!w2 && a.xh == nullptr)
-      dq_stage_x(xs, a, ki, p0, base, np);
-    else
-      dq_stage_async(xs, rows_s, w2 ? a.fp : a.d, ki, np);
-    cp_async_commit();
-  };
-  stage(false, 0);
-  const uint64_t pol = l2_evict_first_policy();
-  auto claim = [&]() {
-    int t = 0;
-    if (lane == 0) t = atomicAdd(next, 1);
-    return __shfl_sync(0xFFFFFFFFu, t, 0);
-  };
-  // The staged rows land first: issued after the weight stream they would
-  // queue behind every SM's weight requests (microseconds), issued alone they
-  // take one round trip.  Then the warp's pipeline is primed with D - 1 items.
-  cp_async_wait<0>();
-  DQ_T(62);
-  int queue[D];
-#pragma unroll
-  for (int q = 0; q < D - 1; ++q) {
-    queue[q] = claim();
-    if (queue[q] < total)
-      dq_issue(a, e, dq_item(queue[q], n1, c1, c2, s.g, s.G, passes), ring + q * a.stage_bytes, lane, pol);
-    cp_async_commit();
-  }
-  const int nphases = 2 * passes;
-  DQ_T(2);
-  __syncthreads();
-  DQ_T(3);
-  int nitem = 0;
-  int phase = 0;
-  int* arrive = a.sync + e;  // zeroed before every forward
-  for (int seq = 0;; ++seq) {
-    // keep D - 1 items in flight: claim and issue one more, then wait for the oldest
-    queue[D - 1] = claim();
-    if (queue[D - 1] < total)
-      dq_issue(a, e, dq_item(queue[D - 1], n1, c1, c2, s.g, s.G, passes), ring + ((seq + D - 1) % D) * a.stage_bytes,
-               lane, pol);
-    cp_async_commit();
-    const int t = queue[0];
-#pragma unroll
-    for (int q = 0; q < D - 1; ++q) queue[q] = queue[q + 1];
-    const DqItem it = t < total ? dq_item(t, n1, c1, c2, s.g, s.G, passes) : DqItem{true, passes, 0};
-    // the epilogue's bias values, fetched while the item's weights arrive
-    float bias = 0.0f;
-    if (t < total && lane < kDqRows)
-      bias = it.w2 ? __ldg(a.b2 + static_cast<uint64_t>(e) * a.d + dq_row(it, lane)) * a.bias_mult
-                   : __ldg(a.b1 + static_cast<uint64_t>(e) * (2u * a.fp) + dq_row(it, lane));
-    const int ph = t < total ? (it.w2 ? passes + it.pass : it.pass) : nphases;
-    // cross every phase boundary before this item (all warps do, in order)
-    while (phase < ph && phase + 1 < nphases) {
-      ++phase;
-      DQ_T(56);
-      __syncthreads();  // the previous phase's items are done
-      DQ_T(57);
-      const bool to_w2 = phase >= passes;
-      if (phase == passes) {
-        if (threadIdx.x == 0) {
-          // this block's SwiGLU columns are written: meet the expert's other blocks
-          __threadfence();
-          // (test hook: block 0 stays silent, so its expert's wait runs out)
-          if (!(a.skip_arrival && blockIdx.x == 0)) atomicAdd(arrive, 1);
-          const unsigned long long t0 = global_timer_ns();
-          const unsigned long long limit = a.wait_ns ? a.wait_ns : kWaitTimeoutNs;
-          while (true) {
-            int v;
-            asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(arrive) : "memory");
-            if (v >= s.G) break;
-            if (global_timer_ns() - t0 > limit) {
-              atomicCAS(a.err, 0, kDqErrExpert);
-              break;
-            }
-          }
-        }
-      }
-      DQ_T(58);
-      stage(to_w2, to_w2 ? phase - passes : phase);
-      cp_async_wait<0>();
-      __syncthreads();
-      DQ_T(59);
-    }
-    if (t >= total) break;
-    if (nitem < 12) DQ_T(4 + 4 * nitem);
-    cp_async_wait<D - 1>();  // this item's group has landed
+    if (lane < kDqMaxPairs) tb.ident[lane] = lane;
     __syncwarp();
-    if (nitem < 12) DQ_T(5 + 4 * nitem);
-    const uint8_t* sb = ring + (seq % D) * a.stage_bytes;
-    const int np = min(a.ps, cnt - it.pass * a.ps);
-    // groups of up to four staged rows, each with its own unrolled kernel
-    for (int j0 = 0; j0 < np; j0 += 4) {
-      switch (min(4, np - j0)) {
-        case 1: dq_finish<KI, 1>(a, it, sb, xs, rw, pos_s, lane, j0, bias); break;
-        case 2: dq_finish<KI, 2>(a, it, sb, xs, rw, pos_s, lane, j0, bias); break;
-        case 3: dq_finish<KI, 3>(a, it, sb, xs, rw, pos_s, lane, j0, bias); break;
-        default: dq_finish<KI, 4>(a, it, sb, xs, rw, pos_s, lane, j0, bias); break;
+    const int er = lane < nv ? tb.exp[lane] : -1;
+    const int eprev = __shfl_up_sync(0xFFFFFFFFu, er, 1);
+    const bool first = lane < nv && (lane == 0 || eprev != er);
+    const uint32_t fm = __ballot_sync(0xFFFFFFFFu, first);
+    if (first) {
+      const int i = __popc(fm & ((1u << lane) - 1u));
+      tb.te_exp[i] = er;
+      tb.te_lo[i] = lane;
+    }
+    if (lane == 0) {
+      tb.n = nv;
+      tb.nt = __popc(fm);
+      tb.te_lo[__popc(fm)] = nv;
+    }
+    // fused forward: block 0 writes the canonical routing maps
+    if (a.fused && blockIdx.x == 0 && lane < a.P) {
+      a.inv_c[lane] = ok ? rank : -1;
+      if (ok) a.perm_c[rank] = lane;
+    }
+  }
+  __syncthreads();
+  DQ_T(1);
+  if (a.fused && blockIdx.x == 0) {
+    for (int e = threadIdx.x; e <= a.E; e += kDqThreads) {
+      int c = 0;
+      for (int r = 0; r < tb.n; ++r) c += tb.exp[r] < e ? 1 : 0;
+      a.offsets[e] = c;
+    }
+  }
+  const int B = gridDim.x, b = blockIdx.x, nt = tb.nt;
+  const int U = nt * a.fp;
+  DqWalk walk;
+  // (32-bit products: U <= 8 * 4096 and d <= 4096 times at most a few hundred blocks)
+  walk.u = U * b / B;
+  walk.u1 = U * (b + 1) / B;
+  walk.fp = a.fp;
+  walk.cu = a.cu;
+  walk.c0 = a.d * b / B;
+  walk.c1 = a.d * (b + 1) / B;
+  walk.c = walk.c0;
+  walk.ei = 0;
+  walk.nt = nt;
+  walk.cr = a.cr;
+  const int ubase = walk.u, nu = walk.u1 - walk.u;
+  const int ntok = (a.P + a.pair_k - 1) / a.pair_k;  // tokens of the launch
+  const int col0 = walk.c0, ncol = walk.c1 - walk.c0;
+  const unsigned long long limit = a.wait_ns ? a.wait_ns : kWaitTimeoutNs;
+
+  // The block's small reads (the W1 input rows and the biases of its rows)
+  // are issued first; the weight stream is queued behind them.
+  if (warp < kDqWarps) {
+    if (a.xh != nullptr) dq_stage_async(xs, a.xh, tb.ident, a.d, ntok, a.d, KI);
+    for (int i = threadIdx.x; i < 2 * nu; i += kDqConsumers) {
+      const int u = ubase + i / 2, e = tb.te_exp[u / a.fp], m = u % a.fp;
+      cp_async4(smem_u32(bias1 + i), a.b1 + static_cast<uint64_t>(e) * (2u * a.fp) + w1_packed_row(m, i & 1));
+    }
+    for (int i = threadIdx.x; i < nt * ncol; i += kDqConsumers) {
+      const int ei = i / ncol, cc = i - ei * ncol;
+      cp_async4(smem_u32(bias2 + ei * kDqMaxCols + cc), a.b2 + static_cast<uint64_t>(tb.te_exp[ei]) * a.d + col0 + cc);
+    }
+    cp_async_commit();
+  }
+  __syncthreads();
+
+  if (warp == kDqWarps) {
+    // ---------------------------------------------------------------- copy warp
+    // Chunk c goes to slot c % S once the slot's previous chunk is consumed,
+    // and only after chunk c - ahead has landed.
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      DqChunk ch;
+      for (int c = 0; walk.next(ch); ++c) {
+        const int sl = c % S, use = c / S;
+        uint8_t* dst = slots + static_cast<size_t>(sl) * SB;
+        if (use > 0 && !mbar_wait(&empty_bar[sl], (use - 1) & 1, a.err, kDqErrCopy, limit)) break;
+        if (c >= a.ahead) {
+          const int p = c - a.ahead;
+          if (!mbar_wait(&full_bar[p % S], (p / S) & 1, a.err, kDqErrCopy, limit)) break;
+        }
+        const int e = tb.te_exp[ch.ei];
+        if (!ch.w2) {
+          const uint64_t base = static_cast<uint64_t>(e) * 2u * a.fp;
+          const uint64_t g = base + w1_packed_row(ch.r0, 0), l = base + w1_packed_row(ch.r0, 1);
+          const uint32_t cb = ch.len * rb1, sb = ch.len * a.sr1;
+          mbar_arrive_expect_tx(&full_bar[sl], 2u * (cb + sb));
+          bulk_load_hint(dst, a.w1q + g * rb1, cb, &full_bar[sl], pol);
+          bulk_load_hint(dst + a.cu * rb1, a.w1q + l * rb1, cb, &full_bar[sl], pol);
+          bulk_load_hint(dst + 2u * a.cu * rb1, a.w1sr + g * a.sr1, sb, &full_bar[sl], pol);
+          bulk_load_hint(dst + 2u * a.cu * rb1 + a.cu * a.sr1, a.w1sr + l * a.sr1, sb, &full_bar[sl], pol);
+        } else {
+          const uint64_t row = static_cast<uint64_t>(e) * a.d + ch.r0;
+          const uint32_t cb = ch.len * rb2, sb = ch.len * a.sr2;
+          mbar_arrive_expect_tx(&full_bar[sl], cb + sb);
+          bulk_load_hint(dst, a.w2q + row * rb2, cb, &full_bar[sl], pol);
+          bulk_load_hint(dst + a.cr * rb2, a.w2sr + row * a.sr2, sb, &full_bar[sl], pol);
+        }
       }
     }
-    __syncwarp();  // the buffer is refilled by a later dq_issue of this warp
-    if (nitem < 12) DQ_T(6 + 4 * nitem);
-    ++nitem;
+    return;
   }
-  cp_async_wait<0>();
-  if (a.fused) {
-    // the last block to finish combines (every block's y_pair rows are written)
-    __syncthreads();
+
+  // ------------------------------------------------------------------ compute warps
+  // W1 input: the router's f16 token rows (copies above), or x normalized here
+  if (a.xh == nullptr) dq_stage_x(xs, a, ntok, KI);
+  cp_async_wait_all();
+  dq_bar();
+  DQ_T(2);
+  // The grid barrier: every block's SwiGLU rows are written before any block
+  // reads them; then the block stages its pairs' SwiGLU rows.
+  auto grid_barrier = [&]() {
+    dq_bar();  // this block's act writes are done
     if (threadIdx.x == 0) {
       __threadfence();
-      last_block = atomicAdd(a.done, 1) == static_cast<int>(gridDim.x) - 1;
+      // (test hook: block 0 stays silent, so every block's wait runs out)
+      if (!(a.skip_arrival && blockIdx.x == 0)) atomicAdd(a.sync, 1);
+      const unsigned long long t0 = global_timer_ns();
+      while (true) {
+        int v;
+        asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(a.sync) : "memory");
+        if (v >= static_cast<int>(gridDim.x)) break;
+        if (global_timer_ns() - t0 > limit) {
+          // the first timeout also records the arrivals seen and expected
+          if (atomicCAS(a.err, 0, kDqErrGrid) == 0) {
+            a.err[2] = -1;
+            a.err[3] = v;
+            a.err[4] = static_cast<int>(gridDim.x);
+          }
+          break;
+        }
+      }
     }
-    __syncthreads();
-    if (last_block) {
-      __threadfence();
-      dq_combine_and_maps(a, tk_s);
+    dq_bar();
+    DQ_T(4);
+    dq_stage_async(xs, a.act, tb.pair, a.fp, tb.n, a.fp, KI);
+    cp_async_commit();
+    cp_async_wait_all();
+    dq_bar();
+    DQ_T(5);
+  };
+  // Items go to the compute warps round robin over the block's whole W1 unit
+  // sequence (then its W2 column pairs), so chunks smaller than 16 items
+  // still keep every warp busy; every warp releases every chunk.
+  DqChunk ch;
+  bool in_w2 = false;
+  int item0 = 0;  // block-relative index of the chunk's first item
+  for (int c = 0; walk.next(ch); ++c) {
+    if (ch.w2 && !in_w2) {
+      DQ_T(3);
+      grid_barrier();
+      in_w2 = true;
+      item0 = 0;
     }
+    const int sl = c % S;
+    const uint8_t* sb = slots + static_cast<size_t>(sl) * SB;
+    const int j0 = tb.te_lo[ch.ei], np = tb.te_lo[ch.ei + 1] - j0;
+    const int nitem = ch.w2 ? (ch.len + 1) / 2 : ch.len;
+    const int first = (warp - item0 % kDqWarps + kDqWarps) % kDqWarps;
+    if (first < nitem) mbar_wait(&full_bar[sl], (c / S) & 1, a.err, kDqErrCopy, limit);
+    if (!ch.w2) {
+      const uint8_t* sc = sb + 2u * a.cu * rb1;
+      for (int i = first; i < nitem; i += kDqWarps) {
+        const int m = ch.r0 + i, j = item0 + i;
+        const float bias = lane < kDqRows ? bias1[2 * j + lane] : 0.0f;
+        dq_item<KI, false>(a, tb, sb + i * rb1, sb + (a.cu + i) * rb1, sc + i * a.sr1, sc + (a.cu + i) * a.sr1, xs,
+                           lane, j0, np, m, 2, col0, bias, partial);
+      }
+    } else {
+      const uint8_t* sc = sb + a.cr * rb2;
+      for (int i = first; i < nitem; i += kDqWarps) {
+        const int r = 2 * i, nrow = min(2, ch.len - r), r1 = r + nrow - 1, col = ch.r0 + r;
+        const float bias = lane < nrow ? bias2[ch.ei * kDqMaxCols + col - col0 + lane] * a.bias_mult : 0.0f;
+        dq_item<KI, true>(a, tb, sb + r * rb2, sb + r1 * rb2, sc + r * a.sr2, sc + r1 * a.sr2, xs, lane, j0, np, col,
+                          nrow, col0, bias, partial);
+      }
+    }
+    item0 += nitem;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[sl]);
   }
-  DQ_T(63);
+  if (!in_w2) grid_barrier();  // a block without W2 rows still meets the others
+  if (!a.fused) return;
+  // fused forward: y = x + the pairs' rows of each token in increasing expert order
+  dq_bar();
+  for (int idx = threadIdx.x; idx < a.n_tok * ncol; idx += kDqConsumers) {
+    const int t = idx / ncol, cc = idx - t * ncol, col = col0 + cc;
+    float acc = 0.0f;
+    for (int r = 0; r < tb.n; ++r)
+      if (tb.tok[r] == t) acc = __fadd_rn(acc, partial[r * kDqMaxCols + cc]);
+    const uint64_t o = static_cast<uint64_t>(t) * a.d + col;
+    if (a.residual) {
+      const float xv = a.x_dtype == kDqSrcF32 ? __ldg(static_cast<const float*>(a.x) + o)
+                                              : __bfloat162float(__ldg(static_cast<const __nv_bfloat16*>(a.x) + o));
+      acc = __fadd_rn(xv, acc);
+    }
+    if (a.y_dtype == kDqSrcF32)
+      static_cast<float*>(a.y)[o] = acc;
+    else
+      static_cast<__nv_bfloat16*>(a.y)[o] = __float2bfloat16_rn(acc);
+  }
+  DQ_T(6);
 }
 
-// Cooperative launch: the blocks of an expert wait for each other between W1
-// and W2, so all blocks must be resident at once.
-template <int D, int KI>
+// Cooperative launch: the blocks meet between W1 and W2, so all of them must
+// be resident at once.
+template <int KI>
 cudaError_t dq_launch(const DqParams& a, size_t smem, int grid, cudaStream_t st) {
-  const auto fn = mxmoe_dqgemv_ffn_kernel<D, KI>;
+  const auto fn = mxmoe_dqgemv_ffn_kernel<KI>;
   const cudaError_t e = ensure_dynamic_smem(reinterpret_cast<const void*>(fn), smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg{};
@@ -724,7 +672,7 @@ cudaError_t dq_launch(const DqParams& a, size_t smem, int grid, cudaStream_t st)
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   // a runtime that refuses the two attributes together gets the cooperative
-  // launch alone (the kernel then starts after the permutation completes)
+  // launch alone (the kernel then starts after the router completes)
   static bool pdl_refused = false;
   cfg.numAttrs = pdl_enabled() && !pdl_refused ? 2 : 1;
   cudaError_t r = cudaLaunchKernelEx(&cfg, fn, a);
@@ -736,12 +684,6 @@ cudaError_t dq_launch(const DqParams& a, size_t smem, int grid, cudaStream_t st)
     r = cudaLaunchKernelEx(&cfg, fn, a);
   }
   return r;
-}
-
-size_t dq_smem_bytes(const DqParams& a, int D) {
-  const int ki = (std::max(a.d, a.fp) / 32 + 31) / 32;
-  return static_cast<size_t>(kDqWarps) * D * a.stage_bytes + static_cast<size_t>(a.ps) * ki * 2048 +
-         16 * sizeof(float) + 16 * sizeof(int) + 16 * sizeof(void*) + 16;
 }
 
 }  // namespace
@@ -756,32 +698,39 @@ extern "C" __attribute__((visibility("default"))) int mxmoe_dq_trace_clear() {
 }
 #endif
 
-cudaError_t launch_dqgemv_ffn(DqParams a, int max_pairs_per_expert, int max_experts, int num_sms, size_t smem_limit,
-                              cudaStream_t st) {
-  if (a.d % 32 != 0 || a.fp % 64 != 0 || a.d > kDqMaxK || a.fp > kDqMaxK || a.ps <= 0 || a.ps > 16)
+cudaError_t launch_dqgemv_ffn(DqParams a, int num_sms, size_t smem_limit, cudaStream_t st) {
+  const int grid = num_sms;
+  if (a.d % 32 != 0 || a.fp % 64 != 0 || a.d > kDqMaxK || a.fp > kDqMaxK || a.P < 0 || a.P > kDqMaxPairs ||
+      grid <= 0 || a.d > kDqMaxCols * grid || (kDqMaxPairs * a.fp + grid - 1) / grid > kDqMaxUnits)
     return cudaErrorInvalidValue;
   const uint32_t rb1 = static_cast<uint32_t>(a.kp1) / 2, rb2 = static_cast<uint32_t>(a.kp2) / 2;
-  a.stage_bytes = (kDqRows * std::max(rb1 + a.sr1, rb2 + a.sr2) + 127u) / 128u * 128u;
-  // three stage buffers per warp when they fit beside the staged rows, else two
-  const int D = dq_smem_bytes(a, 3) + 2048 <= smem_limit ? 3 : 2;
-  const size_t smem = dq_smem_bytes(a, D);
-  if (smem + 2048 > smem_limit) return cudaErrorInvalidValue;
-  (void)max_pairs_per_expert;
-  const int grid = std::max(num_sms, max_experts);  // every touched expert gets a block
+  const uint32_t unit = 2u * (rb1 + a.sr1), row2 = rb2 + a.sr2;
   const int ki = (std::max(a.d, a.fp) / 32 + 31) / 32;
-  if (D == 3) {
-    switch (ki) {
-      case 1: return dq_launch<3, 1>(a, smem, grid, st);
-      case 2: return dq_launch<3, 2>(a, smem, grid, st);
-      case 3: return dq_launch<3, 3>(a, smem, grid, st);
-      default: return dq_launch<3, 4>(a, smem, grid, st);
+  a.xs_rows = dq_pow2(std::max(a.P, 1));
+  const size_t fixed = static_cast<size_t>(a.xs_rows) * ki * 2048 + kDqScratchFloats * sizeof(float);
+  const size_t budget = smem_limit > fixed + 2048 ? smem_limit - fixed - 2048 : 0;
+  // Chunks of 8 GLU units (two chunks feed the 16 compute warps); about 48 KB
+  // in flight per SM, the rest of the ring holding landed chunks.
+  a.slots = 0;
+  for (int cu : {8, 4, 2, 1}) {
+    const uint32_t sb = (std::max(cu * unit, 2u * row2) + 127u) / 128u * 128u;
+    const int s = static_cast<int>(std::min<size_t>(kDqMaxSlots, budget / sb));
+    if (s >= 3 || (cu == 1 && s >= 2)) {
+      a.cu = cu;
+      a.slot_bytes = sb;
+      a.slots = s;
+      break;
     }
   }
+  if (a.slots == 0) return cudaErrorInvalidValue;
+  a.cr = static_cast<int>(a.slot_bytes / row2) & ~1;
+  a.ahead = std::max(1, std::min(a.slots - 1, static_cast<int>((48u * 1024u + a.slot_bytes - 1) / a.slot_bytes)));
+  const size_t smem = static_cast<size_t>(a.slots) * a.slot_bytes + fixed;
   switch (ki) {
-    case 1: return dq_launch<2, 1>(a, smem, grid, st);
-    case 2: return dq_launch<2, 2>(a, smem, grid, st);
-    case 3: return dq_launch<2, 3>(a, smem, grid, st);
-    default: return dq_launch<2, 4>(a, smem, grid, st);
+    case 1: return dq_launch<1>(a, smem, grid, st);
+    case 2: return dq_launch<2>(a, smem, grid, st);
+    case 3: return dq_launch<3>(a, smem, grid, st);
+    default: return dq_launch<4>(a, smem, grid, st);
   }
 }
 

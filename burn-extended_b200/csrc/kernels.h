@@ -113,13 +113,10 @@ struct DqParams {
   uint32_t sr2;
   const float* b2;         // [E][d]
   float bias_mult;
-  int E;
-  const int32_t* poff;     // [E] first pair position of each expert
-  const int32_t* counts;   // [E]
-  const int32_t* perm;     // [pairs] position -> canonical pair t * k + s
-  const int32_t* topk_idx; // [P] canonical expert ids (fused mode, P <= 64)
-  int P;
-  int pair_k;
+  int E;                   // local experts
+  const int32_t* topk_idx; // [P] local expert of each pair (canonical order); out of range: no expert
+  int P;                   // routed pairs (at most 8)
+  int pair_k;              // pairs per token
   const __half* xh;        // [n][d] normalized token rows * x_scale as f16 (router output), or null
   const void* x;           // [n][d] token rows (staged from here when xh is null)
   int x_dtype;             // kDqSrcF32 / kDqSrcBf16
@@ -128,10 +125,11 @@ struct DqParams {
   float x_scale, inv_x_scale;      // power of two on the staged f16 token rows
   float alpha, limit;
   float act_scale, inv_act_scale;  // power of two on the f16 SwiGLU rows
-  __half* act;             // [pairs][fp] SwiGLU rows (W1 -> W2)
-  float* y_pair;           // [pairs][d] f32
-  const float* topk_w;     // [pairs] canonical route weights
-  int fused;               // pairs from topk_idx, act / y_pair rows by canonical pair, combine here
+  __half* act;             // [P][fp] SwiGLU rows by canonical pair (W1 -> W2)
+  float* y_pair;           // not fused: [rows][d] f32, row inv[pair]
+  const int32_t* inv;      // not fused: [P] pair -> y_pair row
+  const float* topk_w;     // [P] canonical route weights
+  int fused;               // write y (expert-order sum + residual) and the canonical maps
   int n_tok;               // fused: tokens
   int residual;            // fused: y = x + moe(x)
   void* y;                 // fused: [n][d] layer output
@@ -139,16 +137,20 @@ struct DqParams {
   int32_t* offsets;        // fused: canonical maps written for the caller ([E + 1], [P], [P])
   int32_t* perm_c;
   int32_t* inv_c;
-  int* done;               // fused: finished-block counter, zero at launch
-  int* err;                // status word
-  int* sync;               // [E] per-expert arrival counters, zero at launch
+  int* err;                // status block (word 0 code, words 2-4 where the grid wait gave up)
+  int* sync;               // grid arrival counter, zero at launch
   int skip_arrival;        // test hook: block 0 never signals its W1 completion
-  unsigned long long wait_ns;  // limit of the W1 -> W2 wait (0: the default 2 s)
-  int ps;                  // pairs staged per pass (shared memory: ps * 2 KB per 1024 columns)
-  uint32_t stage_bytes;    // set by the launcher
+  unsigned long long wait_ns;  // limit of the device-side waits (0: the default 2 s)
+  // set by the launcher
+  int cu, cr;              // W1 units / W2 rows per chunk
+  int slots;               // shared-memory ring slots
+  int ahead;               // chunks in flight at most
+  uint32_t slot_bytes;
+  int xs_rows;             // staged activation rows (pairs rounded up to a power of two)
 };
-cudaError_t launch_dqgemv_ffn(DqParams a, int max_pairs_per_expert, int max_experts, int num_sms, size_t smem_limit,
-                              cudaStream_t st);
+// One block per SM; pairs P <= 8, d and fp <= kDqMaxK, d <= 64 * num_sms,
+// 8 * fp <= 256 * num_sms.
+cudaError_t launch_dqgemv_ffn(DqParams a, int num_sms, size_t smem_limit, cudaStream_t st);
 cudaError_t launch_simt_w1(const void* x, int x_dtype, int d, int k, const float* gamma, const float* rscale,
                            const uint8_t* w1q, const uint8_t* w1sf, const float* b1, int fp, int kp1, int E,
                            const int32_t* poff, const int32_t* counts, const int32_t* perm_p, float alpha, float limit,

@@ -5,6 +5,8 @@ MXMOE_ERR_TIMEOUT and returns, and the next forward on the same layer is
 correct again.  Covers the tensor-core GEMM's mbarrier waits (kind::mxf4
 decode tiles and E4M3 tokens-as-A tiles) and the dequant-GEMV's W1 -> W2
 wait."""
+import re
+
 import pytest
 
 import mxmoe
@@ -35,6 +37,9 @@ def test_withheld_signal_times_out_then_recovers(name, shape):
     with pytest.raises(mxmoe.MxMoeError) as ei:
         layer.sync_status()
     assert ei.value.code == MXMOE_ERR_TIMEOUT, (name, ei.value)
+    if name == "gemv":  # block 0 withheld its arrival: one short of the grid
+        m = re.search(r"saw (\d+) of (\d+) block arrivals", str(ei.value))
+        assert m and int(m.group(1)) == int(m.group(2)) - 1, str(ei.value)
     # the context is healthy and the layer computes correctly again, twice
     # (direct launch, then the graph-captured replay path)
     for i in range(3):
