@@ -251,7 +251,7 @@ def measure_decode_batches(args, local, dev, hbm_peak):
                         "bytes": nbytes, "gbs": nbytes / (us / 1e6) / 1e9,
                         "hbm_frac": nbytes / (us / 1e6) / 1e9 / hbm_peak,
                         "x_touched_bytes_at_peak": us / (nbytes / (hbm_peak * 1e9) * 1e6),
-                        "path": "dequant-GEMV (fused)" if n * base.k <= 4 else "kind::mxf4 tensor-core tiles"}
+                        "path": "dequant-GEMV (fused)" if n * base.k <= 8 else "kind::mxf4 tensor-core tiles"}
     L.close()
     return {"config": "gptoss20b_moe_decode at batch 1..16 (32 experts, top-4), bf16 x, default dispatch",
             "rotation": "32 token batches per n (different experts each)", **out}

@@ -1,4 +1,4 @@
-"""GPU parity of the decode dequant-GEMV path (at most 4 routed pairs in a
+"""GPU parity of the decode dequant-GEMV path (at most 8 routed pairs in a
 forward, e.g. batch 1 at top-4): one fused kernel after the router runs the
 expert FFN, the combine and the canonical routing maps.  Checked against the
 CPU oracle, against the tensor-core path on the same inputs, and for
@@ -52,6 +52,19 @@ def run(torch, inp, tag, flags=0, **kw):
 
 def test_gptoss20b_batch1(torch):
     run(torch, synth.make_config("decode", seed=101, n=1), "dqgemv 20b decode n=1")
+
+
+def test_gptoss20b_batch2(torch):
+    # 8 routed pairs, the most the kernel takes
+    run(torch, synth.make_config("decode", seed=102, n=2), "dqgemv 20b decode n=2")
+
+
+@pytest.mark.parametrize("n,k", [(8, 1), (4, 2)])
+def test_eight_pairs_on_one_expert(torch, n, k):
+    inp = synth.make_inputs(1024, 512, 4, k, n, True, seed=40 + n)
+    inp.gate_b = inp.gate_b.copy()
+    inp.gate_b[0] = 50.0
+    run(torch, inp, f"dqgemv one expert n={n} k={k}")
 
 
 def test_gptoss120b_batch1(torch):
