@@ -209,7 +209,7 @@ def measure_decode(args, local, dev, hbm_peak):
 def measure_decode_batches(args, local, dev, hbm_peak):
     """Small-batch decode of the GPT-OSS-20B-shaped layer (32 experts, top-4)
     at 1, 2, 4, 8 and 16 tokens through the default dispatch (the fused
-    dequant-GEMV kernel up to 4 routed pairs, the kind::mxf4 tensor-core tiles
+    dequant-GEMV kernel up to 8 routed pairs, the kind::mxf4 tensor-core tiles
     above).  GB/s = bytes of the experts the batch touches (codes, scales,
     biases) plus router weights and x / y, per layer forward.  The weights
     (423 MB) exceed the 126 MB L2, and consecutive forwards use different
@@ -255,6 +255,66 @@ def measure_decode_batches(args, local, dev, hbm_peak):
     L.close()
     return {"config": "gptoss20b_moe_decode at batch 1..16 (32 experts, top-4), bf16 x, default dispatch",
             "rotation": "32 token batches per n (different experts each)", **out}
+
+
+def measure_attention(args, local, dev, hbm_peak):
+    """Streaming multi-query attention decode step (mxmqa_forward_streaming)
+    at the GPT-OSS shape: d_model 2880, 64 query heads over 8 KV heads of 64,
+    learned sinks, bf16 weights, RoPE base 150000 with YaRN x32, a 128-token
+    sliding window over a 160-slot ring cache (and a 4096-token full cache).
+    A step is one new token per sequence after a 2048-token prompt.  GB/s =
+    the q/k/v/o weights (53.1 MB bf16) plus the KV rows read (window x 8
+    heads x 64 x 4 B x 2 per sequence) plus x / y, per step; the weights and a
+    flushed L2 make every step stream from HBM."""
+    import torch
+    sys.path.insert(0, os.path.join(ROOT, "burn-extended_b200"))
+    from mxmoe.attention import (AttnWindow, RopeConfig, StreamingMqaCache, StreamingMqaParams,
+                                 StreamingMultiQueryAttentionConfig)
+    d, nH, kvH, dk = 2880, 64, 8, 64
+    rng = np.random.default_rng(args.seed + 11)
+
+    def w(shape, sc):
+        a = rng.standard_normal(shape).astype(np.float32) * np.float32(sc)
+        u = a.view(np.uint32).astype(np.uint64)
+        return ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32).view(np.float32)
+    jq, jk = nH * dk, kvH * dk
+    m = StreamingMultiQueryAttentionConfig(d, nH, kvH, dk).init(local)
+    m.set_weights(w((d, jq), d ** -0.5), w((jq,), 0.02), w((d, jk), d ** -0.5), w((jk,), 0.02),
+                  w((d, jk), d ** -0.5), w((jk,), 0.02), w((jq, d), jq ** -0.5), w((d,), 0.02), bf16=True)
+    m.set_sinks(rng.standard_normal((kvH, nH // kvH)).astype(np.float32))
+    m.set_rope(RopeConfig(131072, 150000.0, 32.0, 4096.0, 1.0, 32.0))
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    wbytes = 2 * (d * (jq + 2 * jk) + jq * d)
+    out = {}
+    for B in (1, 8, 32):
+        for name, cap, win in (("window128", 160, 128), ("full4096", 4096, None)):
+            cache = StreamingMqaCache(m, B, cap, 0)
+            prompt = torch.randn(B, 2048 if win is None else 128, d, device=dev).to(torch.bfloat16)
+            pos = prompt.shape[1]
+            m.forward_streaming(prompt, cache, StreamingMqaParams(0, AttnWindow(win)))
+            x = torch.randn(B, 1, d, device=dev).to(torch.bfloat16)
+            for _ in range(3):
+                m.forward_streaming(x, cache, StreamingMqaParams(pos, AttnWindow(win)))
+                pos += 1
+            times = []
+            for _ in range(max(args.steps, 5)):
+                flush.zero_()
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record()
+                m.forward_streaming(x, cache, StreamingMqaParams(pos, AttnWindow(win)))
+                e.record()
+                torch.cuda.synchronize()
+                times.append(s.elapsed_time(e) * 1e3)
+                pos += 1
+            us = float(np.median(times))
+            keys = min(pos, cap) if win is None else win
+            nbytes = wbytes + B * keys * kvH * dk * 4 * 2 + 2 * B * d * 2
+            out[f"B{B}_{name}"] = {"us_per_step": us, "tokens_per_s": B / (us / 1e6), "bytes": nbytes,
+                                   "gbs": nbytes / (us / 1e6) / 1e9, "hbm_frac": nbytes / (us / 1e6) / 1e9 / hbm_peak}
+            cache.close()
+    m.close()
+    return {"config": "gptoss attention decode step (d 2880, 64 q / 8 kv heads x 64, sinks, bf16 weights, YaRN)",
+            "l2": "256 MB buffer zeroed before every timed step", **out}
 
 
 def measure_microbench(args, local, dev, hbm_peak):
@@ -366,6 +426,9 @@ def run_ours(args, world, rank, local):
         return
     if args.only == "gptoss120b":
         print(json.dumps({"gptoss120b": measure_120b(args, local, dev)}), flush=True)
+        return
+    if args.only == "attention":
+        print(json.dumps({"attention": measure_attention(args, local, dev, hbm_peak)}), flush=True)
         return
 
     # one model on every rank (seeded once); each rank routes its own tokens
@@ -541,7 +604,7 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=24)
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["all", "prefill", "decode", "decode_batches", "microbench", "gptoss120b"],
+    ap.add_argument("--only", choices=["all", "prefill", "decode", "decode_batches", "microbench", "gptoss120b", "attention"],
                     default="all",
                     help="run only that leg (profiling runs); 'all' adds decode, microbench and gptoss120b as extras")
     args = ap.parse_args()
