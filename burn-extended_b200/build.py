@@ -38,7 +38,7 @@ def build(verbose: bool = False) -> str:
             print(" ".join(cmd))
         subprocess.run(cmd, check=True)
         objs.append(o)
-    cmd = [NVCC, *FLAGS, "-shared", *objs, "-o", OUT]
+    cmd = [NVCC, *FLAGS, "-shared", *objs, "-lcublas", "-o", OUT]
     if verbose:
         print(" ".join(cmd))
     subprocess.run(cmd, check=True)
