@@ -291,6 +291,18 @@ struct mxmoe_layer {
   // expert parallelism over peer memory: the workspace is shared with peers and must not move
   bool ep_reserved = false;
   uint32_t ep_world = 0, ep_max_tokens = 0;
+  // mxmoe_ep_attach: this rank's place and the peers' buffers, as device tables
+  struct EpAttach {
+    bool on = false;
+    uint32_t rank = 0;
+    void** bufs = nullptr;        // [3][world] layout buffers (device table)
+    void** ret = nullptr;         // [world] return buffers (device table)
+    int32_t** counts = nullptr;   // [world] count tables (device table)
+    void* own_ret = nullptr;
+    int32_t* own_counts = nullptr;
+    mxmoe_ep_barrier_fn barrier = nullptr;
+    void* ctx = nullptr;
+  } epa;
   cudaEvent_t ev[8] = {};
 };
 
@@ -883,6 +895,9 @@ int mxmoe_destroy(mxmoe_layer* L) {
   dfree(L->w1q); dfree(L->w1sf); dfree(L->b1); dfree(L->w2q); dfree(L->w2sf); dfree(L->b2);
   dfree(L->w1sr); dfree(L->w2sr);
   dfree(L->err);
+  if (L->epa.bufs) cudaFree(L->epa.bufs);
+  if (L->epa.ret) cudaFree(L->epa.ret);
+  if (L->epa.counts) cudaFree(L->epa.counts);
   for (auto& e : L->ev)
     if (e) cudaEventDestroy(e);
   if (L->graph.exec) cudaGraphExecDestroy(L->graph.exec);
@@ -1683,6 +1698,71 @@ int mxmoe_ep_experts(mxmoe_layer* L, mxmoe_dtype x_dtype, void* const* peer_ret,
   CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff, w.counts,
                             static_cast<int>(L->e_count), w.pos_slot, static_cast<int>(L->ep_world), peer_ret,
                             ret_rows, L->err, st));
+  return MXMOE_OK;
+}
+
+int mxmoe_ep_attach(mxmoe_layer* L, uint32_t rank, uint32_t world, void* const* peer_bufs, void* const* peer_ret,
+                    int32_t* const* peer_counts, mxmoe_ep_barrier_fn barrier, void* barrier_ctx) {
+  TRY(check_layer(L));
+  if (!L->ep_reserved) return fail(MXMOE_ERR_NOT_READY, "mxmoe_ep_reserve first");
+  if (world != L->ep_world || rank >= world)
+    return fail(MXMOE_ERR_INVALID_ARG, "rank %u of %u does not match the reservation for %u ranks", rank, world,
+                L->ep_world);
+  if (!peer_bufs || !peer_ret || !peer_counts || !barrier) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  for (uint32_t i = 0; i < world; ++i) {
+    if (!peer_ret[i] || !peer_counts[i]) return fail(MXMOE_ERR_INVALID_ARG, "null peer buffer for rank %u", i);
+    for (int b = 0; b < kEpBuffers; ++b)
+      if (!peer_bufs[b * world + i]) return fail(MXMOE_ERR_INVALID_ARG, "null peer buffer for rank %u", i);
+  }
+  DeviceGuard g(L->cfg.device);
+  auto& a = L->epa;
+  if (!a.bufs) {
+    CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&a.bufs), kEpBuffers * world * sizeof(void*)));
+    CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&a.ret), world * sizeof(void*)));
+    CUDA_TRY(cudaMalloc(reinterpret_cast<void**>(&a.counts), world * sizeof(int32_t*)));
+  }
+  CUDA_TRY(cudaMemcpy(a.bufs, peer_bufs, kEpBuffers * world * sizeof(void*), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(a.ret, peer_ret, world * sizeof(void*), cudaMemcpyHostToDevice));
+  CUDA_TRY(cudaMemcpy(a.counts, peer_counts, world * sizeof(int32_t*), cudaMemcpyHostToDevice));
+  a.own_ret = peer_ret[rank];
+  a.own_counts = peer_counts[rank];
+  a.rank = rank;
+  a.barrier = barrier;
+  a.ctx = barrier_ctx;
+  a.on = true;
+  return MXMOE_OK;
+}
+
+int mxmoe_ep_forward(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, void* y,
+                     mxmoe_dtype y_dtype, void* stream) {
+  TRY(check_layer(L));
+  auto& a = L->epa;
+  if (!a.on) return fail(MXMOE_ERR_NOT_READY, "mxmoe_ep_attach first");
+  if (n_tokens > L->ep_max_tokens) return fail(MXMOE_ERR_TOO_LARGE, "%u tokens > reserved %u", n_tokens, L->ep_max_tokens);
+  if (n_tokens > 0 && (!x || !y)) return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
+  if (!aligned16(x) || !aligned16(y)) return fail(MXMOE_ERR_INVALID_ARG, "x and y must be 16-byte aligned");
+  DeviceGuard g(L->cfg.device);
+  Workspace& w = L->ws;
+  cudaStream_t st = as_stream(stream);
+  const int world = static_cast<int>(L->ep_world), rank = static_cast<int>(a.rank);
+  // 1. route this rank's tokens (full router) and sort its pairs by expert
+  if (n_tokens > 0)
+    TRY(mxmoe_route(L, x, x_dtype, n_tokens, w.rscale, w.topk_idx, w.topk_w, w.offsets, w.perm_c, w.inv_c, stream));
+  // 2. this rank's pairs per expert into every rank's count table
+  CUDA_TRY(launch_ep_push_counts(n_tokens > 0 ? w.offsets : nullptr, static_cast<int>(L->E_total), rank, world,
+                                 a.counts, st));
+  if (a.barrier(a.ctx, stream) != 0) return fail(MXMOE_ERR_CUDA, "ep barrier failed after the count exchange");
+  // 3. quantize and write every pair into its owner's layout
+  TRY(mxmoe_ep_dispatch(L, x, x_dtype, n_tokens, w.rscale, w.topk_idx, w.topk_w, w.inv_c, w.offsets, a.own_counts,
+                        a.rank, a.bufs, stream));
+  if (a.barrier(a.ctx, stream) != 0) return fail(MXMOE_ERR_CUDA, "ep barrier failed after the dispatch");
+  // 4. this rank's experts over every source's pairs, outputs pushed back to the sources
+  TRY(mxmoe_ep_experts(L, x_dtype, a.ret, L->ep_max_tokens * L->k, stream));
+  if (a.barrier(a.ctx, stream) != 0) return fail(MXMOE_ERR_CUDA, "ep barrier failed after the expert FFN");
+  // 5. combine in expert order (+ residual)
+  if (n_tokens > 0)
+    TRY(mxmoe_combine(x, x_dtype, n_tokens, L->d, L->k, w.topk_idx, w.inv_c, a.own_ret, MXMOE_BF16,
+                      (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1, y, y_dtype, stream));
   return MXMOE_OK;
 }
 

@@ -1850,6 +1850,21 @@ cudaError_t launch_return_pairs(const void* y_bf16, int d, int R, const uint32_t
   return cudaGetLastError();
 }
 
+__global__ void ep_push_counts_kernel(const int32_t* __restrict__ offsets, int E, int rank, int world,
+                                      int32_t* const* __restrict__ peer_counts) {
+  griddep_wait();
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < E; e += gridDim.x * blockDim.x) {
+    const int c = offsets ? offsets[e + 1] - offsets[e] : 0;
+    for (int r = 0; r < world; ++r) peer_counts[r][static_cast<size_t>(rank) * E + e] = c;
+  }
+}
+
+cudaError_t launch_ep_push_counts(const int32_t* offsets, int E, int rank, int world, int32_t* const* peer_counts,
+                                  cudaStream_t st) {
+  return launch_kernel(ep_push_counts_kernel, dim3((E + 255) / 256), dim3(256), 0, st, offsets, E, rank, world,
+                       peer_counts);
+}
+
 cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, int epr, int pad, int n_tile,
                              int32_t* src_base, int32_t* poff, int32_t* seg_counts, int32_t* ntile_prefix,
                              cudaStream_t st) {

@@ -77,6 +77,11 @@ cudaError_t launch_dispatch_pairs(const void* x, int x_dtype, int d, int k, int 
                                   uint32_t recv_cap, int* err, cudaStream_t st);
 cudaError_t launch_return_pairs(const void* y_bf16, int d, int R, const uint32_t* slot, int world,
                                 void* const* peer_ret, uint32_t ret_rows, int* err, cudaStream_t st);
+// Source side of the count exchange: this rank's pairs per expert
+// (offsets[e + 1] - offsets[e], or zeros when offsets is null) into row
+// `rank` of every rank's [world][E] count table (peer memory).
+cudaError_t launch_ep_push_counts(const int32_t* offsets, int E, int rank, int world, int32_t* const* peer_counts,
+                                  cudaStream_t st);
 cudaError_t launch_ep_layout(const int32_t* counts, int world, int rank, int E, int epr, int pad, int n_tile,
                              int32_t* src_base, int32_t* poff, int32_t* seg_counts, int32_t* ntile_prefix,
                              cudaStream_t st);

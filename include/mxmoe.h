@@ -393,6 +393,37 @@ MXMOE_API int mxmoe_ep_dispatch(mxmoe_layer* layer, const void* x, mxmoe_dtype x
 MXMOE_API int mxmoe_ep_experts(mxmoe_layer* layer, mxmoe_dtype x_dtype, void* const* peer_ret, uint32_t ret_rows,
                      void* stream);
 
+/* ---- expert-parallel step behind the C ABI ----
+ * One call per rank and step runs the whole expert-parallel layer: route ->
+ * count exchange -> quantized dispatch -> expert FFN -> return -> combine
+ * (the QuantizedPeerMoe step of the Python host, without Python).  Between
+ * the phases the ranks meet three times through the caller's barrier:
+ *   barrier(ctx, stream) must return once every rank of the group has called
+ *   it for this phase, with each rank's work enqueued on its stream before the
+ *   call complete before any rank's work enqueued after it starts (a stream
+ *   synchronize plus a host barrier, or a collective enqueued on `stream`).
+ *   Non-zero means failure; mxmoe_ep_forward then returns MXMOE_ERR_CUDA.
+ * The library never waits on another rank inside a kernel, so ranks may also
+ * share one GPU (each on its own stream and thread).
+ *
+ * mxmoe_ep_attach (after mxmoe_ep_reserve on every rank): peer_bufs is a host
+ * array of 3 x world device pointers grouped by buffer ([codes of ranks
+ * 0..world-1][scales ...][metadata ...], mxmoe_ep_buffers of each rank, opened
+ * with mxmoe_ipc_open); peer_ret[r] is rank r's bf16 return buffer of
+ * max_tokens * k x d_model values, peer_counts[r] rank r's int32 count table
+ * of world x num_experts values (both caller-allocated, mxmoe_ipc_alloc for
+ * ranks on other GPUs), each as this process sees it. */
+typedef int (*mxmoe_ep_barrier_fn)(void* ctx, void* stream);
+MXMOE_API int mxmoe_ep_attach(mxmoe_layer* layer, uint32_t rank, uint32_t world, void* const* peer_bufs,
+                              void* const* peer_ret, int32_t* const* peer_counts, mxmoe_ep_barrier_fn barrier,
+                              void* barrier_ctx);
+/* One expert-parallel step of this rank: x [n_tokens][d_model] device (f32 or
+ * bf16, n_tokens <= the reserved max_tokens, may be 0), y likewise; y = x +
+ * MoE(x) over all ranks' experts.  Every rank of the group must call it for
+ * every step with the same x dtype.  16-byte aligned buffers. */
+MXMOE_API int mxmoe_ep_forward(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
+                               void* y, mxmoe_dtype y_dtype, void* stream);
+
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
  * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers, each

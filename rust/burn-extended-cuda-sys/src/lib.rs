@@ -92,6 +92,9 @@ pub struct mxmoe_modelbin_header {
     pub file_bytes: u64,
 }
 
+/// The caller's barrier for mxmoe_ep_forward (0 = success).
+pub type mxmoe_ep_barrier_fn = Option<unsafe extern "C" fn(ctx: *mut c_void, stream: *mut c_void) -> c_int>;
+
 /// Opaque layer handle.
 #[repr(C)]
 pub struct mxmoe_layer {
@@ -337,6 +340,25 @@ extern "C" {
         counts: *const i32,
         rank: u32,
         peer_bufs: *const *mut c_void,
+        stream: *mut c_void,
+    ) -> c_int;
+    pub fn mxmoe_ep_attach(
+        layer: *mut mxmoe_layer,
+        rank: u32,
+        world: u32,
+        peer_bufs: *const *mut c_void,
+        peer_ret: *const *mut c_void,
+        peer_counts: *const *mut i32,
+        barrier: mxmoe_ep_barrier_fn,
+        barrier_ctx: *mut c_void,
+    ) -> c_int;
+    pub fn mxmoe_ep_forward(
+        layer: *mut mxmoe_layer,
+        x: *const c_void,
+        x_dtype: mxmoe_dtype,
+        n_tokens: u32,
+        y: *mut c_void,
+        y_dtype: mxmoe_dtype,
         stream: *mut c_void,
     ) -> c_int;
     pub fn mxmoe_ep_experts(
