@@ -132,7 +132,7 @@ constexpr unsigned long long kFaultWaitNs = 1000ull * 1000ull;  // 1 ms
 
 // mxmoe_forward_host splits large batches into up to this many chunks so
 // that the copies of one chunk overlap the forward of another.
-constexpr int kHostChunksMax = 4;
+constexpr int kHostChunksMax = 8;
 constexpr uint32_t kHostChunkMinTokens = 1024;
 
 // The dequant-GEMV takes forwards of at most this many routed pairs (so at
@@ -1253,6 +1253,17 @@ int mxmoe_forward_host(mxmoe_layer* L, const void* x_host, mxmoe_dtype x_dtype, 
     chunks = 2;
     bounds[1] = round_up(n_tokens / 2, 128);
     bounds[2] = n_tokens;
+  }
+  if (const char* env = std::getenv("MXMOE_HOST_CHUNKS_EXPERIMENT")) {
+    chunks = 0;
+    uint32_t acc = 0;
+    const char* q = env;
+    while (*q && chunks < kHostChunksMax) {
+      acc += static_cast<uint32_t>(std::strtoul(q, const_cast<char**>(&q), 10));
+      bounds[++chunks] = std::min(acc, n_tokens);
+      if (*q == ',') ++q;
+    }
+    bounds[chunks] = n_tokens;
   }
   for (uint32_t i = 0; i < chunks; ++i) h.status[i] = 0;
   uint32_t used = 0;

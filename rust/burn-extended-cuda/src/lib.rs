@@ -14,7 +14,9 @@
 //!   src/loader/mxfp4.rs          -> loader::mxfp4
 //!   src/loader/modelbin.rs (MoE) -> loader::modelbin
 //!   src/models/gpt_oss.rs (MoE)  -> models::gpt_oss
+//!   src/attention/streaming_mqa.rs -> attention
 
+pub mod attention;
 pub mod error;
 pub mod loader;
 pub mod models;
