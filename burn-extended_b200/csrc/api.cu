@@ -1508,6 +1508,7 @@ int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens, uint32_
   if (!y || (residual && !x) || (k > 0 && (!topk_idx || !inv || !pair_out)))
     return fail(MXMOE_ERR_INVALID_ARG, "null pointer");
   if (k > static_cast<uint32_t>(kMaxTopK)) return fail(MXMOE_ERR_UNSUPPORTED, "k=%u", k);
+  if (d_model % 4 != 0) return fail(MXMOE_ERR_UNSUPPORTED, "d_model must be a multiple of 4");
   if (!aligned16(x) || !aligned16(pair_out) || !aligned16(y))
     return fail(MXMOE_ERR_INVALID_ARG, "x, pair_out and y must be 16-byte aligned");
   CUDA_TRY(launch_combine(x, x_dtype, pair_out, pair_dtype, topk_idx, inv, n_tokens, d_model, k, residual, y, y_dtype,

@@ -427,7 +427,7 @@ MXMOE_API int mxmoe_ep_forward(mxmoe_layer* layer, const void* x, mxmoe_dtype x_
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
  * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers, each
- * starting on a 16-byte boundary. */
+ * starting on a 16-byte boundary; d_model a multiple of 4. */
 MXMOE_API int mxmoe_combine(const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
                   uint32_t d_model, uint32_t k, const int32_t* topk_idx,
                   const int32_t* inv, const void* pair_out,
