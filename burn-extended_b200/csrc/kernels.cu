@@ -7,6 +7,7 @@
 #include <cuda_fp8.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <type_traits>
 
 #include "kernels.h"
@@ -1329,6 +1330,115 @@ __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const vo
   }
 }
 
+// The same sum for bf16 pair rows, one warp per (token, column strip): the
+// token's pairs are put in increasing expert order once (ranks by
+// comparison, no sorting loop), then each lane takes 8-column groups with
+// 16-byte loads, two groups' k rows and residuals in flight at once.  Small
+// batches spread a token's row over `slices` warps.  Needs d % 8 == 0 and
+// 16-byte aligned rows.
+__device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    v[2 * h] = __uint_as_float(w[h] << 16);
+    v[2 * h + 1] = __uint_as_float(w[h] & 0xFFFF0000u);
+  }
+}
+
+__global__ void __launch_bounds__(256) combine_rows_kernel(const void* __restrict__ x, int x_dtype,
+                                                           const __nv_bfloat16* __restrict__ y_pair,
+                                                           const int32_t* __restrict__ topk_idx,
+                                                           const int32_t* __restrict__ inv_p, int n, int d, int k,
+                                                           int residual, void* y, int y_dtype, int slices) {
+  griddep_wait();
+  const int wg = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) >> 5);
+  const int t = wg / slices, strip = wg - t * slices;
+  const int lane = threadIdx.x & 31;
+  if (t >= n) return;
+  int ex[kMaxTopK], ord[kMaxTopK];
+#pragma unroll
+  for (int s = 0; s < kMaxTopK; ++s) {
+    ex[s] = s < k ? __ldg(topk_idx + static_cast<uint64_t>(t) * k + s) : 0x7FFFFFFF;
+    ord[s] = s < k ? __ldg(inv_p + static_cast<uint64_t>(t) * k + s) : 0;
+  }
+  // row of rank r = the pair with r smaller expert ids (ties by slot keep the
+  // insertion sort's stable order)
+  uint64_t row[kMaxTopK];
+#pragma unroll
+  for (int r = 0; r < kMaxTopK; ++r) row[r] = 0;
+#pragma unroll
+  for (int s = 0; s < kMaxTopK; ++s) {
+    int rank = 0;
+#pragma unroll
+    for (int u = 0; u < kMaxTopK; ++u) rank += (ex[u] < ex[s] || (ex[u] == ex[s] && u < s)) ? 1 : 0;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r)
+      if (rank == r && s < k) row[r] = static_cast<uint64_t>(ord[s]) * d;
+  }
+  const int ng = d / 8;
+  const uint64_t xo = static_cast<uint64_t>(t) * d;
+  constexpr int U = 2;
+  const int gs = 32 * slices;  // group stride of a warp
+  for (int g0 = lane + 32 * strip; g0 < ng; g0 += gs * U) {
+    uint4 q[U][kMaxTopK];
+    float xv[U][8];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = g0 + gs * u;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) xv[u][i] = 0.0f;
+      if (g >= ng) continue;
+#pragma unroll
+      for (int r = 0; r < kMaxTopK; ++r)
+        if (r < k) q[u][r] = __ldcg(reinterpret_cast<const uint4*>(y_pair + row[r] + g * 8));
+      if (residual || k == 0) {
+        if (x_dtype == 0) {
+          const float4* xp = reinterpret_cast<const float4*>(static_cast<const float*>(x) + xo + g * 8);
+          const float4 a = __ldg(xp), b = __ldg(xp + 1);
+          xv[u][0] = a.x; xv[u][1] = a.y; xv[u][2] = a.z; xv[u][3] = a.w;
+          xv[u][4] = b.x; xv[u][5] = b.y; xv[u][6] = b.z; xv[u][7] = b.w;
+        } else {
+          bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(x) + xo + g * 8)),
+                        xv[u]);
+        }
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = g0 + gs * u;
+      if (g >= ng) continue;
+      float acc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+#pragma unroll
+      for (int r = 0; r < kMaxTopK; ++r) {
+        if (r < k) {
+          float v[8];
+          bf16x8_to_f32(q[u][r], v);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], v[i]);
+        }
+      }
+      float o[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) o[i] = k == 0 ? xv[u][i] : residual ? __fadd_rn(xv[u][i], acc[i]) : acc[i];
+      if (y_dtype == 0) {
+        float4* yp = reinterpret_cast<float4*>(static_cast<float*>(y) + xo + g * 8);
+        yp[0] = make_float4(o[0], o[1], o[2], o[3]);
+        yp[1] = make_float4(o[4], o[5], o[6], o[7]);
+      } else {
+        uint32_t w[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(o[2 * h], o[2 * h + 1]);
+          w[h] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+        *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + xo + g * 8) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ expert-parallel helpers
 // Global -> local expert ids for the receive side; ids outside the shard are
 // reported through *err (code 7) and mapped to expert 0 so indexing stays safe.
@@ -1719,6 +1829,8 @@ static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, cons
     if (re != cudaSuccess) return re;
   }
   const bool fuse = E <= kRouterGroup;
+  // large batches with the gate resident in shared memory (two or more chunks
+  // per row: the kernel's 1/rms double buffer assumes it)
   int32_t* fi = fuse ? topk_idx : nullptr;
   float* fw = fuse ? topk_w : nullptr;
   // large batches: 16 tokens x 32 experts per block (8x8 per thread);
@@ -1807,6 +1919,16 @@ cudaError_t launch_combine(const void* x, int x_dtype, const void* y_pair, int p
                            const int32_t* inv_p, int n, int d, int k, int residual, void* y, int y_dtype,
                            cudaStream_t st) {
   if (n == 0) return cudaSuccess;
+  const auto a16 = [](const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  if (pair_dtype == 1 && d % 8 == 0 && k <= kMaxTopK && a16(y_pair) && a16(y) && (x == nullptr || a16(x))) {
+    // about 2400 warps (16 per SM) in flight, at most one 32-group strip per warp
+    const int max_slices = std::max(1, (d / 8 + 31) / 32);
+    const int slices = std::min(max_slices, std::max(1, 2400 / std::max(n, 1)));
+    const uint64_t warps = static_cast<uint64_t>(n) * slices;
+    return launch_kernel(combine_rows_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), 0, st, x, x_dtype,
+                         static_cast<const __nv_bfloat16*>(y_pair), topk_idx, inv_p, n, d, k, residual, y, y_dtype,
+                         slices);
+  }
   return launch_kernel(combine_kernel, dim3(n), dim3(256), 0, st, x, x_dtype, y_pair, pair_dtype, topk_idx, inv_p, n, d,
                        k, residual, y, y_dtype);
 }
