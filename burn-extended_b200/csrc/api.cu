@@ -1092,9 +1092,16 @@ static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, voi
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[0], st));
   // the dequant-GEMV stages the router's normalized f16 token rows
   __half* xh = tp.gemv ? w.xh : nullptr;
+  // small batches on tensor-core tiles: the router's last block also runs the
+  // permutation (its ticket is a status word the memset above cleared)
+  const int pad = tp.fp4 ? tp.pair_tile : kRowBlock;
+  const bool fold = !tp.gemv && router_folds_permute(static_cast<int>(n_tokens), static_cast<int>(L->d),
+                                                     static_cast<int>(L->E_total), static_cast<int>(k));
+  const PermFold pf{L->err + kStatusSyncOffset, pad, tp.pair_tile, w.offsets, w.perm_c, w.inv_c, w.poff, w.counts,
+                    w.ntile_prefix, w.perm_p, w.inv_p};
   CUDA_TRY(launch_router(x, x_dtype, n_tokens, L->d, L->E_total, k, L->gamma, L->gate_w, L->gate_b, L->cfg.rms_eps,
                          w.logits, w.topk_idx, w.topk_w, w.rscale, st, xh, L->dq_x_scale, w.tok_ctr,
-                         tp.gemv ? L->err : nullptr, status_words));
+                         tp.gemv ? L->err : nullptr, status_words, fold ? &pf : nullptr));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[1], st));
   if (tp.gemv) {
     // router -> one fused kernel (expert FFN, combine, routing maps)
@@ -1102,9 +1109,9 @@ static int forward_chain(mxmoe_layer* L, const void* x, mxmoe_dtype x_dtype, voi
     TRY(run_dqgemv(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, w.topk_idx, nullptr, st, xh, y, y_dtype));
     return MXMOE_OK;
   }
-  CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, tp.fp4 ? tp.pair_tile : kRowBlock, tp.pair_tile,
-                          w.offsets, w.perm_c,
-                          w.inv_c, w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
+  if (!fold)
+    CUDA_TRY(launch_permute(w.topk_idx, static_cast<int>(P), E, pad, tp.pair_tile, w.offsets, w.perm_c, w.inv_c,
+                            w.poff, w.counts, w.ntile_prefix, w.perm_p, w.inv_p, st, w.perm_scratch));
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[2], st));
   TRY(run_experts(L, x, x_dtype, n_tokens, k, w.rscale, w.topk_w, tp, xt, st));
   const int residual = (L->cfg.flags & MXMOE_FLAG_NO_RESIDUAL) ? 0 : 1;

@@ -422,12 +422,15 @@ __global__ void __launch_bounds__(kRouterThreads)
 // independent loads: the step is latency-bound at these sizes.
 constexpr int kRouterSmallMaxN = 512;
 constexpr int kRouterSmallMaxD = 8192;
+__device__ void permute_block(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
+                              int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
+                              int32_t* perm_p, int32_t* inv_p, int32_t* cnt);
 template <typename XT>
 __global__ void __launch_bounds__(1024)
     router_small_kernel(const XT* __restrict__ x, int n, int d, int E, int k, const float* __restrict__ gamma,
                         const float* __restrict__ gate_packed, const float* __restrict__ gate_b, float eps,
                         float* __restrict__ logits_out, int32_t* __restrict__ topk_idx, float* __restrict__ topk_w,
-                        float* __restrict__ rscale, int x_aligned) {
+                        float* __restrict__ rscale, int x_aligned, PermFold pf) {
   const int C = kRouterChunk;
   const int nch = (d + C - 1) / C;
   extern __shared__ __align__(16) float router_small_smem[];
@@ -512,6 +515,20 @@ __global__ void __launch_bounds__(1024)
     const float v[1] = {lane < E ? lg_s[lane] : 0.0f};
     warp_topk_softmax<1>(v, E, k, lane, topk_idx + static_cast<uint64_t>(t) * k, topk_w + static_cast<uint64_t>(t) * k);
   }
+  if (pf.ticket == nullptr) return;
+  // Folded permutation: the block that takes the last ticket sorts all pairs
+  // (every block's top-k row is visible by then: its writers fence before the
+  // block's ticket, the last block fences after it).
+  __shared__ int last;
+  if (warp == 0) __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) last = atomicAdd(pf.ticket, 1) == static_cast<int>(gridDim.x) - 1 ? 1 : 0;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  permute_block(topk_idx, n * k, E, pf.pad, pf.N, pf.offsets, pf.perm_c, pf.inv_c, pf.poff, pf.counts,
+                pf.ntile_prefix, pf.perm_p, pf.inv_p, reinterpret_cast<int32_t*>(router_small_smem));
+  if (threadIdx.x == 0) *pf.ticket = 0;
 }
 
 // Tiny batches (decode, at most kRouterTinyMaxN tokens, d <= 4096): the
@@ -662,7 +679,8 @@ __device__ __forceinline__ void stage_expert_ids(const int32_t* __restrict__ top
 #pragma unroll
   for (int b = 0; b < kPermBatch; ++b) {
     const int p = base0 + 32 * b + lane;
-    const int id = p < p_end ? __ldg(topk_idx + p) : -1;
+    // (coherent loads: the router that folds the permutation in wrote the ids in the same launch)
+    const int id = p < p_end ? __ldcg(topk_idx + p) : -1;
     v[b] = id >= 0 && id < E ? id : -1;  // ids outside [0, E) are absent from the maps
   }
   __syncwarp();  // the previous batch is consumed
@@ -671,12 +689,12 @@ __device__ __forceinline__ void stage_expert_ids(const int32_t* __restrict__ top
   __syncwarp();
 }
 
-__global__ void __launch_bounds__(kPermThreads)
-    permute_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
-                   int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
-                   int32_t* perm_p, int32_t* inv_p) {
-  griddep_wait();
-  extern __shared__ int32_t cnt[];  // [32 warps][E], canonical and padded starts [E] each, staging
+// The counting sort of one block of kPermThreads threads; cnt: shared
+// memory of permute_smem_ints(E) ints.
+__device__ void permute_block(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
+                              int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
+                              int32_t* perm_p, int32_t* inv_p, int32_t* cnt) {
+  // cnt: [32 warps][E], canonical and padded starts [E] each, staging
   int32_t* cstart = cnt + 32 * E;
   int32_t* pstart = cstart + E;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -802,6 +820,15 @@ __global__ void __launch_bounds__(kPermThreads)
       __syncwarp();
     }
   }
+}
+
+__global__ void __launch_bounds__(kPermThreads)
+    permute_kernel(const int32_t* __restrict__ topk_idx, int P, int E, int pad, int N, int32_t* offsets,
+                   int32_t* perm_c, int32_t* inv_c, int32_t* poff, int32_t* counts, int32_t* ntile_prefix,
+                   int32_t* perm_p, int32_t* inv_p) {
+  griddep_wait();
+  extern __shared__ int32_t perm_smem[];
+  permute_block(topk_idx, P, E, pad, N, offsets, perm_c, inv_c, poff, counts, ntile_prefix, perm_p, inv_p, perm_smem);
 }
 
 // Multi-block form of the same permutation for large pair counts: chunks of
@@ -1333,7 +1360,7 @@ __global__ void combine_kernel(const void* __restrict__ x, int x_dtype, const vo
 // The same sum for bf16 pair rows, one warp per (token, column strip): the
 // token's pairs are put in increasing expert order once (ranks by
 // comparison, no sorting loop), then each lane takes 8-column groups with
-// 16-byte loads, two groups' k rows and residuals in flight at once.  Small
+// 16-byte loads, U groups' k rows and residuals in flight at once.  Small
 // batches spread a token's row over `slices` warps.  Needs d % 8 == 0 and
 // 16-byte aligned rows.
 __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
@@ -1345,7 +1372,8 @@ __device__ __forceinline__ void bf16x8_to_f32(uint4 u, float (&v)[8]) {
   }
 }
 
-__global__ void __launch_bounds__(256) combine_rows_kernel(const void* __restrict__ x, int x_dtype,
+template <int KM, int U>
+__global__ void __launch_bounds__(256, KM <= 4 ? 3 : 2) combine_rows_kernel(const void* __restrict__ x, int x_dtype,
                                                            const __nv_bfloat16* __restrict__ y_pair,
                                                            const int32_t* __restrict__ topk_idx,
                                                            const int32_t* __restrict__ inv_p, int n, int d, int k,
@@ -1355,32 +1383,31 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(const void* __restric
   const int t = wg / slices, strip = wg - t * slices;
   const int lane = threadIdx.x & 31;
   if (t >= n) return;
-  int ex[kMaxTopK], ord[kMaxTopK];
+  int ex[KM], ord[KM];
 #pragma unroll
-  for (int s = 0; s < kMaxTopK; ++s) {
+  for (int s = 0; s < KM; ++s) {
     ex[s] = s < k ? __ldg(topk_idx + static_cast<uint64_t>(t) * k + s) : 0x7FFFFFFF;
     ord[s] = s < k ? __ldg(inv_p + static_cast<uint64_t>(t) * k + s) : 0;
   }
   // row of rank r = the pair with r smaller expert ids (ties by slot keep the
   // insertion sort's stable order)
-  uint64_t row[kMaxTopK];
+  uint64_t row[KM];
 #pragma unroll
-  for (int r = 0; r < kMaxTopK; ++r) row[r] = 0;
+  for (int r = 0; r < KM; ++r) row[r] = 0;
 #pragma unroll
-  for (int s = 0; s < kMaxTopK; ++s) {
+  for (int s = 0; s < KM; ++s) {
     int rank = 0;
 #pragma unroll
-    for (int u = 0; u < kMaxTopK; ++u) rank += (ex[u] < ex[s] || (ex[u] == ex[s] && u < s)) ? 1 : 0;
+    for (int u = 0; u < KM; ++u) rank += (ex[u] < ex[s] || (ex[u] == ex[s] && u < s)) ? 1 : 0;
 #pragma unroll
-    for (int r = 0; r < kMaxTopK; ++r)
+    for (int r = 0; r < KM; ++r)
       if (rank == r && s < k) row[r] = static_cast<uint64_t>(ord[s]) * d;
   }
   const int ng = d / 8;
   const uint64_t xo = static_cast<uint64_t>(t) * d;
-  constexpr int U = 2;
   const int gs = 32 * slices;  // group stride of a warp
   for (int g0 = lane + 32 * strip; g0 < ng; g0 += gs * U) {
-    uint4 q[U][kMaxTopK];
+    uint4 q[U][KM];
     float xv[U][8];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
@@ -1389,7 +1416,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(const void* __restric
       for (int i = 0; i < 8; ++i) xv[u][i] = 0.0f;
       if (g >= ng) continue;
 #pragma unroll
-      for (int r = 0; r < kMaxTopK; ++r)
+      for (int r = 0; r < KM; ++r)
         if (r < k) q[u][r] = __ldcg(reinterpret_cast<const uint4*>(y_pair + row[r] + g * 8));
       if (residual || k == 0) {
         if (x_dtype == 0) {
@@ -1411,7 +1438,7 @@ __global__ void __launch_bounds__(256) combine_rows_kernel(const void* __restric
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
 #pragma unroll
-      for (int r = 0; r < kMaxTopK; ++r) {
+      for (int r = 0; r < KM; ++r) {
         if (r < k) {
           float v[8];
           bf16x8_to_f32(q[u][r], v);
@@ -1790,6 +1817,13 @@ static cudaError_t launch_router_tile(const XT* x, int n, int d, int E, int k, c
                        aligned, k, topk_idx, topk_w);
 }
 
+size_t permute_smem_ints(int E) { return static_cast<size_t>(34) * E + 32 * 32 * kPermBatch; }
+
+bool router_folds_permute(int n, int d, int E, int k) {
+  return n > kRouterTinyMaxN && n <= kRouterSmallMaxN && E <= kRouterGroup && d <= kRouterSmallMaxD &&
+         static_cast<int64_t>(n) * k < kPermMultiBlockMin;
+}
+
 // rms_kernel, then the logits; with E <= 32 the logits blocks hold every
 // expert of their tokens and also write top-k + softmax, else a separate
 // top-k kernel follows.
@@ -1797,7 +1831,8 @@ template <typename XT>
 static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, const float* gamma,
                                    const float* gate_packed, const float* gate_b, float eps, float* logits,
                                    int32_t* topk_idx, float* topk_w, float* rscale, __half* xh, float xh_scale,
-                                   int* tok_ctr, int* status, int status_words, cudaStream_t st) {
+                                   int* tok_ctr, int* status, int status_words, cudaStream_t st,
+                                   const PermFold* fold) {
   const int aligned = (reinterpret_cast<uintptr_t>(x) % 16 == 0) && ((static_cast<size_t>(d) * sizeof(XT)) % 16 == 0);
   if (tok_ctr != nullptr && n <= kRouterTinyMaxN && d <= 32 * kRouterChunk) {
     const size_t smem = static_cast<size_t>(d) * sizeof(float) + (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16;
@@ -1815,13 +1850,20 @@ static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, cons
     return go(router_tiny_kernel<XT, 32>);
   }
   if (n <= kRouterSmallMaxN && E <= kRouterGroup && d <= kRouterSmallMaxD) {
-    const size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float) +
-                        (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16 + static_cast<size_t>(d) * sizeof(float);
+    size_t smem = static_cast<size_t>((d + kRouterChunk - 1) / kRouterChunk) * kRouterChunk * sizeof(float) +
+                  (static_cast<size_t>(d) * sizeof(XT) + 15) / 16 * 16 + static_cast<size_t>(d) * sizeof(float);
+    PermFold pf{};
+    if (fold != nullptr && router_folds_permute(n, d, E, k)) {
+      pf = *fold;
+      smem = std::max(smem, permute_smem_ints(E) * sizeof(int32_t));
+    }
     const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(router_small_kernel<XT>), smem);
     if (ce != cudaSuccess) return ce;
-    // one warp per expert, and at least 8 warps to stage and normalize the row
-    return launch_kernel(router_small_kernel<XT>, dim3(n), dim3(32 * (E < 8 ? 8 : E)), smem, st,
-                         x, n, d, E, k, gamma, gate_packed, gate_b, eps, logits, topk_idx, topk_w, rscale, aligned);
+    // one warp per expert, and at least 8 warps to stage and normalize the
+    // row; a block that may run the permutation has the sort's 1024 threads
+    const int threads = pf.ticket != nullptr ? kPermThreads : 32 * (E < 8 ? 8 : E);
+    return launch_kernel(router_small_kernel<XT>, dim3(n), dim3(threads), smem, st, x, n, d, E, k, gamma, gate_packed,
+                         gate_b, eps, logits, topk_idx, topk_w, rscale, aligned, pf);
   }
   {
     const cudaError_t re = launch_kernel(rms_kernel<XT>, dim3((n + 7) / 8), dim3(256), 0, st, x, n, d, eps, rscale,
@@ -1847,14 +1889,14 @@ static cudaError_t launch_router_x(const XT* x, int n, int d, int E, int k, cons
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st, __half* xh, float xh_scale, int* tok_ctr,
-                          int* status, int status_words) {
+                          int* status, int status_words, const PermFold* fold) {
   if (n == 0) return cudaSuccess;
   return x_dtype == 0 ? launch_router_x(static_cast<const float*>(x), n, d, E, k, gamma, gate_packed, gate_b, eps,
                                         logits, topk_idx, topk_w, rscale, xh, xh_scale, tok_ctr, status, status_words,
-                                        st)
+                                        st, fold)
                       : launch_router_x(static_cast<const __nv_bfloat16*>(x), n, d, E, k, gamma, gate_packed, gate_b,
                                         eps, logits, topk_idx, topk_w, rscale, xh, xh_scale, tok_ctr, status,
-                                        status_words, st);
+                                        status_words, st, fold);
 }
 
 size_t permute_scratch_ints(int P, int E) {
@@ -1882,7 +1924,7 @@ cudaError_t launch_permute(const int32_t* topk_idx, int P, int E, int pad, int N
     return launch_kernel(perm_scatter_kernel, dim3(nch), dim3(kPermChunkThreads), ssmem, st, topk_idx, P, E, scratch,
                          perm_c, inv_c, perm_p, inv_p);
   }
-  const size_t smem = (static_cast<size_t>(34) * E + 32 * 32 * kPermBatch) * sizeof(int32_t);
+  const size_t smem = permute_smem_ints(E) * sizeof(int32_t);
   {
     const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(permute_kernel), smem);
     if (ce != cudaSuccess) return ce;
@@ -1925,7 +1967,9 @@ cudaError_t launch_combine(const void* x, int x_dtype, const void* y_pair, int p
     const int max_slices = std::max(1, (d / 8 + 31) / 32);
     const int slices = std::min(max_slices, std::max(1, 2400 / std::max(n, 1)));
     const uint64_t warps = static_cast<uint64_t>(n) * slices;
-    return launch_kernel(combine_rows_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), 0, st, x, x_dtype,
+    // top-k <= 4 (GPT-OSS): smaller rank arrays, three blocks per SM
+    const auto fn = k <= 4 ? combine_rows_kernel<4, 2> : combine_rows_kernel<kMaxTopK, 2>;
+    return launch_kernel(fn, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), 0, st, x, x_dtype,
                          static_cast<const __nv_bfloat16*>(y_pair), topk_idx, inv_p, n, d, k, residual, y, y_dtype,
                          slices);
   }

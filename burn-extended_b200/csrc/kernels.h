@@ -40,10 +40,24 @@ inline void pack_router_gate(const float* w, int E, int d, float* out) {
 // With tok_ctr ([n] ints, zero; the kernel leaves them zero) batches of at
 // most 8 tokens run on many blocks per token (router_tiny_kernel), which
 // also zeroes status[0 .. status_words) when status is given.
+// The permutation folded into the small-batch router (router_folds_permute):
+// the router block that finishes last, by an atomic ticket on *ticket (zero
+// before the launch), runs launch_permute's one-block counting sort over all
+// n * k pairs with these outputs and arguments.
+struct PermFold {
+  int* ticket;
+  int pad, N;
+  int32_t *offsets, *perm_c, *inv_c, *poff, *counts, *ntile_prefix, *perm_p, *inv_p;
+};
+// Whether launch_router with a PermFold runs the permutation for this shape
+// (the small-batch router without token rows for the dequant-GEMV, and a
+// one-block permutation).
+bool router_folds_permute(int n, int d, int E, int k);
 cudaError_t launch_router(const void* x, int x_dtype, int n, int d, int E, int k, const float* gamma,
                           const float* gate_packed, const float* gate_b, float eps, float* logits, int32_t* topk_idx,
                           float* topk_w, float* rscale, cudaStream_t st, __half* xh = nullptr, float xh_scale = 1.0f,
-                          int* tok_ctr = nullptr, int* status = nullptr, int status_words = 0);
+                          int* tok_ctr = nullptr, int* status = nullptr, int status_words = 0,
+                          const PermFold* fold = nullptr);
 // Canonical permutation.  With scratch (permute_scratch_ints(P, E) int32,
 // zeroed once before first use) and P >= kPermMultiBlockMin it runs on many
 // blocks; otherwise on one block with no scratch.
