@@ -304,6 +304,9 @@ struct mxmoe_layer {
     void* ctx = nullptr;
   } epa;
   cudaEvent_t ev[8] = {};
+  // expert-parallel return of W2's first expert half (run_experts with a ReturnSplit)
+  cudaStream_t ret_stream = nullptr;
+  cudaEvent_t ret_ev[2] = {};
 };
 
 namespace {
@@ -477,6 +480,14 @@ bool gemv_ok(const mxmoe_layer* L) {
 // Few pairs per expert (decode) with two-term activations: stacked 64-pair
 // tiles, both terms in one MMA operand, so the tensor work per weight byte is
 // halved.
+// W2 in two launches over halves of the layer's experts; once the first half
+// is done, its rows go back to their sources on a side stream while the
+// second half computes (expert-parallel step).
+struct ReturnSplit {
+  void* const* peer_ret;
+  uint32_t ret_rows;
+};
+
 struct TilePlan {
   bool tok;
   int pair_tile;
@@ -684,7 +695,7 @@ int run_dqgemv(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint3
 int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint32_t k, const float* rscale,
                 const float* route_w, const TilePlan& tp, int x_terms, cudaStream_t st,
                 void* const* ret_ptrs = nullptr, const uint32_t* ret_slot = nullptr, bool y_by_pair = false,
-                bool input_quantized = false, const int32_t* perm = nullptr) {
+                bool input_quantized = false, const int32_t* perm = nullptr, const ReturnSplit* split = nullptr) {
   Workspace& w = L->ws;
   const uint64_t P = static_cast<uint64_t>(n_tok) * k;
   const int N = tp.pair_tile;
@@ -781,8 +792,37 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   p.y_by_pair = y_by_pair ? 1 : 0;
   w.pair_dtype = MXMOE_BF16;
   grid = static_cast<int>(std::min<uint64_t>(L->num_sms, p.m_tiles * max_pair_tiles));
-  CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tp.stacked ? w.tmap_act_stk[tp.tw] : w.tmap_act[tp.tw], p, grid,
-                          st));
+  const CUtensorMap& tm_act = tp.stacked ? w.tmap_act_stk[tp.tw] : w.tmap_act[tp.tw];
+  if (split == nullptr || L->e_count < 2) {
+    CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tm_act, p, grid, st));
+    if (split != nullptr)
+      CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff, w.counts,
+                                static_cast<int>(L->e_count), w.pos_slot, static_cast<int>(L->ep_world),
+                                split->peer_ret, split->ret_rows, L->err, st));
+  } else {
+    if (!L->ret_stream) {
+      CUDA_TRY(cudaStreamCreateWithFlags(&L->ret_stream, cudaStreamNonBlocking));
+      CUDA_TRY(cudaEventCreateWithFlags(&L->ret_ev[0], cudaEventDisableTiming));
+      CUDA_TRY(cudaEventCreateWithFlags(&L->ret_ev[1], cudaEventDisableTiming));
+    }
+    const int eh = static_cast<int>(L->e_count / 2);
+    p.e_lo = 0;
+    p.e_hi = eh;
+    CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tm_act, p, grid, st));
+    CUDA_TRY(cudaEventRecord(L->ret_ev[0], st));
+    CUDA_TRY(cudaStreamWaitEvent(L->ret_stream, L->ret_ev[0], 0));
+    CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff, w.counts, eh,
+                              w.pos_slot, static_cast<int>(L->ep_world), split->peer_ret, split->ret_rows, L->err,
+                              L->ret_stream, 64));
+    CUDA_TRY(cudaEventRecord(L->ret_ev[1], L->ret_stream));
+    p.e_lo = eh;
+    p.e_hi = static_cast<int>(L->e_count);
+    CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tm_act, p, grid, st));
+    CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff + eh, w.counts + eh,
+                              static_cast<int>(L->e_count) - eh, w.pos_slot, static_cast<int>(L->ep_world),
+                              split->peer_ret, split->ret_rows, L->err, st));
+    CUDA_TRY(cudaStreamWaitEvent(st, L->ret_ev[1], 0));
+  }
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
   return MXMOE_OK;
 }
@@ -902,6 +942,9 @@ int mxmoe_destroy(mxmoe_layer* L) {
     if (e) cudaEventDestroy(e);
   if (L->graph.exec) cudaGraphExecDestroy(L->graph.exec);
   if (L->cap_stream) cudaStreamDestroy(L->cap_stream);
+  if (L->ret_stream) cudaStreamDestroy(L->ret_stream);
+  for (cudaEvent_t e : L->ret_ev)
+    if (e) cudaEventDestroy(e);
   {
     auto& h = L->hs;
     if (h.dx) cudaFree(h.dx);
@@ -1704,12 +1747,11 @@ int mxmoe_ep_experts(mxmoe_layer* L, mxmoe_dtype x_dtype, void* const* peer_ret,
                             static_cast<int>(w.rows), w.poff, w.counts, static_cast<int>(L->e_count), w.pos_rscale,
                             w.pos_weight, w.pos_slot, w.xsf, static_cast<uint64_t>(w.row_blocks) * kc1 * kSfAtomBytes,
                             static_cast<int>(kc1), tp.pair_tile, tp.stacked ? 1 : 0, st));
-  // rows are their own pairs (identity permutation, one pair per row)
+  // rows are their own pairs (identity permutation, one pair per row); W2
+  // runs in two halves and the first half's rows return while the second computes
+  const ReturnSplit split{peer_ret, ret_rows};
   TRY(run_experts(L, nullptr, x_dtype, L->ep_world * L->ep_max_tokens * L->k, 1, w.pos_rscale, w.pos_weight, tp, xt,
-                  st, nullptr, nullptr, false, true, w.iota));
-  CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff, w.counts,
-                            static_cast<int>(L->e_count), w.pos_slot, static_cast<int>(L->ep_world), peer_ret,
-                            ret_rows, L->err, st));
+                  st, nullptr, nullptr, false, true, w.iota, &split));
   return MXMOE_OK;
 }
 

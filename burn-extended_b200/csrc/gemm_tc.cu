@@ -232,15 +232,16 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
-  const int total_tiles = p.m_tiles * __ldg(p.ntile_prefix + p.E);
+  const int t_lo = p.m_tiles * __ldg(p.ntile_prefix + p.e_lo);
+  const int total_tiles = p.m_tiles * __ldg(p.ntile_prefix + (p.e_hi > 0 ? p.e_hi : p.E));
   // With a programmatic launch the setup above overlapped the previous
   // kernel.  So can the first weight boxes: the tile list comes from the
   // permutation, which completed before the previous kernel started its
   // work, and the weights never change -- prefetch them into L2, then wait
   // for the previous kernel's output (the activation operand).
-  if (kTok && warp == 0 && lane == 0 && static_cast<int>(blockIdx.x) < total_tiles) {
+  if (kTok && warp == 0 && lane == 0 && t_lo + static_cast<int>(blockIdx.x) < total_tiles) {
     int e, wt, pt;
-    decode_tile(p, blockIdx.x, e, wt, pt);
+    decode_tile(p, t_lo + static_cast<int>(blockIdx.x), e, wt, pt);
     const int nk = min(p.stages, p.k_tiles);
     for (int kt = 0; kt < nk; ++kt) tma_prefetch_3d(&tmap_w, kt * (kF4 ? 128 : kTileK), wt * 256, e);
   }
@@ -264,7 +265,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     const uint32_t tx = w_tx + terms * x_tx + kSfAtomBytes * (natoms_w + nsf_x);
     const uint64_t w_policy = kF4 ? l2_evict_first_policy() : 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+    for (int t = t_lo + static_cast<int>(blockIdx.x); t < total_tiles && ok; t += gridDim.x) {
       int e, wt, pt;
       decode_tile(p, t, e, wt, pt);
       const int row0 = __ldg(p.poff + e) + pt * PT;  // first activation row of the tile
@@ -274,7 +275,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
           ok = false;
           break;
         }
-        if (p.skip_stage && blockIdx.x == 0 && t == static_cast<int>(blockIdx.x) && kt == 0) {
+        if (p.skip_stage && blockIdx.x == 0 && t == t_lo && kt == 0) {
           // test hook: this stage is never armed; the MMA issuer's wait for it runs out
           if (++stage == S) {
             stage = 0;
@@ -364,7 +365,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     const uint32_t a_fmt = kTok ? 0u : 5u, b_fmt = kTok ? 5u : 0u;
     const uint32_t mma_n = kTok ? 256u : static_cast<uint32_t>(N);
     bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+    for (int t = t_lo + static_cast<int>(blockIdx.x); t < total_tiles && ok; t += gridDim.x) {
       if (!mbar_wait(&tmem_empty[acc], acc_phase[acc] ^ 1u, err, kDevTimeoutTmemEmpty, wait_ns)) break;
       acc_phase[acc] ^= 1u;
       tc_fence_after();
@@ -453,7 +454,7 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     uint32_t phase = 0;
     bool ok = true;
     const int mma_terms = (kTok && p.stacked) ? 1 : terms;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+    for (int t = t_lo + static_cast<int>(blockIdx.x); t < total_tiles && ok; t += gridDim.x) {
       for (int kt = 0; kt < p.k_tiles; ++kt) {
         if (!mbar_wait(&full_bar[stage], phase, err, kDevTimeoutFull, wait_ns)) {
           ok = false;
@@ -494,9 +495,9 @@ __global__ void __launch_bounds__(num_threads(kKind != 0), 1)
     // accumulator, no stores -- and runs while the first tile's MMAs do, so
     // the epilogue's long straight-line code is in the instruction cache
     // before the first real accumulator arrives.
-    for (int t = static_cast<int>(blockIdx.x) - (kTok ? static_cast<int>(gridDim.x) : 0); t < total_tiles;
+    for (int t = t_lo + static_cast<int>(blockIdx.x) - (kTok ? static_cast<int>(gridDim.x) : 0); t < total_tiles;
          t += gridDim.x) {
-      const bool dry = kTok && t < 0;
+      const bool dry = kTok && t < t_lo;
       int e = 0, wt = 0, pt = 0;
       if (!dry) {
         decode_tile(p, t, e, wt, pt);

@@ -1623,7 +1623,7 @@ __global__ void ep_return_kernel(const __nv_bfloat16* __restrict__ y, uint32_t r
   __syncthreads();
   const int pos = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (pos >= rows || pos >= seg[epr]) return;
+  if (pos >= rows || pos < seg[0] || pos >= seg[epr]) return;  // rows of this launch's experts only
   int el = 0;
   while (el + 1 < epr && seg[el + 1] <= pos) ++el;
   if (pos - seg[el] >= seg[epr + 1 + el]) return;  // padding row
@@ -2064,14 +2064,15 @@ cudaError_t launch_ep_quantize_dispatch(const void* x, int x_dtype, int n, int d
 
 cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t* poff, const int32_t* seg_counts,
                              int epr, const uint32_t* slot, int world, void* const* peer_ret, uint32_t ret_rows,
-                             int* err, cudaStream_t st) {
-  if (rows == 0) return cudaSuccess;
+                             int* err, cudaStream_t st, int threads) {
+  if (rows == 0 || epr == 0) return cudaSuccess;
+  const int wpb = threads / 32;
   const size_t smem = (2ull * epr + 1) * sizeof(int32_t);
   {
     const cudaError_t ce = ensure_dynamic_smem(reinterpret_cast<const void*>(ep_return_kernel), smem);
     if (ce != cudaSuccess) return ce;
   }
-  ep_return_kernel<<<(rows + 7) / 8, 256, smem, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
+  ep_return_kernel<<<(rows + wpb - 1) / wpb, threads, smem, st>>>(static_cast<const __nv_bfloat16*>(y_bf16),
                                                        static_cast<uint32_t>(d) * 2u, rows, poff, seg_counts, epr,
                                                        slot, world, peer_ret, ret_rows, err);
   return cudaGetLastError();

@@ -110,9 +110,11 @@ cudaError_t launch_ep_unpack(const void* meta, const uint8_t* sf_rows, uint32_t 
                              int rows, const int32_t* poff, const int32_t* seg_counts, int epr, float* rs, float* wt,
                              uint32_t* slot, uint8_t* xsf, uint64_t sf_term_stride, int kchunks, int pt, int stacked,
                              cudaStream_t st);
+// threads: block size (a warp per row); 64-thread blocks fit beside a
+// tensor-core GEMM CTA on every SM, so a return can run while a GEMM does.
 cudaError_t launch_ep_return(const void* y_bf16, int d, int rows, const int32_t* poff, const int32_t* seg_counts,
                              int epr, const uint32_t* slot, int world, void* const* peer_ret, uint32_t ret_rows,
-                             int* err, cudaStream_t st);
+                             int* err, cudaStream_t st, int threads = 256);
 cudaError_t launch_iota(int32_t* a, int n, cudaStream_t st);
 cudaError_t launch_split_meta(const uint32_t* meta, int R, float* rscale, int32_t* expert, float* weight,
                               uint32_t* slot, cudaStream_t st);

@@ -53,6 +53,9 @@ struct TcParams {
   void* const* ret_ptrs;
   const uint32_t* ret_slot;
   int y_by_pair;  // W2 output row = the pair's own index (received row) instead of its sorted position
+  // Expert range [e_lo, e_hi) of this launch (e_hi = 0: all E): its tiles are
+  // m_tiles * ntile_prefix[e_lo] .. m_tiles * ntile_prefix[e_hi], read on the device.
+  int e_lo, e_hi;
   int d;
   int* err;                 // device status word (0 = ok)
   // Test hook (mxmoe_set_fault_injection): with skip_stage set, CTA 0's
