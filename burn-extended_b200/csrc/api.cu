@@ -132,6 +132,7 @@ constexpr unsigned long long kFaultWaitNs = 1000ull * 1000ull;  // 1 ms
 
 // mxmoe_forward_host splits large batches into up to this many chunks so
 // that the copies of one chunk overlap the forward of another.
+constexpr int kReturnParts = 2;  // W2 expert ranges of the expert-parallel return overlap (4 measured slower: launch tails)
 constexpr int kHostChunksMax = 4;
 constexpr uint32_t kHostChunkMinTokens = 1024;
 
@@ -306,7 +307,7 @@ struct mxmoe_layer {
   cudaEvent_t ev[8] = {};
   // expert-parallel return of W2's first expert half (run_experts with a ReturnSplit)
   cudaStream_t ret_stream = nullptr;
-  cudaEvent_t ret_ev[2] = {};
+  cudaEvent_t ret_ev[kReturnParts + 1] = {};
 };
 
 namespace {
@@ -480,9 +481,9 @@ bool gemv_ok(const mxmoe_layer* L) {
 // Few pairs per expert (decode) with two-term activations: stacked 64-pair
 // tiles, both terms in one MMA operand, so the tensor work per weight byte is
 // halved.
-// W2 in two launches over halves of the layer's experts; once the first half
-// is done, its rows go back to their sources on a side stream while the
-// second half computes (expert-parallel step).
+// W2 in launches over up to kReturnParts ranges of the layer's experts; once
+// a range is done, its rows go back to their sources on a side stream while
+// the next range computes (expert-parallel step).
 struct ReturnSplit {
   void* const* peer_ret;
   uint32_t ret_rows;
@@ -802,26 +803,27 @@ int run_experts(mxmoe_layer* L, const void* x, int x_dtype, uint32_t n_tok, uint
   } else {
     if (!L->ret_stream) {
       CUDA_TRY(cudaStreamCreateWithFlags(&L->ret_stream, cudaStreamNonBlocking));
-      CUDA_TRY(cudaEventCreateWithFlags(&L->ret_ev[0], cudaEventDisableTiming));
-      CUDA_TRY(cudaEventCreateWithFlags(&L->ret_ev[1], cudaEventDisableTiming));
+      for (cudaEvent_t& e : L->ret_ev) CUDA_TRY(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
     }
-    const int eh = static_cast<int>(L->e_count / 2);
-    p.e_lo = 0;
-    p.e_hi = eh;
-    CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tm_act, p, grid, st));
-    CUDA_TRY(cudaEventRecord(L->ret_ev[0], st));
-    CUDA_TRY(cudaStreamWaitEvent(L->ret_stream, L->ret_ev[0], 0));
-    CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff, w.counts, eh,
-                              w.pos_slot, static_cast<int>(L->ep_world), split->peer_ret, split->ret_rows, L->err,
-                              L->ret_stream, 64));
-    CUDA_TRY(cudaEventRecord(L->ret_ev[1], L->ret_stream));
-    p.e_lo = eh;
-    p.e_hi = static_cast<int>(L->e_count);
-    CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tm_act, p, grid, st));
-    CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff + eh, w.counts + eh,
-                              static_cast<int>(L->e_count) - eh, w.pos_slot, static_cast<int>(L->ep_world),
-                              split->peer_ret, split->ret_rows, L->err, st));
-    CUDA_TRY(cudaStreamWaitEvent(st, L->ret_ev[1], 0));
+    // up to kReturnParts expert ranges; each range's rows go back on the side
+    // stream while the next range's W2 runs, only the last range's push is exposed
+    const int E = static_cast<int>(L->e_count), parts = std::min(kReturnParts, E);
+    for (int i = 0; i < parts; ++i) {
+      const int e0 = E * i / parts, e1 = E * (i + 1) / parts;
+      p.e_lo = e0;
+      p.e_hi = e1;
+      CUDA_TRY(tc_gemm_launch(tok, L->tmap_w2[tok ? 1 : 0], tm_act, p, grid, st));
+      const bool last = i == parts - 1;
+      if (!last) {
+        CUDA_TRY(cudaEventRecord(L->ret_ev[i], st));
+        CUDA_TRY(cudaStreamWaitEvent(L->ret_stream, L->ret_ev[i], 0));
+      }
+      CUDA_TRY(launch_ep_return(w.y_pair, static_cast<int>(L->d), static_cast<int>(w.rows), w.poff + e0,
+                                w.counts + e0, e1 - e0, w.pos_slot, static_cast<int>(L->ep_world), split->peer_ret,
+                                split->ret_rows, L->err, last ? st : L->ret_stream, last ? 256 : 64));
+    }
+    CUDA_TRY(cudaEventRecord(L->ret_ev[kReturnParts], L->ret_stream));
+    CUDA_TRY(cudaStreamWaitEvent(st, L->ret_ev[kReturnParts], 0));
   }
   if (L->profiling) CUDA_TRY(cudaEventRecord(L->ev[5], st));
   return MXMOE_OK;
