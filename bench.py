@@ -9,7 +9,9 @@ activations, MXFP4 weights), seeded synthetic inputs (no dataset or
 checkpoint exists here).  A step is one full layer forward (router, permute,
 W1 + SwiGLU, W2, combine).  At N > 1 each rank runs its own 8192-token batch
 with the experts sharded expert-parallel (E / N per GPU) and the routed pairs
-exchanged by NCCL all-to-all (weak scaling).
+exchanged over NVLink peer memory (weak scaling).  --workload gptoss120b_moe
+runs BASELINE configs[4] instead: 128 experts, Zipf(1.1)-skewed routing,
+4096 tokens per GPU, 128 / N experts per GPU.
 
 --impl reference times the CPU restatement of the reference's path (the
 reference's own Rust/wgpu code cannot be built or run on this box) on a
@@ -130,7 +132,8 @@ def run_reference(args, world, rank):
         return
     import oracle
     from mxmoe import synth
-    inp = synth.make_config("prefill", seed=args.seed)
+    cfg_name, data_desc = WORKLOADS[args.workload]
+    inp = synth.make_config(cfg_name, seed=args.seed)
     sample = args.ref_sample
     for _ in range(args.warmup):
         cpu_reference(inp, sample)
@@ -141,11 +144,11 @@ def run_reference(args, world, rank):
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded, BASELINE configs[3] shapes)",
-        "config": {"workload": "gptoss20b_moe_prefill", "tokens_per_step": sample, "d_model": inp.d,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": data_desc,
+        "config": {"workload": args.workload, "tokens_per_step": sample, "d_model": inp.d,
                    "ffn_hidden": inp.f, "experts": inp.E, "top_k": inp.k},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{sample} tokens of the 8192-token prefill batch per step (C oracle, OpenMP)"},
+                         "sample": f"{sample} tokens of the {inp.n}-token batch per step (C oracle, OpenMP)"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         "note": "burn-extended's MoE path is Rust + wgpu (Metal); no Rust toolchain or graphics stack exists on "
                 "this box, so the timed reference is the C restatement of its CPU semantics",
@@ -404,6 +407,13 @@ def measure_120b(args, local, dev):
             "expert_load_max_over_mean": float(load.max() / load.mean()), "experts_unused": int((load == 0).sum())}
 
 
+# workload name -> (synth config, data description)
+WORKLOADS = {
+    "gptoss20b_moe_prefill": ("prefill", "synthetic (seeded, BASELINE configs[3] shapes)"),
+    "gptoss120b_moe": ("gptoss120b", "synthetic (seeded, BASELINE configs[4] shapes, Zipf(1.1) router bias)"),
+}
+
+
 def run_ours(args, world, rank, local):
     import torch
     import mxmoe
@@ -432,7 +442,8 @@ def run_ours(args, world, rank, local):
         return
 
     # one model on every rank (seeded once); each rank routes its own tokens
-    inp = synth.make_config("prefill", seed=args.seed)
+    cfg_name, data_desc = WORKLOADS[args.workload]
+    inp = synth.make_config(cfg_name, seed=args.seed)
     if world > 1:
         inp = synth.rank_tokens(inp, rank, args.seed)
     n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
@@ -508,10 +519,10 @@ def run_ours(args, world, rank, local):
             line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
                     "vs_baseline": None, "dtype": "e2m1 x e4m3(2 terms), f32 accum",
-                    "data": "synthetic (seeded, BASELINE configs[3] shapes)",
-                    "config": {"workload": "gptoss20b_moe_prefill", "tokens_per_gpu": n, "experts": E,
+                    "data": data_desc,
+                    "config": {"workload": args.workload, "tokens_per_gpu": n, "experts": E,
                                "experts_per_gpu": E // world, "top_k": k, "parallelism": f"ep{world}",
-                               "l2": "working set > 126 MB L2 (expert weights alone 423 MB)"},
+                               "l2": "working set > 126 MB L2 (expert weights alone 423 MB per 32 experts)"},
                     "e2e": e2e, "clocks": clocks, "stages_ms": stages,
                     "gpu_launches": runner.launches_per_step * args.steps}
             print(json.dumps(line), flush=True)
@@ -541,7 +552,8 @@ def run_ours(args, world, rank, local):
                 "peak_source": f"{peak_src} bf16 burst (kernel timed alone)",
                 "frac_of_mxf4_peak": achieved / (4.0 * tc_burst),
                 "mxf4_peak_source": f"4 x {peak_src} bf16 burst (nominal MXF4 : bf16 dense = 9 : 2.25)",
-                "traffic": W1_PREFILL_TRAFFIC, "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
+                "traffic": W1_PREFILL_TRAFFIC if args.workload == "gptoss20b_moe_prefill" else None,
+                "traffic_source": "ncu dram__bytes_read.sum + dram__bytes_write.sum "
                 "of one W1 launch (profiles/tc_moe_gemm_prefill_gptoss20b.txt)",
                 "flops_per_launch": w1_flops}
     layer_flops = w1_flops + w2_flops
@@ -564,8 +576,9 @@ def run_ours(args, world, rank, local):
     e2e = {"value": n / e2e_s, "unit": UNIT, "h2d_bytes_per_step": xh.numel() * xh.element_size(),
            "d2h_bytes_per_step": yh.numel() * yh.element_size()}
 
-    extra["decode"] = measure_decode(args, local, dev, hbm_peak)
-    if args.only == "all":
+    if args.workload == "gptoss20b_moe_prefill":
+        extra["decode"] = measure_decode(args, local, dev, hbm_peak)
+    if args.only == "all" and args.workload == "gptoss20b_moe_prefill":
         extra["decode_batches"] = measure_decode_batches(args, local, dev, hbm_peak)
         extra["microbench"] = measure_microbench(args, local, dev, hbm_peak)
         extra["gptoss120b"] = measure_120b(args, local, dev)
@@ -577,14 +590,14 @@ def run_ours(args, world, rank, local):
         cpu_reference(inp, 2)
         dt = cpu_reference(inp, sample)
         cpu = {"value": sample / dt, "unit": UNIT, "cores": oracle.num_threads(), "kind": "port",
-               "sample": f"{sample} tokens of the 8192-token prefill batch (C oracle, OpenMP, all host threads)"}
+               "sample": f"{sample} tokens of the {n}-token batch (C oracle, OpenMP, all host threads)"}
 
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e2m1 x e4m3(2 terms), f32 accum",
-        "data": "synthetic (seeded, BASELINE configs[3] shapes)",
-        "config": {"workload": "gptoss20b_moe_prefill", "tokens": n, "d_model": d, "ffn_hidden": f, "experts": E,
+        "data": data_desc,
+        "config": {"workload": args.workload, "tokens": n, "d_model": d, "ffn_hidden": f, "experts": E,
                    "top_k": k, "parallelism": "ep1",
                    "l2": "inputs+weights > 126 MB L2 (expert weights alone 423 MB); no flush"},
         "roofline": roofline, "cpu_baseline": cpu, "e2e": e2e, "clocks": clocks, "stages_ms": stages,
@@ -604,6 +617,9 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=24)
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", choices=list(WORKLOADS), default="gptoss20b_moe_prefill",
+                    help="gptoss20b_moe_prefill (configs[3], the headline) or gptoss120b_moe (configs[4]: 128 "
+                         "experts, Zipf-skewed routing, 4096 tokens per GPU; expert-parallel at N > 1)")
     ap.add_argument("--only", choices=["all", "prefill", "decode", "decode_batches", "microbench", "gptoss120b", "attention"],
                     default="all",
                     help="run only that leg (profiling runs); 'all' adds decode, microbench and gptoss120b as extras")

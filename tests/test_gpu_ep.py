@@ -99,15 +99,18 @@ def test_peer_dispatch_emulated_on_one_gpu(world, n_per, E, k, flags):
     full.close()
 
 
-@pytest.mark.parametrize("world,n_per,E,k", [(2, 100, 8, 4), (4, 64, 8, 2), (4, 300, 16, 4), (2, 40, 4, 2)])
-def test_quantized_dispatch_emulated_on_one_gpu(world, n_per, E, k):
+@pytest.mark.parametrize("world,n_per,E,k,zipf", [(2, 100, 8, 4, None), (4, 64, 8, 2, None), (4, 300, 16, 4, None),
+                                                  (2, 40, 4, 2, None), (4, 96, 128, 4, 1.1), (8, 48, 128, 4, 1.1)])
+def test_quantized_dispatch_emulated_on_one_gpu(world, n_per, E, k, zipf):
     """Quantized dispatch into the owners' layouts with `world` ranks emulated
     on one GPU (each rank its own layer and workspace; the pointer tables
     stand in for the IPC-opened peers).  Every rank's output must match the
-    single-layer forward."""
+    single-layer forward.  The 128-expert cases carry the Zipf(1.1) router
+    bias of the GPT-OSS-120B-shaped workload: owners get very uneven loads and
+    some experts none."""
     import torch
     from mxmoe.ep import QuantizedPeerMoe
-    inp = synth.make_inputs(512, 384, E, k, world * n_per, True, seed=41 + world + E)
+    inp = synth.make_inputs(512, 384, E, k, world * n_per, True, seed=41 + world + E, zipf_router_bias=zipf)
     full = make_layer(inp)
     x_all = to_device_x(inp)
     cfg = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k)
