@@ -449,7 +449,13 @@ def run_ours(args, world, rank, local):
     n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
     if world > 1:
         from mxmoe import ep
-        runner = ep.build_quantized_peer_rank(inp, world, rank, dev)
+        placement = None
+        if args.workload == "gptoss120b_moe":
+            # skewed routing: load-balanced expert placement from the router
+            # loads of one seeded calibration batch, the same on every rank
+            cal = synth.rank_tokens(inp, 0, args.seed + 1)
+            placement = ep.balanced_placement(ep.expert_loads(cal.x, cal.gamma, cal.gate_w, cal.gate_b, k), world)
+        runner = ep.build_quantized_peer_rank(inp, world, rank, dev, placement=placement)
         step = lambda x: runner.forward(x)  # noqa: E731
         x = torch.from_numpy(inp.x).to(torch.bfloat16).to(dev)
     else:
@@ -522,6 +528,8 @@ def run_ours(args, world, rank, local):
                     "data": data_desc,
                     "config": {"workload": args.workload, "tokens_per_gpu": n, "experts": E,
                                "experts_per_gpu": E // world, "top_k": k, "parallelism": f"ep{world}",
+                               "placement": "contiguous" if placement is None else
+                               "load-balanced (greedy on the router loads of a seeded calibration batch)",
                                "l2": "working set > 126 MB L2 (expert weights alone 423 MB per 32 experts)"},
                     "e2e": e2e, "clocks": clocks, "stages_ms": stages,
                     "gpu_launches": runner.launches_per_step * args.steps}

@@ -46,6 +46,55 @@ def slice_host(host: MoeQuantLayerHost, begin: int, count: int) -> MoeQuantLayer
         host.w2_blocks[begin:begin + count], host.w2_scales[begin:begin + count])
 
 
+def expert_loads(x, gamma, gate_w, gate_b, k: int, rms_eps: float = 1e-5):
+    """Pairs per expert that the router (RmsNorm, gate, top-k) gives the
+    tokens x [n, d] (numpy, f32 arithmetic).  A placement heuristic only: the
+    layer's own router decides the real routing."""
+    import numpy as np
+    x = np.asarray(x, dtype=np.float32)
+    xn = x / np.sqrt(np.mean(x * x, axis=1, keepdims=True) + rms_eps) * np.asarray(gamma, dtype=np.float32)
+    logits = xn @ np.asarray(gate_w, dtype=np.float32).T + np.asarray(gate_b, dtype=np.float32)
+    top = np.argpartition(-logits, k - 1, axis=1)[:, :k]
+    return np.bincount(top.ravel(), minlength=logits.shape[1])
+
+
+def balanced_placement(loads, world: int):
+    """Expert order for load-balanced contiguous shards: rank r owns the
+    experts order[r * E / world:(r + 1) * E / world].  Greedy longest-first:
+    experts in decreasing load go to the rank with the least load that still
+    has a free slot (ties to the lower rank), so that each rank gets E / world
+    experts.  Within a rank the experts keep increasing id order."""
+    import numpy as np
+    loads = np.asarray(loads, dtype=np.float64)
+    E = loads.shape[0]
+    if E % world != 0:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    per = E // world
+    total = np.zeros(world)
+    slots = [[] for _ in range(world)]
+    for e in sorted(range(E), key=lambda i: (-loads[i], i)):
+        r = min((r for r in range(world) if len(slots[r]) < per), key=lambda r: (total[r], r))
+        slots[r].append(e)
+        total[r] += loads[e]
+    return np.array([e for r in range(world) for e in sorted(slots[r])], dtype=np.int64)
+
+
+def renumber_experts(order, gate_w, gate_b, host: MoeQuantLayerHost, b1, b2):
+    """Layer tensors with expert i of the result = expert order[i] of the
+    input: the gate rows, gate bias, MXFP4 blocks and scales and both biases
+    are permuted together.  The renumbered layer computes the same function
+    of x; only the combine's expert-order summation (and the top-k tie rule
+    between exactly equal logits) follow the new ids, so outputs agree within
+    f32 rounding.  The caller maps routing results back with order[id]."""
+    import numpy as np
+    o = np.asarray(order, dtype=np.int64)
+    if sorted(o.tolist()) != list(range(host.w1_desc.experts)):
+        raise ValueError("order must be a permutation of the experts")
+    h = MoeQuantLayerHost(host.w1_desc, host.w2_desc, host.w1_blocks[o], host.w1_scales[o], host.w2_blocks[o],
+                          host.w2_scales[o])
+    return np.asarray(gate_w)[o], np.asarray(gate_b)[o], h, np.asarray(b1)[o], np.asarray(b2)[o]
+
+
 @dataclass
 class Routed:
     rscale: object    # [n] 1 / rms per token
@@ -575,9 +624,15 @@ class QuantizedPeerMoe:
             self.own_ret = None
 
 
-def build_quantized_peer_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig] = None, group=None):
-    """QuantizedPeerMoe over libmxmoe for synthetic inputs `inp` (mxmoe.synth)."""
+def build_quantized_peer_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig] = None, group=None,
+                              placement=None):
+    """QuantizedPeerMoe over libmxmoe for synthetic inputs `inp` (mxmoe.synth).
+    placement: optional expert order (balanced_placement) applied to the
+    layer's tensors before sharding, identical on every rank."""
     cfg = cfg or MoeConfig(inp.d, inp.f, inp.E, inp.k)
     begin, count = shard_bounds(inp.E, world, rank)
-    be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    gate_w, gate_b, host, b1, b2 = inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2
+    if placement is not None:
+        gate_w, gate_b, host, b1, b2 = renumber_experts(placement, gate_w, gate_b, host, b1, b2)
+    be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, gate_w, gate_b, host, b1, b2)
     return QuantizedPeerMoe(be, world, rank, inp.n, group=group)

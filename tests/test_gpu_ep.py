@@ -110,15 +110,22 @@ def test_quantized_dispatch_emulated_on_one_gpu(world, n_per, E, k, zipf):
     some experts none."""
     import torch
     from mxmoe.ep import QuantizedPeerMoe
+    from mxmoe.ep import balanced_placement, expert_loads, renumber_experts
     inp = synth.make_inputs(512, 384, E, k, world * n_per, True, seed=41 + world + E, zipf_router_bias=zipf)
     full = make_layer(inp)
     x_all = to_device_x(inp)
     cfg = mxmoe.MoeConfig(inp.d, inp.f, inp.E, inp.k)
     rets = [torch.zeros(n_per * k, inp.d, dtype=torch.bfloat16, device="cuda:0") for _ in range(world)]
+    gate_w, gate_b, host, b1, b2 = inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2
+    if zipf is not None:
+        # skewed routing: the ranks hold load-balanced renumbered shards, the
+        # reference layer keeps the original numbering
+        order = balanced_placement(expert_loads(inp.x, inp.gamma, gate_w, gate_b, k), world)
+        gate_w, gate_b, host, b1, b2 = renumber_experts(order, gate_w, gate_b, host, b1, b2)
     ranks = []
     for r in range(world):
         b, c = shard_bounds(inp.E, world, r)
-        be = CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+        be = CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, gate_w, gate_b, host, b1, b2)
         ranks.append(QuantizedPeerMoe(be, world, r, n_per, peers=[]))
     table = [(m.local_peers()[0], rets[r].data_ptr()) for r, m in enumerate(ranks)]
     for m in ranks:

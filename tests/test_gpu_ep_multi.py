@@ -29,7 +29,7 @@ def _port():
     return p
 
 
-@pytest.mark.parametrize("world,n,E,k", [(2, 300, 8, 4), (2, 64, 4, 2), (4, 300, 8, 4), (8, 256, 32, 4)])
+@pytest.mark.parametrize("world,n,E,k", [(2, 300, 8, 4), (2, 64, 4, 2), (4, 300, 8, 4), (4, 256, 128, 4), (8, 256, 32, 4)])
 def test_quantized_peer_ep_across_gpus(world, n, E, k):
     if _gpus() < world:
         pytest.skip(f"needs {world} GPUs")
