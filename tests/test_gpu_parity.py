@@ -92,7 +92,7 @@ def test_permute_all_to_one_expert_and_empty_experts(torch):
         assert np.array_equal(g.cpu().numpy(), w)
 
 
-@pytest.mark.parametrize("name,n", [("tiny", 16), ("decode", 64), ("gptoss120b", 256)])
+@pytest.mark.parametrize("name,n", [("tiny", 16), ("decode", 64), ("gptoss120b", 256), ("prefill", 4500), ("gptoss120b", 4100)])
 def test_router_bit_exact(torch, name, n):
     inp = synth.make_config(name, seed=0, n=n)
     layer = make_layer(inp)
