@@ -449,13 +449,19 @@ def run_ours(args, world, rank, local):
     n, d, f, E, k = inp.n, inp.d, inp.f, inp.E, inp.k
     if world > 1:
         from mxmoe import ep
-        placement = None
+        placement = replicas = None
         if args.workload == "gptoss120b_moe":
-            # skewed routing: load-balanced expert placement from the router
-            # loads of one seeded calibration batch, the same on every rank
+            # skewed routing: one extra expert slot per GPU for copies of the
+            # hottest experts, then load-balanced placement of the slots, both
+            # from the router loads of one seeded calibration batch (the same
+            # on every rank)
             cal = synth.rank_tokens(inp, 0, args.seed + 1)
-            placement = ep.balanced_placement(ep.expert_loads(cal.x, cal.gamma, cal.gate_w, cal.gate_b, k), world)
-        runner = ep.build_quantized_peer_rank(inp, world, rank, dev, placement=placement)
+            loads = ep.expert_loads(cal.x, cal.gamma, cal.gate_w, cal.gate_b, k)
+            if not args.no_replicas:
+                replicas = ep.plan_replicas(loads, world)
+                loads = np.array([loads[e] / np.count_nonzero(replicas == e) for e in replicas])
+            placement = ep.balanced_placement(loads, world)
+        runner = ep.build_quantized_peer_rank(inp, world, rank, dev, placement=placement, replicas=replicas)
         step = lambda x: runner.forward(x)  # noqa: E731
         x = torch.from_numpy(inp.x).to(torch.bfloat16).to(dev)
     else:
@@ -527,9 +533,12 @@ def run_ours(args, world, rank, local):
                     "vs_baseline": None, "dtype": "e2m1 x e4m3(2 terms), f32 accum",
                     "data": data_desc,
                     "config": {"workload": args.workload, "tokens_per_gpu": n, "experts": E,
-                               "experts_per_gpu": E // world, "top_k": k, "parallelism": f"ep{world}",
+                               "experts_per_gpu": runner.E // world, "top_k": k, "parallelism": f"ep{world}",
                                "placement": "contiguous" if placement is None else
                                "load-balanced (greedy on the router loads of a seeded calibration batch)",
+                               "expert_slots": runner.E,
+                               "replicas": None if replicas is None else
+                               f"{len(replicas) - E} copies of the hottest experts, pairs split by token",
                                "l2": "working set > 126 MB L2 (expert weights alone 423 MB per 32 experts)"},
                     "e2e": e2e, "clocks": clocks, "stages_ms": stages,
                     "gpu_launches": runner.launches_per_step * args.steps}
@@ -625,6 +634,8 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=24)
     ap.add_argument("--ref-sample", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-replicas", action="store_true",
+                    help="gptoss120b_moe at N > 1: placement only, no copies of hot experts")
     ap.add_argument("--workload", choices=list(WORKLOADS), default="gptoss20b_moe_prefill",
                     help="gptoss20b_moe_prefill (configs[3], the headline) or gptoss120b_moe (configs[4]: 128 "
                          "experts, Zipf-skewed routing, 4096 tokens per GPU; expert-parallel at N > 1)")

@@ -95,6 +95,94 @@ def renumber_experts(order, gate_w, gate_b, host: MoeQuantLayerHost, b1, b2):
     return np.asarray(gate_w)[o], np.asarray(gate_b)[o], h, np.asarray(b1)[o], np.asarray(b2)[o]
 
 
+def plan_replicas(loads, extra: int):
+    """Hot-expert replication plan: `extra` additional expert slots, each a
+    copy of an existing expert, handed out greedily to the expert with the
+    largest load per copy.  Returns src, the original expert of every slot
+    (slots 0 .. E - 1 are the experts themselves, E .. E + extra - 1 the
+    copies)."""
+    import numpy as np
+    loads = np.asarray(loads, dtype=np.float64)
+    copies = np.ones(loads.shape[0], dtype=np.int64)
+    src = list(range(loads.shape[0]))
+    for _ in range(extra):
+        e = int(np.argmax(loads / copies))
+        copies[e] += 1
+        src.append(e)
+    return np.array(src, dtype=np.int64)
+
+
+def replicate_experts(src, gate_w, gate_b, host: MoeQuantLayerHost, b1, b2):
+    """Layer tensors over the slots of plan_replicas: every slot gets its
+    original expert's weights, scales and biases; copy slots get a zero gate
+    row and a gate bias of -1e30, so that the router never picks them and
+    top-k and softmax are those of the original experts.  ReplicaRemap then
+    moves part of each hot expert's pairs onto its copies."""
+    import numpy as np
+    src = np.asarray(src, dtype=np.int64)
+    E = np.asarray(gate_w).shape[0]
+    gw = np.concatenate([np.asarray(gate_w, dtype=np.float32), np.zeros((len(src) - E, gate_w.shape[1]), np.float32)])
+    gb = np.concatenate([np.asarray(gate_b, dtype=np.float32), np.full(len(src) - E, -1e30, np.float32)])
+    d1, d2 = host.w1_desc, host.w2_desc
+    h = MoeQuantLayerHost(QuantLinearMxFp4Desc(len(src), d1.rows, d1.cols, d1.bpr, d1.gpr, d1.ue8_offset),
+                          QuantLinearMxFp4Desc(len(src), d2.rows, d2.cols, d2.bpr, d2.gpr, d2.ue8_offset),
+                          host.w1_blocks[src], host.w1_scales[src], host.w2_blocks[src], host.w2_scales[src])
+    return gw, gb, h, np.asarray(b1)[src], np.asarray(b2)[src]
+
+
+class ReplicaRemap:
+    """Moves the pairs of replicated experts onto their copies after the
+    router: the pair of token t on expert e goes to copy t % c_e of e (c_e
+    copies, the expert itself first), then the canonical maps are rebuilt
+    for the remapped ids.  Stream-ordered torch and libmxmoe calls; nothing
+    waits on the host.  groups: the slot ids of each original expert, after
+    any renumbering (replica_groups)."""
+
+    def __init__(self, groups, device):
+        import torch
+        self.torch = torch
+        self.S = sum(len(g) for g in groups) if groups else 0
+        width = max(len(g) for g in groups)
+        table = torch.full((self.S, width), -1, dtype=torch.int64)
+        ncopy = torch.ones(self.S, dtype=torch.int64)
+        for g in groups:
+            for sid in g:
+                table[sid, :len(g)] = torch.tensor(g)
+                ncopy[sid] = len(g)
+        self.table = table.to(device)
+        self.ncopy = ncopy.to(device)
+
+    def apply(self, r: "Routed") -> "Routed":
+        t = self.torch
+        idx = r.topk_idx.to(t.int64)
+        n = idx.shape[0]
+        if n == 0:
+            return r
+        tok = t.arange(n, device=idx.device).unsqueeze(1)
+        new = self.table[idx, tok % self.ncopy[idx]]
+        flat = new.reshape(-1)
+        # canonical maps: pairs sorted by expert, increasing pair index within one
+        counts = t.zeros(self.S, dtype=t.int64, device=idx.device).scatter_add_(0, flat, t.ones_like(flat))
+        offsets = t.zeros(self.S + 1, dtype=t.int32, device=idx.device)
+        offsets[1:] = t.cumsum(counts, 0).to(t.int32)
+        perm = t.sort(flat, stable=True).indices
+        inv = t.empty_like(perm)
+        inv[perm] = t.arange(perm.numel(), device=idx.device)
+        return Routed(r.rscale, new.to(t.int32).contiguous(), r.topk_w, offsets, perm.to(t.int32), inv.to(t.int32))
+
+
+def replica_groups(src, order=None):
+    """Slot ids grouped by original expert, after the renumbering `order`
+    (slot i of the renumbered layer = slot order[i] before it)."""
+    import numpy as np
+    src = np.asarray(src)
+    new_of = np.arange(len(src)) if order is None else np.argsort(np.asarray(order))
+    groups = {}
+    for slot, e in enumerate(src.tolist()):
+        groups.setdefault(e, []).append(int(new_of[slot]))
+    return [groups[e] for e in sorted(groups)]
+
+
 @dataclass
 class Routed:
     rscale: object    # [n] 1 / rms per token
@@ -536,6 +624,12 @@ class QuantizedPeerMoe:
         self.peer_ret = t.tensor([table[r][1] for r in range(self.world)], dtype=t.int64, device=self.dev)
         self.ret = table[self.rank][1]
 
+    remap = None  # ReplicaRemap when hot experts are replicated
+
+    def route(self, x):
+        r = self.backend.route(x)
+        return self.remap.apply(r) if self.remap is not None else r
+
     def counts(self, r):
         o = r.offsets
         return (o[1:] - o[:-1]).to(self.torch.int32)
@@ -582,7 +676,7 @@ class QuantizedPeerMoe:
             raise ValueError(f"{x.shape[0]} tokens > max_tokens {self.max_tokens}")
         if x.dtype != self.x_dtype:
             raise ValueError(f"x dtype {x.dtype} != {self.x_dtype}")
-        r = self.backend.route(x)
+        r = self.route(x)
         allc = self.all_counts(self.counts(r))
         self.dispatch(x, r, allc)
         self.barrier()  # every pair is in its owner's layout
@@ -597,7 +691,7 @@ class QuantizedPeerMoe:
         for _ in range(steps):
             ev = [t.cuda.Event(enable_timing=True) for _ in range(6)]
             ev[0].record()
-            r = self.backend.route(x)
+            r = self.route(x)
             ev[1].record()
             allc = self.all_counts(self.counts(r))
             ev[2].record()
@@ -625,14 +719,25 @@ class QuantizedPeerMoe:
 
 
 def build_quantized_peer_rank(inp, world: int, rank: int, device, cfg: Optional[MoeConfig] = None, group=None,
-                              placement=None):
+                              placement=None, replicas=None):
     """QuantizedPeerMoe over libmxmoe for synthetic inputs `inp` (mxmoe.synth).
-    placement: optional expert order (balanced_placement) applied to the
-    layer's tensors before sharding, identical on every rank."""
-    cfg = cfg or MoeConfig(inp.d, inp.f, inp.E, inp.k)
-    begin, count = shard_bounds(inp.E, world, rank)
+    replicas: optional slot plan (plan_replicas) that copies hot experts into
+    extra slots; placement: optional order of the (slot) experts
+    (balanced_placement) applied before sharding.  Both identical on every
+    rank."""
+    from dataclasses import replace
     gate_w, gate_b, host, b1, b2 = inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2
+    S = inp.E
+    if replicas is not None:
+        gate_w, gate_b, host, b1, b2 = replicate_experts(replicas, gate_w, gate_b, host, b1, b2)
+        S = len(replicas)
+    cfg = cfg or MoeConfig(inp.d, inp.f, inp.E, inp.k)
+    cfg = replace(cfg, num_experts=S)
+    begin, count = shard_bounds(S, world, rank)
     if placement is not None:
         gate_w, gate_b, host, b1, b2 = renumber_experts(placement, gate_w, gate_b, host, b1, b2)
     be = CudaExpertBackend(cfg, device, begin, count, inp.gamma, gate_w, gate_b, host, b1, b2)
-    return QuantizedPeerMoe(be, world, rank, inp.n, group=group)
+    m = QuantizedPeerMoe(be, world, rank, inp.n, group=group)
+    if replicas is not None:
+        m.remap = ReplicaRemap(replica_groups(replicas, placement), be.device)
+    return m

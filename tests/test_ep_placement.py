@@ -59,3 +59,47 @@ def test_renumbered_layer_same_outputs():
     # the renumbered router picks the same experts under their new ids
     assert (np.sort(order[idx2], axis=1) == np.sort(idx, axis=1)).all()
     assert_close(got, want, "renumbered layer")
+
+
+def test_replica_plan_and_replicated_layer():
+    loads = np.array([100, 40, 10, 10, 0, 0, 0, 0])
+    src = ep.plan_replicas(loads, 4)
+    assert list(src[:8]) == list(range(8))
+    # copies go to the largest load per copy: 100 -> 50 -> 40 (expert 1) -> 33.3 -> ...
+    assert sorted(src[8:].tolist()) == [0, 0, 0, 1]
+    groups = ep.replica_groups(src)
+    assert sorted(sum(groups, [])) == list(range(12))
+    order = ep.balanced_placement(np.array([loads[e] / np.count_nonzero(src == e) for e in src]), 4)
+    g2 = ep.replica_groups(src, order)
+    inv = np.argsort(order)
+    assert sorted(g2[0]) == sorted(int(inv[s]) for s in np.flatnonzero(src == 0))
+    # copy slots never win the router: the replicated layer routes and computes as the original
+    inp = synth.make_inputs(128, 64, 8, 2, 24, True, seed=11, zipf_router_bias=1.1)
+    c = oracle.cfg(inp.d, inp.f, inp.E, inp.k)
+    want, idx, _ = oracle.moe_forward(c, inp.x, inp.gamma, inp.gate_w, inp.gate_b, inp.host.w1_blocks,
+                                      inp.host.w1_scales, inp.b1, inp.host.w2_blocks, inp.host.w2_scales, inp.b2)
+    src = ep.plan_replicas(ep.expert_loads(inp.x, inp.gamma, inp.gate_w, inp.gate_b, inp.k), 2)
+    gw, gb, h, b1, b2 = ep.replicate_experts(src, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    c2 = oracle.cfg(inp.d, inp.f, len(src), inp.k)
+    got, idx2, _ = oracle.moe_forward(c2, inp.x, inp.gamma, gw, gb, h.w1_blocks, h.w1_scales, b1, h.w2_blocks,
+                                      h.w2_scales, b2)
+    assert (idx2 < inp.E).all() and (idx2 == idx).all()
+    assert_close(got, want, "replicated layer")
+
+
+def test_replica_remap_gives_canonical_maps():
+    import torch
+    src = np.array([0, 1, 2, 3, 0, 0, 1, 2])
+    rm = ep.ReplicaRemap(ep.replica_groups(src), "cpu")
+    rng = np.random.default_rng(3)
+    idx = torch.from_numpy(np.stack([rng.permutation(4)[:3] for _ in range(50)]).astype(np.int32))
+    out = rm.apply(ep.Routed(None, idx, None, None, None, None))
+    new = out.topk_idx.numpy()
+    assert (src[new] == idx.numpy()).all()  # every pair stays on a copy of its expert
+    for e, n_copies in ((0, 3), (1, 2), (2, 2), (3, 1)):
+        used = np.unique(new[src[new] == e])
+        assert len(used) == n_copies
+    offs, perm, inv = oracle.permute(new, len(src))
+    assert np.array_equal(offs, out.offsets.numpy())
+    assert np.array_equal(perm, out.perm.numpy())
+    assert np.array_equal(inv, out.inv.numpy())

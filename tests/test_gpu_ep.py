@@ -145,3 +145,56 @@ def test_quantized_dispatch_emulated_on_one_gpu(world, n_per, E, k, zipf):
             want = full.forward(xs[r], out_dtype=torch.float32)
             assert_close(ys[r].cpu().numpy(), want.cpu().numpy(), f"quantized EP rank {r}/{world}")
     full.close()
+
+
+@pytest.mark.parametrize("world,n_per,E,extra", [(4, 96, 16, 4), (2, 120, 32, 2)])
+def test_replicated_hot_experts_emulated_on_one_gpu(world, n_per, E, extra):
+    """Hot experts copied into extra slots (plan_replicas), the slots placed
+    by load (balanced_placement), and each replicated expert's pairs spread
+    over its copies by token (ReplicaRemap); ranks emulated on one GPU.  Every
+    rank's output must match the original single layer."""
+    import numpy as np
+    import torch
+    from mxmoe import ep
+    k = 4
+    inp = synth.make_inputs(512, 384, E, k, world * n_per, True, seed=61 + world + E, zipf_router_bias=1.1)
+    full = make_layer(inp)
+    x_all = to_device_x(inp)
+    loads = ep.expert_loads(inp.x, inp.gamma, inp.gate_w, inp.gate_b, k)
+    src = ep.plan_replicas(loads, extra)
+    slot_loads = np.array([loads[e] / np.count_nonzero(src == e) for e in src])
+    order = ep.balanced_placement(slot_loads, world)
+    gw, gb, host, b1, b2 = ep.replicate_experts(src, inp.gate_w, inp.gate_b, inp.host, inp.b1, inp.b2)
+    gw, gb, host, b1, b2 = ep.renumber_experts(order, gw, gb, host, b1, b2)
+    S = len(src)
+    cfg = mxmoe.MoeConfig(inp.d, inp.f, S, k)
+    rets = [torch.zeros(n_per * k, inp.d, dtype=torch.bfloat16, device="cuda:0") for _ in range(world)]
+    ranks = []
+    for r in range(world):
+        b, c = shard_bounds(S, world, r)
+        be = CudaExpertBackend(cfg, "cuda:0", b, c, inp.gamma, gw, gb, host, b1, b2)
+        m = ep.QuantizedPeerMoe(be, world, r, n_per, peers=[])
+        m.remap = ep.ReplicaRemap(ep.replica_groups(src, order), "cuda:0")
+        ranks.append(m)
+    table = [(m.local_peers()[0], rets[r].data_ptr()) for r, m in enumerate(ranks)]
+    for m in ranks:
+        m.set_peers(table)
+    xs = [x_all[r * n_per:(r + 1) * n_per].contiguous() for r in range(world)]
+    for _ in range(2):
+        routes = [m.route(x) for m, x in zip(ranks, xs)]
+        # the copies receive pairs
+        cnt = sum(m.counts(rt).cpu().numpy() for m, rt in zip(ranks, routes))
+        copies = [int(np.argsort(order)[s]) for s in range(E, S)]
+        assert cnt[copies].sum() > 0
+        allc = torch.cat([m.counts(rt) for m, rt in zip(ranks, routes)])
+        for m, x, rt in zip(ranks, xs, routes):
+            m.dispatch(x, rt, allc)
+        for m in ranks:
+            m.experts()
+        ys = [m.combine(x, rt, out_dtype=torch.float32) for m, x, rt in zip(ranks, xs, routes)]
+        torch.cuda.synchronize()
+        for r in range(world):
+            ranks[r].backend.layer.sync_status()
+            want = full.forward(xs[r], out_dtype=torch.float32)
+            assert_close(ys[r].cpu().numpy(), want.cpu().numpy(), f"replicated EP rank {r}/{world}")
+    full.close()
