@@ -294,9 +294,13 @@ class ExpertParallelMoe:
         self._a2a(mr, meta, recv, send)
         return send, recv, xr, mr
 
+    remap = None  # ReplicaRemap when hot experts are replicated
+
     def forward(self, x, out_dtype=None):
         b = self.backend
         r = b.route(x)
+        if self.remap is not None:
+            r = self.remap.apply(r)
         send, recv, xr, mr = self._dispatch(x, r)
         out = b.local(xr, mr)
         back = b.empty((sum(send), x.shape[1]), out.dtype)
