@@ -35,6 +35,11 @@ W1_PREFILL_TRAFFIC = 500.8e6 + 174.2e6
 W1_DECODE_TRAFFIC = 297.2e6 + 4.4e6  # ncu dram read + write of one FP4 W1 launch (profiles/tc_moe_gemm_decode_gptoss20b.txt)
 
 METRIC = "MoE layer tokens/s (GPT-OSS-20B-shaped MXFP4 layer, prefill 8192 tokens/GPU)"
+METRIC_120B = "MoE layer tokens/s (GPT-OSS-120B-shaped MXFP4 layer, 128 experts, Zipf routing, 4096 tokens/GPU)"
+
+
+def metric_of(args):
+    return METRIC_120B if args.workload == "gptoss120b_moe" else METRIC
 UNIT = "tokens/s"
 # kernels one mxmoe_forward launches: rms, router logits, top-k, permute,
 # activation quantization, W1, W2, combine
@@ -142,7 +147,7 @@ def run_reference(args, world, rank):
     value = sample * args.steps / total
     cores = oracle.num_threads()
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "impl": "reference", "metric": metric_of(args), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": data_desc,
         "config": {"workload": args.workload, "tokens_per_step": sample, "d_model": inp.d,
@@ -528,7 +533,7 @@ def run_ours(args, world, rank, local):
                "h2d_bytes_per_step": xh.numel() * xh.element_size(),
                "d2h_bytes_per_step": yh.numel() * yh.element_size(), "per": "rank"}
         if rank == 0:
-            line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            line = {"metric": metric_of(args), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
                     "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
                     "vs_baseline": None, "dtype": "e2m1 x e4m3(2 terms), f32 accum",
                     "data": data_desc,
@@ -578,7 +583,7 @@ def run_ours(args, world, rank, local):
              "w2_tflops": w2_flops / (stages["w2_gemm"] / 1e3) / 1e12}
 
     if args.only == "prefill":
-        print(json.dumps({"metric": METRIC, "value": value, "unit": UNIT, "ms_per_step": ms_per_step,
+        print(json.dumps({"metric": metric_of(args), "value": value, "unit": UNIT, "ms_per_step": ms_per_step,
                           "stages_ms": stages, "roofline": roofline, "clocks": clocks}), flush=True)
         layer.close()
         return
@@ -610,7 +615,8 @@ def run_ours(args, world, rank, local):
                "sample": f"{sample} tokens of the {n}-token batch (C oracle, OpenMP, all host threads)"}
 
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "metric": metric_of(args), "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup,
         "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "e2m1 x e4m3(2 terms), f32 accum",
         "data": data_desc,
