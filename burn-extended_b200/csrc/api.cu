@@ -1833,4 +1833,55 @@ int mxmoe_ep_buffers(mxmoe_layer* L, void** ptrs) {
   return MXMOE_OK;
 }
 
+// Hot-expert copies: each extra slot goes to the expert with the largest load
+// per copy (lowest id on ties).
+int mxmoe_ep_plan_replicas(const double* loads, uint32_t num_experts, uint32_t extra, int32_t* src) {
+  if (num_experts == 0 || !loads || !src) return fail(MXMOE_ERR_INVALID_ARG, "bad replica plan arguments");
+  if (static_cast<uint64_t>(num_experts) + extra > INT32_MAX) return fail(MXMOE_ERR_TOO_LARGE, "too many slots");
+  std::vector<int64_t> copies(num_experts, 1);
+  for (uint32_t e = 0; e < num_experts; ++e) src[e] = static_cast<int32_t>(e);
+  for (uint32_t i = 0; i < extra; ++i) {
+    uint32_t best = 0;
+    double best_v = loads[0] / static_cast<double>(copies[0]);
+    for (uint32_t e = 1; e < num_experts; ++e) {
+      const double v = loads[e] / static_cast<double>(copies[e]);
+      if (v > best_v) {
+        best_v = v;
+        best = e;
+      }
+    }
+    ++copies[best];
+    src[num_experts + i] = static_cast<int32_t>(best);
+  }
+  return MXMOE_OK;
+}
+
+// Greedy longest-first placement into world ranks of num_experts / world slots.
+int mxmoe_ep_balanced_placement(const double* loads, uint32_t num_experts, uint32_t world, int32_t* order) {
+  if (num_experts == 0 || world == 0 || !loads || !order) return fail(MXMOE_ERR_INVALID_ARG, "bad placement arguments");
+  if (num_experts % world != 0)
+    return fail(MXMOE_ERR_INVALID_ARG, "%u experts do not split over %u ranks", num_experts, world);
+  const uint32_t per = num_experts / world;
+  std::vector<uint32_t> ids(num_experts);
+  for (uint32_t e = 0; e < num_experts; ++e) ids[e] = e;
+  std::stable_sort(ids.begin(), ids.end(), [&](uint32_t a, uint32_t b) { return loads[a] > loads[b]; });
+  std::vector<double> total(world, 0.0);
+  std::vector<std::vector<uint32_t>> slots(world);
+  for (uint32_t e : ids) {
+    uint32_t best = world;
+    for (uint32_t r = 0; r < world; ++r) {
+      if (slots[r].size() >= per) continue;
+      if (best == world || total[r] < total[best]) best = r;
+    }
+    slots[best].push_back(e);
+    total[best] += loads[e];
+  }
+  uint32_t o = 0;
+  for (uint32_t r = 0; r < world; ++r) {
+    std::sort(slots[r].begin(), slots[r].end());
+    for (uint32_t e : slots[r]) order[o++] = static_cast<int32_t>(e);
+  }
+  return MXMOE_OK;
+}
+
 }  // extern "C"

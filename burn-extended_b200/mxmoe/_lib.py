@@ -128,6 +128,8 @@ _SIGS = {
     "mxmoe_ep_attach": ([_vp, _u32, _u32, _vp, _vp, _vp, _vp, _vp], _i32),
     "mxmoe_ep_forward": ([_vp, _vp, _i32, _u32, _vp, _i32, _vp], _i32),
     "mxmoe_ep_buffers": ([_vp, _vp], _i32),
+    "mxmoe_ep_plan_replicas": ([_vp, _u32, _u32, _vp], _i32),
+    "mxmoe_ep_balanced_placement": ([_vp, _u32, _u32, _vp], _i32),
     "mxmoe_modelbin_info": ([ctypes.c_char_p, ctypes.POINTER(ModelBinHeader)], _i32),
     "mxmoe_safetensors_load_layer": ([ctypes.POINTER(ctypes.c_char_p), _u32, _u32, ctypes.POINTER(Config), _u32, _u32,
                                       _vp, ctypes.POINTER(_vp)], _i32),

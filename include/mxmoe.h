@@ -424,6 +424,22 @@ MXMOE_API int mxmoe_ep_attach(mxmoe_layer* layer, uint32_t rank, uint32_t world,
 MXMOE_API int mxmoe_ep_forward(mxmoe_layer* layer, const void* x, mxmoe_dtype x_dtype, uint32_t n_tokens,
                                void* y, mxmoe_dtype y_dtype, void* stream);
 
+/* ---- expert placement for skewed routing (host only, no device work) ----
+ * New surface: the reference is single-rank (docs/gpt-oss-architecture.md:22).
+ * mxmoe_ep_plan_replicas: `extra` copy slots handed out greedily to the
+ * expert with the largest load per copy (lowest id on ties); src[0 .. E +
+ * extra) receives the original expert of every slot (src[e] = e for e < E).
+ * mxmoe_ep_balanced_placement: expert order for contiguous shards of
+ * E / world experts: experts in decreasing load (ties to the lower id) go to
+ * the rank with the least load that has a free slot (ties to the lower rank);
+ * order[r * E / world ..] lists rank r's experts in increasing id.  The caller
+ * permutes the gate rows, gate bias, weights, scales and biases by `order`
+ * before mxmoe_set_router / mxmoe_upload_experts.  Both give the results of
+ * mxmoe.ep.plan_replicas / balanced_placement in the Python mirror. */
+MXMOE_API int mxmoe_ep_plan_replicas(const double* loads, uint32_t num_experts, uint32_t extra, int32_t* src);
+MXMOE_API int mxmoe_ep_balanced_placement(const double* loads, uint32_t num_experts, uint32_t world,
+                                          int32_t* order);
+
 /* Combine (src/moe/mod.rs:405-411): y[t] = x[t] + sum over the token's k
  * pairs in increasing expert index of pair_out[inv[t*k+s]] (pair_out in
  * permuted order, pair_dtype).  residual = 0 omits x.  Device pointers, each

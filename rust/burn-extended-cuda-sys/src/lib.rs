@@ -361,6 +361,8 @@ extern "C" {
         y_dtype: mxmoe_dtype,
         stream: *mut c_void,
     ) -> c_int;
+    pub fn mxmoe_ep_plan_replicas(loads: *const f64, num_experts: u32, extra: u32, src: *mut i32) -> c_int;
+    pub fn mxmoe_ep_balanced_placement(loads: *const f64, num_experts: u32, world: u32, order: *mut i32) -> c_int;
     pub fn mxmoe_ep_experts(
         layer: *mut mxmoe_layer,
         x_dtype: mxmoe_dtype,

@@ -103,3 +103,26 @@ def test_replica_remap_gives_canonical_maps():
     assert np.array_equal(offs, out.offsets.numpy())
     assert np.array_equal(perm, out.perm.numpy())
     assert np.array_equal(inv, out.inv.numpy())
+
+
+def test_c_abi_placement_matches_python():
+    """mxmoe_ep_plan_replicas / mxmoe_ep_balanced_placement (host-only C
+    entry points, no GPU needed) give the Python mirror's results."""
+    from mxmoe import _lib
+    lib = _lib.lib()
+    rng = np.random.default_rng(7)
+    for E, world, extra in ((128, 8, 8), (32, 4, 4), (8, 2, 0), (12, 3, 3)):
+        loads = rng.zipf(1.5, E).astype(np.float64)
+        loads[::5] = loads[1]  # ties
+        src = np.empty(E + extra, dtype=np.int32)
+        assert lib.mxmoe_ep_plan_replicas(loads.ctypes.data, E, extra, src.ctypes.data) == 0
+        assert np.array_equal(src, ep.plan_replicas(loads, extra))
+        S = E + extra
+        if S % world:
+            continue
+        sl = np.array([loads[e] / np.count_nonzero(src == e) for e in src], dtype=np.float64)
+        order = np.empty(S, dtype=np.int32)
+        assert lib.mxmoe_ep_balanced_placement(sl.ctypes.data, S, world, order.ctypes.data) == 0
+        assert np.array_equal(order, ep.balanced_placement(sl, world))
+    bad = np.empty(7, dtype=np.int32)
+    assert lib.mxmoe_ep_balanced_placement(np.ones(7).ctypes.data, 7, 2, bad.ctypes.data) != 0
